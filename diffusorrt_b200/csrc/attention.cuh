@@ -1,0 +1,323 @@
+// Prefix-KV attention for block diffusion on the 5th-generation tensor cores.
+//
+// Semantics follow the reference SDPA (python/src/edllm/backends/mlx_ops.py:347-443) with the
+// d2f_hybrid additive mask (mlx_ops.py:191-288, graph/numpyref.py:167-233): with
+// eff(p) = -1 if p < prompt_len else (p - prompt_len) // block_size, query position q sees key
+// position k iff eff(k) <= eff(q); "bidirectional" sees every key < kv_len. BD3 uses
+// prompt_len = 0, so every 32-token block attends to itself and all earlier blocks.
+//
+// Work unit: one KV head g, one query tile and one slice of the keys. The query tile packs
+// `rep` = nq/nkv query heads x P positions as the M = 128 rows of the UMMA (row r = position
+// r / rep, head g*rep + r % rep), so GQA needs no K/V duplication. Per 128-key tile:
+//   S = Q K^T       (tcgen05.mma, A = Q tile [128 x 128d], B = K tile [128 keys x 128d], TMEM)
+//   P = softmax     (one thread per row: online max/sum in the log2 domain, P as bf16 in smem)
+//   O_t = P V       (tcgen05.mma, A = P [128 x 128 keys], B = V^T tile [128d x 128 keys])
+//   o = o * alpha + O_t in registers.
+// K is cached as [nkv][pos][128] and V transposed as [nkv][128][pos], so both B operands are
+// K-major 128-byte-swizzled TMA tiles. With splits > 1 each CTA leaves (o, m, l) partials and
+// attn_combine_kernel merges them in a fixed order.
+#pragma once
+#include "common.cuh"
+
+namespace drt {
+
+struct AttnArgs {
+  int nq, nkv, rep;       // query heads, kv heads, nq / nkv
+  int tile_pos;           // query positions per tile (P); rep * P <= 128
+  int rows;               // query rows (positions) covered by the grid
+  const int* rows_dev;    // optional device-side row count
+  int q_pos0;             // absolute position of query row 0
+  const int* q_pos0_dev;
+  int kv_len;             // keys [0, kv_len) are valid
+  const int* kv_len_dev;
+  int prompt_len, block_size, bidirectional;
+  int kv_plane0;          // first plane of this layer in the [L*nkv] cache planes
+  int splits, tiles_per_split;
+  __nv_bfloat16* out;     // [rows][nq*128] (splits == 1)
+  float* ws_o;            // [splits][rows][nq][128]
+  float* ws_ml;           // [splits][rows][nq][2]
+  int* status;
+  float scale_log2;       // log2(e) / sqrt(head_dim)
+};
+
+__device__ __forceinline__ int attn_limit(const AttnArgs& a, int q_pos, int kv_len) {
+  if (a.bidirectional) return kv_len;
+  int lim;
+  if (q_pos < a.prompt_len) lim = a.prompt_len;
+  else lim = a.prompt_len + ((q_pos - a.prompt_len) / a.block_size + 1) * a.block_size;
+  return min(lim, kv_len);
+}
+
+constexpr int kAttnQBytes = 2 * 128 * 128;     // two 64-column atoms x 128 rows
+constexpr int kAttnKBytes = 2 * 128 * 128;     // 128 keys x 128 d
+constexpr int kAttnVBytes = 2 * 128 * 128;     // 128 d x 128 keys
+constexpr int kAttnStageBytes = kAttnKBytes + kAttnVBytes;
+constexpr int kAttnPBytes = 2 * 128 * 128;
+constexpr int kAttnStages = 2;
+constexpr size_t kAttnSmemBytes = 1024 + kAttnQBytes + kAttnStages * kAttnStageBytes + kAttnPBytes + 256;
+
+__global__ void __launch_bounds__(128, 1)
+    attn_prefix_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + kAttnQBytes;
+  uint8_t* sP = sKV + kAttnStages * kAttnStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kAttnPBytes);
+  uint64_t* barQ = bars;
+  uint64_t* fullKV = bars + 1;  // [kAttnStages]
+  uint64_t* barS = bars + 1 + kAttnStages;
+  uint64_t* barO = barS + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(barO + 1);
+  int* sflag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int qt = blockIdx.x;
+  const int g = blockIdx.y;
+  const int split = blockIdx.z;
+
+  if (tid == 0) {
+    mbar_init(barQ, 1);
+    for (int s = 0; s < kAttnStages; ++s) mbar_init(&fullKV[s], 1);
+    mbar_init(barS, 1);
+    mbar_init(barO, 1);
+    sflag[0] = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  __syncwarp();
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_s = tmem;
+  const uint32_t tmem_o = tmem + 128;
+
+  griddep_wait();
+  griddep_launch_dependents();
+
+  int rows_valid = a.rows;
+  if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
+  const int q_pos0 = a.q_pos0_dev != nullptr ? *a.q_pos0_dev : a.q_pos0;
+  const int kv_len = a.kv_len_dev != nullptr ? *a.kv_len_dev : a.kv_len;
+  const int row0 = qt * a.tile_pos;  // first query row of this tile
+
+  // Key range of this CTA.
+  const int last_row = min(row0 + a.tile_pos, rows_valid) - 1;
+  const int kv_hi = last_row >= row0 ? attn_limit(a, q_pos0 + last_row, kv_len) : 0;
+  const int n_kv_tiles = (kv_hi + 127) / 128;
+  const int t_begin = split * a.tiles_per_split;
+  const int t_end = min(n_kv_tiles, t_begin + a.tiles_per_split);
+  const int ntiles = max(0, t_end - t_begin);
+
+  // This thread's query row.
+  const int r_local = tid / a.rep;
+  const int h_local = tid - r_local * a.rep;
+  const int q_row = row0 + r_local;
+  const bool row_ok = (r_local < a.tile_pos) && (q_row < rows_valid);
+  const int head = g * a.rep + h_local;
+  const int lim = row_ok ? attn_limit(a, q_pos0 + q_row, kv_len) : 0;
+
+  const int plane = a.kv_plane0 + g;
+  if (tid == 0 && ntiles > 0) {
+    const uint32_t qbytes = static_cast<uint32_t>(64 * a.rep * a.tile_pos * 2);
+    mbar_expect_tx(barQ, 2 * qbytes);
+    tma_load_3d(sQ, &tmQ, barQ, 0, g * a.rep, row0);
+    tma_load_3d(sQ + 128 * 128, &tmQ, barQ, 64, g * a.rep, row0);
+    for (int j = 0; j < min(kAttnStages, ntiles); ++j) {
+      uint8_t* st = sKV + j * kAttnStageBytes;
+      const int key0 = (t_begin + j) * 128;
+      mbar_expect_tx(&fullKV[j], kAttnStageBytes);
+      tma_load_3d(st, &tmK, &fullKV[j], 0, key0, plane);
+      tma_load_3d(st + 128 * 128, &tmK, &fullKV[j], 64, key0, plane);
+      tma_load_3d(st + kAttnKBytes, &tmV, &fullKV[j], key0, 0, plane);
+      tma_load_3d(st + kAttnKBytes + 128 * 128, &tmV, &fullKV[j], key0 + 64, 0, plane);
+    }
+  }
+
+  float o_acc[128];
+#pragma unroll
+  for (int d = 0; d < 128; ++d) o_acc[d] = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;
+  const uint32_t idesc = idesc_bf16_f32(128, 128);
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  bool failed = false;
+
+  for (int j = 0; j < ntiles; ++j) {
+    const int s = j % kAttnStages;
+    uint8_t* st = sKV + s * kAttnStageBytes;
+    const int key0 = (t_begin + j) * 128;
+    if (tid == 0) {
+      bool ok = (j > 0 || mbar_wait(barQ, 0)) && mbar_wait(&fullKV[s], (j / kAttnStages) & 1);
+      if (!ok) {
+        record_error(a.status, DEV_TIMEOUT_TMA);
+        sflag[0] = 1;
+      } else {
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ);
+        const uint32_t k_addr = smem_u32(st);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+          umma_bf16(tmem_s, sdesc_kmajor_sw128(q_addr + off), sdesc_kmajor_sw128(k_addr + off), idesc,
+                    kk != 0 ? 1u : 0u);
+        }
+      }
+      umma_commit(barS);
+    }
+    if (!mbar_wait(barS, j & 1)) { record_error(a.status, DEV_TIMEOUT_MMA); sflag[0] = 1; }
+    tc_fence_after();
+    __syncthreads();
+    if (sflag[0]) { failed = true; break; }
+
+    // Row softmax over this key tile: pass 1 max, pass 2 exponentials (TMEM re-read).
+    float tile_max = -INFINITY;
+#pragma unroll
+    for (int cb = 0; cb < 128; cb += 32) {
+      float sv[32];
+      tmem_ld32(tmem_s + lane_off + cb, sv);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int kp = key0 + cb + i;
+        const float x = (kp < lim) ? sv[i] * a.scale_log2 : -INFINITY;
+        tile_max = fmaxf(tile_max, x);
+      }
+    }
+    const float m_new = fmaxf(m_run, tile_max);
+    const float alpha = (m_new == -INFINITY) ? 1.0f : exp2f(m_run - m_new);
+    float psum = 0.0f;
+#pragma unroll
+    for (int cb = 0; cb < 128; cb += 32) {
+      float sv[32];
+      tmem_ld32(tmem_s + lane_off + cb, sv);
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const int kp = key0 + cb + i;
+        const float p0 = (kp < lim && m_new != -INFINITY) ? exp2f(sv[i] * a.scale_log2 - m_new) : 0.0f;
+        const float p1 = (kp + 1 < lim && m_new != -INFINITY) ? exp2f(sv[i + 1] * a.scale_log2 - m_new) : 0.0f;
+        const __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+        psum += __low2float(pb) + __high2float(pb);
+        *reinterpret_cast<__nv_bfloat162*>(sP + sw128_offset(tid, cb + i, 128)) = pb;
+      }
+    }
+    l_run = l_run * alpha + psum;
+    m_run = m_new;
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t p_addr = smem_u32(sP);
+      const uint32_t v_addr = smem_u32(st + kAttnKBytes);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+        umma_bf16(tmem_o, sdesc_kmajor_sw128(p_addr + off), sdesc_kmajor_sw128(v_addr + off), idesc,
+                  kk != 0 ? 1u : 0u);
+      }
+      umma_commit(barO);
+    }
+    if (!mbar_wait(barO, j & 1)) { record_error(a.status, DEV_TIMEOUT_MMA); sflag[0] = 1; }
+    tc_fence_after();
+    __syncwarp();
+#pragma unroll
+    for (int cb = 0; cb < 128; cb += 32) {
+      float ov[32];
+      tmem_ld32(tmem_o + lane_off + cb, ov);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o_acc[cb + i] = o_acc[cb + i] * alpha + ov[i];
+    }
+    // Stage s is free (its O MMA completed): refill it with tile j + kAttnStages.
+    if (tid == 0 && j + kAttnStages < ntiles && !sflag[0]) {
+      const int key1 = (t_begin + j + kAttnStages) * 128;
+      mbar_expect_tx(&fullKV[s], kAttnStageBytes);
+      tma_load_3d(st, &tmK, &fullKV[s], 0, key1, plane);
+      tma_load_3d(st + 128 * 128, &tmK, &fullKV[s], 64, key1, plane);
+      tma_load_3d(st + kAttnKBytes, &tmV, &fullKV[s], key1, 0, plane);
+      tma_load_3d(st + kAttnKBytes + 128 * 128, &tmV, &fullKV[s], key1 + 64, 0, plane);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (sflag[0]) { failed = true; break; }
+  }
+
+  if (!failed && row_ok) {
+    if (a.splits == 1) {
+      const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      __nv_bfloat16* dst = a.out + static_cast<size_t>(q_row) * a.nq * 128 + static_cast<size_t>(head) * 128;
+#pragma unroll
+      for (int d = 0; d < 128; d += 8) {
+        __align__(16) __nv_bfloat16 t[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) t[e] = __float2bfloat16_rn(o_acc[d + e] * inv);
+        *reinterpret_cast<uint4*>(dst + d) = *reinterpret_cast<const uint4*>(t);
+      }
+    } else {
+      const size_t slot = (static_cast<size_t>(split) * a.rows + q_row) * a.nq + head;
+      float* dst = a.ws_o + slot * 128;
+#pragma unroll
+      for (int d = 0; d < 128; d += 4) {
+        *reinterpret_cast<float4*>(dst + d) = make_float4(o_acc[d], o_acc[d + 1], o_acc[d + 2], o_acc[d + 3]);
+      }
+      a.ws_ml[slot * 2 + 0] = m_run;
+      a.ws_ml[slot * 2 + 1] = l_run;
+    }
+  }
+  if (failed && tid == 0) {
+    mbar_wait(barQ, 0);
+    for (int s = 0; s < min(kAttnStages, ntiles); ++s) mbar_wait(&fullKV[s], 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// Merge split-KV partials: one warp per (query row, head), fixed split order.
+__global__ void attn_combine_kernel(const AttnArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  int rows_valid = a.rows;
+  if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
+  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int row = warp_global / a.nq;
+  const int head = warp_global - row * a.nq;
+  if (row >= rows_valid) return;
+  float m_all = -INFINITY;
+  for (int s = 0; s < a.splits; ++s) {
+    const size_t slot = (static_cast<size_t>(s) * a.rows + row) * a.nq + head;
+    m_all = fmaxf(m_all, a.ws_ml[slot * 2]);
+  }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float l_all = 0.0f;
+  for (int s = 0; s < a.splits; ++s) {
+    const size_t slot = (static_cast<size_t>(s) * a.rows + row) * a.nq + head;
+    const float m = a.ws_ml[slot * 2];
+    const float l = a.ws_ml[slot * 2 + 1];
+    if (l == 0.0f || m == -INFINITY) continue;
+    const float w = exp2f(m - m_all);
+    l_all += l * w;
+    const float4 o = *reinterpret_cast<const float4*>(a.ws_o + slot * 128 + lane * 4);
+    acc.x += o.x * w;
+    acc.y += o.y * w;
+    acc.z += o.z * w;
+    acc.w += o.w * w;
+  }
+  const float inv = l_all > 0.0f ? 1.0f / l_all : 0.0f;
+  __nv_bfloat16* dst = a.out + static_cast<size_t>(row) * a.nq * 128 + static_cast<size_t>(head) * 128 + lane * 4;
+  dst[0] = __float2bfloat16_rn(acc.x * inv);
+  dst[1] = __float2bfloat16_rn(acc.y * inv);
+  dst[2] = __float2bfloat16_rn(acc.z * inv);
+  dst[3] = __float2bfloat16_rn(acc.w * inv);
+}
+
+}  // namespace drt

@@ -1,0 +1,1360 @@
+// Native runtime behind the C ABI in include/diffusorrt_b200.h: model weights, per-request
+// sessions (K/V cache, activations, CUDA graphs), and the kernel-level entry points.
+//
+// One process per GPU; a model and its sessions live on the device given at creation. All
+// device work of a session runs on the session's own stream; kernels are chained with
+// programmatic dependent launch so each kernel's weight prefetch overlaps its predecessor.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/diffusorrt_b200.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "policy.cuh"
+#include "rowops.cuh"
+#include "selector.cuh"
+
+using namespace drt;
+
+// ======================================================================= errors
+namespace {
+thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+}  // namespace
+
+#define CK(expr)                                                                                         \
+  do {                                                                                                   \
+    cudaError_t _e = (expr);                                                                             \
+    if (_e != cudaSuccess)                                                                               \
+      return set_error(DRT_INTERNAL_ERROR, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__, \
+                       __LINE__);                                                                        \
+  } while (0)
+#define TRY(expr)                 \
+  do {                            \
+    int _r = (expr);              \
+    if (_r != DRT_OK) return _r;  \
+  } while (0)
+#define REQUIRE(cond, ...)                                     \
+  do {                                                         \
+    if (!(cond)) return set_error(DRT_INVALID_ARGUMENT, __VA_ARGS__); \
+  } while (0)
+
+// ======================================================================= TMA descriptors
+namespace {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor map with 128-byte swizzle; dims/strides innermost first (strides: rank-1 entries).
+int make_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+             const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return set_error(DRT_INTERNAL_ERROR, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return set_error(DRT_INTERNAL_ERROR, "tensor map base not 16-byte aligned");
+  cuuint64_t d[3], s[2];
+  cuuint32_t b[3], e[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) { d[i] = dims[i]; b[i] = box[i]; }
+  for (int i = 0; i < rank - 1; ++i) {
+    s[i] = strides[i];
+    if (s[i] % 16 != 0) return set_error(DRT_INTERNAL_ERROR, "tensor map stride not a multiple of 16 bytes");
+  }
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(DRT_INTERNAL_ERROR, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return DRT_OK;
+}
+
+// Row-major bf16 matrix [rows][cols], box {64 cols, box_rows rows}.
+int map_matrix(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(cols) * 2};
+  const uint32_t box[2] = {64, static_cast<uint32_t>(box_rows)};
+  return make_map(map, base, 2, dims, strides, box);
+}
+
+thread_local int64_t g_launches = 0;  // kernels enqueued by this thread (launch accounting)
+
+template <typename Kern, typename... Args>
+cudaError_t launch_k(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, Args... args) {
+  ++g_launches;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+int g_num_sms_cache[64] = {0};
+int num_sms(int device) {
+  if (device < 0 || device >= 64) return 148;
+  if (g_num_sms_cache[device] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+    g_num_sms_cache[device] = n > 0 ? n : 148;
+  }
+  return g_num_sms_cache[device];
+}
+
+int configure_kernels() {
+  static int result = -1;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    result = DRT_OK;
+    if (cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess)
+      result = DRT_INTERNAL_ERROR;
+  });
+  if (result != DRT_OK) return set_error(DRT_INTERNAL_ERROR, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return DRT_OK;
+}
+
+void split_k(int tiles, int kb, int target, int* splits, int* kbps) {
+  int sp = std::max(1, std::min(kb, (target + tiles / 2) / std::max(1, tiles)));
+  const int per = (kb + sp - 1) / sp;
+  *kbps = per;
+  *splits = (kb + per - 1) / per;
+}
+
+constexpr double kTieRel = 9.094947017729282e-13;  // 2^-40
+}  // namespace
+
+// ======================================================================= model
+struct LayerW {
+  __nv_bfloat16 *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr;
+  float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *bqkv = nullptr;
+  CUtensorMap m_qkv, m_o, m_gu, m_down;
+};
+
+struct drt_model {
+  drt_model_config cfg;
+  int device = 0;
+  int H = 0, nq = 0, nkv = 0, I = 0, V = 0, L = 0, rep = 0, tile_pos = 0;
+  int qkv_rows = 0, gu_rows = 0;
+  std::vector<void*> allocs;
+  __nv_bfloat16* embed = nullptr;
+  __nv_bfloat16* lm_head = nullptr;
+  float* final_norm = nullptr;
+  std::vector<LayerW> layers;
+  CUtensorMap m_lm;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  int rope_pos = 0;
+  int64_t bytes = 0;
+};
+
+namespace {
+template <typename T>
+int dalloc(drt_model* m, T** p, size_t count) {
+  void* q = nullptr;
+  CK(cudaMalloc(&q, std::max<size_t>(count * sizeof(T), 256)));
+  m->allocs.push_back(q);
+  m->bytes += static_cast<int64_t>(count * sizeof(T));
+  *p = static_cast<T*>(q);
+  return DRT_OK;
+}
+
+int fill_f32(float* p, int64_t n, float v, cudaStream_t st) {
+  fill_f32_kernel<<<static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 4096)), 256, 0, st>>>(p, n, v);
+  CK(cudaGetLastError());
+  return DRT_OK;
+}
+
+// Host RoPE tables in the reference's float32 arithmetic (mlx_forward.py:1566-1595); used when
+// the caller does not install tables of its own.
+void host_rope(std::vector<float>& c, std::vector<float>& s, int n_pos, float theta) {
+  c.resize(static_cast<size_t>(n_pos) * 64);
+  s.resize(static_cast<size_t>(n_pos) * 64);
+  for (int i = 0; i < 64; ++i) {
+    const float expo = static_cast<float>(i) / 64.0f;
+    const float inv = 1.0f / powf(theta, expo);
+    for (int p = 0; p < n_pos; ++p) {
+      const float f = static_cast<float>(p) * inv;
+      c[static_cast<size_t>(p) * 64 + i] = cosf(f);
+      s[static_cast<size_t>(p) * 64 + i] = sinf(f);
+    }
+  }
+}
+
+int parse_layer_key(const char* key, int* layer, std::string* rest) {
+  const char* pre = "model.layers.";
+  if (strncmp(key, pre, strlen(pre)) != 0) return 0;
+  const char* p = key + strlen(pre);
+  char* end = nullptr;
+  long l = strtol(p, &end, 10);
+  if (end == p || *end != '.') return 0;
+  *layer = static_cast<int>(l);
+  *rest = std::string(end + 1);
+  return 1;
+}
+
+// Where a logical tensor lives in the packed layout. grp/grp_stride/grp_off describe the
+// row map (see rowops.cuh); f32 tensors (norms, biases) have dst_f32 set.
+struct Slot {
+  __nv_bfloat16* dst = nullptr;
+  float* dst_f32 = nullptr;
+  int64_t rows = 0, cols = 0;
+  int64_t grp = 1, grp_stride = 1, grp_off = 0;
+  int64_t f32_offset = 0;
+};
+
+int resolve_slot(drt_model* m, const char* key, Slot* out) {
+  Slot s;
+  const int64_t H = m->H;
+  if (strcmp(key, "model.embed_tokens.weight") == 0) {
+    s.dst = m->embed; s.rows = m->V; s.cols = H;
+  } else if (strcmp(key, "lm_head.weight") == 0) {
+    if (m->cfg.tied_lm_head) return set_error(DRT_INVALID_ARGUMENT, "lm_head.weight is tied to the embedding in this model");
+    s.dst = m->lm_head; s.rows = m->V; s.cols = H;
+  } else if (strcmp(key, "model.norm.weight") == 0) {
+    s.dst_f32 = m->final_norm; s.rows = 1; s.cols = H;
+  } else {
+    int l = -1;
+    std::string rest;
+    if (!parse_layer_key(key, &l, &rest) || l < 0 || l >= m->L) return set_error(DRT_INVALID_ARGUMENT, "unknown weight key %s", key);
+    LayerW& w = m->layers[l];
+    const int64_t qr = static_cast<int64_t>(m->nq) * 128, kr = static_cast<int64_t>(m->nkv) * 128;
+    if (rest == "input_layernorm.weight") { s.dst_f32 = w.in_norm; s.rows = 1; s.cols = H; }
+    else if (rest == "post_attention_layernorm.weight") { s.dst_f32 = w.post_norm; s.rows = 1; s.cols = H; }
+    else if (rest == "self_attn.q_norm.weight") { if (!w.q_norm) return set_error(DRT_INVALID_ARGUMENT, "model has no QK norm"); s.dst_f32 = w.q_norm; s.rows = 1; s.cols = 128; }
+    else if (rest == "self_attn.k_norm.weight") { if (!w.k_norm) return set_error(DRT_INVALID_ARGUMENT, "model has no QK norm"); s.dst_f32 = w.k_norm; s.rows = 1; s.cols = 128; }
+    else if (rest == "self_attn.q_proj.weight") { s.dst = w.wqkv; s.rows = qr; s.cols = H; s.grp = qr; s.grp_stride = 0; s.grp_off = 0; }
+    else if (rest == "self_attn.k_proj.weight") { s.dst = w.wqkv; s.rows = kr; s.cols = H; s.grp = kr; s.grp_stride = 0; s.grp_off = qr; }
+    else if (rest == "self_attn.v_proj.weight") { s.dst = w.wqkv; s.rows = kr; s.cols = H; s.grp = kr; s.grp_stride = 0; s.grp_off = qr + kr; }
+    else if (rest == "self_attn.q_proj.bias") { if (!w.bqkv) return set_error(DRT_INVALID_ARGUMENT, "model has no qkv bias"); s.dst_f32 = w.bqkv; s.rows = 1; s.cols = qr; s.f32_offset = 0; }
+    else if (rest == "self_attn.k_proj.bias") { if (!w.bqkv) return set_error(DRT_INVALID_ARGUMENT, "model has no qkv bias"); s.dst_f32 = w.bqkv; s.rows = 1; s.cols = kr; s.f32_offset = qr; }
+    else if (rest == "self_attn.v_proj.bias") { if (!w.bqkv) return set_error(DRT_INVALID_ARGUMENT, "model has no qkv bias"); s.dst_f32 = w.bqkv; s.rows = 1; s.cols = kr; s.f32_offset = qr + kr; }
+    else if (rest == "self_attn.o_proj.weight") { s.dst = w.wo; s.rows = H; s.cols = qr; }
+    else if (rest == "mlp.gate_proj.weight") { s.dst = w.wgu; s.rows = m->I; s.cols = H; s.grp = 64; s.grp_stride = 128; s.grp_off = 0; }
+    else if (rest == "mlp.up_proj.weight") { s.dst = w.wgu; s.rows = m->I; s.cols = H; s.grp = 64; s.grp_stride = 128; s.grp_off = 64; }
+    else if (rest == "mlp.down_proj.weight") { s.dst = w.wdown; s.rows = H; s.cols = m->I; }
+    else return set_error(DRT_INVALID_ARGUMENT, "unknown weight key %s", key);
+  }
+  if (s.grp == 1 && s.grp_stride == 1) { s.grp = s.rows; s.grp_stride = 0; }
+  *out = s;
+  return DRT_OK;
+}
+}  // namespace
+
+extern "C" int drt_abi_version(int32_t* major, int32_t* minor, int32_t* patch) {
+  if (major) *major = DRT_ABI_VERSION_MAJOR;
+  if (minor) *minor = DRT_ABI_VERSION_MINOR;
+  if (patch) *patch = DRT_ABI_VERSION_PATCH;
+  return DRT_OK;
+}
+
+extern "C" const char* drt_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int drt_device_count(int32_t* count) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) n = 0;
+  if (count) *count = n;
+  return DRT_OK;
+}
+
+extern "C" int drt_model_create(const drt_model_config* cfg, int32_t device, drt_model** out) {
+  REQUIRE(cfg != nullptr && out != nullptr, "null argument");
+  *out = nullptr;
+  REQUIRE(cfg->head_dim == 128, "head_dim must be 128 (got %d)", cfg->head_dim);
+  REQUIRE(cfg->layer_count > 0 && cfg->hidden_size > 0 && cfg->vocab_size > 0, "bad model geometry");
+  REQUIRE(cfg->hidden_size % 128 == 0, "hidden_size must be a multiple of 128");
+  REQUIRE(cfg->intermediate_size % 64 == 0, "intermediate_size must be a multiple of 64");
+  REQUIRE(cfg->vocab_size % 128 == 0, "vocab_size must be a multiple of 128");
+  REQUIRE(cfg->num_kv_heads > 0 && cfg->attention_heads % cfg->num_kv_heads == 0, "attention_heads must divide by num_kv_heads");
+  REQUIRE(cfg->attention_heads / cfg->num_kv_heads <= 128, "GQA group too large");
+  REQUIRE(cfg->max_seq > 0 && cfg->max_seq % 8 == 0, "max_seq must be a positive multiple of 8");
+  CK(cudaSetDevice(device));
+  TRY(configure_kernels());
+  drt_model* m = new drt_model();
+  m->cfg = *cfg;
+  m->device = device;
+  m->H = cfg->hidden_size;
+  m->nq = cfg->attention_heads;
+  m->nkv = cfg->num_kv_heads;
+  m->I = cfg->intermediate_size;
+  m->V = cfg->vocab_size;
+  m->L = cfg->layer_count;
+  m->rep = m->nq / m->nkv;
+  m->tile_pos = 128 / m->rep;
+  m->qkv_rows = (m->nq + 2 * m->nkv) * 128;
+  m->gu_rows = 2 * m->I;
+  m->layers.resize(m->L);
+  auto fail = [&](int rc) { drt_model_destroy(m); return rc; };
+  int rc;
+  if ((rc = dalloc(m, &m->embed, static_cast<size_t>(m->V) * m->H)) != DRT_OK) return fail(rc);
+  if (cfg->tied_lm_head) m->lm_head = m->embed;
+  else if ((rc = dalloc(m, &m->lm_head, static_cast<size_t>(m->V) * m->H)) != DRT_OK) return fail(rc);
+  if ((rc = dalloc(m, &m->final_norm, m->H)) != DRT_OK) return fail(rc);
+  for (int l = 0; l < m->L; ++l) {
+    LayerW& w = m->layers[l];
+    if ((rc = dalloc(m, &w.wqkv, static_cast<size_t>(m->qkv_rows) * m->H)) != DRT_OK) return fail(rc);
+    if ((rc = dalloc(m, &w.wo, static_cast<size_t>(m->H) * m->nq * 128)) != DRT_OK) return fail(rc);
+    if ((rc = dalloc(m, &w.wgu, static_cast<size_t>(m->gu_rows) * m->H)) != DRT_OK) return fail(rc);
+    if ((rc = dalloc(m, &w.wdown, static_cast<size_t>(m->H) * m->I)) != DRT_OK) return fail(rc);
+    if ((rc = dalloc(m, &w.in_norm, m->H)) != DRT_OK) return fail(rc);
+    if ((rc = dalloc(m, &w.post_norm, m->H)) != DRT_OK) return fail(rc);
+    if (cfg->qk_norm) {
+      if ((rc = dalloc(m, &w.q_norm, 128)) != DRT_OK) return fail(rc);
+      if ((rc = dalloc(m, &w.k_norm, 128)) != DRT_OK) return fail(rc);
+    }
+    if (cfg->qkv_bias && (rc = dalloc(m, &w.bqkv, m->qkv_rows)) != DRT_OK) return fail(rc);
+    if ((rc = map_matrix(&w.m_qkv, w.wqkv, m->qkv_rows, m->H, 128)) != DRT_OK) return fail(rc);
+    if ((rc = map_matrix(&w.m_o, w.wo, m->H, static_cast<int64_t>(m->nq) * 128, 128)) != DRT_OK) return fail(rc);
+    if ((rc = map_matrix(&w.m_gu, w.wgu, m->gu_rows, m->H, 128)) != DRT_OK) return fail(rc);
+    if ((rc = map_matrix(&w.m_down, w.wdown, m->H, m->I, 128)) != DRT_OK) return fail(rc);
+  }
+  if ((rc = map_matrix(&m->m_lm, m->lm_head, m->V, m->H, 128)) != DRT_OK) return fail(rc);
+  // Norm weights default to 1; RoPE tables default to the host float32 construction.
+  if ((rc = fill_f32(m->final_norm, m->H, 1.0f, 0)) != DRT_OK) return fail(rc);
+  for (auto& w : m->layers) {
+    if ((rc = fill_f32(w.in_norm, m->H, 1.0f, 0)) != DRT_OK) return fail(rc);
+    if ((rc = fill_f32(w.post_norm, m->H, 1.0f, 0)) != DRT_OK) return fail(rc);
+    if (w.q_norm && (rc = fill_f32(w.q_norm, 128, 1.0f, 0)) != DRT_OK) return fail(rc);
+    if (w.k_norm && (rc = fill_f32(w.k_norm, 128, 1.0f, 0)) != DRT_OK) return fail(rc);
+    if (w.bqkv && (rc = fill_f32(w.bqkv, m->qkv_rows, 0.0f, 0)) != DRT_OK) return fail(rc);
+  }
+  {
+    std::vector<float> c, s;
+    host_rope(c, s, cfg->max_seq, cfg->rope_theta);
+    if ((rc = drt_model_set_rope(m, c.data(), s.data(), cfg->max_seq)) != DRT_OK) return fail(rc);
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "model init failed: %s", cudaGetErrorString(cudaGetLastError())));
+  *out = m;
+  return DRT_OK;
+}
+
+extern "C" int drt_model_set_rope(drt_model* m, const float* cos_half, const float* sin_half, int32_t n_pos) {
+  REQUIRE(m && cos_half && sin_half && n_pos > 0, "null argument");
+  CK(cudaSetDevice(m->device));
+  if (m->rope_pos < n_pos) {
+    int rc;
+    if ((rc = dalloc(m, &m->rope_cos, static_cast<size_t>(n_pos) * 64)) != DRT_OK) return rc;
+    if ((rc = dalloc(m, &m->rope_sin, static_cast<size_t>(n_pos) * 64)) != DRT_OK) return rc;
+  }
+  CK(cudaMemcpy(m->rope_cos, cos_half, sizeof(float) * n_pos * 64, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(m->rope_sin, sin_half, sizeof(float) * n_pos * 64, cudaMemcpyHostToDevice));
+  m->rope_pos = n_pos;
+  return DRT_OK;
+}
+
+extern "C" int drt_model_init_synthetic(drt_model* m, uint64_t seed, float linear_std, float embed_std, float bias_std) {
+  REQUIRE(m != nullptr, "null model");
+  CK(cudaSetDevice(m->device));
+  const double unit = std::sqrt(21845.0);  // std of the 4-byte Irwin-Hall sum
+  const float s_lin = static_cast<float>(static_cast<double>(linear_std) / unit);
+  const float s_emb = static_cast<float>(static_cast<double>(embed_std) / unit);
+  const float s_bias = static_cast<float>(static_cast<double>(bias_std) / unit);
+  auto fill = [&](__nv_bfloat16* dst, int64_t rows, int64_t cols, uint32_t tid, float scale, int64_t grp, int64_t grp_stride,
+                  int64_t grp_off) -> int {
+    const int64_t total = rows * cols;
+    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 65535));
+    synth_fill_kernel<<<blocks, 256>>>(dst, rows, cols, seed, tid, scale, grp, grp_stride, grp_off);
+    CK(cudaGetLastError());
+    return DRT_OK;
+  };
+  const int64_t H = m->H, qr = static_cast<int64_t>(m->nq) * 128, kr = static_cast<int64_t>(m->nkv) * 128;
+  TRY(fill(m->embed, m->V, H, 1, s_emb, m->V, 0, 0));
+  if (!m->cfg.tied_lm_head) TRY(fill(m->lm_head, m->V, H, 2, s_emb, m->V, 0, 0));
+  for (int l = 0; l < m->L; ++l) {
+    LayerW& w = m->layers[l];
+    const uint32_t b = 16u + static_cast<uint32_t>(l) * 16u;
+    TRY(fill(w.wqkv, qr, H, b + 0, s_lin, qr, 0, 0));
+    TRY(fill(w.wqkv, kr, H, b + 1, s_lin, kr, 0, qr));
+    TRY(fill(w.wqkv, kr, H, b + 2, s_lin, kr, 0, qr + kr));
+    TRY(fill(w.wo, H, qr, b + 3, s_lin, H, 0, 0));
+    TRY(fill(w.wgu, m->I, H, b + 4, s_lin, 64, 128, 0));
+    TRY(fill(w.wgu, m->I, H, b + 5, s_lin, 64, 128, 64));
+    TRY(fill(w.wdown, H, m->I, b + 6, s_lin, H, 0, 0));
+    if (w.bqkv) {
+      // Biases are bf16 values held in f32: generate bf16 into a scratch row, widen.
+      __nv_bfloat16* tmp = nullptr;
+      CK(cudaMalloc(&tmp, sizeof(__nv_bfloat16) * m->qkv_rows));
+      int rc = fill(tmp, 1, qr, b + 7, s_bias, 1, 0, 0);
+      if (rc == DRT_OK) rc = fill(tmp + qr, 1, kr, b + 8, s_bias, 1, 0, 0);
+      if (rc == DRT_OK) rc = fill(tmp + qr + kr, 1, kr, b + 9, s_bias, 1, 0, 0);
+      if (rc == DRT_OK) {
+        bf16_to_f32_kernel<<<64, 256>>>(w.bqkv, tmp, m->qkv_rows);
+        if (cudaGetLastError() != cudaSuccess) rc = set_error(DRT_INTERNAL_ERROR, "bias widen failed");
+      }
+      cudaDeviceSynchronize();
+      cudaFree(tmp);
+      TRY(rc);
+    }
+  }
+  CK(cudaDeviceSynchronize());
+  return DRT_OK;
+}
+
+extern "C" int drt_model_set_tensor(drt_model* m, const char* key, const void* data, int32_t dtype, int64_t rows, int64_t cols) {
+  REQUIRE(m && key && data, "null argument");
+  REQUIRE(dtype == 0 || dtype == 1, "dtype must be 0 (bf16) or 1 (f32)");
+  Slot s;
+  TRY(resolve_slot(m, key, &s));
+  REQUIRE(rows * cols == s.rows * s.cols, "%s: expected %lld x %lld elements, got %lld x %lld", key,
+          static_cast<long long>(s.rows), static_cast<long long>(s.cols), static_cast<long long>(rows), static_cast<long long>(cols));
+  CK(cudaSetDevice(m->device));
+  const int64_t n = s.rows * s.cols;
+  if (s.dst_f32 != nullptr) {
+    std::vector<float> tmp(n);
+    if (dtype == 1) {
+      memcpy(tmp.data(), data, sizeof(float) * n);
+    } else {
+      const uint16_t* src = static_cast<const uint16_t*>(data);
+      for (int64_t i = 0; i < n; ++i) {
+        uint32_t bits = static_cast<uint32_t>(src[i]) << 16;
+        memcpy(&tmp[i], &bits, 4);
+      }
+    }
+    CK(cudaMemcpy(s.dst_f32 + s.f32_offset, tmp.data(), sizeof(float) * n, cudaMemcpyHostToDevice));
+    return DRT_OK;
+  }
+  REQUIRE(dtype == 0, "%s: matrices must be bf16", key);
+  __nv_bfloat16* staging = nullptr;
+  CK(cudaMalloc(&staging, sizeof(__nv_bfloat16) * n));
+  cudaError_t e = cudaMemcpy(staging, data, sizeof(__nv_bfloat16) * n, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 65535));
+    pack_rows_kernel<<<blocks, 256>>>(s.dst, staging, s.rows, s.cols, s.grp, s.grp_stride, s.grp_off);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  }
+  cudaFree(staging);
+  if (e != cudaSuccess) return set_error(DRT_INTERNAL_ERROR, "set_tensor %s: %s", key, cudaGetErrorString(e));
+  return DRT_OK;
+}
+
+extern "C" int drt_model_get_tensor(drt_model* m, const char* key, void* data, int32_t dtype, int64_t rows, int64_t cols) {
+  REQUIRE(m && key && data, "null argument");
+  REQUIRE(dtype == 0 || dtype == 1, "dtype must be 0 (bf16) or 1 (f32)");
+  Slot s;
+  TRY(resolve_slot(m, key, &s));
+  REQUIRE(rows * cols == s.rows * s.cols, "%s: element count mismatch", key);
+  CK(cudaSetDevice(m->device));
+  const int64_t n = s.rows * s.cols;
+  if (s.dst_f32 != nullptr) {
+    std::vector<float> tmp(n);
+    CK(cudaMemcpy(tmp.data(), s.dst_f32 + s.f32_offset, sizeof(float) * n, cudaMemcpyDeviceToHost));
+    if (dtype == 1) {
+      memcpy(data, tmp.data(), sizeof(float) * n);
+    } else {
+      uint16_t* dst = static_cast<uint16_t*>(data);
+      for (int64_t i = 0; i < n; ++i) {
+        uint32_t bits;
+        memcpy(&bits, &tmp[i], 4);
+        dst[i] = static_cast<uint16_t>(bits >> 16);
+      }
+    }
+    return DRT_OK;
+  }
+  std::vector<uint16_t> row(static_cast<size_t>(s.cols));
+  for (int64_t r = 0; r < s.rows; ++r) {
+    const int64_t dr = (r / s.grp) * s.grp_stride + s.grp_off + r % s.grp;
+    CK(cudaMemcpy(row.data(), s.dst + dr * s.cols, sizeof(uint16_t) * s.cols, cudaMemcpyDeviceToHost));
+    if (dtype == 0) {
+      memcpy(static_cast<uint16_t*>(data) + r * s.cols, row.data(), sizeof(uint16_t) * s.cols);
+    } else {
+      float* dst = static_cast<float*>(data) + r * s.cols;
+      for (int64_t c = 0; c < s.cols; ++c) {
+        uint32_t bits = static_cast<uint32_t>(row[c]) << 16;
+        memcpy(&dst[c], &bits, 4);
+      }
+    }
+  }
+  return DRT_OK;
+}
+
+extern "C" int64_t drt_model_device_bytes(const drt_model* m) { return m ? m->bytes : 0; }
+
+extern "C" void drt_model_destroy(drt_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  cudaDeviceSynchronize();
+  for (void* p : m->allocs) cudaFree(p);
+  delete m;
+}
+
+// ======================================================================= session
+struct drt_session {
+  drt_model* m = nullptr;
+  drt_session_config cfg;
+  int device = 0;
+  int max_seq = 0, rows_cap = 0, planes = 0;
+  std::vector<void*> allocs;
+  int64_t bytes = 0;
+  cudaStream_t stream = nullptr;
+  // device buffers
+  int* canvas = nullptr;
+  float* h = nullptr;
+  __nv_bfloat16 *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *xf = nullptr;
+  float* logits = nullptr;
+  __nv_bfloat16 *kcache = nullptr, *vtcache = nullptr;
+  float* gemm_ws = nullptr;
+  int* gemm_cnt = nullptr;
+  size_t gemm_ws_floats = 0, gemm_cnt_n = 0;
+  float *attn_ws_o = nullptr, *attn_ws_ml = nullptr;
+  float* sel_pmax = nullptr;
+  int* sel_pidx = nullptr;
+  double* sel_psum = nullptr;
+  int* sel_cnt = nullptr;
+  double *sel_amax = nullptr, *sel_sum = nullptr, *conf = nullptr;
+  int* token = nullptr;
+  int* scope_rows = nullptr;
+  int* status = nullptr;
+  DecodeState* state = nullptr;
+  StepTrace* trace = nullptr;
+  int trace_cap = 0;
+  // host mirrors
+  DecodeState* hstate = nullptr;   // pinned
+  int* hflags = nullptr;           // pinned ring of stopped flags
+  int canvas_len = 0;
+  int origin = 0, block_size = 32, mask_id = 0;
+  bool started = false;
+  // launch geometry
+  int sms = 148;
+  int attn_splits = 1, attn_tps = 1;
+  int sel_chunks = 1;
+  // tensor maps over the activation buffers
+  CUtensorMap m_xn64, m_xn128, m_attn64, m_attn128, m_act64, m_act128, m_xf64, m_q, m_k, m_v;
+  // graphs
+  int g_step_kernels = 0;             // kernels in one replay of g_step
+  cudaGraphExec_t g_step = nullptr;   // plan + forward + score + commit
+  cudaGraphExec_t g_fwd = nullptr;    // forward + score (host policy)
+  int g_step_geom[2] = {-1, -1};      // (mask origin, block size) baked into each graph
+  int g_fwd_geom[2] = {-1, -1};
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  // metrics
+  int64_t m_forwards = 0, m_rows = 0, m_prefill_rows = 0, m_committed = 0, m_near = 0, m_exact = 0;
+  double m_ms = 0.0;
+};
+
+namespace {
+template <typename T>
+int salloc(drt_session* s, T** p, size_t count) {
+  void* q = nullptr;
+  CK(cudaMalloc(&q, std::max<size_t>(count * sizeof(T), 256)));
+  s->allocs.push_back(q);
+  s->bytes += static_cast<int64_t>(count * sizeof(T));
+  *p = static_cast<T*>(q);
+  return DRT_OK;
+}
+
+int check_status(drt_session* s) {
+  int code = 0;
+  CK(cudaMemcpy(&code, s->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    cudaMemset(s->status, 0, sizeof(int));
+    if (code == DEV_BAD_SHAPE) return set_error(DRT_INVALID_ARGUMENT, "device rejected an input (token id out of range)");
+    return set_error(DRT_DEVICE_TIMEOUT, "device wait expired (code %d)", code);
+  }
+  return DRT_OK;
+}
+
+struct Fwd {
+  bool decode;                 // static decode shapes (graph-capturable)
+  int rows;                    // rows covered by the grid
+  const int* rows_dev;
+  int pos0;
+  const int* pos0_dev;
+  int kv_len;
+  const int* kv_len_dev;
+  int prompt_len, block_size, bidirectional;
+};
+
+GemmArgs base_args(drt_session* s, int n_out, int K, const Fwd& f) {
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.n_out = n_out;
+  a.K = K;
+  a.rows = f.rows;
+  a.rows_dev = f.rows_dev;
+  a.splits = 1;
+  a.kb_per_split = K / 64;
+  a.workspace = s->gemm_ws;
+  a.counters = s->gemm_cnt;
+  a.status = s->status;
+  a.pos0 = f.pos0;
+  a.pos0_dev = f.pos0_dev;
+  return a;
+}
+
+template <int BN>
+int run_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a, bool allow_split) {
+  const int tiles_m = a.n_out / 128;
+  const int tiles_n = (a.rows + BN - 1) / BN;
+  const int kb = a.K / 64;
+  if (allow_split) split_k(tiles_m * tiles_n, kb, s->sms, &a.splits, &a.kb_per_split);
+  else { a.splits = 1; a.kb_per_split = kb; }
+  const int max_stages = (200 * 1024) / GemmCfg<BN>::kStageBytes;
+  a.stages = std::max(1, std::min(a.kb_per_split, max_stages));
+  if (a.splits > 1) {
+    const size_t need = static_cast<size_t>(tiles_m) * tiles_n * a.splits * BN * 128;
+    if (need > s->gemm_ws_floats || static_cast<size_t>(tiles_m) * tiles_n > s->gemm_cnt_n)
+      return set_error(DRT_INTERNAL_ERROR, "split-K workspace too small (%zu floats needed)", need);
+  }
+  dim3 grid(tiles_m, tiles_n, a.splits);
+  CK(launch_k(gemm_swapab_kernel<BN>, grid, dim3(128), GemmCfg<BN>::smem_bytes(a.stages), s->stream, true, mA, mB, a));
+  return DRT_OK;
+}
+
+int run_rmsnorm(drt_session* s, const float* h, const int* row_index, int rows, const int* rows_dev, const float* w,
+                __nv_bfloat16* out) {
+  drt_model* m = s->m;
+  CK(launch_k(rmsnorm_bf16_kernel, dim3(rows), dim3(256), 0, s->stream, true, h, m->H, row_index, rows, rows_dev, w,
+              m->cfg.rms_norm_eps, m->H, out, m->H));
+  return DRT_OK;
+}
+
+// Enqueue the transformer layers for the rows described by f (embedding through the last
+// layer's residual). K/V of every forwarded row is written into the cache.
+int enqueue_layers(drt_session* s, const Fwd& f) {
+  drt_model* m = s->m;
+  const int H = m->H, qd = m->nq * 128;
+  CK(launch_k(embed_rows_kernel, dim3(f.rows), dim3(128), 0, s->stream, true, static_cast<const int*>(s->canvas), f.pos0,
+              f.pos0_dev, f.rows, f.rows_dev, static_cast<const __nv_bfloat16*>(m->embed), H, s->h, m->V, s->status));
+  for (int l = 0; l < m->L; ++l) {
+    LayerW& w = m->layers[l];
+    TRY(run_rmsnorm(s, s->h, nullptr, f.rows, f.rows_dev, w.in_norm, s->xn));
+    // QKV + QK-norm + RoPE + K/V cache write.
+    GemmArgs a = base_args(s, m->qkv_rows, H, f);
+    a.epi = EPI_QKV;
+    a.out_bf16 = s->q;
+    a.bias = w.bqkv;
+    a.qnorm_w = w.q_norm;
+    a.knorm_w = w.k_norm;
+    a.rope_cos = m->rope_cos;
+    a.rope_sin = m->rope_sin;
+    a.nq = m->nq;
+    a.nkv = m->nkv;
+    a.kcache = s->kcache + static_cast<size_t>(l) * m->nkv * s->max_seq * 128;
+    a.vtcache = s->vtcache + static_cast<size_t>(l) * m->nkv * 128 * s->max_seq;
+    a.max_seq = s->max_seq;
+    a.eps = m->cfg.rms_norm_eps;
+    if (f.decode) TRY(run_gemm<64>(s, w.m_qkv, s->m_xn64, a, true));
+    else TRY(run_gemm<128>(s, w.m_qkv, s->m_xn128, a, false));
+    // Attention.
+    AttnArgs t;
+    memset(&t, 0, sizeof(t));
+    t.nq = m->nq;
+    t.nkv = m->nkv;
+    t.rep = m->rep;
+    t.tile_pos = m->tile_pos;
+    t.rows = f.rows;
+    t.rows_dev = f.rows_dev;
+    t.q_pos0 = f.pos0;
+    t.q_pos0_dev = f.pos0_dev;
+    t.kv_len = f.kv_len;
+    t.kv_len_dev = f.kv_len_dev;
+    t.prompt_len = f.prompt_len;
+    t.block_size = f.block_size;
+    t.bidirectional = f.bidirectional;
+    t.kv_plane0 = l * m->nkv;
+    t.out = s->attn;
+    t.ws_o = s->attn_ws_o;
+    t.ws_ml = s->attn_ws_ml;
+    t.status = s->status;
+    t.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(128.0));
+    const int qtiles = (f.rows + m->tile_pos - 1) / m->tile_pos;
+    if (f.decode && qtiles == 1) {
+      t.splits = s->attn_splits;
+      t.tiles_per_split = s->attn_tps;
+    } else {
+      t.splits = 1;
+      t.tiles_per_split = (s->max_seq + 127) / 128;
+    }
+    CK(launch_k(attn_prefix_kernel, dim3(qtiles, m->nkv, t.splits), dim3(128), kAttnSmemBytes, s->stream, true, s->m_q, s->m_k,
+                s->m_v, t));
+    if (t.splits > 1) {
+      const int warps = f.rows * m->nq;
+      CK(launch_k(attn_combine_kernel, dim3((warps + 3) / 4), dim3(128), 0, s->stream, true, t));
+    }
+    // o_proj + residual.
+    GemmArgs o = base_args(s, H, qd, f);
+    o.epi = EPI_RESID;
+    o.out_f32 = s->h;
+    o.ld_out = H;
+    if (f.decode) TRY(run_gemm<64>(s, w.m_o, s->m_attn64, o, true));
+    else TRY(run_gemm<128>(s, w.m_o, s->m_attn128, o, false));
+    TRY(run_rmsnorm(s, s->h, nullptr, f.rows, f.rows_dev, w.post_norm, s->xn));
+    // gate/up + SwiGLU.
+    GemmArgs g = base_args(s, m->gu_rows, H, f);
+    g.epi = EPI_SWIGLU;
+    g.out_bf16 = s->act;
+    g.ld_out = m->I;
+    if (f.decode) TRY(run_gemm<64>(s, w.m_gu, s->m_xn64, g, true));
+    else TRY(run_gemm<128>(s, w.m_gu, s->m_xn128, g, false));
+    // down + residual.
+    GemmArgs d = base_args(s, H, m->I, f);
+    d.epi = EPI_RESID;
+    d.out_f32 = s->h;
+    d.ld_out = H;
+    if (f.decode) TRY(run_gemm<64>(s, w.m_down, s->m_act64, d, true));
+    else TRY(run_gemm<128>(s, w.m_down, s->m_act128, d, false));
+  }
+  return DRT_OK;
+}
+
+// Final norm over the frontier rows (row_index into the forwarded rows), lm_head, selector.
+int enqueue_head(drt_session* s, const int* row_index, int rows, const int* rows_dev, bool with_selector) {
+  drt_model* m = s->m;
+  TRY(run_rmsnorm(s, s->h, row_index, rows, rows_dev, m->final_norm, s->xf));
+  Fwd f = {};
+  f.rows = rows;
+  f.rows_dev = rows_dev;
+  GemmArgs a = base_args(s, m->V, m->H, f);
+  a.epi = EPI_STORE_F32;
+  a.out_f32 = s->logits;
+  a.ld_out = m->V;
+  TRY(run_gemm<64>(s, m->m_lm, s->m_xf64, a, false));
+  if (with_selector) {
+    SelArgs sa;
+    memset(&sa, 0, sizeof(sa));
+    sa.logits = s->logits;
+    sa.ld = m->V;
+    sa.rows = rows;
+    sa.rows_dev = rows_dev;
+    sa.vocab = m->V;
+    sa.chunk = kSelChunk;
+    sa.nchunks = s->sel_chunks;
+    sa.mode = SEL_MAXPROB;
+    sa.exclude = -1;
+    sa.exclude_dev = &s->state->exclude_token;
+    sa.part_max = s->sel_pmax;
+    sa.part_idx = s->sel_pidx;
+    sa.part_sum = s->sel_psum;
+    sa.counters = s->sel_cnt;
+    sa.row_amax = s->sel_amax;
+    sa.row_sum = s->sel_sum;
+    sa.conf = s->conf;
+    sa.token = s->token;
+    sa.status = s->status;
+    CK(launch_k(sel_pass1_kernel, dim3(s->sel_chunks, rows), dim3(kSelThreads), 0, s->stream, true, sa));
+  }
+  return DRT_OK;
+}
+
+Fwd decode_fwd(drt_session* s) {
+  Fwd f = {};
+  f.decode = true;
+  f.rows = kMaxFwdRows;
+  f.rows_dev = &s->state->fwd_rows;
+  f.pos0_dev = &s->state->fwd_pos0;
+  f.kv_len = s->max_seq;
+  f.kv_len_dev = &s->state->kv_len;
+  f.prompt_len = s->origin;
+  f.block_size = s->block_size;
+  f.bidirectional = 0;
+  return f;
+}
+
+int capture(drt_session* s, bool with_policy, cudaGraphExec_t* out) {
+  cudaGraph_t graph = nullptr;
+  CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = DRT_OK;
+  if (with_policy) {
+    if (launch_k(plan_kernel, dim3(1), dim3(32), 0, s->stream, true, s->state, static_cast<const int*>(s->canvas)) != cudaSuccess)
+      rc = set_error(DRT_INTERNAL_ERROR, "plan launch failed");
+  }
+  if (rc == DRT_OK) rc = enqueue_layers(s, decode_fwd(s));
+  if (rc == DRT_OK) rc = enqueue_head(s, s->state->frontier_row, kMaxFrontier, &s->state->n_frontier, true);
+  if (rc == DRT_OK && with_policy) {
+    if (launch_k(commit_kernel, dim3(1), dim3(32), 0, s->stream, true, s->state, s->canvas, static_cast<const double*>(s->conf),
+                 static_cast<const int*>(s->token), s->trace) != cudaSuccess)
+      rc = set_error(DRT_INTERNAL_ERROR, "commit launch failed");
+  }
+  cudaError_t e = cudaStreamEndCapture(s->stream, &graph);
+  if (rc != DRT_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return set_error(DRT_INTERNAL_ERROR, "graph capture failed: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(out, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return set_error(DRT_INTERNAL_ERROR, "graph instantiate failed: %s", cudaGetErrorString(e));
+  return DRT_OK;
+}
+
+// Prefill rows [p0, p1) (positions whose tokens are final) into the K/V cache, in chunks.
+int prefill(drt_session* s, int p0, int p1, int prompt_len, int block_size, int bidirectional) {
+  for (int c0 = p0; c0 < p1; c0 += s->rows_cap) {
+    Fwd f = {};
+    f.decode = false;
+    f.rows = std::min(s->rows_cap, p1 - c0);
+    f.pos0 = c0;
+    f.kv_len = c0 + f.rows;
+    f.prompt_len = prompt_len;
+    f.block_size = block_size;
+    f.bidirectional = bidirectional;
+    TRY(enqueue_layers(s, f));
+    s->m_prefill_rows += f.rows;
+  }
+  return DRT_OK;
+}
+}  // namespace
+
+extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt_session** out) {
+  REQUIRE(m && cfg && out, "null argument");
+  *out = nullptr;
+  REQUIRE(cfg->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA || cfg->decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD,
+          "device sessions run only block_threshold and bd3_fixed_quota (got strategy %d)", cfg->decode_strategy);
+  REQUIRE(cfg->attention_mask_kind == DRT_MASK_D2F_HYBRID, "this device session serves the d2f_hybrid graph only");
+  REQUIRE(cfg->block_size >= 1 && cfg->block_size <= 32, "block_size must be in [1, 32]");
+  CK(cudaSetDevice(m->device));
+  drt_session* s = new drt_session();
+  s->m = m;
+  s->cfg = *cfg;
+  s->device = m->device;
+  s->max_seq = ((m->cfg.max_seq + 127) / 128) * 128;
+  s->rows_cap = std::max(64, ((std::max(m->cfg.max_prefill_rows, 64) + 127) / 128) * 128);
+  s->planes = m->L * m->nkv;
+  s->sms = num_sms(m->device);
+  auto fail = [&](int rc) { drt_session_close(s); return rc; };
+  int rc;
+  if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "stream create failed"));
+  if (cudaEventCreate(&s->ev0) != cudaSuccess || cudaEventCreate(&s->ev1) != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "event create failed"));
+  const int H = m->H, qd = m->nq * 128, R = s->rows_cap;
+  if ((rc = salloc(s, &s->canvas, s->max_seq)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->h, static_cast<size_t>(R) * H)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->xn, static_cast<size_t>(R) * H)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->q, static_cast<size_t>(R) * qd)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->attn, static_cast<size_t>(R) * qd)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->act, static_cast<size_t>(R) * m->I)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->xf, static_cast<size_t>(kMaxFrontier) * H)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->logits, static_cast<size_t>(kMaxFrontier) * m->V)) != DRT_OK) return fail(rc);
+  const size_t kv = static_cast<size_t>(s->planes) * s->max_seq * 128;
+  if ((rc = salloc(s, &s->kcache, kv)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->vtcache, kv)) != DRT_OK) return fail(rc);
+  if (cudaMemset(s->kcache, 0, kv * 2) != cudaSuccess || cudaMemset(s->vtcache, 0, kv * 2) != cudaSuccess)
+    return fail(set_error(DRT_INTERNAL_ERROR, "kv memset failed"));
+  // Split-K workspace: the largest decode GEMM (BN = 64, one column tile).
+  size_t ws = 0;
+  int max_tiles = m->V / 128;
+  const int shapes[4][2] = {{m->qkv_rows, H}, {H, qd}, {m->gu_rows, H}, {H, m->I}};
+  for (auto& sh : shapes) {
+    int sp, per;
+    split_k(sh[0] / 128, sh[1] / 64, s->sms, &sp, &per);
+    ws = std::max(ws, static_cast<size_t>(sh[0] / 128) * sp * 64 * 128);
+    max_tiles = std::max(max_tiles, sh[0] / 128);
+  }
+  s->gemm_ws_floats = ws;
+  s->gemm_cnt_n = static_cast<size_t>(max_tiles) * ((R + 63) / 64);
+  if ((rc = salloc(s, &s->gemm_ws, ws)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->gemm_cnt, s->gemm_cnt_n)) != DRT_OK) return fail(rc);
+  if (cudaMemset(s->gemm_cnt, 0, sizeof(int) * s->gemm_cnt_n) != cudaSuccess)
+    return fail(set_error(DRT_INTERNAL_ERROR, "memset failed"));
+  // Split-KV attention for one decode query tile.
+  const int kv_tiles = (s->max_seq + 127) / 128;
+  s->attn_splits = std::max(1, std::min(kv_tiles, s->sms / m->nkv));
+  s->attn_tps = (kv_tiles + s->attn_splits - 1) / s->attn_splits;
+  s->attn_splits = (kv_tiles + s->attn_tps - 1) / s->attn_tps;
+  if ((rc = salloc(s, &s->attn_ws_o, static_cast<size_t>(s->attn_splits) * kMaxFwdRows * m->nq * 128)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->attn_ws_ml, static_cast<size_t>(s->attn_splits) * kMaxFwdRows * m->nq * 2)) != DRT_OK) return fail(rc);
+  // Selector scratch.
+  s->sel_chunks = (m->V + kSelChunk - 1) / kSelChunk;
+  const size_t np = static_cast<size_t>(kMaxFrontier) * s->sel_chunks;
+  if ((rc = salloc(s, &s->sel_pmax, np)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->sel_pidx, np)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->sel_psum, np)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->sel_cnt, kMaxFrontier)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->sel_amax, kMaxFrontier)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->sel_sum, kMaxFrontier)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->conf, kMaxFrontier)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->token, kMaxFrontier)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->scope_rows, kMaxFrontier)) != DRT_OK) return fail(rc);
+  if (cudaMemset(s->sel_cnt, 0, sizeof(int) * kMaxFrontier) != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "memset failed"));
+  if ((rc = salloc(s, &s->status, 1)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->state, 1)) != DRT_OK) return fail(rc);
+  if (cudaMemset(s->status, 0, sizeof(int)) != cudaSuccess || cudaMemset(s->state, 0, sizeof(DecodeState)) != cudaSuccess)
+    return fail(set_error(DRT_INTERNAL_ERROR, "memset failed"));
+  if (cudaMallocHost(&s->hstate, sizeof(DecodeState)) != cudaSuccess || cudaMallocHost(&s->hflags, sizeof(int) * 8) != cudaSuccess)
+    return fail(set_error(DRT_INTERNAL_ERROR, "pinned alloc failed"));
+  memset(s->hstate, 0, sizeof(DecodeState));
+  // Tensor maps over the activation buffers and the K/V cache.
+  if ((rc = map_matrix(&s->m_xn64, s->xn, R, H, 64)) != DRT_OK) return fail(rc);
+  if ((rc = map_matrix(&s->m_xn128, s->xn, R, H, 128)) != DRT_OK) return fail(rc);
+  if ((rc = map_matrix(&s->m_attn64, s->attn, R, qd, 64)) != DRT_OK) return fail(rc);
+  if ((rc = map_matrix(&s->m_attn128, s->attn, R, qd, 128)) != DRT_OK) return fail(rc);
+  if ((rc = map_matrix(&s->m_act64, s->act, R, m->I, 64)) != DRT_OK) return fail(rc);
+  if ((rc = map_matrix(&s->m_act128, s->act, R, m->I, 128)) != DRT_OK) return fail(rc);
+  if ((rc = map_matrix(&s->m_xf64, s->xf, kMaxFrontier, H, 64)) != DRT_OK) return fail(rc);
+  {
+    const uint64_t dq[3] = {128, static_cast<uint64_t>(m->nq), static_cast<uint64_t>(R)};
+    const uint64_t sq[2] = {256, static_cast<uint64_t>(qd) * 2};
+    const uint32_t bq[3] = {64, static_cast<uint32_t>(m->rep), static_cast<uint32_t>(m->tile_pos)};
+    if ((rc = make_map(&s->m_q, s->q, 3, dq, sq, bq)) != DRT_OK) return fail(rc);
+    const uint64_t dk[3] = {128, static_cast<uint64_t>(s->max_seq), static_cast<uint64_t>(s->planes)};
+    const uint64_t sk[2] = {256, static_cast<uint64_t>(s->max_seq) * 256};
+    const uint32_t bk[3] = {64, 128, 1};
+    if ((rc = make_map(&s->m_k, s->kcache, 3, dk, sk, bk)) != DRT_OK) return fail(rc);
+    const uint64_t dv[3] = {static_cast<uint64_t>(s->max_seq), 128, static_cast<uint64_t>(s->planes)};
+    const uint64_t sv[2] = {static_cast<uint64_t>(s->max_seq) * 2, static_cast<uint64_t>(s->max_seq) * 256};
+    const uint32_t bv[3] = {64, 128, 1};
+    if ((rc = make_map(&s->m_v, s->vtcache, 3, dv, sv, bv)) != DRT_OK) return fail(rc);
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "session init failed"));
+  *out = s;
+  return DRT_OK;
+}
+
+extern "C" void drt_session_close(drt_session* s) {
+  if (!s) return;
+  cudaSetDevice(s->device);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  if (s->g_step) cudaGraphExecDestroy(s->g_step);
+  if (s->g_fwd) cudaGraphExecDestroy(s->g_fwd);
+  for (void* p : s->allocs) cudaFree(p);
+  if (s->trace) cudaFree(s->trace);
+  if (s->hstate) cudaFreeHost(s->hstate);
+  if (s->hflags) cudaFreeHost(s->hflags);
+  if (s->ev0) cudaEventDestroy(s->ev0);
+  if (s->ev1) cudaEventDestroy(s->ev1);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  delete s;
+}
+
+extern "C" int drt_session_kv_pointers(drt_session* s, void** k, void** v) {
+  REQUIRE(s, "null session");
+  if (k) *k = s->kcache;
+  if (v) *v = s->vtcache;
+  return DRT_OK;
+}
+
+extern "C" int drt_session_start(drt_session* s, const int32_t* x, int32_t n, int32_t prompt_len, int32_t block_size,
+                                 int32_t mask_token_id, int32_t exact_kv, int32_t steps, int64_t memory_budget_bytes,
+                                 double temperature, uint64_t seed) {
+  (void)exact_kv;
+  (void)seed;
+  REQUIRE(s && x, "null argument");
+  REQUIRE(n > 0 && n <= s->max_seq, "canvas length %d outside [1, %d]", n, s->max_seq);
+  REQUIRE(prompt_len >= 0 && prompt_len <= n, "prompt_len outside the canvas");
+  REQUIRE(block_size >= 1 && block_size <= 32, "block_size must be in [1, 32]");
+  REQUIRE(steps >= 1, "steps must be >= 1");
+  REQUIRE(memory_budget_bytes >= 0, "memory_budget_bytes must be >= 0");
+  if (temperature != 0.0) return set_error(DRT_UNSUPPORTED, "this device session scores at temperature 0 only");
+  if (memory_budget_bytes > 0 && memory_budget_bytes < s->bytes + s->m->bytes)
+    return set_error(DRT_INVALID_ARGUMENT, "memory budget %lld below the session's %lld device bytes",
+                     static_cast<long long>(memory_budget_bytes), static_cast<long long>(s->bytes + s->m->bytes));
+  for (int i = 0; i < n; ++i) REQUIRE(x[i] >= 0 && x[i] < s->m->V, "token %d at position %d outside the vocabulary", x[i], i);
+  CK(cudaSetDevice(s->device));
+  CK(cudaMemcpyAsync(s->canvas, x, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
+  memset(s->hstate, 0, sizeof(DecodeState));
+  s->hstate->canvas_len = n;
+  s->hstate->mask_id = mask_token_id;
+  s->hstate->active_block = -1;
+  CK(cudaMemcpyAsync(s->state, s->hstate, sizeof(DecodeState), cudaMemcpyHostToDevice, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  s->canvas_len = n;
+  s->origin = prompt_len;
+  s->block_size = block_size;
+  s->mask_id = mask_token_id;
+  s->started = true;
+  return DRT_OK;
+}
+
+extern "C" int drt_session_propose(drt_session* s, const int32_t* frontier, int32_t nf, int32_t window_end, int32_t frozen,
+                                   double* scores, int32_t* tokens, int32_t* forwarded) {
+  REQUIRE(s && frontier && scores && tokens, "null argument");
+  REQUIRE(s->started, "propose_device before start_device");
+  REQUIRE(nf >= 1 && nf <= kMaxFrontier, "frontier size %d outside [1, %d]", nf, kMaxFrontier);
+  REQUIRE(window_end >= 1 && window_end <= s->canvas_len, "window_end %d outside [1, %d]", window_end, s->canvas_len);
+  REQUIRE(frozen >= 0 && frozen < window_end, "frozen_prefix %d outside [0, window_end)", frozen);
+  REQUIRE(window_end - frozen <= kMaxFwdRows / 2, "active window of %d rows exceeds %d", window_end - frozen, kMaxFwdRows / 2);
+  for (int i = 0; i < nf; ++i) REQUIRE(frontier[i] >= frozen && frontier[i] < window_end, "frontier position %d outside [%d, %d)", frontier[i], frozen, window_end);
+  CK(cudaSetDevice(s->device));
+  if (s->g_fwd != nullptr && (s->g_fwd_geom[0] != s->origin || s->g_fwd_geom[1] != s->block_size)) {
+    cudaGraphExecDestroy(s->g_fwd);
+    s->g_fwd = nullptr;
+  }
+  if (s->g_fwd == nullptr) {
+    TRY(capture(s, false, &s->g_fwd));
+    s->g_fwd_geom[0] = s->origin;
+    s->g_fwd_geom[1] = s->block_size;
+  }
+  DecodeState* hs = s->hstate;
+  int cache_end = std::min(hs->cache_end, frozen);
+  CK(cudaEventRecord(s->ev0, s->stream));
+  int fwd_rows_total = 0;
+  // Final rows that are not cached yet: prefill them when they exceed one block.
+  if (frozen - cache_end > kMaxFwdRows / 2) {
+    TRY(prefill(s, cache_end, frozen, s->origin, s->block_size, 0));
+    fwd_rows_total += frozen - cache_end;
+    cache_end = frozen;
+  }
+  hs->fwd_pos0 = cache_end;
+  hs->fwd_rows = window_end - cache_end;
+  hs->kv_len = window_end;
+  hs->n_frontier = nf;
+  for (int i = 0; i < nf; ++i) {
+    hs->frontier_pos[i] = frontier[i];
+    hs->frontier_row[i] = frontier[i] - cache_end;
+  }
+  hs->cache_end = frozen;
+  hs->action = PLAN_PROCEED;
+  hs->exclude_token = s->cfg.decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD ? s->mask_id : -1;
+  fwd_rows_total += hs->fwd_rows;
+  CK(cudaMemcpyAsync(s->state, hs, sizeof(DecodeState), cudaMemcpyHostToDevice, s->stream));
+  CK(cudaGraphLaunch(s->g_fwd, s->stream));
+  CK(cudaEventRecord(s->ev1, s->stream));
+  CK(cudaMemcpyAsync(scores, s->conf, sizeof(double) * nf, cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaMemcpyAsync(tokens, s->token, sizeof(int) * nf, cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  TRY(check_status(s));
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, s->ev0, s->ev1);
+  s->m_ms += ms;
+  s->m_forwards += 1;
+  s->m_rows += fwd_rows_total;
+  if (forwarded) *forwarded = fwd_rows_total;
+  return DRT_OK;
+}
+
+extern "C" int drt_session_commit(drt_session* s, const int32_t* positions, const int32_t* tokens, int32_t n) {
+  REQUIRE(s && (n == 0 || (positions && tokens)), "null argument");
+  REQUIRE(s->started, "commit_device before start_device");
+  CK(cudaSetDevice(s->device));
+  for (int i = 0; i < n; ++i) {
+    REQUIRE(positions[i] >= 0 && positions[i] < s->canvas_len, "commit position %d outside the canvas", positions[i]);
+    REQUIRE(tokens[i] >= 0 && tokens[i] < s->m->V, "commit token %d outside the vocabulary", tokens[i]);
+    REQUIRE(positions[i] >= s->hstate->cache_end, "commit position %d is inside the frozen prefix", positions[i]);
+  }
+  for (int i = 0; i < n; ++i)
+    CK(cudaMemcpyAsync(s->canvas + positions[i], tokens + i, sizeof(int), cudaMemcpyHostToDevice, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  s->m_committed += n;
+  return DRT_OK;
+}
+
+extern "C" int drt_session_execute_window(drt_session* s, const int32_t* token_ids, int32_t n_tokens, const int32_t* scope,
+                                          int32_t n_scope, int32_t prompt_len, int32_t block_size, float* logits,
+                                          int32_t* forwarded_rows) {
+  REQUIRE(s && token_ids && scope && logits, "null argument");
+  REQUIRE(n_tokens >= 1 && n_tokens <= s->max_seq, "window length %d outside [1, %d]", n_tokens, s->max_seq);
+  REQUIRE(n_scope >= 1, "empty scope");
+  REQUIRE(prompt_len >= 0 && prompt_len <= n_tokens && block_size >= 1, "bad mask geometry");
+  for (int i = 0; i < n_scope; ++i) REQUIRE(scope[i] >= 0 && scope[i] < n_tokens, "scope position %d outside the window", scope[i]);
+  for (int i = 0; i < n_tokens; ++i) REQUIRE(token_ids[i] >= 0 && token_ids[i] < s->m->V, "token outside the vocabulary");
+  CK(cudaSetDevice(s->device));
+  drt_model* m = s->m;
+  CK(cudaMemcpyAsync(s->canvas, token_ids, sizeof(int) * n_tokens, cudaMemcpyHostToDevice, s->stream));
+  std::vector<int> rows;
+  for (int c0 = 0; c0 < n_tokens; c0 += s->rows_cap) {
+    Fwd f = {};
+    f.rows = std::min(s->rows_cap, n_tokens - c0);
+    f.pos0 = c0;
+    f.kv_len = c0 + f.rows;
+    f.prompt_len = prompt_len;
+    f.block_size = block_size;
+    TRY(enqueue_layers(s, f));
+    // Scope rows inside this chunk, in scope order, up to 64 per head pass.
+    std::vector<int> idx;
+    for (int i = 0; i < n_scope; ++i)
+      if (scope[i] >= c0 && scope[i] < c0 + f.rows) idx.push_back(i);
+    for (size_t b = 0; b < idx.size(); b += kMaxFrontier) {
+      const int cnt = static_cast<int>(std::min<size_t>(kMaxFrontier, idx.size() - b));
+      rows.assign(cnt, 0);
+      for (int j = 0; j < cnt; ++j) rows[j] = scope[idx[b + j]] - c0;
+      CK(cudaMemcpyAsync(s->scope_rows, rows.data(), sizeof(int) * cnt, cudaMemcpyHostToDevice, s->stream));
+      TRY(enqueue_head(s, s->scope_rows, cnt, nullptr, false));
+      for (int j = 0; j < cnt; ++j)
+        CK(cudaMemcpyAsync(logits + static_cast<size_t>(idx[b + j]) * m->V, s->logits + static_cast<size_t>(j) * m->V,
+                           sizeof(float) * m->V, cudaMemcpyDeviceToHost, s->stream));
+      CK(cudaStreamSynchronize(s->stream));
+    }
+  }
+  CK(cudaStreamSynchronize(s->stream));
+  TRY(check_status(s));
+  // The session canvas now holds this window; a later device decode must start again.
+  s->started = false;
+  s->hstate->cache_end = 0;
+  s->m_forwards += 1;
+  s->m_rows += n_tokens;
+  if (forwarded_rows) *forwarded_rows = n_tokens;
+  return DRT_OK;
+}
+
+extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p, const int32_t* prompt, int32_t prompt_len,
+                                    int32_t* out, drt_generate_result* result, drt_step_trace* trace) {
+  REQUIRE(s && p && prompt && out, "null argument");
+  REQUIRE(p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA || p->decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD,
+          "device generation runs bd3_fixed_quota or block_threshold");
+  REQUIRE(p->block_size >= 1 && p->block_size <= 32, "block_size must be in [1, 32]");
+  REQUIRE(p->steps >= 1, "steps must be >= 1");
+  REQUIRE(p->max_tokens >= 0, "max_tokens must be >= 0");
+  REQUIRE(prompt_len >= 1, "device generation requires a non-empty prompt");
+  const int canvas_len = prompt_len + p->max_tokens;
+  REQUIRE(canvas_len <= s->max_seq, "canvas of %d positions exceeds the session capacity %d", canvas_len, s->max_seq);
+  REQUIRE(std::isfinite(p->confidence_threshold) && p->confidence_threshold >= 0.0 && p->confidence_threshold <= 1.0,
+          "confidence_threshold must be finite and in [0, 1]");
+  if (p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA)
+    REQUIRE(prompt_len % p->block_size == 0, "BD3LM Candidate prompt length must be a multiple of block_size");
+  for (int i = 0; i < prompt_len; ++i) {
+    REQUIRE(prompt[i] >= 0 && prompt[i] < s->m->V, "prompt token %d outside the vocabulary", prompt[i]);
+    REQUIRE(prompt[i] != p->mask_token_id, "device generation cannot carry MASK in its prompt");
+  }
+  REQUIRE(p->mask_token_id >= 0 && p->mask_token_id < s->m->V, "mask token outside the vocabulary");
+  CK(cudaSetDevice(s->device));
+  if (p->trace_steps > s->trace_cap) {
+    if (s->trace) cudaFree(s->trace);
+    s->trace = nullptr;
+    CK(cudaMalloc(&s->trace, sizeof(StepTrace) * p->trace_steps));
+    s->trace_cap = p->trace_steps;
+    if (s->g_step) { cudaGraphExecDestroy(s->g_step); s->g_step = nullptr; }
+  }
+  s->origin = 0;
+  s->block_size = p->block_size;
+  if (s->g_step != nullptr && (s->g_step_geom[0] != s->origin || s->g_step_geom[1] != s->block_size)) {
+    cudaGraphExecDestroy(s->g_step);
+    s->g_step = nullptr;
+  }
+  if (s->g_step == nullptr) {
+    const int64_t before = g_launches;
+    TRY(capture(s, true, &s->g_step));
+    s->g_step_kernels = static_cast<int>(g_launches - before);
+    s->g_step_geom[0] = s->origin;
+    s->g_step_geom[1] = s->block_size;
+  }
+
+  std::vector<int> canvas(canvas_len, p->mask_token_id);
+  std::copy(prompt, prompt + prompt_len, canvas.begin());
+  cudaEvent_t e_total0 = nullptr, e_total1 = nullptr;
+  CK(cudaEventCreate(&e_total0));
+  CK(cudaEventCreate(&e_total1));
+  CK(cudaEventRecord(e_total0, s->stream));
+  CK(cudaMemcpyAsync(s->canvas, canvas.data(), sizeof(int) * canvas_len, cudaMemcpyHostToDevice, s->stream));
+  DecodeState* hs = s->hstate;
+  memset(hs, 0, sizeof(DecodeState));
+  hs->canvas_len = canvas_len;
+  hs->prompt_len = prompt_len;
+  hs->gen_len = p->max_tokens;
+  hs->block_size = p->block_size;
+  hs->mask_id = p->mask_token_id;
+  hs->eos_id = p->eos_token_id;
+  hs->threshold = p->confidence_threshold;
+  hs->tie_rel = kTieRel;
+  hs->active_block = -1;
+  hs->trace_cap = std::min(p->trace_steps, s->trace_cap);
+  if (p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA) {
+    hs->policy = POL_BD3_FIXED_QUOTA;
+    hs->exclude_token = -1;
+    const int bs = p->block_size;
+    int count = 0;
+    if (p->max_tokens > 0) {
+      const int first = prompt_len / bs;
+      const int last = (prompt_len + p->max_tokens - 1) / bs;
+      count = last - first + 1;
+    }
+    const int sched = (p->max_tokens + bs - 1) / bs;
+    hs->steps_per_block = sched > 0 ? (p->steps + sched - 1) / sched : 0;
+    hs->iteration_limit = count * hs->steps_per_block;
+  } else {
+    hs->policy = POL_BLOCK_THRESHOLD;
+    hs->iteration_limit = p->steps;
+    hs->exclude_token = p->mask_token_id;
+    hs->rounds_cap = std::max(0, p->rounds_per_block);
+  }
+  hs->cache_end = prompt_len;
+  CK(cudaMemcpyAsync(s->state, hs, sizeof(DecodeState), cudaMemcpyHostToDevice, s->stream));
+  // Prefill the prompt (block-causal with origin 0).
+  CK(cudaEventRecord(s->ev0, s->stream));
+  const int64_t launches0 = g_launches;
+  TRY(prefill(s, 0, prompt_len, 0, p->block_size, 0));
+  const int prefill_launches = static_cast<int>(g_launches - launches0);
+  CK(cudaEventRecord(s->ev1, s->stream));
+  cudaEvent_t e_dec0 = nullptr, e_dec1 = nullptr;
+  cudaEvent_t flag_ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  CK(cudaEventCreate(&e_dec0));
+  CK(cudaEventCreate(&e_dec1));
+  for (auto& e : flag_ev) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  CK(cudaEventRecord(e_dec0, s->stream));
+  const int limit = hs->iteration_limit;
+  int rc = DRT_OK;
+  int replays = 0;
+  for (int i = 0; i < limit; ++i) {
+    ++replays;
+    if (cudaGraphLaunch(s->g_step, s->stream) != cudaSuccess) { rc = set_error(DRT_INTERNAL_ERROR, "graph launch failed"); break; }
+    cudaMemcpyAsync(&s->hflags[i & 3], &s->state->stopped, sizeof(int), cudaMemcpyDeviceToHost, s->stream);
+    cudaEventRecord(flag_ev[i & 3], s->stream);
+    if (i >= 2) {
+      const int j = (i - 2) & 3;
+      if (cudaEventQuery(flag_ev[j]) == cudaSuccess && s->hflags[j]) break;
+    }
+  }
+  cudaEventRecord(e_dec1, s->stream);
+  cudaMemcpyAsync(hs, s->state, sizeof(DecodeState), cudaMemcpyDeviceToHost, s->stream);
+  cudaMemcpyAsync(out, s->canvas, sizeof(int) * canvas_len, cudaMemcpyDeviceToHost, s->stream);
+  cudaEventRecord(e_total1, s->stream);
+  cudaError_t se = cudaStreamSynchronize(s->stream);
+  if (rc == DRT_OK && se != cudaSuccess) rc = set_error(DRT_INTERNAL_ERROR, "decode failed: %s", cudaGetErrorString(se));
+  float pre_ms = 0.f, dec_ms = 0.f, tot_ms = 0.f;
+  cudaEventElapsedTime(&pre_ms, s->ev0, s->ev1);
+  cudaEventElapsedTime(&dec_ms, e_dec0, e_dec1);
+  cudaEventElapsedTime(&tot_ms, e_total0, e_total1);
+  cudaEventDestroy(e_dec0);
+  cudaEventDestroy(e_dec1);
+  cudaEventDestroy(e_total0);
+  cudaEventDestroy(e_total1);
+  for (auto& e : flag_ev) cudaEventDestroy(e);
+  TRY(rc);
+  TRY(check_status(s));
+  if (hs->error) return set_error(DRT_INTERNAL_ERROR, "device plan rejected the request geometry");
+  if (trace != nullptr && p->trace_steps > 0) {
+    const int nt = std::min(hs->forward_count, std::min(p->trace_steps, s->trace_cap));
+    static_assert(sizeof(StepTrace) == sizeof(drt_step_trace), "trace layout");
+    CK(cudaMemcpy(trace, s->trace, sizeof(StepTrace) * nt, cudaMemcpyDeviceToHost));
+  }
+  if (result) {
+    result->forward_count = hs->forward_count;
+    result->iteration_count = hs->iteration_count;
+    result->committed_token_count = hs->committed_count;
+    result->near_tie_steps = hs->near_tie_steps;
+    result->exact_tie_steps = hs->exact_tie_steps;
+    result->stopped = hs->stopped;
+    result->canvas_len = canvas_len;
+    result->prefill_ms = pre_ms;
+    result->decode_ms = dec_ms;
+    result->total_ms = tot_ms;
+    result->kernel_launches = prefill_launches + replays * s->g_step_kernels;
+  }
+  s->m_forwards += hs->forward_count;
+  s->m_committed += hs->committed_count;
+  s->m_near += hs->near_tie_steps;
+  s->m_exact += hs->exact_tie_steps;
+  s->m_ms += pre_ms + dec_ms;
+  s->started = false;
+  return DRT_OK;
+}
+
+extern "C" int drt_session_metrics(drt_session* s, drt_metrics* out) {
+  REQUIRE(s && out, "null argument");
+  out->forward_count = s->m_forwards;
+  out->forwarded_rows = s->m_rows;
+  out->prefill_rows = s->m_prefill_rows;
+  out->committed_token_count = s->m_committed;
+  out->near_tie_steps = s->m_near;
+  out->exact_tie_steps = s->m_exact;
+  out->forward_ms_total = s->m_ms;
+  out->device_bytes = s->bytes;
+  return DRT_OK;
+}
+
+// ======================================================================= kernel-level entry points
+extern "C" size_t drt_selector_scratch_bytes(int32_t n_rows, int32_t vocab) {
+  const size_t chunks = (static_cast<size_t>(std::max(vocab, 1)) + kSelChunk - 1) / kSelChunk;
+  const size_t np = static_cast<size_t>(std::max(n_rows, 1)) * chunks;
+  return 256 + np * (4 + 4 + 8) + static_cast<size_t>(std::max(n_rows, 1)) * (4 + 8 + 8) + 1024;
+}
+
+extern "C" int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows, int32_t vocab, int32_t mode, double temperature,
+                                 void* scratch, double* conf, int32_t* token, void* stream) {
+  REQUIRE(logits && scratch && conf && token, "null argument");
+  REQUIRE(n_rows >= 0 && vocab >= 1 && ld >= vocab, "bad selector geometry");
+  REQUIRE(mode == DRT_SELECT_MAX_PROB || mode == DRT_SELECT_NEG_ENTROPY, "unknown selector mode %d", mode);
+  if (n_rows == 0) return DRT_OK;
+  REQUIRE(n_rows <= 65535, "at most 65535 rows per call");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int chunks = (vocab + kSelChunk - 1) / kSelChunk;
+  const size_t np = static_cast<size_t>(n_rows) * chunks;
+  uint8_t* p = static_cast<uint8_t*>(scratch);
+  auto take = [&](size_t bytes) { uint8_t* q = p; p += (bytes + 255) & ~size_t(255); return q; };
+  SelArgs a;
+  memset(&a, 0, sizeof(a));
+  a.part_sum = reinterpret_cast<double*>(take(np * 8));
+  a.row_amax = reinterpret_cast<double*>(take(static_cast<size_t>(n_rows) * 8));
+  a.row_sum = reinterpret_cast<double*>(take(static_cast<size_t>(n_rows) * 8));
+  a.part_max = reinterpret_cast<float*>(take(np * 4));
+  a.part_idx = reinterpret_cast<int*>(take(np * 4));
+  a.counters = reinterpret_cast<int*>(take(static_cast<size_t>(n_rows) * 4));
+  CK(cudaMemsetAsync(a.counters, 0, sizeof(int) * n_rows, st));
+  a.logits = logits;
+  a.ld = ld;
+  a.rows = n_rows;
+  a.vocab = vocab;
+  a.chunk = kSelChunk;
+  a.nchunks = chunks;
+  a.mode = mode;
+  a.temperature = mode == DRT_SELECT_NEG_ENTROPY ? temperature : 0.0;
+  a.exclude = -1;
+  a.conf = conf;
+  a.token = token;
+  CK(launch_k(sel_pass1_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  if (mode == DRT_SELECT_NEG_ENTROPY) CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  return DRT_OK;
+}
+
+extern "C" size_t drt_linear_scratch_bytes(int32_t rows, int32_t n, int32_t K, int32_t splits) {
+  const size_t tiles = static_cast<size_t>(std::max(n, 128) / 128) * ((std::max(rows, 1) + 63) / 64);
+  return 1024 + tiles * std::max(splits, 1) * 64 * 128 * 4 + tiles * 4 + 4;
+}
+
+extern "C" int drt_linear_bf16(const void* x, const void* w, float* y, int32_t rows, int32_t n, int32_t K, int32_t splits,
+                               int32_t round_bf16, void* scratch, void* stream) {
+  REQUIRE(x && w && y && scratch, "null argument");
+  REQUIRE(rows >= 1 && n >= 128 && n % 128 == 0 && K >= 64 && K % 64 == 0, "linear needs n %% 128 == 0 and K %% 64 == 0");
+  REQUIRE(splits >= 1 && splits <= K / 64, "splits outside [1, K/64]");
+  TRY(configure_kernels());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap ma, mb;
+  TRY(map_matrix(&ma, w, n, K, 128));
+  TRY(map_matrix(&mb, x, rows, K, 64));
+  const int tiles_m = n / 128, tiles_n = (rows + 63) / 64;
+  const int kb = K / 64;
+  const int per = (kb + splits - 1) / splits;
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.n_out = n;
+  a.K = K;
+  a.rows = rows;
+  a.splits = (kb + per - 1) / per;
+  a.kb_per_split = per;
+  a.stages = std::max(1, std::min(per, 8));
+  uint8_t* p = static_cast<uint8_t*>(scratch);
+  a.workspace = reinterpret_cast<float*>(p);
+  a.counters = reinterpret_cast<int*>(p + static_cast<size_t>(tiles_m) * tiles_n * a.splits * 64 * 128 * 4);
+  a.status = a.counters + static_cast<size_t>(tiles_m) * tiles_n;
+  CK(cudaMemsetAsync(a.counters, 0, sizeof(int) * (static_cast<size_t>(tiles_m) * tiles_n + 1), st));
+  a.epi = round_bf16 ? EPI_STORE_F32 : EPI_STORE_RAW;
+  a.out_f32 = y;
+  a.ld_out = n;
+  CK(launch_k(gemm_swapab_kernel<64>, dim3(tiles_m, tiles_n, a.splits), dim3(128), GemmCfg<64>::smem_bytes(a.stages), st, false, ma,
+              mb, a));
+  return DRT_OK;
+}

@@ -1,0 +1,363 @@
+// Skinny-M linear layers on the 5th-generation tensor cores.
+//
+// Every linear in the decode step is y = x @ W^T with W [n_out, K] bf16 and x [rows, K] bf16
+// (rows = 32..64 active canvas rows per denoising step, up to thousands for a prompt
+// prefill). The kernel computes the transposed product D^T = W . x^T so the weight tile is
+// the M = 128 operand of tcgen05.mma and the activation rows are the N operand (N = BN); the
+// f32 accumulator lives in TMEM with weight row m in TMEM lane m and activation row n in
+// column n. Weights stream from HBM through a TMA ring (SWIZZLE_128B, evict-first hint); the
+// activation tile for the same K block arrives on its own barrier so that, under
+// programmatic dependent launch, the weight prefetch of this kernel overlaps the tail of the
+// kernel that produces x.
+//
+// Split-K: grid.z CTAs share one output tile; each writes its f32 partial to a workspace slot
+// and the last CTA to arrive (per-tile counter) sums the partials in a fixed order and runs
+// the epilogue, so results do not depend on arrival order. The counter is reset by that CTA.
+//
+// Epilogues follow the MLX precision contract of the reference forward
+// (python/src/edllm/backends/mlx_ops.py:97-130 linear, :21-35 rms_norm, :133-144 rope,
+// :147-154 swiglu): the bf16 x bf16 matmul output is rounded to bf16 and widened to f32,
+// bias is added in f32, and the residual stream stays f32.
+#pragma once
+#include "common.cuh"
+
+namespace drt {
+
+enum GemmEpilogue : int {
+  EPI_STORE_F32 = 0,  // out_f32[row, n] = bf16r(acc) + bias        (logits, tests)
+  EPI_RESID = 1,      // out_f32[row, n] += bf16r(acc) + bias       (o_proj / down_proj)
+  EPI_SWIGLU = 2,     // out_bf16[row, j] = bf16(silu(g) * u)       (gate/up interleaved per tile)
+  EPI_QKV = 3,        // q/k RMSNorm + RoPE; q -> q buffer, k -> K cache, v -> V^T cache
+  EPI_STORE_RAW = 4,  // out_f32[row, n] = acc (no rounding; tests)
+};
+
+struct GemmArgs {
+  int n_out;             // rows of W; multiple of 128
+  int K;                 // multiple of 64
+  int rows;              // activation rows covered by the grid
+  const int* rows_dev;   // optional device-side row count (<= rows) for static graphs
+  int splits;            // split-K factor
+  int kb_per_split;      // K blocks of 64 per split (the last split takes the remainder)
+  int stages;            // smem ring depth
+  float* workspace;      // split partials
+  int* counters;         // per-tile arrival counters (zero at rest)
+  int* status;           // device error word
+  int epi;
+  // epilogue operands
+  float* out_f32;
+  __nv_bfloat16* out_bf16;
+  int ld_out;            // row stride (elements) of out_f32 / out_bf16
+  const float* bias;     // optional [n_out] (f32 copy of the bf16 bias)
+  // EPI_QKV
+  const float* qnorm_w;  // [128] or null (no QK-norm)
+  const float* knorm_w;  // [128] or null
+  const float* rope_cos; // [max_pos][64]
+  const float* rope_sin; // [max_pos][64]
+  int pos0;              // absolute position of activation row 0
+  const int* pos0_dev;   // optional device-side pos0
+  int nq, nkv;
+  __nv_bfloat16* kcache; // this layer: [nkv][max_seq][128]
+  __nv_bfloat16* vtcache;// this layer: [nkv][128][max_seq]
+  int max_seq;
+  float eps;
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kABytes = 128 * 128;       // 128 rows x 64 bf16
+  static constexpr int kBBytes = BN * 128;        // BN rows x 64 bf16
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static size_t smem_bytes(int stages) {
+    return 1024 + static_cast<size_t>(stages) * kStageBytes + 256;
+  }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Epilogue for one chunk of 32 accumulator columns (activation rows col0 .. col0+ncols-1).
+// v[i] holds this thread's weight row (m0 + tid) for activation row col0 + i.
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int col0,
+                                                    int ncols, int m0, int tid, float* xs,
+                                                    int pos0) {
+  const int n = m0 + tid;
+  const float b = a.bias != nullptr ? a.bias[n] : 0.0f;
+  switch (a.epi) {
+    case EPI_STORE_RAW: {
+      for (int i = 0; i < ncols; ++i) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = v[i];
+      break;
+    }
+    case EPI_STORE_F32: {
+      for (int i = 0; i < ncols; ++i)
+        a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = __fadd_rn(bf16_round(v[i]), b);
+      break;
+    }
+    case EPI_RESID: {
+      for (int i = 0; i < ncols; ++i) {
+        float* p = a.out_f32 + static_cast<size_t>(col0 + i) * a.ld_out + n;
+        *p = __fadd_rn(*p, __fadd_rn(bf16_round(v[i]), b));
+      }
+      break;
+    }
+    case EPI_SWIGLU: {
+      // Tile layout (set by the weight packer): lanes 0..63 = gate rows j0..j0+63,
+      // lanes 64..127 = up rows j0..j0+63 of the same intermediate features.
+      const int j0 = (m0 >> 1);
+      if (tid >= 64) {
+        for (int i = 0; i < 32; ++i) xs[i * 64 + (tid - 64)] = __fadd_rn(bf16_round(v[i]), b);
+      }
+      __syncthreads();
+      if (tid < 64) {
+        for (int i = 0; i < ncols; ++i) {
+          const float g = __fadd_rn(bf16_round(v[i]), b);
+          const float u = xs[i * 64 + tid];
+          const float sig = 1.0f / (1.0f + expf(-g));
+          const float act = __fmul_rn(__fmul_rn(g, sig), u);
+          a.out_bf16[static_cast<size_t>(col0 + i) * a.ld_out + j0 + tid] = __float2bfloat16_rn(act);
+        }
+      }
+      __syncthreads();
+      break;
+    }
+    case EPI_QKV: {
+      const int tile = m0 >> 7;
+      const bool is_q = tile < a.nq;
+      const bool is_k = !is_q && tile < a.nq + a.nkv;
+      if (!is_q && !is_k) {
+        // V: no norm, no rope. Written transposed: V^T[g][d][pos], contiguous along pos.
+        const int g = tile - a.nq - a.nkv;
+        __nv_bfloat16* dst = a.vtcache + (static_cast<size_t>(g) * 128 + tid) * a.max_seq + pos0 + col0;
+        const bool vec = (ncols == 32) && (((pos0 + col0) & 7) == 0);
+        if (vec) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            __align__(16) __nv_bfloat16 t[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) t[e] = __float2bfloat16_rn(__fadd_rn(bf16_round(v[q * 8 + e]), b));
+            *reinterpret_cast<uint4*>(dst + q * 8) = *reinterpret_cast<const uint4*>(t);
+          }
+        } else {
+          for (int i = 0; i < ncols; ++i) dst[i] = __float2bfloat16_rn(__fadd_rn(bf16_round(v[i]), b));
+        }
+        break;
+      }
+      const float* nw = is_q ? a.qnorm_w : a.knorm_w;
+      for (int i = 0; i < 32; ++i) {
+        const float val = __fadd_rn(bf16_round(v[i]), b);
+        v[i] = val;
+        xs[i * 128 + tid] = val;
+      }
+      __syncthreads();
+      float* rs = xs + 32 * 128;  // 32 per-row scales
+      const int warp = tid >> 5, lane = tid & 31;
+      if (nw != nullptr) {
+        for (int i = warp * 8; i < warp * 8 + 8; ++i) {
+          float ss = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float x = xs[i * 128 + lane + 32 * j];
+            ss = __fmaf_rn(x, x, ss);
+          }
+          ss = warp_sum(ss);
+          if (lane == 0) rs[i] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
+        }
+      }
+      __syncthreads();
+      const int partner = tid ^ 64;
+      const float w_self = nw != nullptr ? nw[tid] : 1.0f;
+      const float w_part = nw != nullptr ? nw[partner] : 1.0f;
+      const int head = is_q ? tile : tile - a.nq;
+      for (int i = 0; i < ncols; ++i) {
+        float x = v[i];
+        float xp = xs[i * 128 + partner];
+        if (nw != nullptr) {
+          x = __fmul_rn(__fmul_rn(x, rs[i]), w_self);
+          xp = __fmul_rn(__fmul_rn(xp, rs[i]), w_part);
+        }
+        const int pos = pos0 + col0 + i;
+        const float c = a.rope_cos[static_cast<size_t>(pos) * 64 + (tid & 63)];
+        const float s = a.rope_sin[static_cast<size_t>(pos) * 64 + (tid & 63)];
+        const float rot = tid < 64 ? -xp : xp;
+        const float out = __fadd_rn(__fmul_rn(x, c), __fmul_rn(rot, s));
+        if (is_q) {
+          a.out_bf16[(static_cast<size_t>(col0 + i) * a.nq + head) * 128 + tid] = __float2bfloat16_rn(out);
+        } else {
+          a.kcache[(static_cast<size_t>(head) * a.max_seq + pos) * 128 + tid] = __float2bfloat16_rn(out);
+        }
+      }
+      __syncthreads();
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(128, 1)
+    gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const GemmArgs a) {
+  using Cfg = GemmCfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stages = a.stages;
+  uint8_t* ring = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + static_cast<size_t>(stages) * Cfg::kStageBytes);
+  uint64_t* fullA = bars;
+  uint64_t* fullB = bars + stages;
+  uint64_t* empty = bars + 2 * stages;
+  uint64_t* accum = bars + 3 * stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] error, [1] last-CTA
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int m0 = blockIdx.x * 128;
+  const int n0 = blockIdx.y * BN;
+  const int split = blockIdx.z;
+  const int kb_total = a.K >> 6;
+  const int kb0 = split * a.kb_per_split;
+  const int nkb = min(a.kb_per_split, kb_total - kb0);
+
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&fullA[s], 1);
+      mbar_init(&fullB[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  __syncwarp();
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // Weight prefetch: independent of the producer kernel, so it runs before the PDL wait.
+  const int npre = min(stages, nkb);
+  uint64_t policy = 0;
+  if (tid == 0) {
+    policy = l2_policy_evict_first();
+    for (int i = 0; i < npre; ++i) {
+      mbar_expect_tx(&fullA[i], Cfg::kABytes);
+      tma_load_2d_hint(ring + static_cast<size_t>(i) * Cfg::kStageBytes, &tmA, &fullA[i], (kb0 + i) * 64, m0, policy);
+    }
+  }
+  griddep_wait();
+  griddep_launch_dependents();
+
+  if (tid == 0) {
+    bool ok = true;
+    for (int i = 0; i < nkb && ok; ++i) {
+      const int s = i % stages;
+      uint8_t* st = ring + static_cast<size_t>(s) * Cfg::kStageBytes;
+      if (i >= stages) {
+        if (!mbar_wait(&empty[s], ((i / stages) - 1) & 1)) { ok = false; break; }
+        mbar_expect_tx(&fullA[s], Cfg::kABytes);
+        tma_load_2d_hint(st, &tmA, &fullA[s], (kb0 + i) * 64, m0, policy);
+      }
+      mbar_expect_tx(&fullB[s], Cfg::kBBytes);
+      tma_load_2d(st + Cfg::kABytes, &tmB, &fullB[s], (kb0 + i) * 64, n0);
+    }
+    if (!ok) { record_error(a.status, DEV_TIMEOUT_TMA); flags[0] = 1; }
+  } else if (tid == 32) {
+    const uint32_t idesc = idesc_bf16_f32(128, BN);
+    bool ok = true;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % stages;
+      const uint32_t ph = (i / stages) & 1;
+      if (!mbar_wait(&fullA[s], ph) || !mbar_wait(&fullB[s], ph)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t a_addr = smem_u32(ring + static_cast<size_t>(s) * Cfg::kStageBytes);
+      const uint32_t b_addr = a_addr + Cfg::kABytes;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        umma_bf16(tmem, sdesc_kmajor_sw128(a_addr + kk * 32), sdesc_kmajor_sw128(b_addr + kk * 32), idesc,
+                  (i | kk) != 0 ? 1u : 0u);
+      }
+      umma_commit(&empty[s]);
+    }
+    if (!ok) { record_error(a.status, DEV_TIMEOUT_MMA); flags[0] = 1; }
+    umma_commit(accum);
+  }
+
+  // ---------------- epilogue (all four warps; warp w owns TMEM lanes [32w, 32w+32))
+  const bool acc_ok = mbar_wait(accum, 0);
+  tc_fence_after();
+  if (!acc_ok) { record_error(a.status, DEV_TIMEOUT_EPI); flags[0] = 1; }
+  __syncthreads();
+  const bool failed = flags[0] != 0;
+  int rows_valid = a.rows;
+  if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
+  const int pos0 = a.pos0_dev != nullptr ? *a.pos0_dev : a.pos0;
+  const int ncol_valid = max(0, min(BN, rows_valid - n0));
+  float* xs = reinterpret_cast<float*>(ring);  // epilogue exchange reuses the (drained) ring
+  const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+
+  if (!failed && ncol_valid > 0) {
+    if (a.splits == 1) {
+      for (int cb = 0; cb < ncol_valid; cb += 32) {
+        float v[32];
+        tmem_ld32(lane_addr + cb, v);
+        gemm_epilogue_chunk(a, v, n0 + cb, min(32, ncol_valid - cb), m0, tid, xs, pos0);
+      }
+    } else {
+      const int tile_id = blockIdx.y * gridDim.x + blockIdx.x;
+      float* ws_tile = a.workspace + static_cast<size_t>(tile_id) * a.splits * BN * 128;
+      float* mine = ws_tile + static_cast<size_t>(split) * BN * 128;
+      for (int cb = 0; cb < ncol_valid; cb += 32) {
+        float v[32];
+        tmem_ld32(lane_addr + cb, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mine[(cb + i) * 128 + tid] = v[i];
+      }
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) {
+        const int old = atomicAdd(&a.counters[tile_id], 1);
+        flags[1] = (old == a.splits - 1) ? 1 : 0;
+      }
+      __syncthreads();
+      if (flags[1]) {
+        __threadfence();
+        for (int cb = 0; cb < ncol_valid; cb += 32) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+          for (int s = 0; s < a.splits; ++s) {
+            const float* src = ws_tile + static_cast<size_t>(s) * BN * 128;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += __ldcg(&src[(cb + i) * 128 + tid]);
+          }
+          gemm_epilogue_chunk(a, v, n0 + cb, min(32, ncol_valid - cb), m0, tid, xs, pos0);
+        }
+        if (tid == 0) a.counters[tile_id] = 0;
+      }
+    }
+  }
+  if (failed && tid == 0) {
+    // Drain loads that may still be landing in this CTA's shared memory (bounded).
+    for (int s = 0; s < min(stages, nkb); ++s) {
+      mbar_wait(&fullA[s], 0);
+      mbar_wait(&fullB[s], 0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, Cfg::kTmemCols);
+}
+
+}  // namespace drt

@@ -1,0 +1,125 @@
+// Row-wise kernels of the decode step: embedding gather into the f32 residual stream,
+// RMSNorm to the bf16 matmul input, and the seeded synthetic weight generator.
+#pragma once
+#include "common.cuh"
+
+namespace drt {
+
+// h[r, :] = f32(E[tokens[pos0 + r], :])   (python/src/edllm/backends/mlx_forward.py:1538-1557)
+__global__ void embed_rows_kernel(const int* __restrict__ tokens, int pos0, const int* pos0_dev, int rows,
+                                  const int* rows_dev, const __nv_bfloat16* __restrict__ table, int H,
+                                  float* __restrict__ h, int vocab, int* status) {
+  griddep_wait();
+  griddep_launch_dependents();
+  int rows_valid = rows;
+  if (rows_dev != nullptr) rows_valid = min(rows_valid, *rows_dev);
+  const int r = blockIdx.x;
+  if (r >= rows_valid) return;
+  const int p0 = pos0_dev != nullptr ? *pos0_dev : pos0;
+  const int tok = tokens[p0 + r];
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0) record_error(status, DEV_BAD_SHAPE);
+    return;
+  }
+  const __nv_bfloat16* src = table + static_cast<size_t>(tok) * H;
+  float* dst = h + static_cast<size_t>(r) * H;
+  for (int k = threadIdx.x * 2; k < H; k += blockDim.x * 2) {
+    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(src + k);
+    *reinterpret_cast<float2*>(dst + k) = make_float2(__low2float(v), __high2float(v));
+  }
+}
+
+// out[r, :] = bf16((x * (1 / sqrt(mean(x^2) + eps))) * w) with x = h[src_row(r), :] in f32.
+// The reference rms_norm (mlx_ops.py:21-35) keeps the f32 residual dtype and multiplies the
+// weight in f32; the bf16 cast is the one the following linear applies (mlx_ops.py:122-125).
+// src_row(r) = row_index[r] when row_index is given (the frontier gather before lm_head).
+__global__ void rmsnorm_bf16_kernel(const float* __restrict__ h, int ld_h, const int* row_index, int rows,
+                                    const int* rows_dev, const float* __restrict__ w, float eps, int H,
+                                    __nv_bfloat16* __restrict__ out, int ld_out) {
+  griddep_wait();
+  griddep_launch_dependents();
+  int rows_valid = rows;
+  if (rows_dev != nullptr) rows_valid = min(rows_valid, *rows_dev);
+  const int r = blockIdx.x;
+  if (r >= rows_valid) return;
+  const int src = row_index != nullptr ? row_index[r] : r;
+  const float* x = h + static_cast<size_t>(src) * ld_h;
+  __shared__ float red[32];
+  float ss = 0.0f;
+  for (int k = threadIdx.x; k < H; k += blockDim.x) ss = __fmaf_rn(x[k], x[k], ss);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float var = __fdiv_rn(red[0], static_cast<float>(H));
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  __nv_bfloat16* y = out + static_cast<size_t>(r) * ld_out;
+  for (int k = threadIdx.x; k < H; k += blockDim.x) {
+    y[k] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(x[k], scale), w[k]));
+  }
+}
+
+// ---------------------------------------------------------------- synthetic weights
+// A seeded, counter-based generator whose every step is integer arithmetic plus one f32
+// multiply, so a NumPy restatement reproduces each bf16 weight bit for bit:
+//   z = splitmix64_finalize(seed * K1 + tensor_id * K2 + index)
+//   u = byte0(z) + byte1(z) + byte2(z) + byte3(z) - 510          (Irwin-Hall of 4 bytes)
+//   w = bf16_rn(f32(u) * f32(std / 147.80020))                    (unit variance of u is 147.8^2)
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ float synth_value(uint64_t seed, uint32_t tensor_id, uint64_t index, float scale) {
+  const uint64_t z = mix64(seed * 0x9E3779B97F4A7C15ull + static_cast<uint64_t>(tensor_id) * 0xD1B54A32D192ED03ull + index);
+  const int u = static_cast<int>(z & 0xFF) + static_cast<int>((z >> 8) & 0xFF) + static_cast<int>((z >> 16) & 0xFF) +
+                static_cast<int>((z >> 24) & 0xFF) - 510;
+  return __fmul_rn(static_cast<float>(u), scale);
+}
+
+// Fill logical rows [0, rows) x cols of tensor `tensor_id` into a packed destination:
+// logical row r lands at dst row (r / grp) * grp_stride + grp_off + r % grp.
+__global__ void synth_fill_kernel(__nv_bfloat16* dst, int64_t rows, int64_t cols, uint64_t seed, uint32_t tensor_id,
+                                  float scale, int64_t grp, int64_t grp_stride, int64_t grp_off) {
+  const int64_t total = rows * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    const int64_t dr = (r / grp) * grp_stride + grp_off + r % grp;
+    dst[dr * cols + c] = __float2bfloat16_rn(synth_value(seed, tensor_id, static_cast<uint64_t>(i), scale));
+  }
+}
+
+// Copy logical rows of a host-provided bf16 tensor (already on the device) into the packed
+// destination with the same row map as synth_fill_kernel.
+__global__ void pack_rows_kernel(__nv_bfloat16* dst, const __nv_bfloat16* src, int64_t rows, int64_t cols, int64_t grp,
+                                 int64_t grp_stride, int64_t grp_off) {
+  const int64_t total = rows * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    const int64_t dr = (r / grp) * grp_stride + grp_off + r % grp;
+    dst[dr * cols + c] = src[i];
+  }
+}
+
+__global__ void fill_f32_kernel(float* dst, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = v;
+}
+
+__global__ void bf16_to_f32_kernel(float* dst, const __nv_bfloat16* src, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = __bfloat162float(src[i]);
+}
+
+}  // namespace drt

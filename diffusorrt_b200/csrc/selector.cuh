@@ -1,0 +1,210 @@
+// Fused unmask selector: per-row vocabulary softmax statistics in float64, confidence and
+// committed token, in one pass over HBM for max-prob and two for entropy.
+//
+// Max-prob (TopConfidence, python/src/edllm/backends/diffusion_runtime.py:179-192):
+//   p = exp(f64(x) - max) / sum(exp(f64(x) - max)); conf = max p = 1 / S; token = argmax p.
+//   exp is monotone and 1/S scales every entry equally, so argmax p is the FIRST index of the
+//   largest f32 logit (integer-exact), and conf = 1 / S with S accumulated in f64.
+// Entropy (NegEntropy, diffusion_runtime.py:90-114 without top-p):
+//   a = f64(x) / T (T > 0), p = softmax(a), conf = f32(sum p * log(p + 1e-10)), token = argmax p.
+//
+// Layout: grid (chunks, rows); each CTA reduces one chunk of a row to (max, first argmax,
+// sum exp(x - chunk_max)); the last CTA of a row (arrival counter, reset by that CTA) merges
+// the row's chunk partials in chunk order, so the result is independent of scheduling.
+// S differs from NumPy's pairwise sum of its own exp in the last bits; the decode policy
+// flags ranking decisions closer than the certified bound (see policy.cuh).
+#pragma once
+#include "common.cuh"
+
+namespace drt {
+
+enum SelMode : int { SEL_MAXPROB = 0, SEL_ENTROPY = 1 };
+
+struct SelArgs {
+  const float* logits;
+  int64_t ld;             // row stride in floats
+  const int* row_index;   // optional: row r reads logits row row_index[r]
+  int rows;
+  const int* rows_dev;    // optional device-side row count
+  int vocab;
+  int chunk;              // elements per CTA (kSelChunk)
+  int nchunks;
+  int mode;
+  double temperature;     // entropy only; <= 0 means no scaling
+  int exclude;            // token index scored as -inf (MASK exclusion), -1 for none
+  const int* exclude_dev; // optional device-side override of `exclude`
+  float* part_max;        // [rows * nchunks]
+  int* part_idx;
+  double* part_sum;
+  int* counters;          // [rows]
+  double* row_amax;       // [rows] adjusted max (entropy)
+  double* row_sum;        // [rows] S (entropy)
+  double* conf;           // [rows]
+  int* token;             // [rows]
+  int* status;
+};
+
+constexpr int kSelThreads = 256;
+constexpr int kSelChunk = 8192;  // logits per CTA: 32 per thread
+
+__device__ __forceinline__ void argmax_merge(float& m, int& idx, float m2, int idx2) {
+  if (m2 > m || (m2 == m && idx2 < idx)) {
+    m = m2;
+    idx = idx2;
+  }
+}
+
+__device__ __forceinline__ double sel_adjust(double x, double T) { return T > 0.0 ? x / T : x; }
+
+// Pass 1: chunk max / argmax / sum of exp relative to the chunk's adjusted max.
+__global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  int rows_valid = a.rows;
+  if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
+  const int r = blockIdx.y;
+  if (r >= rows_valid) return;
+  const int c = blockIdx.x;
+  const int src = a.row_index != nullptr ? a.row_index[r] : r;
+  const float* x = a.logits + static_cast<int64_t>(src) * a.ld;
+  const int lo = c * a.chunk;
+  const int hi = min(a.vocab, lo + a.chunk);
+  const int tid = threadIdx.x;
+  const bool vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
+  const int excl = a.exclude_dev != nullptr ? *a.exclude_dev : a.exclude;
+
+  // Stage the thread's 32 values in registers (chunk = 8 x 256 float4 groups).
+  float vals[32];
+  float m = -INFINITY;
+  int idx = INT_MAX;
+#pragma unroll
+  for (int k = 0; k < kSelChunk / (kSelThreads * 4); ++k) {
+    const int base = lo + (k * kSelThreads + tid) * 4;
+    if (vec && base + 4 <= hi) {
+      const float4 q = __ldcs(reinterpret_cast<const float4*>(x + base));
+      vals[k * 4 + 0] = q.x;
+      vals[k * 4 + 1] = q.y;
+      vals[k * 4 + 2] = q.z;
+      vals[k * 4 + 3] = q.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) vals[k * 4 + e] = base + e < hi ? x[base + e] : -INFINITY;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (base + e == excl) vals[k * 4 + e] = -INFINITY;
+      if (vals[k * 4 + e] > m) { m = vals[k * 4 + e]; idx = base + e; }
+    }
+  }
+  __shared__ float s_m[kSelThreads / 32];
+  __shared__ int s_i[kSelThreads / 32];
+  __shared__ double s_s[kSelThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+    argmax_merge(m, idx, m2, i2);
+  }
+  if ((tid & 31) == 0) { s_m[tid >> 5] = m; s_i[tid >> 5] = idx; }
+  __syncthreads();
+  float bm = s_m[0];
+  int bi = s_i[0];
+  for (int w = 1; w < kSelThreads / 32; ++w) argmax_merge(bm, bi, s_m[w], s_i[w]);
+
+  const double amax = sel_adjust(static_cast<double>(bm), a.temperature);
+  double sum = 0.0;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (vals[i] != -INFINITY) sum += exp(sel_adjust(static_cast<double>(vals[i]), a.temperature) - amax);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((tid & 31) == 0) s_s[tid >> 5] = sum;
+  __syncthreads();
+  __shared__ int s_last;
+  if (tid == 0) {
+    double bs = 0.0;
+    for (int w = 0; w < kSelThreads / 32; ++w) bs += s_s[w];
+    const int slot = r * a.nchunks + c;
+    a.part_max[slot] = bm;
+    a.part_idx[slot] = bi;
+    a.part_sum[slot] = bs;
+    __threadfence();
+    const int old = atomicAdd(&a.counters[r], 1);
+    s_last = (old == a.nchunks - 1);
+  }
+  __syncthreads();
+  if (!s_last || tid != 0) return;
+  __threadfence();
+  // Merge the row's chunks in chunk order.
+  float gm = -INFINITY;
+  int gi = INT_MAX;
+  for (int k = 0; k < a.nchunks; ++k) argmax_merge(gm, gi, __ldcg(&a.part_max[r * a.nchunks + k]), __ldcg(&a.part_idx[r * a.nchunks + k]));
+  const double gam = sel_adjust(static_cast<double>(gm), a.temperature);
+  double S = 0.0;
+  for (int k = 0; k < a.nchunks; ++k) {
+    const float cm = __ldcg(&a.part_max[r * a.nchunks + k]);
+    const double cs = __ldcg(&a.part_sum[r * a.nchunks + k]);
+    if (cm == -INFINITY) continue;
+    const double cam = sel_adjust(static_cast<double>(cm), a.temperature);
+    S += (cam == gam) ? cs : cs * exp(cam - gam);
+  }
+  a.token[r] = gi;
+  if (a.mode == SEL_MAXPROB) {
+    a.conf[r] = 1.0 / S;
+  } else {
+    a.row_amax[r] = gam;
+    a.row_sum[r] = S;
+  }
+  a.counters[r] = 0;
+}
+
+// Pass 2 (entropy): sum p log(p + 1e-10) with the row's global max and S.
+__global__ void __launch_bounds__(kSelThreads) sel_entropy_kernel(const SelArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  int rows_valid = a.rows;
+  if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
+  const int r = blockIdx.y;
+  if (r >= rows_valid) return;
+  const int c = blockIdx.x;
+  const int src = a.row_index != nullptr ? a.row_index[r] : r;
+  const float* x = a.logits + static_cast<int64_t>(src) * a.ld;
+  const int lo = c * a.chunk;
+  const int hi = min(a.vocab, lo + a.chunk);
+  const int tid = threadIdx.x;
+  const double amax = a.row_amax[r];
+  const double S = a.row_sum[r];
+  const int excl = a.exclude_dev != nullptr ? *a.exclude_dev : a.exclude;
+  double acc = 0.0;
+  for (int i = lo + tid; i < hi; i += kSelThreads) {
+    const float v = i == excl ? -INFINITY : x[i];
+    if (v == -INFINITY) continue;  // p = 0 contributes 0 * log(1e-10) = 0
+    const double e = exp(sel_adjust(static_cast<double>(v), a.temperature) - amax);
+    const double p = __ddiv_rn(e, S);
+    acc = __dadd_rn(acc, __dmul_rn(p, log(__dadd_rn(p, 1e-10))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ double s_s[kSelThreads / 32];
+  __shared__ int s_last;
+  if ((tid & 31) == 0) s_s[tid >> 5] = acc;
+  __syncthreads();
+  if (tid == 0) {
+    double bs = 0.0;
+    for (int w = 0; w < kSelThreads / 32; ++w) bs += s_s[w];
+    a.part_sum[r * a.nchunks + c] = bs;
+    __threadfence();
+    const int old = atomicAdd(&a.counters[r], 1);
+    s_last = (old == a.nchunks - 1);
+  }
+  __syncthreads();
+  if (!s_last || tid != 0) return;
+  __threadfence();
+  double H = 0.0;
+  for (int k = 0; k < a.nchunks; ++k) H += __ldcg(&a.part_sum[r * a.nchunks + k]);
+  a.conf[r] = static_cast<double>(static_cast<float>(H));
+  a.counters[r] = 0;
+}
+
+}  // namespace drt

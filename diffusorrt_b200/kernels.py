@@ -1,0 +1,58 @@
+"""Kernel-level entry points on torch CUDA tensors (device memory and streams come from torch).
+
+These call the C ABI directly with device pointers; they are the unit-level surface used by the
+selector microbenchmark and the kernel parity tests.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _stream_ptr(stream: torch.cuda.Stream | None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+def selector_scratch(n_rows: int, vocab: int, device) -> torch.Tensor:
+    nbytes = int(_lib.load().drt_selector_scratch_bytes(int(n_rows), int(vocab)))
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def select_rows(logits: torch.Tensor, *, mode: int = _lib.SELECT_MAX_PROB, temperature: float = 0.0,
+                scratch: torch.Tensor | None = None, conf: torch.Tensor | None = None,
+                token: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None):
+    """Per-row (confidence f64, token i32) of f32 logits [rows, vocab] (row stride may exceed vocab)."""
+    if logits.dtype != torch.float32 or not logits.is_cuda or logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a row-major CUDA float32 [rows, vocab] tensor")
+    rows, vocab = logits.shape
+    dev = logits.device
+    if scratch is None:
+        scratch = selector_scratch(rows, vocab, dev)
+    if conf is None:
+        conf = torch.empty(rows, dtype=torch.float64, device=dev)
+    if token is None:
+        token = torch.empty(rows, dtype=torch.int32, device=dev)
+    _lib.check(_lib.load().drt_selector_rows(logits.data_ptr(), logits.stride(0), rows, vocab, int(mode),
+                                             float(temperature), scratch.data_ptr(), conf.data_ptr(),
+                                             token.data_ptr(), _stream_ptr(stream)))
+    return conf, token
+
+
+def linear_bf16(x: torch.Tensor, w: torch.Tensor, *, splits: int = 1, round_bf16: bool = True,
+                out: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """y = x @ w^T on the tcgen05 path: x [rows, K] bf16, w [n, K] bf16 -> y [rows, n] f32."""
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or not x.is_contiguous() or not w.is_contiguous():
+        raise ValueError("x and w must be contiguous bf16 CUDA tensors")
+    rows, K = x.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty(rows, n, dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    if scratch is None:
+        scratch = torch.empty(int(lib.drt_linear_scratch_bytes(rows, n, K, splits)), dtype=torch.uint8, device=x.device)
+    _lib.check(lib.drt_linear_bf16(x.data_ptr(), w.data_ptr(), out.data_ptr(), rows, n, K, int(splits),
+                                   int(bool(round_bf16)), scratch.data_ptr(), _stream_ptr(stream)))
+    return out

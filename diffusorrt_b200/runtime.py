@@ -1,0 +1,324 @@
+"""Drop-in device-session provider for the DiffusorRT SDK's ``cuda_native`` route.
+
+The SDK opens ``diffusorrt_runtime.Runtime(package_dir, device="cuda", engine_config=...,
+precision=..., device_ordinal=..., creation_memory_budget_bytes=...)``
+(python/src/edllm/model.py:873-920), then ``runtime.session(session_config)``
+(model.py:1055-1067) and drives the session from ``generate_device_tokens`` /
+``generate_window_tokens`` (python/src/edllm/backends/device_runtime.py:108-365):
+
+    start_device(x, *, prompt_len, block_size, mask_token_id, exact_kv, steps,
+                 memory_budget_bytes, temperature, seed)
+    propose_device(frontier, *, window_end, frozen_prefix) -> (scores, token_ids, forwarded)
+    commit_device(positions, token_ids)
+    execute_window(token_ids, scope, *, mask_geometry=(prompt_len, block_size))
+        -> .logits (LE f32 bytes [n_rows * n_vocab]), .n_rows, .n_vocab, .forwarded_rows
+    device_metrics() -> dict
+
+This module binds those calls to the native library (include/diffusorrt_b200.h) and adds
+``Session.generate``: the whole request on the GPU (prefill, then CUDA-graph denoising steps
+with plan / score / select / commit on the device), bit-compatible with driving the same
+policy from the host through propose/commit.
+
+Errors follow the reference boundary: contract violations raise ``ValueError``; unsupported
+requests raise ``NotImplementedError``; device failures raise ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Any, Mapping, Sequence
+
+import numpy as np
+
+from . import _lib
+from .config import QWEN3_06B_BD3LM, SYNTHETIC_STD, rope_half_tables
+
+_STRATEGY_IDS = {"block_threshold": _lib.STRATEGY_BLOCK_THRESHOLD, "bd3_fixed_quota": _lib.STRATEGY_BD3_FIXED_QUOTA}
+_COMMIT_IDS = {"threshold": _lib.COMMIT_THRESHOLD, "fixed_quota": _lib.COMMIT_FIXED_QUOTA}
+_MASK_IDS = {"bidirectional": _lib.MASK_BIDIRECTIONAL, "d2f_hybrid": _lib.MASK_D2F_HYBRID}
+
+
+def _raise(exc: _lib.DrtError):
+    if exc.status == _lib.INVALID_ARGUMENT:
+        raise ValueError(str(exc)) from None
+    if exc.status == _lib.UNSUPPORTED:
+        raise NotImplementedError(str(exc)) from None
+    raise RuntimeError(str(exc)) from None
+
+
+def _call(status: int) -> None:
+    try:
+        _lib.check(status)
+    except _lib.DrtError as exc:
+        _raise(exc)
+
+
+@dataclass(frozen=True)
+class WindowResult:
+    """What ``execute_window`` returns (device_runtime.py:354-363)."""
+
+    logits: bytes
+    n_rows: int
+    n_vocab: int
+    forwarded_rows: int
+
+
+def _as_int_list(values, name: str) -> list[int]:
+    out = []
+    for v in values:
+        if isinstance(v, bool) or int(v) != v:
+            raise ValueError(f"{name} must contain integers")
+        out.append(int(v))
+    return out
+
+
+def _bf16_bits(array) -> np.ndarray:
+    """uint16 bf16 encoding of an array: uint16 input is taken as bf16 bits, floats are rounded
+    to nearest-even."""
+    a = np.asarray(array)
+    if a.dtype == np.uint16:
+        return np.ascontiguousarray(a)
+    if str(a.dtype) == "bfloat16":
+        return np.ascontiguousarray(a.view(np.uint16))
+    f = np.ascontiguousarray(a, dtype=np.float32)
+    bits = f.view(np.uint32).astype(np.uint64)
+    bits = (bits + np.uint64(0x7FFF) + ((bits >> np.uint64(16)) & np.uint64(1))) >> np.uint64(16)
+    return bits.astype(np.uint16)
+
+
+class Runtime:
+    """One model resident on one GPU (``diffusorrt_runtime.Runtime``)."""
+
+    def __init__(self, package_dir: str | Path | None = None, *, device: str = "cuda",
+                 engine_config: Mapping[str, Any] | None = None, precision: Mapping[str, Any] | None = None,
+                 device_ordinal: int = 0, creation_memory_budget_bytes: int = 0,
+                 model_config: Mapping[str, Any] | None = None, weights: Mapping[str, Any] | None = None,
+                 synthetic_seed: int | None = None, max_seq: int = 4608 + 128, max_prefill_rows: int = 4096):
+        if device != "cuda":
+            raise ValueError(f"this runtime serves device='cuda' only, not {device!r}")
+        engine_config = dict(engine_config or {})
+        if engine_config.get("compute_dtype", 0) not in (0, "bf16", "bfloat16"):
+            raise NotImplementedError("the B200 engine computes with bf16 weights (compute_dtype 0)")
+        if engine_config.get("linear_quant_bits"):
+            raise NotImplementedError("quantized linear weights are not served by this build")
+        if precision is not None and precision.get("weight_type", "bf16") != "bf16":
+            raise NotImplementedError(f"precision {precision.get('scheme')!r} is not served by this build")
+        cfg = dict(QWEN3_06B_BD3LM)
+        if package_dir is not None:
+            meta = Path(package_dir) / "model.json"
+            if meta.exists():
+                doc = json.loads(meta.read_text())
+                cfg.update({k: v for k, v in doc.get("runtime_config", doc).items() if k in cfg})
+                if synthetic_seed is None and "synthetic_seed" in doc:
+                    synthetic_seed = int(doc["synthetic_seed"])
+        if model_config:
+            cfg.update(model_config)
+        self.config = cfg
+        self.device_ordinal = int(device_ordinal)
+        self._lib = _lib.load()
+        mc = _lib.ModelConfig(
+            layer_count=cfg["layer_count"], hidden_size=cfg["hidden_size"], attention_heads=cfg["attention_heads"],
+            num_kv_heads=cfg["num_kv_heads"], head_dim=cfg["head_dim"], intermediate_size=cfg["intermediate_size"],
+            vocab_size=cfg["vocab_size"], qk_norm=int(bool(cfg["qk_norm"])), qkv_bias=int(bool(cfg["qkv_bias"])),
+            tied_lm_head=int(bool(cfg["tied_lm_head"])), rms_norm_eps=float(cfg["rms_norm_eps"]),
+            rope_theta=float(cfg["rope_theta"]), max_seq=int(max_seq), max_prefill_rows=int(max_prefill_rows))
+        handle = ctypes.c_void_p()
+        _call(self._lib.drt_model_create(ctypes.byref(mc), self.device_ordinal, ctypes.byref(handle)))
+        self._model = handle
+        self.max_seq = int(max_seq)
+        cos, sin = rope_half_tables(self.max_seq, cfg["head_dim"], float(cfg["rope_theta"]))
+        _call(self._lib.drt_model_set_rope(self._model, cos.ctypes.data, sin.ctypes.data, self.max_seq))
+        if synthetic_seed is not None:
+            self.init_synthetic(synthetic_seed)
+        if weights is not None:
+            self.load_weights(weights)
+        if creation_memory_budget_bytes and self.device_bytes > int(creation_memory_budget_bytes):
+            self.close()
+            raise ValueError("model weights exceed creation_memory_budget_bytes")
+
+    # ------------------------------------------------------------------ weights
+    def init_synthetic(self, seed: int, *, linear_std: float | None = None, embed_std: float | None = None,
+                       bias_std: float | None = None) -> None:
+        std = dict(SYNTHETIC_STD)
+        for k, v in (("linear_std", linear_std), ("embed_std", embed_std), ("bias_std", bias_std)):
+            if v is not None:
+                std[k] = v
+        _call(self._lib.drt_model_init_synthetic(self._model, int(seed) & (2**64 - 1), std["linear_std"],
+                                                 std["embed_std"], std["bias_std"]))
+
+    def load_weights(self, weights: Mapping[str, Any]) -> None:
+        """Install tensors by package key (``model.layers.N.self_attn.q_proj.weight`` ...)."""
+        for key, value in weights.items():
+            if key == "lm_head.weight" and self.config["tied_lm_head"]:
+                continue
+            arr = np.asarray(value)
+            rows = arr.shape[0] if arr.ndim == 2 else 1
+            cols = arr.shape[-1]
+            if arr.ndim == 1 or key.endswith("norm.weight") or key.endswith(".bias"):
+                data = np.ascontiguousarray(arr, dtype=np.float32)
+                _call(self._lib.drt_model_set_tensor(self._model, key.encode(), data.ctypes.data, 1, rows, cols))
+            else:
+                data = _bf16_bits(arr)
+                _call(self._lib.drt_model_set_tensor(self._model, key.encode(), data.ctypes.data, 0, rows, cols))
+
+    def get_tensor(self, key: str, shape: tuple[int, int]) -> np.ndarray:
+        """A resident tensor as float32 (bf16 values widened)."""
+        out = np.empty(shape, dtype=np.float32)
+        _call(self._lib.drt_model_get_tensor(self._model, key.encode(), out.ctypes.data, 1, shape[0], shape[1]))
+        return out
+
+    @property
+    def device_bytes(self) -> int:
+        return int(self._lib.drt_model_device_bytes(self._model))
+
+    # ------------------------------------------------------------------ sessions
+    def session(self, session_config: Mapping[str, Any] | None = None) -> "Session":
+        return Session(self, dict(session_config or {}))
+
+    def close(self) -> None:
+        if getattr(self, "_model", None):
+            self._lib.drt_model_destroy(self._model)
+            self._model = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _enum(value, table: dict, name: str) -> int:
+    if isinstance(value, str):
+        if value not in table:
+            raise ValueError(f"{name}={value!r} is not served by this device session")
+        return table[value]
+    if int(value) not in table.values():
+        raise ValueError(f"{name}={value!r} is not served by this device session")
+    return int(value)
+
+
+class Session:
+    """One decode request's device state (K/V cache, canvas, graphs). Single-threaded."""
+
+    def __init__(self, runtime: Runtime, session_config: dict):
+        self.runtime = runtime
+        self._lib = runtime._lib
+        strategy = _enum(session_config.get("decode_strategy", "bd3_fixed_quota"), _STRATEGY_IDS, "decode_strategy")
+        default_commit = "threshold" if strategy == _lib.STRATEGY_BLOCK_THRESHOLD else "fixed_quota"
+        commit = _enum(session_config.get("commit_policy", default_commit), _COMMIT_IDS, "commit_policy")
+        mask = _enum(session_config.get("attention_mask_kind", "d2f_hybrid"), _MASK_IDS, "attention_mask_kind")
+        self.block_size = int(session_config.get("block_size", runtime.config.get("block_size", 32)))
+        sc = _lib.SessionConfig(decode_strategy=strategy, commit_policy=commit, attention_mask_kind=mask,
+                                block_size=self.block_size, steps=int(session_config.get("steps", 128)),
+                                max_tokens=int(session_config.get("max_tokens", 0)))
+        handle = ctypes.c_void_p()
+        _call(self._lib.drt_session_open(runtime._model, ctypes.byref(sc), ctypes.byref(handle)))
+        self._s = handle
+        self.decode_strategy = strategy
+        self.vocab = int(runtime.config["vocab_size"])
+
+    # ------------------------------------------------------------------ reference surface
+    def start_device(self, x: Sequence[int], *, prompt_len: int, block_size: int, mask_token_id: int,
+                     exact_kv: bool, steps: int, memory_budget_bytes: int = 0, temperature: float = 0.0,
+                     seed: int = 0) -> None:
+        ids = _as_int_list(x, "x")
+        arr = _lib.i32_array(ids)
+        _call(self._lib.drt_session_start(self._s, arr, len(ids), int(prompt_len), int(block_size),
+                                          int(mask_token_id), int(bool(exact_kv)), int(steps),
+                                          int(memory_budget_bytes), float(temperature), int(seed) & (2**64 - 1)))
+
+    def propose_device(self, frontier: Sequence[int], *, window_end: int, frozen_prefix: int):
+        fr = _as_int_list(frontier, "frontier")
+        n = len(fr)
+        scores = (ctypes.c_double * max(1, n))()
+        tokens = (ctypes.c_int32 * max(1, n))()
+        forwarded = ctypes.c_int32()
+        _call(self._lib.drt_session_propose(self._s, _lib.i32_array(fr), n, int(window_end), int(frozen_prefix),
+                                            scores, tokens, ctypes.byref(forwarded)))
+        return [float(scores[i]) for i in range(n)], [int(tokens[i]) for i in range(n)], int(forwarded.value)
+
+    def commit_device(self, positions: Sequence[int], token_ids: Sequence[int]) -> None:
+        pos = _as_int_list(positions, "positions")
+        tok = _as_int_list(token_ids, "token_ids")
+        if len(pos) != len(tok):
+            raise ValueError("commit positions and token ids differ in length")
+        _call(self._lib.drt_session_commit(self._s, _lib.i32_array(pos), _lib.i32_array(tok), len(pos)))
+
+    def execute_window(self, token_ids: Sequence[int], scope: Sequence[int], *, mask_geometry=None) -> WindowResult:
+        ids = _as_int_list(token_ids, "token_ids")
+        sc = _as_int_list(scope, "scope")
+        if mask_geometry is None:
+            raise NotImplementedError("this device session executes d2f_hybrid windows; pass mask_geometry")
+        prompt_len, block_size = (int(v) for v in mask_geometry)
+        out = np.empty((len(sc), self.vocab), dtype="<f4")
+        forwarded = ctypes.c_int32()
+        _call(self._lib.drt_session_execute_window(self._s, _lib.i32_array(ids), len(ids), _lib.i32_array(sc), len(sc),
+                                                   prompt_len, block_size, out.ctypes.data, ctypes.byref(forwarded)))
+        return WindowResult(logits=out.tobytes(), n_rows=len(sc), n_vocab=self.vocab,
+                            forwarded_rows=int(forwarded.value))
+
+    def device_metrics(self) -> dict:
+        m = _lib.Metrics()
+        _call(self._lib.drt_session_metrics(self._s, ctypes.byref(m)))
+        return {name: getattr(m, name) for name, _ in _lib.Metrics._fields_}
+
+    # ------------------------------------------------------------------ device-resident request
+    def generate(self, prompt: Sequence[int], *, max_tokens: int, steps: int, block_size: int | None = None,
+                 decode_strategy: str = "bd3_fixed_quota", mask_token_id: int | None = None,
+                 eos_token_id: int | None = None, confidence_threshold: float = 0.9, rounds_per_block: int = 0,
+                 trace_steps: int = 0) -> dict:
+        cfg = self.runtime.config
+        ids = _as_int_list(prompt, "prompt")
+        params = _lib.GenerateParams(
+            decode_strategy=_enum(decode_strategy, _STRATEGY_IDS, "decode_strategy"), steps=int(steps),
+            block_size=int(block_size or self.block_size), max_tokens=int(max_tokens),
+            mask_token_id=int(cfg["mask_token_id"] if mask_token_id is None else mask_token_id),
+            eos_token_id=int(cfg["eos_token_id"] if eos_token_id is None else eos_token_id),
+            confidence_threshold=float(confidence_threshold), rounds_per_block=int(rounds_per_block),
+            trace_steps=int(trace_steps))
+        out = (ctypes.c_int32 * (len(ids) + int(max_tokens)))()
+        res = _lib.GenerateResult()
+        trace = (_lib.StepTrace * max(1, int(trace_steps)))() if trace_steps else None
+        _call(self._lib.drt_session_generate(self._s, ctypes.byref(params), _lib.i32_array(ids), len(ids), out,
+                                             ctypes.byref(res), trace))
+        result = {name: getattr(res, name) for name, _ in _lib.GenerateResult._fields_}
+        result["x"] = list(out)
+        if trace is not None:
+            steps_out = []
+            for t in trace[: min(res.forward_count, int(trace_steps))]:
+                n = t.n_frontier
+                steps_out.append({"step": t.step, "frontier": list(t.frontier_pos[:n]), "tokens": list(t.token[:n]),
+                                  "scores": list(t.conf[:n]), "tie": t.tie,
+                                  "chosen": [i for i in range(n) if (t.chosen_mask >> i) & 1]})
+            result["trace"] = steps_out
+        return result
+
+    def kv_pointers(self) -> tuple[int, int]:
+        k, v = ctypes.c_void_p(), ctypes.c_void_p()
+        _call(self._lib.drt_session_kv_pointers(self._s, ctypes.byref(k), ctypes.byref(v)))
+        return int(k.value or 0), int(v.value or 0)
+
+    def close(self) -> None:
+        if getattr(self, "_s", None):
+            self._lib.drt_session_close(self._s)
+            self._s = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,221 @@
+/*
+ * diffusorrt_b200 — C ABI of the B200 (sm_100a) denoising-decode engine.
+ *
+ * This library is the native provider behind the DiffusorRT SDK's `cuda_native` route: the
+ * SDK imports `diffusorrt_runtime` lazily (python/src/edllm/model.py:888-920) and drives a
+ * device session through start_device / propose_device / commit_device / execute_window /
+ * device_metrics (python/src/edllm/backends/device_runtime.py:140-183, 354-363). Each entry
+ * point below replaces one of those calls; the Python module diffusorrt_b200.runtime binds
+ * them with ctypes under the same names.
+ *
+ * Conventions
+ *   - Every function returns a drt_status. The values 0..4 are the reference AbiStatus
+ *     (python/src/edllm/abi/forward.py:20-25); DRT_DEVICE_TIMEOUT is added for a bounded
+ *     device wait that ran out. drt_last_error() describes the last failure of this thread.
+ *   - Host pointers are borrowed for the duration of the call (Ownership.BORROWED,
+ *     python/src/edllm/abi/buffers.py:37-40). Device memory is owned by the library.
+ *   - A session is single-threaded (python/src/edllm/abi/handles.py:28): calls on one session
+ *     must not overlap. Different sessions may run on different threads.
+ *   - Kernel-level entry points take device pointers and a cudaStream_t passed as void*.
+ */
+#ifndef DIFFUSORRT_B200_H_
+#define DIFFUSORRT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ABI version; must equal the reference ABI_VERSION (python/src/edllm/abi/__init__.py:14). */
+#define DRT_ABI_VERSION_MAJOR 0
+#define DRT_ABI_VERSION_MINOR 1
+#define DRT_ABI_VERSION_PATCH 0
+
+typedef enum drt_status {
+  DRT_OK = 0,                 /* AbiStatus.OK */
+  DRT_VERSION_MISMATCH = 1,   /* AbiStatus.VERSION_MISMATCH */
+  DRT_INVALID_ARGUMENT = 2,   /* AbiStatus.INVALID_ARGUMENT */
+  DRT_UNSUPPORTED = 3,        /* AbiStatus.UNSUPPORTED */
+  DRT_INTERNAL_ERROR = 4,     /* AbiStatus.INTERNAL_ERROR */
+  DRT_DEVICE_TIMEOUT = 5      /* a bounded device wait expired; the context stays usable */
+} drt_status;
+
+/* Decode strategies and commit policies: the ABI integers of
+ * python/src/edllm/abi/enums.py:14-31. Only these are served by a device session. */
+#define DRT_STRATEGY_BLOCK_THRESHOLD 0
+#define DRT_STRATEGY_BD3_FIXED_QUOTA 7
+#define DRT_COMMIT_THRESHOLD 2
+#define DRT_COMMIT_FIXED_QUOTA 3
+/* Attention mask kinds: python/src/edllm/abi/enums.py:40-43. */
+#define DRT_MASK_BIDIRECTIONAL 0
+#define DRT_MASK_D2F_HYBRID 1
+
+/* Selector modes. */
+#define DRT_SELECT_MAX_PROB 0   /* TopConfidence: raw softmax max-probability */
+#define DRT_SELECT_NEG_ENTROPY 1 /* NegEntropy: sum p log(p + 1e-10) of softmax(x / T) */
+
+/* Step certification bits (drt_step_trace.tie, drt_metrics counters). */
+#define DRT_TIE_NEAR 1
+#define DRT_TIE_EXACT 2
+
+typedef struct drt_model drt_model;
+typedef struct drt_session drt_session;
+
+/* Model geometry: python/src/edllm/abi/lifetimes.py ModelGeometry plus the architecture
+ * flags of python/src/edllm/model_definitions.py:417-448. */
+typedef struct drt_model_config {
+  int32_t layer_count;
+  int32_t hidden_size;
+  int32_t attention_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;          /* must be 128 */
+  int32_t intermediate_size;
+  int32_t vocab_size;
+  int32_t qk_norm;           /* Qwen3 per-head QK RMSNorm */
+  int32_t qkv_bias;          /* q/k/v projection bias (Qwen2 / Dream) */
+  int32_t tied_lm_head;      /* lm_head.weight is model.embed_tokens.weight */
+  float rms_norm_eps;
+  float rope_theta;
+  int32_t max_seq;           /* K/V capacity in positions */
+  int32_t max_prefill_rows;  /* rows per prefill chunk (activation capacity) */
+} drt_model_config;
+
+/* Session config: the keys RuntimeHandle._generate_cuda_native passes to
+ * runtime.session(...) (python/src/edllm/model.py:1055-1066). */
+typedef struct drt_session_config {
+  int32_t decode_strategy;     /* DRT_STRATEGY_* */
+  int32_t commit_policy;       /* DRT_COMMIT_* */
+  int32_t attention_mask_kind; /* DRT_MASK_* */
+  int32_t block_size;
+  int32_t steps;
+  int32_t max_tokens;
+} drt_session_config;
+
+/* Device-resident decode request (drt_session_generate). */
+typedef struct drt_generate_params {
+  int32_t decode_strategy;     /* DRT_STRATEGY_BD3_FIXED_QUOTA or DRT_STRATEGY_BLOCK_THRESHOLD */
+  int32_t steps;               /* requested denoising steps (the loop's iteration limit) */
+  int32_t block_size;
+  int32_t max_tokens;          /* generated canvas length */
+  int32_t mask_token_id;
+  int32_t eos_token_id;
+  double confidence_threshold; /* block threshold tau */
+  int32_t rounds_per_block;    /* block threshold: per-block round budget, 0 = none */
+  int32_t trace_steps;         /* record up to this many drt_step_trace entries */
+} drt_generate_params;
+
+typedef struct drt_generate_result {
+  int32_t forward_count;
+  int32_t iteration_count;
+  int32_t committed_token_count;
+  int32_t near_tie_steps;
+  int32_t exact_tie_steps;
+  int32_t stopped;
+  int32_t canvas_len;
+  float prefill_ms;            /* device time of the prompt prefill */
+  float decode_ms;             /* device time of all denoising steps */
+  float total_ms;              /* device time from the prompt upload to the canvas download */
+  int32_t kernel_launches;     /* kernels this call launched (prefill + graph replays) */
+} drt_generate_result;
+
+/* One recorded denoising step (device-resident loop). */
+typedef struct drt_step_trace {
+  int32_t step, n_frontier, n_chosen, tie;
+  int32_t frontier_pos[64];
+  int32_t token[64];
+  double conf[64];
+  uint64_t chosen_mask;
+} drt_step_trace;
+
+typedef struct drt_metrics {
+  int64_t forward_count;
+  int64_t forwarded_rows;
+  int64_t prefill_rows;
+  int64_t committed_token_count;
+  int64_t near_tie_steps;
+  int64_t exact_tie_steps;
+  double forward_ms_total;     /* device time of proposes / steps */
+  int64_t device_bytes;        /* device memory held by the session */
+} drt_metrics;
+
+/* ------------------------------------------------------------------ library */
+/* Reference: python/src/edllm/abi/__init__.py:14 (ABI_VERSION). */
+int drt_abi_version(int32_t* major, int32_t* minor, int32_t* patch);
+/* Text of the last error raised on this thread ("" if none). */
+const char* drt_last_error(void);
+/* Number of visible CUDA devices (0 on a host without a GPU). */
+int drt_device_count(int32_t* count);
+
+/* ------------------------------------------------------------------ model (weights) */
+/* Reference: diffusorrt_runtime.Runtime(package_dir, engine_config, precision, device_ordinal)
+ * (python/src/edllm/model.py:873-920). Allocates device weights for `config`. */
+int drt_model_create(const drt_model_config* config, int32_t device_ordinal, drt_model** out);
+/* Seeded synthetic weights (counter-based generator, reproducible bit for bit on the host):
+ * linears N(0, linear_std^2)-shaped, embedding embed_std, biases bias_std, norms 1. */
+int drt_model_init_synthetic(drt_model* model, uint64_t seed, float linear_std, float embed_std, float bias_std);
+/* Load one tensor by its package key (python/src/edllm/graph/emitter.py:88-276 names, e.g.
+ * "model.layers.3.self_attn.q_proj.weight", "model.norm.weight", "lm_head.weight").
+ * data: host bf16 (dtype 0) or f32 (dtype 1) [rows x cols], row-major. */
+int drt_model_set_tensor(drt_model* model, const char* key, const void* data, int32_t dtype, int64_t rows, int64_t cols);
+/* Copy one tensor back to the host as bf16 (dtype 0) or f32 (dtype 1). */
+int drt_model_get_tensor(drt_model* model, const char* key, void* data, int32_t dtype, int64_t rows, int64_t cols);
+/* RoPE half tables cos/sin [n_pos x head_dim/2] f32, as built by the reference
+ * (python/src/edllm/backends/mlx_forward.py:1566-1595). */
+int drt_model_set_rope(drt_model* model, const float* cos_half, const float* sin_half, int32_t n_pos);
+int64_t drt_model_device_bytes(const drt_model* model);
+void drt_model_destroy(drt_model* model);
+
+/* ------------------------------------------------------------------ session */
+/* Reference: Runtime.session(session_config) (python/src/edllm/model.py:1055-1067). */
+int drt_session_open(drt_model* model, const drt_session_config* config, drt_session** out);
+/* Reference: session.start_device(x, prompt_len, block_size, mask_token_id, exact_kv, steps,
+ * memory_budget_bytes, temperature, seed) (python/src/edllm/backends/device_runtime.py:140-150).
+ * `prompt_len` is the mask-geometry origin (0 for BD3's absolute blocks). */
+int drt_session_start(drt_session* s, const int32_t* x, int32_t n, int32_t prompt_len, int32_t block_size,
+                      int32_t mask_token_id, int32_t exact_kv, int32_t steps, int64_t memory_budget_bytes,
+                      double temperature, uint64_t seed);
+/* Reference: session.propose_device(frontier, window_end=, frozen_prefix=) -> (scores,
+ * token_ids, forwarded) in frontier order (device_runtime.py:152-178). scores: f64 raw
+ * max-probability; token_ids: argmax; forwarded: rows computed by this forward. */
+int drt_session_propose(drt_session* s, const int32_t* frontier, int32_t n_frontier, int32_t window_end,
+                        int32_t frozen_prefix, double* scores, int32_t* token_ids, int32_t* forwarded);
+/* Reference: session.commit_device(positions, token_ids) (diffusion_runtime.py:749-753). */
+int drt_session_commit(drt_session* s, const int32_t* positions, const int32_t* token_ids, int32_t n);
+/* Reference: session.execute_window(token_ids, scope, mask_geometry=(prompt_len, block_size))
+ * (device_runtime.py:354-363): selection-ready f32 logits [n_scope x vocab] of the scope
+ * rows, in scope order. No cache: the whole window is forwarded. */
+int drt_session_execute_window(drt_session* s, const int32_t* token_ids, int32_t n_tokens, const int32_t* scope,
+                               int32_t n_scope, int32_t prompt_len, int32_t block_size, float* logits,
+                               int32_t* forwarded_rows);
+/* Whole request on the device: prefill, then CUDA-graph denoising steps whose plan, score,
+ * select and commit all run on the GPU. prompt/out are host buffers; out receives the final
+ * canvas (prompt + max_tokens). trace (optional, host) receives params->trace_steps entries. */
+int drt_session_generate(drt_session* s, const drt_generate_params* params, const int32_t* prompt,
+                         int32_t prompt_len, int32_t* out, drt_generate_result* result, drt_step_trace* trace);
+/* Reference: session.device_metrics() (python/src/edllm/model.py:1087). */
+int drt_session_metrics(drt_session* s, drt_metrics* out);
+/* Raw device pointers of the session's K/V cache planes (tests): K [L*nkv][max_seq][128],
+ * V^T [L*nkv][128][max_seq], both bf16. */
+int drt_session_kv_pointers(drt_session* s, void** k_cache, void** vt_cache);
+void drt_session_close(drt_session* s);
+
+/* ------------------------------------------------------------------ kernels (device pointers) */
+/* Fused selector over rows of f32 logits (reference _raw_max_prob_rows_exact,
+ * diffusion_runtime.py:179-192, and _entropy_confidence without top-p, :90-114).
+ * conf[r] (f64) and token[r] (i32) for r < n_rows. scratch: see drt_selector_scratch_bytes. */
+size_t drt_selector_scratch_bytes(int32_t n_rows, int32_t vocab);
+int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows, int32_t vocab, int32_t mode,
+                      double temperature, void* scratch, double* conf, int32_t* token, void* stream);
+/* y = x @ W^T on the tensor cores with the MLX rounding contract (bf16 output rounding when
+ * round_bf16 != 0). x [rows x K] bf16, w [n x K] bf16, y [rows x n] f32; n % 128 == 0,
+ * K % 64 == 0. scratch: see drt_linear_scratch_bytes (split-K partials + counters). */
+size_t drt_linear_scratch_bytes(int32_t rows, int32_t n, int32_t K, int32_t splits);
+int drt_linear_bf16(const void* x, const void* w, float* y, int32_t rows, int32_t n, int32_t K, int32_t splits,
+                    int32_t round_bf16, void* scratch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DIFFUSORRT_B200_H_ */

@@ -1,0 +1,171 @@
+"""Transformer forward restated on the CPU (test infrastructure and the timed CPU baseline).
+
+Two precision contracts:
+
+* ``forward_mlx`` — the reference MLX path with bf16 resident weights
+  (``python/src/edllm/backends/mlx_ops.py``, ``mlx_forward.py``): f32 embedding rows and residual
+  stream; RMSNorm in f32 with the weight multiplied after the normalize (mlx_ops.py:21-35);
+  every linear casts its f32 input to bf16, multiplies bf16 x bf16 with an f32 accumulator and
+  returns the bf16-rounded result widened to f32, bias added in f32 (mlx_ops.py:97-130);
+  per-head QK-RMSNorm then split-half RoPE in f32 with float32 angle tables
+  (mlx_forward.py:1164-1361, 1566-1595); SDPA in f32 with the additive d2f_hybrid mask
+  (mlx_ops.py:191-288, 347-443); SwiGLU in f32 (mlx_ops.py:147-154); f32 logits.
+* ``forward_fp64`` — the float64 executable spec (``python/src/edllm/graph/numpyref.py``:
+  op_rms_norm :80-85, op_rope_split_half :123-142 with float64 tables, attention :152-233,
+  op_linear :236-241, op_mlp_swiglu :244-252, interpret_graph :507-559).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from .numerics import bf16_round, rope_half_tables
+
+
+def visible_mask(q_pos: np.ndarray, kv_len: int, *, prompt_len: int, block_size: int, bidirectional: bool) -> np.ndarray:
+    """[len(q_pos), kv_len] bool: eff(p) = -1 if p < prompt_len else (p - prompt_len) // block;
+    visible iff eff(key) <= eff(query); everything visible when bidirectional."""
+    keys = np.arange(kv_len, dtype=np.int64)
+    if bidirectional:
+        return np.ones((len(q_pos), kv_len), dtype=bool)
+
+    def eff(p):
+        p = np.asarray(p, dtype=np.int64)
+        return np.where(p < prompt_len, np.int64(-1), (p - prompt_len) // block_size)
+
+    return eff(keys)[None, :] <= eff(q_pos)[:, None]
+
+
+def _rms32(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    var = np.mean(x * x, axis=-1, keepdims=True, dtype=np.float32)
+    scale = np.float32(1.0) / np.sqrt(var + np.float32(eps))
+    return (x * scale).astype(np.float32) * np.asarray(w, dtype=np.float32)
+
+
+def _lin32(x: np.ndarray, w: np.ndarray, b=None) -> np.ndarray:
+    y = bf16_round(bf16_round(x) @ np.asarray(w, dtype=np.float32).T)
+    if b is not None:
+        y = (y + np.asarray(b, dtype=np.float32)).astype(np.float32)
+    return y
+
+
+def _rope32(x: np.ndarray, cos_h: np.ndarray, sin_h: np.ndarray) -> np.ndarray:
+    # x [S, heads, d]; cos_h/sin_h [S, d/2] -> full tables [S, 1, d]
+    cos = np.concatenate([cos_h, cos_h], axis=-1)[:, None, :]
+    sin = np.concatenate([sin_h, sin_h], axis=-1)[:, None, :]
+    half = x.shape[-1] // 2
+    rot = np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+    return (x * cos + rot * sin).astype(np.float32)
+
+
+def _sdpa32(q, k, v, visible):
+    # q [S, nq, d], k/v [T, nkv, d] -> [S, nq*d]
+    S, nq, d = q.shape
+    rep = nq // k.shape[1]
+    kk = np.repeat(k, rep, axis=1)
+    vv = np.repeat(v, rep, axis=1)
+    scale = np.float32(1.0 / math.sqrt(d))
+    scores = np.einsum("shd,thd->hst", q, kk, optimize=True).astype(np.float32) * scale
+    scores = np.where(visible[None, :, :], scores, np.float32(-np.inf))
+    scores = scores - scores.max(axis=-1, keepdims=True)
+    e = np.exp(scores)
+    p = e / e.sum(axis=-1, keepdims=True)
+    out = np.einsum("hst,thd->shd", p, vv, optimize=True).astype(np.float32)
+    return out.reshape(S, nq * d)
+
+
+def forward_mlx(weights: dict, cfg: dict, token_ids, *, prompt_len: int = 0, block_size: int = 32,
+                bidirectional: bool = False, output_rows=None, rope=None) -> np.ndarray:
+    """Logits [len(output_rows) (or S), V] f32 of a full-window forward (no cache)."""
+    ids = np.asarray(token_ids, dtype=np.int64)
+    S = len(ids)
+    H, nq, nkv, d = cfg["hidden_size"], cfg["attention_heads"], cfg["num_kv_heads"], cfg["head_dim"]
+    eps = float(cfg.get("rms_norm_eps", 1e-6))
+    if rope is None:
+        rope = rope_half_tables(S, d, float(cfg.get("rope_theta", 1e6)))
+    cos_h, sin_h = rope[0][:S], rope[1][:S]
+    vis = visible_mask(np.arange(S), S, prompt_len=prompt_len, block_size=block_size, bidirectional=bidirectional)
+    h = np.asarray(weights["model.embed_tokens.weight"], dtype=np.float32)[ids].copy()
+    for layer in range(cfg["layer_count"]):
+        p = f"model.layers.{layer}."
+        g = lambda key: weights.get(p + key)  # noqa: E731
+        n = _rms32(h, g("input_layernorm.weight"), eps)
+        q = _lin32(n, g("self_attn.q_proj.weight"), g("self_attn.q_proj.bias")).reshape(S, nq, d)
+        k = _lin32(n, g("self_attn.k_proj.weight"), g("self_attn.k_proj.bias")).reshape(S, nkv, d)
+        v = _lin32(n, g("self_attn.v_proj.weight"), g("self_attn.v_proj.bias")).reshape(S, nkv, d)
+        if g("self_attn.q_norm.weight") is not None:
+            q = _rms32(q, g("self_attn.q_norm.weight"), eps)
+            k = _rms32(k, g("self_attn.k_norm.weight"), eps)
+        q = _rope32(q, cos_h, sin_h)
+        k = _rope32(k, cos_h, sin_h)
+        attn = _sdpa32(q, k, v, vis)
+        h = (h + _lin32(attn, g("self_attn.o_proj.weight"))).astype(np.float32)
+        n2 = _rms32(h, g("post_attention_layernorm.weight"), eps)
+        gate = _lin32(n2, g("mlp.gate_proj.weight"))
+        up = _lin32(n2, g("mlp.up_proj.weight"))
+        act = (gate * (np.float32(1.0) / (np.float32(1.0) + np.exp(-gate))) * up).astype(np.float32)
+        h = (h + _lin32(act, g("mlp.down_proj.weight"))).astype(np.float32)
+    rows = np.arange(S) if output_rows is None else np.asarray(output_rows, dtype=np.int64)
+    hn = _rms32(h[rows], weights["model.norm.weight"], eps)
+    return _lin32(hn, weights["lm_head.weight"])
+
+
+def forward_fp64(weights: dict, cfg: dict, token_ids, *, prompt_len: int = 0, block_size: int = 32,
+                 bidirectional: bool = False, output_rows=None, cast=None) -> np.ndarray:
+    """Float64 logits of the executable spec. ``cast(key)`` may supply cached float64 weights."""
+    ids = np.asarray(token_ids, dtype=np.int64)
+    S = len(ids)
+    H, nq, nkv, d = cfg["hidden_size"], cfg["attention_heads"], cfg["num_kv_heads"], cfg["head_dim"]
+    eps = float(cfg.get("rms_norm_eps", 1e-6))
+    theta = float(cfg.get("rope_theta", 1e6))
+    W = cast or (lambda key: None if weights.get(key) is None else np.asarray(weights[key], dtype=np.float64))
+
+    def rms(x, w):
+        var = np.mean(x * x, axis=-1, keepdims=True)
+        return x / np.sqrt(var + eps) * w
+
+    half = d // 2
+    inv = 1.0 / (theta ** (np.arange(0, half, dtype=np.float64) / half))
+    ang = np.einsum("i,j->ij", np.arange(S, dtype=np.float64), inv)
+    cos, sin = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+
+    def rope(x):
+        out = np.empty_like(x)
+        out[..., :half] = x[..., :half] * cos - x[..., half:] * sin
+        out[..., half:] = x[..., :half] * sin + x[..., half:] * cos
+        return out
+
+    vis = visible_mask(np.arange(S), S, prompt_len=prompt_len, block_size=block_size, bidirectional=bidirectional)
+    bias = np.where(vis, 0.0, -np.inf)
+    h = W("model.embed_tokens.weight")[ids]
+    for layer in range(cfg["layer_count"]):
+        p = f"model.layers.{layer}."
+
+        def lin(x, key, bkey=None):
+            y = x @ W(p + key).T
+            b = W(p + bkey) if bkey else None
+            return y if b is None else y + b
+
+        n = rms(h, W(p + "input_layernorm.weight"))
+        q = lin(n, "self_attn.q_proj.weight", "self_attn.q_proj.bias").reshape(S, nq, d)
+        k = lin(n, "self_attn.k_proj.weight", "self_attn.k_proj.bias").reshape(S, nkv, d)
+        v = lin(n, "self_attn.v_proj.weight", "self_attn.v_proj.bias").reshape(S, nkv, d)
+        if W(p + "self_attn.q_norm.weight") is not None:
+            q = rms(q, W(p + "self_attn.q_norm.weight"))
+            k = rms(k, W(p + "self_attn.k_norm.weight"))
+        q, k = rope(q), rope(k)
+        rep = nq // nkv
+        kk, vv = np.repeat(k, rep, axis=1), np.repeat(v, rep, axis=1)
+        sc = np.einsum("thd,shd->hts", q, kk, optimize=True) / math.sqrt(float(d)) + bias
+        sc = np.exp(sc - sc.max(axis=-1, keepdims=True))
+        pr = sc / sc.sum(axis=-1, keepdims=True)
+        attn = np.einsum("hts,shd->thd", pr, vv, optimize=True).reshape(S, nq * d)
+        h = h + attn @ W(p + "self_attn.o_proj.weight").T
+        n2 = rms(h, W(p + "post_attention_layernorm.weight"))
+        gate = n2 @ W(p + "mlp.gate_proj.weight").T
+        up = n2 @ W(p + "mlp.up_proj.weight").T
+        h = h + (gate / (1.0 + np.exp(-gate)) * up) @ W(p + "mlp.down_proj.weight").T
+    rows = np.arange(S) if output_rows is None else np.asarray(output_rows, dtype=np.int64)
+    hn = rms(h[rows], W("model.norm.weight"))
+    return hn @ W("lm_head.weight").T

@@ -1,0 +1,244 @@
+"""Device-session parity on the GPU, through the C ABI (diffusorrt_b200.runtime):
+
+* the seeded synthetic weights on the device equal the CPU restatement bit for bit;
+* execute_window logits match the CPU oracle of the reference MLX forward within a bf16
+  tolerance (d2f_hybrid block-causal mask, QK-norm, GQA, RoPE);
+* propose_device (prefix K/V cache) agrees with a cache-free window forward;
+* the device-resident decode loop equals the host-driven loop over the same session calls,
+  step for step, for BD3 fixed-quota and block-threshold;
+* the whole decode agrees with the CPU oracle decode on every certified step.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import forward as ofwd  # noqa: E402
+from oracle import policy as opol  # noqa: E402
+from oracle import selector as osel  # noqa: E402
+from oracle.numerics import synth_weights  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(layer_count=2, hidden_size=256, attention_heads=4, num_kv_heads=2, head_dim=128,
+             intermediate_size=512, vocab_size=4096, qk_norm=True, qkv_bias=False, tied_lm_head=True,
+             rms_norm_eps=1e-6, rope_theta=1e6, mask_token_id=4000, eos_token_id=4001, block_size=32)
+STD = dict(linear_std=0.05, embed_std=0.5)
+SEED = 3
+
+
+@pytest.fixture(scope="module")
+def rt():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from diffusorrt_b200 import Runtime, build
+
+    build.build()
+    r = Runtime(model_config=SMALL, max_seq=512, max_prefill_rows=256)
+    r.init_synthetic(SEED, **STD)
+    yield r
+    r.close()
+
+
+@pytest.fixture(scope="module")
+def weights():
+    return synth_weights(SMALL, SEED, **STD)
+
+
+def _prompt(n, seed, vocab=4000):
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, size=n)]
+
+
+def test_synthetic_weights_match_cpu_generator(rt, weights):
+    H = SMALL["hidden_size"]
+    for key, shape in [("model.embed_tokens.weight", (4096, H)), ("model.layers.1.self_attn.k_proj.weight", (256, H)),
+                       ("model.layers.0.mlp.up_proj.weight", (512, H)), ("model.layers.1.mlp.down_proj.weight", (H, 512)),
+                       ("model.layers.0.self_attn.o_proj.weight", (H, 512))]:
+        np.testing.assert_array_equal(rt.get_tensor(key, shape), weights[key])
+
+
+def _window_logits(s, ids, scope):
+    res = s.execute_window(ids, scope, mask_geometry=(0, 32))
+    return np.frombuffer(res.logits, dtype="<f4").reshape(res.n_rows, res.n_vocab)
+
+
+def test_execute_window_matches_oracle(rt, weights):
+    ids = _prompt(96, 1)
+    for p in (70, 71, 80, 90, 95):
+        ids[p] = SMALL["mask_token_id"]
+    scope = [64, 70, 71, 80, 90, 95, 3, 33]
+    with rt.session({"decode_strategy": "bd3_fixed_quota", "block_size": 32}) as s:
+        got = _window_logits(s, ids, scope)
+    want = ofwd.forward_mlx(weights, SMALL, ids, prompt_len=0, block_size=32, output_rows=scope)
+    scale = float(np.abs(want).max())
+    err = np.abs(got - want)
+    assert err.max() <= 0.02 * scale, (err.max(), scale)
+    assert float(np.mean(err)) <= 0.002 * scale
+    assert np.mean(np.argmax(got, -1) == np.argmax(want, -1)) >= 0.75
+
+
+def test_execute_window_long_prefix_chunks(rt, weights):
+    """A window longer than one prefill chunk (256 rows) and not a multiple of the tile."""
+    ids = _prompt(301, 2)
+    scope = [0, 255, 256, 288, 300]
+    with rt.session({"decode_strategy": "bd3_fixed_quota", "block_size": 32}) as s:
+        got = _window_logits(s, ids, scope)
+    want = ofwd.forward_mlx(weights, SMALL, ids, prompt_len=0, block_size=32, output_rows=scope)
+    scale = float(np.abs(want).max())
+    assert np.abs(got - want).max() <= 0.02 * scale
+
+
+def test_propose_agrees_with_window_forward(rt):
+    prompt = _prompt(64, 3)
+    mask = SMALL["mask_token_id"]
+    x = prompt + [mask] * 64
+    with rt.session({"decode_strategy": "bd3_fixed_quota", "block_size": 32}) as s:
+        s.start_device(x, prompt_len=0, block_size=32, mask_token_id=mask, exact_kv=False, steps=64)
+        frontier = list(range(64, 96))
+        scores, tokens, fwd = s.propose_device(frontier, window_end=96, frozen_prefix=64)
+        assert fwd == 96
+        ref = _window_logits(s, x[:96], frontier)
+    want_conf, want_tok = osel.max_prob_rows(ref)
+    agree = np.mean(np.asarray(tokens) == np.asarray(want_tok))
+    assert agree >= 0.9
+    np.testing.assert_allclose(scores, want_conf, rtol=0.05)
+
+
+def _host_loop(s, prompt, *, strategy, gen, steps, bs, tau=0.9, cap=0):
+    """The reference run_decode_loop over propose_device / commit_device (oracle policy)."""
+    mask, eos = SMALL["mask_token_id"], SMALL["eos_token_id"]
+    x = list(prompt) + [mask] * gen
+    s.start_device(x, prompt_len=0, block_size=bs, mask_token_id=mask, exact_kv=False, steps=steps)
+    c = opol.Canvas(x, len(prompt), mask, eos)
+    if strategy == "bd3_fixed_quota":
+        pol = opol.BD3FixedQuota(block_size=bs, steps=steps, prompt_len=len(prompt), gen_len=gen)
+        limit = pol.iteration_limit
+    else:
+        pol = opol.BlockThreshold(block_size=bs, threshold=tau, rounds_cap=cap)
+        limit = steps
+    trace = []
+
+    def score(canvas, frontier, window_end, step):
+        frozen = (min(frontier) // bs) * bs
+        sc, tok, _ = s.propose_device(frontier, window_end=window_end, frozen_prefix=frozen)
+        return np.asarray(sc), tok
+
+    orig_select = pol.select
+
+    def select(scores):
+        rows = orig_select(scores)
+        return rows
+
+    pol.select = select
+    out = opol.run_loop(c, pol, score, limit, trace=trace)
+    # commit_device mirrors the host commits
+    return out, trace
+
+
+@pytest.mark.parametrize("strategy,gen,steps,cap", [("bd3_fixed_quota", 96, 96, 0), ("bd3_fixed_quota", 64, 16, 0),
+                                                    ("block_threshold", 64, 48, 8)])
+def test_device_loop_equals_host_loop(rt, strategy, gen, steps, cap):
+    prompt = _prompt(64, 11)
+    mask = SMALL["mask_token_id"]
+    with rt.session({"decode_strategy": strategy, "block_size": 32}) as s:
+        dev = s.generate(prompt, max_tokens=gen, steps=steps, block_size=32, decode_strategy=strategy,
+                         confidence_threshold=0.9, rounds_per_block=cap, trace_steps=256)
+
+    with rt.session({"decode_strategy": strategy, "block_size": 32}) as s:
+        # Host-driven loop: propose on the device, select on the host (oracle), commit on the device.
+        x = list(prompt) + [mask] * gen
+        s.start_device(x, prompt_len=0, block_size=32, mask_token_id=mask, exact_kv=False, steps=steps)
+        c = opol.Canvas(list(x), len(prompt), mask, SMALL["eos_token_id"])
+        if strategy == "bd3_fixed_quota":
+            pol = opol.BD3FixedQuota(block_size=32, steps=steps, prompt_len=len(prompt), gen_len=gen)
+            limit = pol.iteration_limit
+        else:
+            pol = opol.BlockThreshold(block_size=32, threshold=0.9, rounds_cap=cap)
+            limit = steps
+        host_steps = []
+
+        def score(canvas, frontier, window_end, step):
+            frozen = (min(frontier) // 32) * 32
+            sc, tok, _ = s.propose_device(frontier, window_end=window_end, frozen_prefix=frozen)
+            host_steps.append((list(frontier), list(tok), list(sc)))
+            return np.asarray(sc), tok
+
+        commits = []
+        sel = pol.select
+
+        def select(scores):
+            rows = sel(scores)
+            commits.append(sorted(rows))
+            return rows
+
+        pol.select = select
+        # run the loop manually so commits go to the device too
+        out = None
+        forwards = 0
+        for step in range(limit):
+            plan = pol.plan(c, step)
+            if plan.action == "stop":
+                break
+            if plan.action == "skip":
+                continue
+            scores, tokens = score(c, plan.frontier, plan.window_end, step)
+            forwards += 1
+            rows = pol.select(scores)
+            pos = [plan.frontier[r] for r in rows]
+            tok = [int(tokens[r]) for r in rows]
+            s.commit_device(pos, tok)
+            for p, t in zip(pos, tok):
+                c.x[p] = t
+        out = c.finalize()
+
+    assert dev["forward_count"] == forwards
+    assert dev["x"] == c.x
+    for i, (tr, (frontier, tok, sc)) in enumerate(zip(dev["trace"], host_steps)):
+        assert tr["frontier"] == frontier, i
+        assert tr["tokens"] == tok, i
+        np.testing.assert_array_equal(np.asarray(tr["scores"]), np.asarray(sc))
+        assert tr["chosen"] == commits[i], i
+    assert out is not None
+
+
+def test_decode_matches_cpu_oracle_on_certified_steps(rt, weights):
+    """Whole BD3 decode vs the CPU oracle (cache-free MLX-contract forward + reference selector
+    and policy). Steps agree until the first decision whose oracle margin is inside the bf16
+    forward tolerance; the test requires most of the decode to be certified and equal."""
+    prompt = _prompt(64, 21)
+    gen, steps, bs = 64, 64, 32
+    mask, eos = SMALL["mask_token_id"], SMALL["eos_token_id"]
+    with rt.session({"decode_strategy": "bd3_fixed_quota", "block_size": bs}) as s:
+        dev = s.generate(prompt, max_tokens=gen, steps=steps, block_size=bs, trace_steps=256)
+    c = opol.Canvas(list(prompt) + [mask] * gen, len(prompt), mask, eos)
+    pol = opol.BD3FixedQuota(block_size=bs, steps=steps, prompt_len=len(prompt), gen_len=gen)
+    agreed = 0
+    diverged = False
+    for i, tr in enumerate(dev["trace"]):
+        plan = pol.plan(c, tr["step"])
+        assert plan.action == "proceed"
+        assert plan.frontier == tr["frontier"]
+        logits = ofwd.forward_mlx(weights, SMALL, c.x[:plan.window_end], prompt_len=0, block_size=bs,
+                                  output_rows=plan.frontier)
+        conf, tok = osel.max_prob_rows(logits)
+        rows = pol.select(conf)
+        dev_rows = tr["chosen"]
+        same = sorted(rows) == dev_rows and all(tok[r] == tr["tokens"][r] for r in rows)
+        if not same:
+            # Divergence is acceptable only where the oracle's own decision is within tolerance.
+            order = np.sort(conf)[::-1]
+            k = len(rows)
+            gap = (order[k - 1] - order[k]) / order[k - 1] if k < len(order) else 1.0
+            top2 = np.sort(logits[rows[0]])[-2:]
+            logit_gap = float(top2[1] - top2[0])
+            assert gap < 0.05 or logit_gap < 0.05 * float(np.abs(logits).max()), (i, gap, logit_gap)
+            diverged = True
+            break
+        agreed += 1
+        for r in rows:
+            c.x[plan.frontier[r]] = tok[r]
+    if not diverged:
+        assert dev["x"] == c.x
+    assert agreed >= 8

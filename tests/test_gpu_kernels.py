@@ -44,9 +44,10 @@ def test_linear_matches_fp32_reference(dev, rows, n, K, splits):
     torch.cuda.synchronize()
     expect = _bf16_round_torch(ref)
     diff = (rounded - expect).abs()
-    ulp = expect.abs().clamp_min(1e-30) * 2.0 ** -7
-    # bf16 rounding of two f32 values a few ulp apart may land one bf16 step apart.
-    assert bool((diff <= ulp * 1.01).all())
+    # Two f32 values `tol` apart may round to neighbouring bf16 values (one step of 2^-7
+    # relative), including near zero where the f32 accumulation error dominates the value.
+    bound = 2.0 ** -7 * (expect.abs() + tol) + tol
+    assert bool((diff <= bound).all())
     assert (diff > 0).float().mean().item() < 0.01
 
 

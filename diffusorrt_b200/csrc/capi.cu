@@ -1358,3 +1358,85 @@ extern "C" int drt_linear_bf16(const void* x, const void* w, float* y, int32_t r
               mb, a));
   return DRT_OK;
 }
+
+// ======================================================================= selector without allocation
+// drt_selector_rows_noalloc: the fused selector with its scratch (chunk partials, row statistics,
+// arrival counters) in one file-scope device array instead of caller memory, for callers that may
+// not allocate device memory. The array is fixed at kNoAllocScratchBytes (about 0.53 MB) and every
+// GPU that loads this library holds one copy until the process exits.
+namespace {
+constexpr int kNoAllocMaxRows = 1024;
+constexpr int kNoAllocMaxVocab = 262144;
+constexpr size_t kNoAllocMaxParts = static_cast<size_t>(kNoAllocMaxRows) * (kNoAllocMaxVocab / kSelChunk);
+// part_sum f64 + part_max f32 + part_idx i32 per (row, chunk); row_amax f64 + row_sum f64 +
+// counter i32 per row; six 256-byte alignment pads.
+constexpr size_t kNoAllocScratchBytes = kNoAllocMaxParts * (8 + 4 + 4) + static_cast<size_t>(kNoAllocMaxRows) * (8 + 8 + 4) + 6 * 256;
+static __device__ __align__(256) uint8_t g_selector_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of g_selector_scratch on the current device. In host code the symbol is only a
+// host-side stand-in, so the address is looked up once per device (with that device current) and
+// cached.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(DRT_UNSUPPORTED, "device ordinal %d outside [0, 64)", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_selector_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(DRT_INTERNAL_ERROR, "cudaGetSymbolAddress(selector scratch) failed: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return DRT_OK;
+}
+}  // namespace
+
+extern "C" int drt_selector_rows_noalloc(const float* logits, int64_t ld, int32_t n_rows, int32_t vocab, int32_t mode,
+                                         double temperature, double* conf, int32_t* token, void* stream) {
+  REQUIRE(logits && conf && token, "null argument");
+  REQUIRE(n_rows >= 0 && vocab >= 1 && ld >= vocab, "bad selector geometry");
+  REQUIRE(mode == DRT_SELECT_MAX_PROB || mode == DRT_SELECT_NEG_ENTROPY, "unknown selector mode %d", mode);
+  REQUIRE(n_rows <= kNoAllocMaxRows, "drt_selector_rows_noalloc scores at most %d rows per call (got %d); "
+          "use drt_selector_rows with caller scratch for more", kNoAllocMaxRows, n_rows);
+  REQUIRE(vocab <= kNoAllocMaxVocab, "drt_selector_rows_noalloc scores rows of at most %d logits (got %d); "
+          "use drt_selector_rows with caller scratch for more", kNoAllocMaxVocab, vocab);
+  if (n_rows == 0) return DRT_OK;
+  void* base = nullptr;
+  TRY(noalloc_scratch(&base));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int chunks = (vocab + kSelChunk - 1) / kSelChunk;
+  const size_t np = static_cast<size_t>(n_rows) * chunks;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  auto take = [&](size_t bytes) { uint8_t* q = p; p += (bytes + 255) & ~size_t(255); return q; };
+  SelArgs a;
+  memset(&a, 0, sizeof(a));
+  a.part_sum = reinterpret_cast<double*>(take(np * 8));
+  a.row_amax = reinterpret_cast<double*>(take(static_cast<size_t>(n_rows) * 8));
+  a.row_sum = reinterpret_cast<double*>(take(static_cast<size_t>(n_rows) * 8));
+  a.part_max = reinterpret_cast<float*>(take(np * 4));
+  a.part_idx = reinterpret_cast<int*>(take(np * 4));
+  a.counters = reinterpret_cast<int*>(take(static_cast<size_t>(n_rows) * 4));
+  if (static_cast<size_t>(p - static_cast<uint8_t*>(base)) > kNoAllocScratchBytes)
+    return set_error(DRT_INTERNAL_ERROR, "selector scratch layout exceeds the static array");
+  // The array keeps the previous call's contents; the arrival counters must start at zero.
+  CK(cudaMemsetAsync(a.counters, 0, sizeof(int) * n_rows, st));
+  a.logits = logits;
+  a.ld = ld;
+  a.rows = n_rows;
+  a.vocab = vocab;
+  a.chunk = kSelChunk;
+  a.nchunks = chunks;
+  a.mode = mode;
+  a.temperature = mode == DRT_SELECT_NEG_ENTROPY ? temperature : 0.0;
+  a.exclude = -1;
+  a.conf = conf;
+  a.token = token;
+  CK(launch_k(sel_pass1_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  if (mode == DRT_SELECT_NEG_ENTROPY) CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  return DRT_OK;
+}

@@ -208,6 +208,17 @@ void drt_session_close(drt_session* s);
 size_t drt_selector_scratch_bytes(int32_t n_rows, int32_t vocab);
 int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows, int32_t vocab, int32_t mode,
                       double temperature, void* scratch, double* conf, int32_t* token, void* stream);
+/* The same selector without any device allocation, for callers that may not allocate device
+ * memory: a host whose GPU memory is owned by its own pool or fixed budget (outside of which it
+ * may not cudaMalloc), or a latency-critical caller that cannot afford cudaMalloc's implicit
+ * synchronization. No counterpart in the reference. The scratch is one static device array of
+ * about 0.53 MB that every GPU loading this library keeps until exit; calls are limited to
+ * n_rows <= 1024 and vocab <= 262144 (larger calls fail with DRT_INVALID_ARGUMENT). The first call
+ * on a device looks up the array's device address, so make that first call before any stream
+ * capture. All calls share the array: calls that overlap on the GPU (other streams, other
+ * threads) race and must be serialized by the caller. */
+int drt_selector_rows_noalloc(const float* logits, int64_t ld, int32_t n_rows, int32_t vocab, int32_t mode,
+                              double temperature, double* conf, int32_t* token, void* stream);
 /* y = x @ W^T on the tensor cores with the MLX rounding contract (bf16 output rounding when
  * round_bf16 != 0). x [rows x K] bf16, w [n x K] bf16, y [rows x n] f32; n % 128 == 0,
  * K % 64 == 0. scratch: see drt_linear_scratch_bytes (split-K partials + counters). */

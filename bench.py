@@ -178,6 +178,7 @@ def _run_ours(args, world, rank, local) -> dict | None:
     e2e_ms = float(np.mean([r["total_ms"] for r in results]))
     dec_ms = float(np.mean([r["decode_ms"] / max(1, r["forward_count"]) for r in results]))
     pre_ms = float(np.mean([r["prefill_ms"] for r in results]))
+    host_ms = float(np.mean([r["host_enqueue_ms"] for r in results]))
     committed = float(np.mean([r["committed_token_count"] for r in results]))
     forwards = float(np.mean([r["forward_count"] for r in results]))
     stats = torch.tensor([dev_ms, e2e_ms, dec_ms, pre_ms], dtype=torch.float64, device=f"cuda:{local}")
@@ -203,6 +204,7 @@ def _run_ours(args, world, rank, local) -> dict | None:
         "ms_per_denoising_step": round(dec_ms, 5),
         "tokens_per_s_per_request": round(committed / (dev_ms * 1e-3), 3),
         "prefill_ms": round(pre_ms, 4),
+        "host_enqueue_ms_per_request": round(host_ms, 3),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,

@@ -66,7 +66,7 @@ class GenerateResult(ctypes.Structure):
                 ("committed_token_count", ctypes.c_int32), ("near_tie_steps", ctypes.c_int32),
                 ("exact_tie_steps", ctypes.c_int32), ("stopped", ctypes.c_int32), ("canvas_len", ctypes.c_int32),
                 ("prefill_ms", ctypes.c_float), ("decode_ms", ctypes.c_float), ("total_ms", ctypes.c_float),
-                ("kernel_launches", ctypes.c_int32)]
+                ("kernel_launches", ctypes.c_int32), ("host_enqueue_ms", ctypes.c_float)]
 
 
 class StepTrace(ctypes.Structure):

@@ -14,8 +14,9 @@
 //   O_t = P V       (tcgen05.mma, A = P [128 x 128 keys], B = V^T tile [128d x 128 keys])
 //   o = o * alpha + O_t in registers.
 // K is cached as [nkv][pos][128] and V transposed as [nkv][128][pos], so both B operands are
-// K-major 128-byte-swizzled TMA tiles. With splits > 1 each CTA leaves (o, m, l) partials and
-// attn_combine_kernel merges them in a fixed order.
+// K-major 128-byte-swizzled TMA tiles. With splits > 1 the CTAs of one KV head form a thread-
+// block cluster and merge their (o, m, l) partials through distributed shared memory in rank
+// order.
 #pragma once
 #include "common.cuh"
 
@@ -32,10 +33,8 @@ struct AttnArgs {
   const int* kv_len_dev;
   int prompt_len, block_size, bidirectional;
   int kv_plane0;          // first plane of this layer in the [L*nkv] cache planes
-  int splits, tiles_per_split;
-  __nv_bfloat16* out;     // [rows][nq*128] (splits == 1)
-  float* ws_o;            // [splits][rows][nq][128]
-  float* ws_ml;           // [splits][rows][nq][2]
+  int splits, tiles_per_split;  // splits = cluster size along z (1, 4, 8 or 16)
+  __nv_bfloat16* out;     // [rows][nq*128]
   int* status;
   float scale_log2;       // log2(e) / sqrt(head_dim)
 };
@@ -54,7 +53,74 @@ constexpr int kAttnVBytes = 2 * 128 * 128;     // 128 d x 128 keys
 constexpr int kAttnStageBytes = kAttnKBytes + kAttnVBytes;
 constexpr int kAttnPBytes = 2 * 128 * 128;
 constexpr int kAttnStages = 2;
+constexpr int kAttnRowStride = 132;  // floats per received row (conflict-free float4 access)
 constexpr size_t kAttnSmemBytes = 1024 + kAttnQBytes + kAttnStages * kAttnStageBytes + kAttnPBytes + 256;
+
+// Split-KV merge inside one cluster of S CTAs (one KV head). CTA r owns query rows
+// [r*R, (r+1)*R), R = 128 / S. Every thread pushes its row's unnormalized (o, m, l) into the
+// owner's receive buffer recv[src rank * R + row % R] with remote stores; after the cluster
+// barrier the owner merges its rows over the S sources in rank order from local shared memory.
+template <int S>
+__device__ __forceinline__ void attn_push(const float* o_acc, float m_run, float l_run, float* recv, float* recv_ml,
+                                          int tid) {
+  constexpr int R = 128 / S;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t owner = static_cast<uint32_t>(tid / R);
+  const int slot = static_cast<int>(rank) * R + (tid % R);
+  const uint32_t dst = cluster_map(smem_u32(recv) + static_cast<uint32_t>(slot * kAttnRowStride * 4), owner);
+#pragma unroll
+  for (int d = 0; d < 128; d += 4)
+    st_cluster_f32x4(dst + d * 4, make_float4(o_acc[d], o_acc[d + 1], o_acc[d + 2], o_acc[d + 3]));
+  st_cluster_f32x2(cluster_map(smem_u32(recv_ml) + static_cast<uint32_t>(slot * 8), owner), m_run, l_run);
+}
+
+template <int S>
+__device__ __forceinline__ void attn_merge(const AttnArgs& a, const float* recv, const float* recv_ml, int g, int row0,
+                                           int rows_valid, int tid, bool failed) {
+  constexpr int R = 128 / S;
+  constexpr int ITEMS = R / 8;  // (row, 8-wide chunk) items per thread
+  const uint32_t rank = cluster_ctarank();
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const int item = it * 128 + tid;
+    const int lr = item / 16;  // local row in [0, R)
+    const int row = static_cast<int>(rank) * R + lr;
+    const int d0 = (item % 16) * 8;
+    float m_all = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < S; ++p) m_all = fmaxf(m_all, recv_ml[(p * R + lr) * 2]);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float l_all = 0.0f;
+#pragma unroll
+    for (int p = 0; p < S; ++p) {
+      const float m = recv_ml[(p * R + lr) * 2];
+      const float l = recv_ml[(p * R + lr) * 2 + 1];
+      const float w = (l == 0.0f || m == -INFINITY) ? 0.0f : exp2f(m - m_all);
+      l_all += l * w;
+      const float4 lo = *reinterpret_cast<const float4*>(recv + (p * R + lr) * kAttnRowStride + d0);
+      const float4 hi = *reinterpret_cast<const float4*>(recv + (p * R + lr) * kAttnRowStride + d0 + 4);
+      acc[0] += lo.x * w;
+      acc[1] += lo.y * w;
+      acc[2] += lo.z * w;
+      acc[3] += lo.w * w;
+      acc[4] += hi.x * w;
+      acc[5] += hi.y * w;
+      acc[6] += hi.z * w;
+      acc[7] += hi.w * w;
+    }
+    const int r_pos = row / a.rep;
+    const int r_q = row0 + r_pos;
+    if (!failed && r_pos < a.tile_pos && r_q < rows_valid) {
+      const int r_head = g * a.rep + (row - r_pos * a.rep);
+      const float inv = l_all > 0.0f ? 1.0f / l_all : 0.0f;
+      __align__(16) __nv_bfloat16 t[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) t[e] = __float2bfloat16_rn(acc[e] * inv);
+      *reinterpret_cast<uint4*>(a.out + static_cast<size_t>(r_q) * a.nq * 128 + static_cast<size_t>(r_head) * 128 + d0) =
+          *reinterpret_cast<const uint4*>(t);
+    }
+  }
+}
 
 __global__ void __launch_bounds__(128, 1)
     attn_prefix_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -250,8 +316,8 @@ __global__ void __launch_bounds__(128, 1)
     if (sflag[0]) { failed = true; break; }
   }
 
-  if (!failed && row_ok) {
-    if (a.splits == 1) {
+  if (a.splits == 1) {
+    if (!failed && row_ok) {
       const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
       __nv_bfloat16* dst = a.out + static_cast<size_t>(q_row) * a.nq * 128 + static_cast<size_t>(head) * 128;
 #pragma unroll
@@ -261,15 +327,27 @@ __global__ void __launch_bounds__(128, 1)
         for (int e = 0; e < 8; ++e) t[e] = __float2bfloat16_rn(o_acc[d + e] * inv);
         *reinterpret_cast<uint4*>(dst + d) = *reinterpret_cast<const uint4*>(t);
       }
-    } else {
-      const size_t slot = (static_cast<size_t>(split) * a.rows + q_row) * a.nq + head;
-      float* dst = a.ws_o + slot * 128;
-#pragma unroll
-      for (int d = 0; d < 128; d += 4) {
-        *reinterpret_cast<float4*>(dst + d) = make_float4(o_acc[d], o_acc[d + 1], o_acc[d + 2], o_acc[d + 3]);
-      }
-      a.ws_ml[slot * 2 + 0] = m_run;
-      a.ws_ml[slot * 2 + 1] = l_run;
+    }
+  } else {
+    // Split-KV merge across the cluster (dims 1 x 1 x splits). The receive buffer overlays the
+    // K/V stages, which peers may only write once this CTA's loads and UMMAs are done: arrive now,
+    // wait before pushing.
+    cluster_arrive();
+    float* recv = reinterpret_cast<float*>(sKV);      // [128][kAttnRowStride]
+    float* recv_ml = recv + 128 * kAttnRowStride;      // [128][2]
+    const float mr = failed ? -INFINITY : m_run;
+    const float lr = failed ? 0.0f : l_run;
+    cluster_wait();
+    switch (a.splits) {
+      case 4: attn_push<4>(o_acc, mr, lr, recv, recv_ml, tid); break;
+      case 8: attn_push<8>(o_acc, mr, lr, recv, recv_ml, tid); break;
+      default: attn_push<16>(o_acc, mr, lr, recv, recv_ml, tid); break;
+    }
+    cluster_sync();
+    switch (a.splits) {
+      case 4: attn_merge<4>(a, recv, recv_ml, g, row0, rows_valid, tid, failed); break;
+      case 8: attn_merge<8>(a, recv, recv_ml, g, row0, rows_valid, tid, failed); break;
+      default: attn_merge<16>(a, recv, recv_ml, g, row0, rows_valid, tid, failed); break;
     }
   }
   if (failed && tid == 0) {
@@ -279,45 +357,6 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 256);
-}
-
-// Merge split-KV partials: one warp per (query row, head), fixed split order.
-__global__ void attn_combine_kernel(const AttnArgs a) {
-  griddep_wait();
-  griddep_launch_dependents();
-  int rows_valid = a.rows;
-  if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
-  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int row = warp_global / a.nq;
-  const int head = warp_global - row * a.nq;
-  if (row >= rows_valid) return;
-  float m_all = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) {
-    const size_t slot = (static_cast<size_t>(s) * a.rows + row) * a.nq + head;
-    m_all = fmaxf(m_all, a.ws_ml[slot * 2]);
-  }
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float l_all = 0.0f;
-  for (int s = 0; s < a.splits; ++s) {
-    const size_t slot = (static_cast<size_t>(s) * a.rows + row) * a.nq + head;
-    const float m = a.ws_ml[slot * 2];
-    const float l = a.ws_ml[slot * 2 + 1];
-    if (l == 0.0f || m == -INFINITY) continue;
-    const float w = exp2f(m - m_all);
-    l_all += l * w;
-    const float4 o = *reinterpret_cast<const float4*>(a.ws_o + slot * 128 + lane * 4);
-    acc.x += o.x * w;
-    acc.y += o.y * w;
-    acc.z += o.z * w;
-    acc.w += o.w * w;
-  }
-  const float inv = l_all > 0.0f ? 1.0f / l_all : 0.0f;
-  __nv_bfloat16* dst = a.out + static_cast<size_t>(row) * a.nq * 128 + static_cast<size_t>(head) * 128 + lane * 4;
-  dst[0] = __float2bfloat16_rn(acc.x * inv);
-  dst[1] = __float2bfloat16_rn(acc.y * inv);
-  dst[2] = __float2bfloat16_rn(acc.z * inv);
-  dst[3] = __float2bfloat16_rn(acc.w * inv);
 }
 
 }  // namespace drt

@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -107,20 +108,38 @@ int map_matrix(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, i
 
 thread_local int64_t g_launches = 0;  // kernels enqueued by this thread (launch accounting)
 
+// Launch with optional programmatic dependent launch and a cluster of `cluster_z` CTAs along z.
 template <typename Kern, typename... Args>
-cudaError_t launch_k(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, Args... args) {
+cudaError_t launch_kc(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, int cluster_z,
+                      Args... args) {
   ++g_launches;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = pdl ? attr : nullptr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_z > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = static_cast<unsigned>(cluster_z);
+    ++n;
+  }
+  cfg.attrs = n ? attr : nullptr;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <typename Kern, typename... Args>
+cudaError_t launch_k(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, Args... args) {
+  return launch_kc(kernel, grid, block, smem, stream, pdl, 1, args...);
 }
 
 int g_num_sms_cache[64] = {0};
@@ -141,18 +160,23 @@ int configure_kernels() {
     result = DRT_OK;
     if (cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess)
+        cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       result = DRT_INTERNAL_ERROR;
   });
   if (result != DRT_OK) return set_error(DRT_INTERNAL_ERROR, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(cudaGetLastError()));
   return DRT_OK;
 }
 
-void split_k(int tiles, int kb, int target, int* splits, int* kbps) {
-  int sp = std::max(1, std::min(kb, (target + tiles / 2) / std::max(1, tiles)));
-  const int per = (kb + sp - 1) / sp;
-  *kbps = per;
-  *splits = (kb + per - 1) / per;
+// Split-K factor: the smallest power of two (<= max_split, <= kb) giving at least ~0.8 x SMs
+// CTAs. The split CTAs of one tile form one cluster.
+void split_k(int tiles, int kb, int sms, int max_split, int* splits, int* kbps) {
+  int sp = 1;
+  while (sp < max_split && sp * 2 <= kb && tiles * sp < (sms * 4) / 5) sp *= 2;
+  *splits = sp;
+  *kbps = (kb + sp - 1) / sp;
 }
 
 constexpr double kTieRel = 9.094947017729282e-13;  // 2^-40
@@ -528,10 +552,7 @@ struct drt_session {
   __nv_bfloat16 *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *xf = nullptr;
   float* logits = nullptr;
   __nv_bfloat16 *kcache = nullptr, *vtcache = nullptr;
-  float* gemm_ws = nullptr;
-  int* gemm_cnt = nullptr;
-  size_t gemm_ws_floats = 0, gemm_cnt_n = 0;
-  float *attn_ws_o = nullptr, *attn_ws_ml = nullptr;
+  int max_cluster = 16;               // largest cluster the GPU schedules for the split kernels
   float* sel_pmax = nullptr;
   int* sel_pidx = nullptr;
   double* sel_psum = nullptr;
@@ -609,8 +630,6 @@ GemmArgs base_args(drt_session* s, int n_out, int K, const Fwd& f) {
   a.rows_dev = f.rows_dev;
   a.splits = 1;
   a.kb_per_split = K / 64;
-  a.workspace = s->gemm_ws;
-  a.counters = s->gemm_cnt;
   a.status = s->status;
   a.pos0 = f.pos0;
   a.pos0_dev = f.pos0_dev;
@@ -622,17 +641,13 @@ int run_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmA
   const int tiles_m = a.n_out / 128;
   const int tiles_n = (a.rows + BN - 1) / BN;
   const int kb = a.K / 64;
-  if (allow_split) split_k(tiles_m * tiles_n, kb, s->sms, &a.splits, &a.kb_per_split);
+  if (allow_split) split_k(tiles_m * tiles_n, kb, s->sms, s->max_cluster, &a.splits, &a.kb_per_split);
   else { a.splits = 1; a.kb_per_split = kb; }
   const int max_stages = (200 * 1024) / GemmCfg<BN>::kStageBytes;
   a.stages = std::max(1, std::min(a.kb_per_split, max_stages));
-  if (a.splits > 1) {
-    const size_t need = static_cast<size_t>(tiles_m) * tiles_n * a.splits * BN * 128;
-    if (need > s->gemm_ws_floats || static_cast<size_t>(tiles_m) * tiles_n > s->gemm_cnt_n)
-      return set_error(DRT_INTERNAL_ERROR, "split-K workspace too small (%zu floats needed)", need);
-  }
   dim3 grid(tiles_m, tiles_n, a.splits);
-  CK(launch_k(gemm_swapab_kernel<BN>, grid, dim3(128), GemmCfg<BN>::smem_bytes(a.stages), s->stream, true, mA, mB, a));
+  CK(launch_kc(gemm_swapab_kernel<BN>, grid, dim3(128), GemmCfg<BN>::smem_bytes(a.stages), s->stream, true, a.splits, mA,
+               mB, a));
   return DRT_OK;
 }
 
@@ -689,8 +704,6 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     t.bidirectional = f.bidirectional;
     t.kv_plane0 = l * m->nkv;
     t.out = s->attn;
-    t.ws_o = s->attn_ws_o;
-    t.ws_ml = s->attn_ws_ml;
     t.status = s->status;
     t.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(128.0));
     const int qtiles = (f.rows + m->tile_pos - 1) / m->tile_pos;
@@ -701,12 +714,8 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
       t.splits = 1;
       t.tiles_per_split = (s->max_seq + 127) / 128;
     }
-    CK(launch_k(attn_prefix_kernel, dim3(qtiles, m->nkv, t.splits), dim3(128), kAttnSmemBytes, s->stream, true, s->m_q, s->m_k,
-                s->m_v, t));
-    if (t.splits > 1) {
-      const int warps = f.rows * m->nq;
-      CK(launch_k(attn_combine_kernel, dim3((warps + 3) / 4), dim3(128), 0, s->stream, true, t));
-    }
+    CK(launch_kc(attn_prefix_kernel, dim3(qtiles, m->nkv, t.splits), dim3(128), kAttnSmemBytes, s->stream, true, t.splits,
+                 s->m_q, s->m_k, s->m_v, t));
     // o_proj + residual.
     GemmArgs o = base_args(s, H, qd, f);
     o.epi = EPI_RESID;
@@ -865,29 +874,33 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = salloc(s, &s->vtcache, kv)) != DRT_OK) return fail(rc);
   if (cudaMemset(s->kcache, 0, kv * 2) != cudaSuccess || cudaMemset(s->vtcache, 0, kv * 2) != cudaSuccess)
     return fail(set_error(DRT_INTERNAL_ERROR, "kv memset failed"));
-  // Split-K workspace: the largest decode GEMM (BN = 64, one column tile).
-  size_t ws = 0;
-  int max_tiles = m->V / 128;
-  const int shapes[4][2] = {{m->qkv_rows, H}, {H, qd}, {m->gu_rows, H}, {H, m->I}};
-  for (auto& sh : shapes) {
-    int sp, per;
-    split_k(sh[0] / 128, sh[1] / 64, s->sms, &sp, &per);
-    ws = std::max(ws, static_cast<size_t>(sh[0] / 128) * sp * 64 * 128);
-    max_tiles = std::max(max_tiles, sh[0] / 128);
+  // Largest cluster the GPU co-schedules for the split kernels (16 needs the non-portable
+  // opt-in; fall back to 8).
+  {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(1, 1, 16);
+    lc.blockDim = dim3(128);
+    lc.dynamicSmemBytes = kAttnSmemBytes;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 16;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    int n16 = 0;
+    if (cudaOccupancyMaxActiveClusters(&n16, attn_prefix_kernel, &lc) != cudaSuccess || n16 < 1) {
+      cudaGetLastError();
+      s->max_cluster = 8;
+    }
   }
-  s->gemm_ws_floats = ws;
-  s->gemm_cnt_n = static_cast<size_t>(max_tiles) * ((R + 63) / 64);
-  if ((rc = salloc(s, &s->gemm_ws, ws)) != DRT_OK) return fail(rc);
-  if ((rc = salloc(s, &s->gemm_cnt, s->gemm_cnt_n)) != DRT_OK) return fail(rc);
-  if (cudaMemset(s->gemm_cnt, 0, sizeof(int) * s->gemm_cnt_n) != cudaSuccess)
-    return fail(set_error(DRT_INTERNAL_ERROR, "memset failed"));
-  // Split-KV attention for one decode query tile.
+  // Split-KV attention for one decode query tile: a power-of-two cluster of 4..16 CTAs per head.
   const int kv_tiles = (s->max_seq + 127) / 128;
-  s->attn_splits = std::max(1, std::min(kv_tiles, s->sms / m->nkv));
-  s->attn_tps = (kv_tiles + s->attn_splits - 1) / s->attn_splits;
-  s->attn_splits = (kv_tiles + s->attn_tps - 1) / s->attn_tps;
-  if ((rc = salloc(s, &s->attn_ws_o, static_cast<size_t>(s->attn_splits) * kMaxFwdRows * m->nq * 128)) != DRT_OK) return fail(rc);
-  if ((rc = salloc(s, &s->attn_ws_ml, static_cast<size_t>(s->attn_splits) * kMaxFwdRows * m->nq * 2)) != DRT_OK) return fail(rc);
+  int asp = 1;
+  while (asp < s->max_cluster && asp < kv_tiles && m->nkv * asp < (s->sms * 4) / 5) asp *= 2;
+  if (asp == 2) asp = kv_tiles >= 4 ? 4 : 1;
+  s->attn_splits = asp;
+  s->attn_tps = (kv_tiles + asp - 1) / asp;
   // Selector scratch.
   s->sel_chunks = (m->V + kSelChunk - 1) / kSelChunk;
   const size_t np = static_cast<size_t>(kMaxFrontier) * s->sel_chunks;
@@ -1208,6 +1221,7 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
   const int limit = hs->iteration_limit;
   int rc = DRT_OK;
   int replays = 0;
+  const auto host0 = std::chrono::steady_clock::now();
   for (int i = 0; i < limit; ++i) {
     ++replays;
     if (cudaGraphLaunch(s->g_step, s->stream) != cudaSuccess) { rc = set_error(DRT_INTERNAL_ERROR, "graph launch failed"); break; }
@@ -1218,6 +1232,7 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
       if (cudaEventQuery(flag_ev[j]) == cudaSuccess && s->hflags[j]) break;
     }
   }
+  const float host_ms = std::chrono::duration<float, std::milli>(std::chrono::steady_clock::now() - host0).count();
   cudaEventRecord(e_dec1, s->stream);
   cudaMemcpyAsync(hs, s->state, sizeof(DecodeState), cudaMemcpyDeviceToHost, s->stream);
   cudaMemcpyAsync(out, s->canvas, sizeof(int) * canvas_len, cudaMemcpyDeviceToHost, s->stream);
@@ -1253,6 +1268,7 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
     result->decode_ms = dec_ms;
     result->total_ms = tot_ms;
     result->kernel_launches = prefill_launches + replays * s->g_step_kernels;
+    result->host_enqueue_ms = host_ms;
   }
   s->m_forwards += hs->forward_count;
   s->m_committed += hs->committed_count;
@@ -1321,15 +1337,20 @@ extern "C" int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows
 }
 
 extern "C" size_t drt_linear_scratch_bytes(int32_t rows, int32_t n, int32_t K, int32_t splits) {
-  const size_t tiles = static_cast<size_t>(std::max(n, 128) / 128) * ((std::max(rows, 1) + 63) / 64);
-  return 1024 + tiles * std::max(splits, 1) * 64 * 128 * 4 + tiles * 4 + 4;
+  (void)rows;
+  (void)n;
+  (void)K;
+  (void)splits;
+  return 0;  // split-K partials live in the cluster's shared memory
 }
 
 extern "C" int drt_linear_bf16(const void* x, const void* w, float* y, int32_t rows, int32_t n, int32_t K, int32_t splits,
                                int32_t round_bf16, void* scratch, void* stream) {
-  REQUIRE(x && w && y && scratch, "null argument");
+  (void)scratch;
+  REQUIRE(x && w && y, "null argument");
   REQUIRE(rows >= 1 && n >= 128 && n % 128 == 0 && K >= 64 && K % 64 == 0, "linear needs n %% 128 == 0 and K %% 64 == 0");
-  REQUIRE(splits >= 1 && splits <= K / 64, "splits outside [1, K/64]");
+  REQUIRE(splits == 1 || splits == 2 || splits == 4 || splits == 8 || splits == 16, "splits must be 1, 2, 4, 8 or 16");
+  REQUIRE(splits <= K / 64, "splits exceed the K blocks");
   TRY(configure_kernels());
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CUtensorMap ma, mb;
@@ -1337,25 +1358,19 @@ extern "C" int drt_linear_bf16(const void* x, const void* w, float* y, int32_t r
   TRY(map_matrix(&mb, x, rows, K, 64));
   const int tiles_m = n / 128, tiles_n = (rows + 63) / 64;
   const int kb = K / 64;
-  const int per = (kb + splits - 1) / splits;
   GemmArgs a;
   memset(&a, 0, sizeof(a));
   a.n_out = n;
   a.K = K;
   a.rows = rows;
-  a.splits = (kb + per - 1) / per;
-  a.kb_per_split = per;
-  a.stages = std::max(1, std::min(per, 8));
-  uint8_t* p = static_cast<uint8_t*>(scratch);
-  a.workspace = reinterpret_cast<float*>(p);
-  a.counters = reinterpret_cast<int*>(p + static_cast<size_t>(tiles_m) * tiles_n * a.splits * 64 * 128 * 4);
-  a.status = a.counters + static_cast<size_t>(tiles_m) * tiles_n;
-  CK(cudaMemsetAsync(a.counters, 0, sizeof(int) * (static_cast<size_t>(tiles_m) * tiles_n + 1), st));
+  a.splits = splits;
+  a.kb_per_split = (kb + splits - 1) / splits;
+  a.stages = std::max(1, std::min(a.kb_per_split, 8));
   a.epi = round_bf16 ? EPI_STORE_F32 : EPI_STORE_RAW;
   a.out_f32 = y;
   a.ld_out = n;
-  CK(launch_k(gemm_swapab_kernel<64>, dim3(tiles_m, tiles_n, a.splits), dim3(128), GemmCfg<64>::smem_bytes(a.stages), st, false, ma,
-              mb, a));
+  CK(launch_kc(gemm_swapab_kernel<64>, dim3(tiles_m, tiles_n, splits), dim3(128), GemmCfg<64>::smem_bytes(a.stages), st,
+               false, splits, ma, mb, a));
   return DRT_OK;
 }
 

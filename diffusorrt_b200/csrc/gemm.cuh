@@ -8,11 +8,12 @@
 // column n. Weights stream from HBM through a TMA ring (SWIZZLE_128B, evict-first hint); the
 // activation tile for the same K block arrives on its own barrier so that, under
 // programmatic dependent launch, the weight prefetch of this kernel overlaps the tail of the
-// kernel that produces x.
+// kernel that produces x. Warp 0 issues TMA, warp 1 issues UMMA, all four warps run the epilogue.
 //
-// Split-K: grid.z CTAs share one output tile; each writes its f32 partial to a workspace slot
-// and the last CTA to arrive (per-tile counter) sums the partials in a fixed order and runs
-// the epilogue, so results do not depend on arrival order. The counter is reset by that CTA.
+// Split-K: grid.z CTAs share one output tile and form one thread-block cluster. Each pushes
+// column slice r of its f32 partial into CTA r's shared memory (remote stores), and after the
+// cluster barrier CTA r sums its slice over all partials in rank order and runs the epilogue for
+// those columns. No global workspace, no atomics, and results do not depend on scheduling.
 //
 // Epilogues follow the MLX precision contract of the reference forward
 // (python/src/edllm/backends/mlx_ops.py:97-130 linear, :21-35 rms_norm, :133-144 rope,
@@ -36,11 +37,9 @@ struct GemmArgs {
   int K;                 // multiple of 64
   int rows;              // activation rows covered by the grid
   const int* rows_dev;   // optional device-side row count (<= rows) for static graphs
-  int splits;            // split-K factor
+  int splits;            // split-K factor = cluster size along z (1, 2, 4, 8 or 16)
   int kb_per_split;      // K blocks of 64 per split (the last split takes the remainder)
   int stages;            // smem ring depth
-  float* workspace;      // split partials
-  int* counters;         // per-tile arrival counters (zero at rest)
   int* status;           // device error word
   int epi;
   // epilogue operands
@@ -68,9 +67,13 @@ struct GemmCfg {
   static constexpr int kBBytes = BN * 128;        // BN rows x 64 bf16
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  static size_t smem_bytes(int stages) {
-    return 1024 + static_cast<size_t>(stages) * kStageBytes + 256;
+  // Ring, or (split-K) the receive buffer plus the epilogue exchange buffer, whichever is larger.
+  __host__ __device__ static size_t body_bytes(int stages) {
+    const size_t ring = static_cast<size_t>(stages) * kStageBytes;
+    const size_t epi = static_cast<size_t>(BN) * 128 * 4 + (32 * 128 + 64) * 4;
+    return ((ring > epi ? ring : epi) + 1023) & ~size_t(1023);
   }
+  __host__ __device__ static size_t smem_bytes(int stages) { return 1024 + body_bytes(stages) + 256; }
 };
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -79,28 +82,34 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// Epilogue for one chunk of 32 accumulator columns (activation rows col0 .. col0+ncols-1).
-// v[i] holds this thread's weight row (m0 + tid) for activation row col0 + i.
-__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int col0,
-                                                    int ncols, int m0, int tid, float* xs,
-                                                    int pos0) {
+// Epilogue for up to 32 accumulator columns (activation rows col0 .. col0+ncols-1).
+// v[i] holds this thread's weight row (m0 + tid) for activation row col0 + i. All loops run to
+// 32 with a guard so v stays in registers.
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int col0, int ncols, int m0, int tid,
+                                                    float* xs, int pos0) {
   const int n = m0 + tid;
   const float b = a.bias != nullptr ? a.bias[n] : 0.0f;
   switch (a.epi) {
     case EPI_STORE_RAW: {
-      for (int i = 0; i < ncols; ++i) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = v[i];
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = v[i];
       break;
     }
     case EPI_STORE_F32: {
-      for (int i = 0; i < ncols; ++i)
-        a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = __fadd_rn(bf16_round(v[i]), b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = __fadd_rn(bf16_round(v[i]), b);
       break;
     }
     case EPI_RESID: {
-      for (int i = 0; i < ncols; ++i) {
-        float* p = a.out_f32 + static_cast<size_t>(col0 + i) * a.ld_out + n;
-        *p = __fadd_rn(*p, __fadd_rn(bf16_round(v[i]), b));
-      }
+      float cur[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) cur[i] = i < ncols ? a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncols)
+          a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = __fadd_rn(cur[i], __fadd_rn(bf16_round(v[i]), b));
       break;
     }
     case EPI_SWIGLU: {
@@ -108,16 +117,20 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
       // lanes 64..127 = up rows j0..j0+63 of the same intermediate features.
       const int j0 = (m0 >> 1);
       if (tid >= 64) {
+#pragma unroll
         for (int i = 0; i < 32; ++i) xs[i * 64 + (tid - 64)] = __fadd_rn(bf16_round(v[i]), b);
       }
       __syncthreads();
       if (tid < 64) {
-        for (int i = 0; i < ncols; ++i) {
-          const float g = __fadd_rn(bf16_round(v[i]), b);
-          const float u = xs[i * 64 + tid];
-          const float sig = 1.0f / (1.0f + expf(-g));
-          const float act = __fmul_rn(__fmul_rn(g, sig), u);
-          a.out_bf16[static_cast<size_t>(col0 + i) * a.ld_out + j0 + tid] = __float2bfloat16_rn(act);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < ncols) {
+            const float g = __fadd_rn(bf16_round(v[i]), b);
+            const float u = xs[i * 64 + tid];
+            const float sig = 1.0f / (1.0f + expf(-g));
+            const float act = __fmul_rn(__fmul_rn(g, sig), u);
+            a.out_bf16[static_cast<size_t>(col0 + i) * a.ld_out + j0 + tid] = __float2bfloat16_rn(act);
+          }
         }
       }
       __syncthreads();
@@ -141,11 +154,14 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
             *reinterpret_cast<uint4*>(dst + q * 8) = *reinterpret_cast<const uint4*>(t);
           }
         } else {
-          for (int i = 0; i < ncols; ++i) dst[i] = __float2bfloat16_rn(__fadd_rn(bf16_round(v[i]), b));
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < ncols) dst[i] = __float2bfloat16_rn(__fadd_rn(bf16_round(v[i]), b));
         }
         break;
       }
       const float* nw = is_q ? a.qnorm_w : a.knorm_w;
+#pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float val = __fadd_rn(bf16_round(v[i]), b);
         v[i] = val;
@@ -171,7 +187,9 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
       const float w_self = nw != nullptr ? nw[tid] : 1.0f;
       const float w_part = nw != nullptr ? nw[partner] : 1.0f;
       const int head = is_q ? tile : tile - a.nq;
-      for (int i = 0; i < ncols; ++i) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (i >= ncols) continue;
         float x = v[i];
         float xp = xs[i * 128 + partner];
         if (nw != nullptr) {
@@ -197,6 +215,52 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
   }
 }
 
+// Split-K exchange inside one cluster of S CTAs. Each thread holds its weight row's f32 partial
+// for all BN activation rows; column slice j (BN / S columns) belongs to CTA j. Every thread
+// pushes slice j into CTA j's receive buffer recv[src rank][thread][BN / S] with remote
+// shared-memory stores; after the cluster barrier each CTA sums its own slice over the S sources
+// in rank order from local shared memory.
+template <int BN, int S>
+__device__ __forceinline__ void split_push(const float* acc, float* recv, uint32_t rank, int tid) {
+  constexpr int CPR = BN / S;
+  constexpr int QP = CPR / 4;
+  static_assert(CPR >= 4 && CPR <= 32, "split slice must be 4..32 columns");
+  const uint32_t base = smem_u32(recv) + static_cast<uint32_t>(((rank * 128 + tid) * CPR) * 4);
+#pragma unroll
+  for (int j = 0; j < S; ++j) {
+    const uint32_t dst = cluster_map(base, static_cast<uint32_t>(j));
+#pragma unroll
+    for (int q = 0; q < QP; ++q) {
+      const int c = j * CPR + q * 4;
+      st_cluster_f32x4(dst + q * 16, make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]));
+    }
+  }
+}
+
+template <int BN, int S>
+__device__ __forceinline__ int split_sum(const float* recv, uint32_t rank, int tid, float* v, int* c0_out) {
+  constexpr int CPR = BN / S;
+  constexpr int QP = CPR / 4;
+#pragma unroll
+  for (int q = 0; q < QP; ++q) {
+    float4 acc = *reinterpret_cast<const float4*>(recv + tid * CPR + q * 4);
+#pragma unroll
+    for (int p = 1; p < S; ++p) {
+      const float4 t = *reinterpret_cast<const float4*>(recv + (p * 128 + tid) * CPR + q * 4);
+      acc.x += t.x;
+      acc.y += t.y;
+      acc.z += t.z;
+      acc.w += t.w;
+    }
+    v[4 * q] = acc.x;
+    v[4 * q + 1] = acc.y;
+    v[4 * q + 2] = acc.z;
+    v[4 * q + 3] = acc.w;
+  }
+  *c0_out = static_cast<int>(rank) * CPR;
+  return CPR;
+}
+
 template <int BN>
 __global__ void __launch_bounds__(128, 1)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -206,22 +270,23 @@ __global__ void __launch_bounds__(128, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int stages = a.stages;
   uint8_t* ring = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + static_cast<size_t>(stages) * Cfg::kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + Cfg::body_bytes(stages));
   uint64_t* fullA = bars;
   uint64_t* fullB = bars + stages;
   uint64_t* empty = bars + 2 * stages;
   uint64_t* accum = bars + 3 * stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] error, [1] last-CTA
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] error
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
+  const int lane = tid & 31;
   const int m0 = blockIdx.x * 128;
   const int n0 = blockIdx.y * BN;
   const int split = blockIdx.z;
   const int kb_total = a.K >> 6;
   const int kb0 = split * a.kb_per_split;
-  const int nkb = min(a.kb_per_split, kb_total - kb0);
+  const int nkb = max(0, min(a.kb_per_split, kb_total - kb0));
 
   if (tid == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -231,7 +296,6 @@ __global__ void __launch_bounds__(128, 1)
     }
     mbar_init(accum, 1);
     flags[0] = 0;
-    flags[1] = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -246,7 +310,7 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Weight prefetch: independent of the producer kernel, so it runs before the PDL wait.
+  // Weight prefetch: independent of the producer kernel, so it is issued before the PDL wait.
   const int npre = min(stages, nkb);
   uint64_t policy = 0;
   if (tid == 0) {
@@ -259,43 +323,52 @@ __global__ void __launch_bounds__(128, 1)
   griddep_wait();
   griddep_launch_dependents();
 
-  if (tid == 0) {
-    bool ok = true;
-    for (int i = 0; i < nkb && ok; ++i) {
-      const int s = i % stages;
-      uint8_t* st = ring + static_cast<size_t>(s) * Cfg::kStageBytes;
-      if (i >= stages) {
-        if (!mbar_wait(&empty[s], ((i / stages) - 1) & 1)) { ok = false; break; }
-        mbar_expect_tx(&fullA[s], Cfg::kABytes);
-        tma_load_2d_hint(st, &tmA, &fullA[s], (kb0 + i) * 64, m0, policy);
+  // Warp 0: TMA producer. Warp 1: UMMA issuer. One elected lane each; the rest of the warp waits
+  // at the warp barrier instead of spinning beside it.
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < nkb && ok; ++i) {
+        const int s = i % stages;
+        uint8_t* st = ring + static_cast<size_t>(s) * Cfg::kStageBytes;
+        if (i >= stages) {
+          if (!mbar_wait(&empty[s], ((i / stages) - 1) & 1)) { ok = false; break; }
+          mbar_expect_tx(&fullA[s], Cfg::kABytes);
+          tma_load_2d_hint(st, &tmA, &fullA[s], (kb0 + i) * 64, m0, policy);
+        }
+        mbar_expect_tx(&fullB[s], Cfg::kBBytes);
+        tma_load_2d(st + Cfg::kABytes, &tmB, &fullB[s], (kb0 + i) * 64, n0);
       }
-      mbar_expect_tx(&fullB[s], Cfg::kBBytes);
-      tma_load_2d(st + Cfg::kABytes, &tmB, &fullB[s], (kb0 + i) * 64, n0);
+      if (!ok) { record_error(a.status, DEV_TIMEOUT_TMA); flags[0] = 1; }
     }
-    if (!ok) { record_error(a.status, DEV_TIMEOUT_TMA); flags[0] = 1; }
-  } else if (tid == 32) {
-    const uint32_t idesc = idesc_bf16_f32(128, BN);
-    bool ok = true;
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % stages;
-      const uint32_t ph = (i / stages) & 1;
-      if (!mbar_wait(&fullA[s], ph) || !mbar_wait(&fullB[s], ph)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t a_addr = smem_u32(ring + static_cast<size_t>(s) * Cfg::kStageBytes);
-      const uint32_t b_addr = a_addr + Cfg::kABytes;
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(128, BN);
+      bool ok = true;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % stages;
+        const uint32_t ph = (i / stages) & 1;
+        if (!mbar_wait(&fullA[s], ph) || !mbar_wait(&fullB[s], ph)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(ring + static_cast<size_t>(s) * Cfg::kStageBytes);
+        const uint32_t b_addr = a_addr + Cfg::kABytes;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        umma_bf16(tmem, sdesc_kmajor_sw128(a_addr + kk * 32), sdesc_kmajor_sw128(b_addr + kk * 32), idesc,
-                  (i | kk) != 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) {
+          umma_bf16(tmem, sdesc_kmajor_sw128(a_addr + kk * 32), sdesc_kmajor_sw128(b_addr + kk * 32), idesc,
+                    (i | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
       }
-      umma_commit(&empty[s]);
+      if (!ok) { record_error(a.status, DEV_TIMEOUT_MMA); flags[0] = 1; }
+      umma_commit(accum);
     }
-    if (!ok) { record_error(a.status, DEV_TIMEOUT_MMA); flags[0] = 1; }
-    umma_commit(accum);
+    __syncwarp();
   }
 
   // ---------------- epilogue (all four warps; warp w owns TMEM lanes [32w, 32w+32))
-  const bool acc_ok = mbar_wait(accum, 0);
+  bool acc_ok = true;
+  if (nkb > 0) acc_ok = mbar_wait(accum, 0);
   tc_fence_after();
   if (!acc_ok) { record_error(a.status, DEV_TIMEOUT_EPI); flags[0] = 1; }
   __syncthreads();
@@ -304,49 +377,58 @@ __global__ void __launch_bounds__(128, 1)
   if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
   const int pos0 = a.pos0_dev != nullptr ? *a.pos0_dev : a.pos0;
   const int ncol_valid = max(0, min(BN, rows_valid - n0));
-  float* xs = reinterpret_cast<float*>(ring);  // epilogue exchange reuses the (drained) ring
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
 
-  if (!failed && ncol_valid > 0) {
-    if (a.splits == 1) {
+  if (a.splits == 1) {
+    float* xs = reinterpret_cast<float*>(ring);  // exchange buffer over the drained ring
+    if (!failed) {
       for (int cb = 0; cb < ncol_valid; cb += 32) {
         float v[32];
         tmem_ld32(lane_addr + cb, v);
         gemm_epilogue_chunk(a, v, n0 + cb, min(32, ncol_valid - cb), m0, tid, xs, pos0);
       }
-    } else {
-      const int tile_id = blockIdx.y * gridDim.x + blockIdx.x;
-      float* ws_tile = a.workspace + static_cast<size_t>(tile_id) * a.splits * BN * 128;
-      float* mine = ws_tile + static_cast<size_t>(split) * BN * 128;
-      for (int cb = 0; cb < ncol_valid; cb += 32) {
-        float v[32];
-        tmem_ld32(lane_addr + cb, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mine[(cb + i) * 128 + tid] = v[i];
-      }
-      __threadfence();
-      __syncthreads();
-      if (tid == 0) {
-        const int old = atomicAdd(&a.counters[tile_id], 1);
-        flags[1] = (old == a.splits - 1) ? 1 : 0;
-      }
-      __syncthreads();
-      if (flags[1]) {
-        __threadfence();
-        for (int cb = 0; cb < ncol_valid; cb += 32) {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-          for (int s = 0; s < a.splits; ++s) {
-            const float* src = ws_tile + static_cast<size_t>(s) * BN * 128;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] += __ldcg(&src[(cb + i) * 128 + tid]);
-          }
-          gemm_epilogue_chunk(a, v, n0 + cb, min(32, ncol_valid - cb), m0, tid, xs, pos0);
-        }
-        if (tid == 0) a.counters[tile_id] = 0;
-      }
     }
+  } else {
+    // Split-K across the CTAs of one cluster (cluster dims 1 x 1 x splits). The receive buffer
+    // overlays the ring, which a peer's pushes may only reach once this CTA's own UMMAs are done:
+    // arrive here (own accumulator final), wait before pushing (every peer's accumulator final).
+    cluster_arrive();
+    float* recv = reinterpret_cast<float*>(ring);  // [splits][128][BN / splits]
+    float* xs = recv + 128 * BN;
+    const uint32_t rank = cluster_ctarank();
+    float v[32];
+    int c0 = 0, nc = 0;
+    if constexpr (BN == 64) {
+      float acc[BN];
+      if (!failed && nkb > 0) {
+#pragma unroll
+        for (int cb = 0; cb < BN; cb += 32) tmem_ld32(lane_addr + cb, acc + cb);
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) acc[c] = 0.0f;
+      }
+      cluster_wait();
+      switch (a.splits) {
+        case 2: split_push<BN, 2>(acc, recv, rank, tid); break;
+        case 4: split_push<BN, 4>(acc, recv, rank, tid); break;
+        case 8: split_push<BN, 8>(acc, recv, rank, tid); break;
+        default: split_push<BN, 16>(acc, recv, rank, tid); break;
+      }
+      cluster_sync();
+      switch (a.splits) {
+        case 2: nc = split_sum<BN, 2>(recv, rank, tid, v, &c0); break;
+        case 4: nc = split_sum<BN, 4>(recv, rank, tid, v, &c0); break;
+        case 8: nc = split_sum<BN, 8>(recv, rank, tid, v, &c0); break;
+        default: nc = split_sum<BN, 16>(recv, rank, tid, v, &c0); break;
+      }
+    } else {
+      // Wider tiles (prompt prefill) are never split.
+      cluster_wait();
+      cluster_sync();
+      if (tid == 0) record_error(a.status, DEV_BAD_SHAPE);
+    }
+    nc = max(0, min(nc, ncol_valid - c0));
+    if (nc > 0 && !failed) gemm_epilogue_chunk(a, v, n0 + c0, nc, m0, tid, xs, pos0);
   }
   if (failed && tid == 0) {
     // Drain loads that may still be landing in this CTA's shared memory (bounded).

@@ -118,6 +118,7 @@ typedef struct drt_generate_result {
   float decode_ms;             /* device time of all denoising steps */
   float total_ms;              /* device time from the prompt upload to the canvas download */
   int32_t kernel_launches;     /* kernels this call launched (prefill + graph replays) */
+  float host_enqueue_ms;       /* host wall time spent enqueueing the denoising steps */
 } drt_generate_result;
 
 /* One recorded denoising step (device-resident loop). */
@@ -221,7 +222,9 @@ int drt_selector_rows_noalloc(const float* logits, int64_t ld, int32_t n_rows, i
                               double temperature, double* conf, int32_t* token, void* stream);
 /* y = x @ W^T on the tensor cores with the MLX rounding contract (bf16 output rounding when
  * round_bf16 != 0). x [rows x K] bf16, w [n x K] bf16, y [rows x n] f32; n % 128 == 0,
- * K % 64 == 0. scratch: see drt_linear_scratch_bytes (split-K partials + counters). */
+ * K % 64 == 0; splits in {1, 2, 4, 8, 16} (split-K CTAs of a tile form one thread-block cluster
+ * and reduce through distributed shared memory, so scratch may be NULL and
+ * drt_linear_scratch_bytes returns 0). */
 size_t drt_linear_scratch_bytes(int32_t rows, int32_t n, int32_t K, int32_t splits);
 int drt_linear_bf16(const void* x, const void* w, float* y, int32_t rows, int32_t n, int32_t K, int32_t splits,
                     int32_t round_bf16, void* scratch, void* stream);

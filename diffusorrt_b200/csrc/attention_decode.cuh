@@ -1,0 +1,346 @@
+// Prefix-KV attention for one denoising step (at most 128 / rep forwarded positions), tcgen05.
+//
+// Semantics are those of attn_prefix_kernel (attention.cuh): the reference SDPA with the d2f
+// block-causal mask (python/src/edllm/backends/mlx_ops.py:191-288, 347-443), GQA with the rep
+// query heads of one KV head packed with the positions into the M = 128 rows of the UMMA
+// (row r = position r / rep, head g * rep + r % rep).
+//
+// Work split, per KV head g: a cluster of S CTAs (S = 1, 2, 4, 8 or 16) shares the visible keys
+// in balanced runs of 64-key sub-tiles, at most kDaMaxSub sub-tiles per CTA. A CTA
+//   1. streams its K and V^T sub-tiles into shared memory with TMA. Sub-tiles that lie wholly
+//      before the first forwarded position hold final K/V from earlier steps and are requested
+//      before the programmatic-dependent-launch wait, so they stream while the QKV linear that
+//      precedes this kernel is still running; the rest (and Q) are requested after it;
+//   2. computes S_j = Q K_j^T for every sub-tile into TMEM (one 64-column block each);
+//   3. runs a two-pass softmax over all of its keys with two threads per row (pass 1: row max,
+//      pass 2: exp2, the bf16 P written over the consumed K sub-tile), in the log2 domain;
+//   4. accumulates O = sum_j P_j V_j on the tensor cores into TMEM;
+//   5. merges the S partial (O, m, l) rows: CTA p owns a run of R = ceil(rows / S) rows; every
+//      CTA stages its rows in order and sends run p to CTA p with one bulk shared-to-shared copy
+//      completing on CTA p's receive barrier; the owner rescales by exp2(m_i - max m) and sums in
+//      rank order, then normalises and writes bf16.
+// All waits are bounded (common.cuh); on a timeout the CTA records the error and unwinds.
+#pragma once
+#include "attention.cuh"
+
+namespace drt {
+
+constexpr int kDaMaxSub = 5;                    // 64-key sub-tiles per CTA
+constexpr int kDaQBytes = 2 * 128 * 128;        // Q: two 64-d atoms x 128 rows
+constexpr int kDaKBytes = 2 * 64 * 128;         // K sub-tile: two 64-d atoms x 64 keys
+constexpr int kDaVBytes = 128 * 128;            // V^T sub-tile: 128 d rows x 64 keys
+constexpr int kDaSubBytes = kDaKBytes + kDaVBytes;
+constexpr int kDaRowFloats = 132;               // merge row: 128 d + m + l + 2 pad (528 B)
+constexpr int kDaThreads = 256;
+// Q | sub-tiles | row-statistics exchange | barriers
+constexpr size_t kDaBodyBytes = kDaQBytes + static_cast<size_t>(kDaMaxSub) * kDaSubBytes;
+constexpr size_t kDaSmemBytes = 1024 + kDaBodyBytes + 4 * 128 * 4 + 256;
+
+struct DecAttnArgs {
+  int nq, nkv, rep;
+  int rows;               // query positions covered (<= 128 / rep)
+  const int* rows_dev;    // device-side live position count
+  int q_pos0;
+  const int* q_pos0_dev;  // device-side first forwarded position
+  int kv_len;
+  const int* kv_len_dev;
+  int prompt_len, block_size, bidirectional;
+  int kv_plane0;          // first cache plane of this layer
+  int splits;             // CTAs per KV head (= cluster size along x)
+  __nv_bfloat16* out;     // [rows][nq * 128]
+  int* status;
+  float scale_log2;       // log2(e) / sqrt(head_dim)
+};
+
+__device__ __forceinline__ int da_limit(const DecAttnArgs& a, int q_pos, int kv_len) {
+  if (a.bidirectional) return kv_len;
+  int lim;
+  if (q_pos < a.prompt_len) lim = a.prompt_len;
+  else lim = a.prompt_len + ((q_pos - a.prompt_len) / a.block_size + 1) * a.block_size;
+  return min(lim, kv_len);
+}
+
+// Merge of the S staged partials received by this CTA: rows [row0, row0 + R), recv layout
+// [src][R][kDaRowFloats]. Output rows are written as bf16 [position][head * 128 + d].
+template <int S>
+__device__ __forceinline__ void da_merge(const DecAttnArgs& a, const float* recv, int R, int row0, int rows_total,
+                                         int g, int tid) {
+  for (int it = tid; it < R * 32; it += kDaThreads) {
+    const int i = it >> 5;
+    const int d0 = (it & 31) * 4;
+    const int row = row0 + i;
+    if (row >= rows_total) continue;
+    float m[S], l[S];
+#pragma unroll
+    for (int p = 0; p < S; ++p) {
+      m[p] = recv[(p * R + i) * kDaRowFloats + 128];
+      l[p] = recv[(p * R + i) * kDaRowFloats + 129];
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < S; ++p)
+      if (l[p] > 0.0f) mx = fmaxf(mx, m[p]);
+    float L = 0.0f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < S; ++p) {
+      const float w = l[p] > 0.0f ? exp2f(m[p] - mx) : 0.0f;
+      const float4 t = *reinterpret_cast<const float4*>(recv + (p * R + i) * kDaRowFloats + d0);
+      L += l[p] * w;
+      o.x += t.x * w;
+      o.y += t.y * w;
+      o.z += t.z * w;
+      o.w += t.w * w;
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    const int pos = row / a.rep;
+    const int head = g * a.rep + (row - pos * a.rep);
+    __align__(8) __nv_bfloat16 t4[4];
+    t4[0] = __float2bfloat16_rn(o.x * inv);
+    t4[1] = __float2bfloat16_rn(o.y * inv);
+    t4[2] = __float2bfloat16_rn(o.z * inv);
+    t4[3] = __float2bfloat16_rn(o.w * inv);
+    *reinterpret_cast<uint2*>(a.out + (static_cast<size_t>(pos) * a.nq + head) * 128 + d0) = *reinterpret_cast<const uint2*>(t4);
+  }
+}
+
+__global__ void __launch_bounds__(kDaThreads, 1)
+    attn_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK64,
+                       const __grid_constant__ CUtensorMap tmV, const DecAttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sSub = smem + kDaQBytes;  // [kDaMaxSub][K | V^T]
+  float* red = reinterpret_cast<float*>(smem + kDaBodyBytes);  // [4][128]: m halves, l halves
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 4 * 128);
+  uint64_t* barQ = bars;
+  uint64_t* barKV = bars + 1;                 // [kDaMaxSub]
+  uint64_t* barS = bars + 1 + kDaMaxSub;
+  uint64_t* barO = barS + 1;
+  uint64_t* xbar = barS + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(barS + 3);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int S = a.splits;
+  const int split = blockIdx.x;
+  const int g = blockIdx.y;
+  const int plane = a.kv_plane0 + g;
+
+  if (tid == 0) {
+    mbar_init(barQ, 1);
+    for (int j = 0; j < kDaMaxSub; ++j) mbar_init(&barKV[j], 1);
+    mbar_init(barS, 1);
+    mbar_init(barO, 1);
+    mbar_init(xbar, 1);
+    flags[0] = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK64);
+    tma_prefetch_desc(&tmV);
+  }
+  // Device-side geometry: written by the plan kernel of this step, which completed before the
+  // kernel preceding this one started, so it is safe to read before the dependency wait.
+  const int kv_len = a.kv_len_dev != nullptr ? *a.kv_len_dev : a.kv_len;
+  const int q_pos0 = a.q_pos0_dev != nullptr ? *a.q_pos0_dev : a.q_pos0;
+  const int n_sub = (kv_len + 63) / 64;
+  const int sub0 = static_cast<int>((static_cast<long long>(split) * n_sub) / S);
+  const int sub1 = static_cast<int>((static_cast<long long>(split + 1) * n_sub) / S);
+  const int nt = min(kDaMaxSub, max(0, sub1 - sub0));
+  // Sub-tiles wholly before the first forwarded position hold final K/V.
+  const int n_final = max(0, min(nt, q_pos0 / 64 - sub0));
+  auto load_sub = [&](int j) {
+    uint8_t* st = sSub + static_cast<size_t>(j) * kDaSubBytes;
+    const int key0 = (sub0 + j) * 64;
+    mbar_expect_tx(&barKV[j], kDaSubBytes);
+    tma_load_3d(st, &tmK64, &barKV[j], 0, key0, plane);
+    tma_load_3d(st + 64 * 128, &tmK64, &barKV[j], 64, key0, plane);
+    tma_load_3d(st + kDaKBytes, &tmV, &barKV[j], key0, 0, plane);
+  };
+  if (tid == 0)
+    for (int j = 0; j < n_final; ++j) load_sub(j);
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  griddep_wait();
+  int rows_valid = a.rows;
+  if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
+  rows_valid = max(0, min(rows_valid, 128 / a.rep));
+  const int rows_total = rows_valid * a.rep;
+  if (tid == 0) {
+    if (nt > 0) {
+      const uint32_t qbytes = static_cast<uint32_t>(64 * 128 * 2);
+      mbar_expect_tx(barQ, 2 * qbytes);
+      tma_load_3d(sQ, &tmQ, barQ, 0, g * a.rep, 0);
+      tma_load_3d(sQ + 128 * 128, &tmQ, barQ, 64, g * a.rep, 0);
+      for (int j = n_final; j < nt; ++j) load_sub(j);
+    }
+  }
+  griddep_launch_dependents();
+
+  // ---- S_j = Q K_j^T (thread 0 issues; N = 64 keys per sub-tile)
+  if (tid == 0) {
+    bool ok = nt == 0 || mbar_wait(barQ, 0);
+    const uint32_t idesc = idesc_bf16_f32(128, 64);
+    for (int j = 0; j < nt && ok; ++j) {
+      if (!mbar_wait(&barKV[j], 0)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t k_addr = smem_u32(sSub + static_cast<size_t>(j) * kDaSubBytes);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t qo = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+        const uint32_t ko = (kk >> 2) * (64 * 128) + (kk & 3) * 32;
+        umma_bf16(tmem + j * 64, sdesc_kmajor_sw128(q_addr + qo), sdesc_kmajor_sw128(k_addr + ko), idesc, kk != 0 ? 1u : 0u);
+      }
+    }
+    if (!ok) { record_error(a.status, DEV_TIMEOUT_TMA); flags[0] = 1; }
+    umma_commit(barS);
+  }
+  const int r = tid & 127;
+  const int half = tid >> 7;
+  const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+  const int pos = r / a.rep;
+  const bool row_ok = r < rows_total;
+  const int lim = row_ok ? da_limit(a, q_pos0 + pos, kv_len) : 0;
+  if (nt > 0 && !mbar_wait(barS, 0)) { record_error(a.status, DEV_TIMEOUT_MMA); flags[0] = 1; }
+  tc_fence_after();
+
+  // ---- pass 1: row max over this CTA's keys (thread covers 32 keys of every sub-tile)
+  float mpart = -INFINITY;
+  for (int j = 0; j < nt; ++j) {
+    float sv[32];
+    tmem_ld32(tmem + lane_off + j * 64 + half * 32, sv);
+    const int k0 = (sub0 + j) * 64 + half * 32;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (k0 + i < lim) mpart = fmaxf(mpart, sv[i] * a.scale_log2);
+  }
+  red[half * 128 + r] = mpart;
+  __syncthreads();
+  const float m = fmaxf(red[r], red[128 + r]);
+  // ---- pass 2: P = exp2(s - m) as bf16 over the consumed K sub-tile; partial row sums
+  float lpart = 0.0f;
+  for (int j = 0; j < nt; ++j) {
+    float sv[32];
+    tmem_ld32(tmem + lane_off + j * 64 + half * 32, sv);
+    const int k0 = (sub0 + j) * 64 + half * 32;
+    uint8_t* sP = sSub + static_cast<size_t>(j) * kDaSubBytes;  // [128 rows][64 keys] SW128
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      __align__(16) __nv_bfloat16 t[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = c * 8 + e;
+        const float p = (k0 + i < lim) ? exp2f(sv[i] * a.scale_log2 - m) : 0.0f;
+        t[e] = __float2bfloat16_rn(p);
+        lpart += __bfloat162float(t[e]);
+      }
+      const int chunk = ((half * 32 + c * 8) >> 3) ^ (r & 7);
+      *reinterpret_cast<uint4*>(sP + r * 128 + chunk * 16) = *reinterpret_cast<const uint4*>(t);
+    }
+  }
+  red[256 + half * 128 + r] = lpart;
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  const float l = red[256 + r] + red[384 + r];
+
+  // ---- O = sum_j P_j V_j into TMEM columns [0, 128) (the S columns are consumed)
+  if (tid == 0) {
+    tc_fence_after();
+    const uint32_t idesc = idesc_bf16_f32(128, 128);
+    for (int j = 0; j < nt; ++j) {
+      const uint32_t p_addr = smem_u32(sSub + static_cast<size_t>(j) * kDaSubBytes);
+      const uint32_t v_addr = p_addr + kDaKBytes;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16(tmem, sdesc_kmajor_sw128(p_addr + kk * 32), sdesc_kmajor_sw128(v_addr + kk * 32), idesc, (j | kk) != 0 ? 1u : 0u);
+    }
+    umma_commit(barO);
+  }
+  if (nt > 0 && !mbar_wait(barO, 0)) { record_error(a.status, DEV_TIMEOUT_MMA); flags[0] = 1; }
+  tc_fence_after();
+  float o[64];
+  if (nt > 0) {
+    tmem_ld32(tmem + lane_off + half * 64, o);
+    tmem_ld32(tmem + lane_off + half * 64 + 32, o + 32);
+  } else {
+#pragma unroll
+    for (int d = 0; d < 64; ++d) o[d] = 0.0f;
+  }
+  const float m_out = nt > 0 ? m : -INFINITY;
+  const float l_out = nt > 0 ? l : 0.0f;
+
+  if (S == 1) {
+    if (row_ok && flags[0] == 0) {
+      const float inv = l_out > 0.0f ? 1.0f / l_out : 0.0f;
+      const int head = g * a.rep + (r - pos * a.rep);
+      __nv_bfloat16* dst = a.out + (static_cast<size_t>(pos) * a.nq + head) * 128 + half * 64;
+#pragma unroll
+      for (int d = 0; d < 64; d += 8) {
+        __align__(16) __nv_bfloat16 t[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) t[e] = __float2bfloat16_rn(o[d + e] * inv);
+        *reinterpret_cast<uint4*>(dst + d) = *reinterpret_cast<const uint4*>(t);
+      }
+    }
+  } else {
+    // Stage rows in order ([row][kDaRowFloats], over Q and the first sub-tiles) and receive into
+    // the next region; both overlay operands that every CTA of the cluster has finished with once
+    // it passes the barrier below.
+    const int R = (rows_total + S - 1) / S;
+    float* stage = reinterpret_cast<float*>(smem);
+    float* recv = stage + 128 * kDaRowFloats;
+    tc_fence_before();
+    __syncthreads();  // all TMEM reads of this CTA done; Q and sub-tiles are free
+    if (r < S * R) {
+      float* row = stage + r * kDaRowFloats + half * 64;
+#pragma unroll
+      for (int d = 0; d < 64; d += 4) *reinterpret_cast<float4*>(row + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+      if (half == 0) {
+        stage[r * kDaRowFloats + 128] = m_out;
+        stage[r * kDaRowFloats + 129] = l_out;
+      }
+    }
+    if (tid == 0) mbar_expect_tx(xbar, static_cast<uint32_t>(S * R * kDaRowFloats * 4));
+    fence_proxy_async_smem();
+    cluster_sync();
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t run_bytes = static_cast<uint32_t>(R * kDaRowFloats * 4);
+    if (tid < S && R > 0) {
+      const uint32_t dst = cluster_map(smem_u32(recv) + rank * run_bytes, static_cast<uint32_t>(tid));
+      const uint32_t bar = cluster_map(smem_u32(xbar), static_cast<uint32_t>(tid));
+      asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                   "r"(smem_u32(stage) + tid * run_bytes), "r"(run_bytes), "r"(bar)
+                   : "memory");
+    }
+    if (R > 0 && !mbar_wait(xbar, 0)) { record_error(a.status, DEV_TIMEOUT_EPI); flags[0] = 1; }
+    if (flags[0] == 0) {
+      const int row0 = static_cast<int>(rank) * R;
+      switch (S) {
+        case 2: da_merge<2>(a, recv, R, row0, rows_total, g, tid); break;
+        case 4: da_merge<4>(a, recv, R, row0, rows_total, g, tid); break;
+        case 8: da_merge<8>(a, recv, R, row0, rows_total, g, tid); break;
+        default: da_merge<16>(a, recv, R, row0, rows_total, g, tid); break;
+      }
+    }
+    cluster_sync();  // every CTA has received, so every copy out of this CTA's stage is complete
+  }
+  if (flags[0] != 0 && tid == 0) {
+    if (nt > 0) mbar_wait(barQ, 0);
+    for (int j = 0; j < nt; ++j) mbar_wait(&barKV[j], 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace drt

@@ -19,8 +19,10 @@
 
 #include "../../include/diffusorrt_b200.h"
 #include "attention.cuh"
+#include "attention_decode.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
+#include "gemm_decode.cuh"
 #include "policy.cuh"
 #include "rowops.cuh"
 #include "selector.cuh"
@@ -137,6 +139,31 @@ cudaError_t launch_kc(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// Launch with programmatic dependent launch and a cluster of `cluster_x` CTAs along x.
+template <typename Kern, typename... Args>
+cudaError_t launch_cx(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, int cluster_x, Args... args) {
+  ++g_launches;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <typename Kern, typename... Args>
 cudaError_t launch_k(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, Args... args) {
   return launch_kc(kernel, grid, block, smem, stream, pdl, 1, args...);
@@ -163,7 +190,11 @@ int configure_kernels() {
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDaSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       result = DRT_INTERNAL_ERROR;
   });
   if (result != DRT_OK) return set_error(DRT_INTERNAL_ERROR, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(cudaGetLastError()));
@@ -322,6 +353,7 @@ extern "C" int drt_model_create(const drt_model_config* cfg, int32_t device, drt
   REQUIRE(cfg->head_dim == 128, "head_dim must be 128 (got %d)", cfg->head_dim);
   REQUIRE(cfg->layer_count > 0 && cfg->hidden_size > 0 && cfg->vocab_size > 0, "bad model geometry");
   REQUIRE(cfg->hidden_size % 128 == 0, "hidden_size must be a multiple of 128");
+  REQUIRE(cfg->hidden_size <= 4 * kNormVec * 256, "hidden_size above %d", 4 * kNormVec * 256);
   REQUIRE(cfg->intermediate_size % 64 == 0, "intermediate_size must be a multiple of 64");
   REQUIRE(cfg->vocab_size % 128 == 0, "vocab_size must be a multiple of 128");
   REQUIRE(cfg->num_kv_heads > 0 && cfg->attention_heads % cfg->num_kv_heads == 0, "attention_heads must divide by num_kv_heads");
@@ -551,6 +583,7 @@ struct drt_session {
   float* h = nullptr;
   __nv_bfloat16 *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *xf = nullptr;
   float* logits = nullptr;
+  float* ss = nullptr;                // [kMaxFwdRows][H / 128] partial sums of squares of h (decode)
   __nv_bfloat16 *kcache = nullptr, *vtcache = nullptr;
   int max_cluster = 16;               // largest cluster the GPU schedules for the split kernels
   float* sel_pmax = nullptr;
@@ -576,6 +609,8 @@ struct drt_session {
   int sel_chunks = 1;
   // tensor maps over the activation buffers
   CUtensorMap m_xn64, m_xn128, m_attn64, m_attn128, m_act64, m_act128, m_xf64, m_q, m_k, m_v;
+  CUtensorMap m_k64;                  // K cache with 64-key boxes (decode attention)
+  int da_splits = 0;                  // decode attention CTAs per KV head (0: use attn_prefix_kernel)
   // graphs
   int g_step_kernels = 0;             // kernels in one replay of g_step
   cudaGraphExec_t g_step = nullptr;   // plan + forward + score + commit
@@ -651,6 +686,45 @@ int run_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmA
   return DRT_OK;
 }
 
+// Split-K factor for the decode linears: the fewest K blocks per CTA with at most one CTA per SM,
+// and the smallest factor among those that tie.
+void dec_split(int tiles, int kb, int sms, int max_split, int* splits, int* kbps) {
+  int best = 1, best_kb = kb;
+  for (int sp = 2; sp <= std::min(max_split, kb); ++sp) {
+    if (tiles * sp > sms) break;
+    if (!dec_split_supported(sp)) continue;
+    const int k = (kb + sp - 1) / sp;
+    if (k < best_kb) {
+      best = sp;
+      best_kb = k;
+    }
+  }
+  *splits = best;
+  *kbps = best_kb;
+}
+
+// Decode linear over at most kDecRows activation rows (mB: the bf16 activation map, box 64 rows).
+int run_dec_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a) {
+  const int tiles_m = a.n_out / 128;
+  const int kb = a.K / 64;
+  dec_split(tiles_m, kb, s->sms, s->max_cluster, &a.splits, &a.kb_per_split);
+  if (a.kb_per_split > kDecMaxKb) return set_error(DRT_UNSUPPORTED, "decode linear with %d K blocks per CTA", a.kb_per_split);
+  // Ring depth: the deepest ring (up to the whole K slice) that still lets two CTAs share an SM,
+  // so the next kernel's CTAs can stream their weights beside this one; when that leaves fewer
+  // than four stages for a longer slice, the whole slice in one CTA per SM instead.
+  constexpr size_t kHalfSm = 115712;  // (228 KB - 2 x 1 KB reserved) / 2
+  constexpr size_t kFullSm = 218 * 1024;
+  int s_co = 0, s_full = 1;
+  for (int st = 1; st <= a.kb_per_split; ++st) {
+    if (dec_smem_bytes(st, a.kb_per_split) <= kHalfSm) s_co = st;
+    if (dec_smem_bytes(st, a.kb_per_split) <= kFullSm) s_full = st;
+  }
+  a.stages = (s_co >= std::min(a.kb_per_split, 4)) ? s_co : s_full;
+  CK(launch_kc(gemm_decode_kernel, dim3(tiles_m, 1, a.splits), dim3(128), dec_smem_bytes(a.stages, a.kb_per_split), s->stream,
+               true, a.splits, mA, mB, a));
+  return DRT_OK;
+}
+
 int run_rmsnorm(drt_session* s, const float* h, const int* row_index, int rows, const int* rows_dev, const float* w,
                 __nv_bfloat16* out) {
   drt_model* m = s->m;
@@ -665,7 +739,8 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
   drt_model* m = s->m;
   const int H = m->H, qd = m->nq * 128;
   CK(launch_k(embed_rows_kernel, dim3(f.rows), dim3(128), 0, s->stream, true, static_cast<const int*>(s->canvas), f.pos0,
-              f.pos0_dev, f.rows, f.rows_dev, static_cast<const __nv_bfloat16*>(m->embed), H, s->h, m->V, s->status));
+              f.pos0_dev, f.rows, f.rows_dev, static_cast<const __nv_bfloat16*>(m->embed), H, s->h, m->V, s->status,
+              static_cast<float*>(nullptr)));
   for (int l = 0; l < m->L; ++l) {
     LayerW& w = m->layers[l];
     TRY(run_rmsnorm(s, s->h, nullptr, f.rows, f.rows_dev, w.in_norm, s->xn));
@@ -684,8 +759,11 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     a.vtcache = s->vtcache + static_cast<size_t>(l) * m->nkv * 128 * s->max_seq;
     a.max_seq = s->max_seq;
     a.eps = m->cfg.rms_norm_eps;
-    if (f.decode) TRY(run_gemm<64>(s, w.m_qkv, s->m_xn64, a, true));
-    else TRY(run_gemm<128>(s, w.m_qkv, s->m_xn128, a, false));
+    if (f.decode) {
+      TRY(run_dec_gemm(s, w.m_qkv, s->m_xn64, a));
+    } else {
+      TRY(run_gemm<128>(s, w.m_qkv, s->m_xn128, a, false));
+    }
     // Attention.
     AttnArgs t;
     memset(&t, 0, sizeof(t));
@@ -707,6 +785,29 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     t.status = s->status;
     t.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(128.0));
     const int qtiles = (f.rows + m->tile_pos - 1) / m->tile_pos;
+    if (f.decode && s->da_splits > 0) {
+      DecAttnArgs da;
+      memset(&da, 0, sizeof(da));
+      da.nq = m->nq;
+      da.nkv = m->nkv;
+      da.rep = m->rep;
+      da.rows = std::min(f.rows, 128 / m->rep);
+      da.rows_dev = f.rows_dev;
+      da.q_pos0 = f.pos0;
+      da.q_pos0_dev = f.pos0_dev;
+      da.kv_len = f.kv_len;
+      da.kv_len_dev = f.kv_len_dev;
+      da.prompt_len = f.prompt_len;
+      da.block_size = f.block_size;
+      da.bidirectional = f.bidirectional;
+      da.kv_plane0 = l * m->nkv;
+      da.splits = s->da_splits;
+      da.out = s->attn;
+      da.status = s->status;
+      da.scale_log2 = t.scale_log2;
+      CK(launch_cx(attn_decode_kernel, dim3(s->da_splits, m->nkv), dim3(kDaThreads), kDaSmemBytes, s->stream, s->da_splits,
+                   s->m_q, s->m_k64, s->m_v, da));
+    } else {
     if (f.decode && qtiles == 1) {
       t.splits = s->attn_splits;
       t.tiles_per_split = s->attn_tps;
@@ -716,12 +817,13 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     }
     CK(launch_kc(attn_prefix_kernel, dim3(qtiles, m->nkv, t.splits), dim3(128), kAttnSmemBytes, s->stream, true, t.splits,
                  s->m_q, s->m_k, s->m_v, t));
+    }
     // o_proj + residual.
     GemmArgs o = base_args(s, H, qd, f);
     o.epi = EPI_RESID;
     o.out_f32 = s->h;
     o.ld_out = H;
-    if (f.decode) TRY(run_gemm<64>(s, w.m_o, s->m_attn64, o, true));
+    if (f.decode) TRY(run_dec_gemm(s, w.m_o, s->m_attn64, o));
     else TRY(run_gemm<128>(s, w.m_o, s->m_attn128, o, false));
     TRY(run_rmsnorm(s, s->h, nullptr, f.rows, f.rows_dev, w.post_norm, s->xn));
     // gate/up + SwiGLU.
@@ -729,14 +831,14 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     g.epi = EPI_SWIGLU;
     g.out_bf16 = s->act;
     g.ld_out = m->I;
-    if (f.decode) TRY(run_gemm<64>(s, w.m_gu, s->m_xn64, g, true));
+    if (f.decode) TRY(run_dec_gemm(s, w.m_gu, s->m_xn64, g));
     else TRY(run_gemm<128>(s, w.m_gu, s->m_xn128, g, false));
     // down + residual.
     GemmArgs d = base_args(s, H, m->I, f);
     d.epi = EPI_RESID;
     d.out_f32 = s->h;
     d.ld_out = H;
-    if (f.decode) TRY(run_gemm<64>(s, w.m_down, s->m_act64, d, true));
+    if (f.decode) TRY(run_dec_gemm(s, w.m_down, s->m_act64, d));
     else TRY(run_gemm<128>(s, w.m_down, s->m_act128, d, false));
   }
   return DRT_OK;
@@ -753,7 +855,7 @@ int enqueue_head(drt_session* s, const int* row_index, int rows, const int* rows
   a.epi = EPI_STORE_F32;
   a.out_f32 = s->logits;
   a.ld_out = m->V;
-  TRY(run_gemm<64>(s, m->m_lm, s->m_xf64, a, false));
+  TRY(run_dec_gemm(s, m->m_lm, s->m_xf64, a));
   if (with_selector) {
     SelArgs sa;
     memset(&sa, 0, sizeof(sa));
@@ -869,6 +971,7 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = salloc(s, &s->act, static_cast<size_t>(R) * m->I)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->xf, static_cast<size_t>(kMaxFrontier) * H)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->logits, static_cast<size_t>(kMaxFrontier) * m->V)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->ss, static_cast<size_t>(kMaxFwdRows) * (H / 128))) != DRT_OK) return fail(rc);
   const size_t kv = static_cast<size_t>(s->planes) * s->max_seq * 128;
   if ((rc = salloc(s, &s->kcache, kv)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->vtcache, kv)) != DRT_OK) return fail(rc);
@@ -901,6 +1004,14 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if (asp == 2) asp = kv_tiles >= 4 ? 4 : 1;
   s->attn_splits = asp;
   s->attn_tps = (kv_tiles + asp - 1) / asp;
+  // Decode attention: the largest power-of-two cluster (<= max_cluster, <= 64-key sub-tiles, one
+  // CTA per SM over all KV heads) whose runs fit kDaMaxSub sub-tiles; otherwise the general kernel.
+  {
+    const int n_sub = s->max_seq / 64;
+    int sp = 1;
+    while (sp * 2 <= s->max_cluster && sp * 2 <= n_sub && m->nkv * sp * 2 <= s->sms) sp *= 2;
+    s->da_splits = (m->rep * (kMaxFwdRows / 2) <= 128 && (n_sub + sp - 1) / sp <= kDaMaxSub) ? sp : 0;
+  }
   // Selector scratch.
   s->sel_chunks = (m->V + kSelChunk - 1) / kSelChunk;
   const size_t np = static_cast<size_t>(kMaxFrontier) * s->sel_chunks;
@@ -938,6 +1049,8 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
     const uint64_t sk[2] = {256, static_cast<uint64_t>(s->max_seq) * 256};
     const uint32_t bk[3] = {64, 128, 1};
     if ((rc = make_map(&s->m_k, s->kcache, 3, dk, sk, bk)) != DRT_OK) return fail(rc);
+    const uint32_t bk64[3] = {64, 64, 1};
+    if ((rc = make_map(&s->m_k64, s->kcache, 3, dk, sk, bk64)) != DRT_OK) return fail(rc);
     const uint64_t dv[3] = {static_cast<uint64_t>(s->max_seq), 128, static_cast<uint64_t>(s->planes)};
     const uint64_t sv[2] = {static_cast<uint64_t>(s->max_seq) * 2, static_cast<uint64_t>(s->max_seq) * 256};
     const uint32_t bv[3] = {64, 128, 1};

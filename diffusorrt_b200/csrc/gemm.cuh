@@ -59,6 +59,10 @@ struct GemmArgs {
   __nv_bfloat16* vtcache;// this layer: [nkv][128][max_seq]
   int max_seq;
   float eps;
+  // EPI_RESID: optional per-row partial sums of squares of the updated rows, for the RMSNorm that
+  // the next linear fuses into its activation load: ss_out[row * ss_ld + m0 / 128].
+  float* ss_out;
+  int ss_ld;
 };
 
 template <int BN>
@@ -107,9 +111,25 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
 #pragma unroll
       for (int i = 0; i < 32; ++i) cur[i] = i < ncols ? a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] : 0.0f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < ncols)
-          a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = __fadd_rn(cur[i], __fadd_rn(bf16_round(v[i]), b));
+      for (int i = 0; i < 32; ++i) {
+        cur[i] = __fadd_rn(cur[i], __fadd_rn(bf16_round(v[i]), b));
+        if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = cur[i];
+      }
+      if (a.ss_out != nullptr) {
+        // Sum of squares over this tile's 128 features for each row: warp tree, then the four
+        // warps in order (fixed order, so the result does not depend on scheduling).
+        const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float t = warp_sum(__fmul_rn(cur[i], cur[i]));
+          if (lane == 0) xs[warp * 32 + i] = t;
+        }
+        __syncthreads();
+        if (tid < ncols)
+          a.ss_out[static_cast<size_t>(col0 + tid) * a.ss_ld + (m0 >> 7)] =
+              __fadd_rn(__fadd_rn(__fadd_rn(xs[tid], xs[32 + tid]), xs[64 + tid]), xs[96 + tid]);
+        __syncthreads();
+      }
       break;
     }
     case EPI_SWIGLU: {

@@ -6,9 +6,12 @@
 namespace drt {
 
 // h[r, :] = f32(E[tokens[pos0 + r], :])   (python/src/edllm/backends/mlx_forward.py:1538-1557)
+// With ss != null (blockDim.x == 128, H % 128 == 0) it also writes the per-row partial sums of
+// squares over each group of 128 features, ss[r * (H / 128) + g], reduced in the same fixed order
+// as the residual epilogue of the decode linears (warp tree, then the four warps in order).
 __global__ void embed_rows_kernel(const int* __restrict__ tokens, int pos0, const int* pos0_dev, int rows,
                                   const int* rows_dev, const __nv_bfloat16* __restrict__ table, int H,
-                                  float* __restrict__ h, int vocab, int* status) {
+                                  float* __restrict__ h, int vocab, int* status, float* ss) {
   griddep_wait();
   griddep_launch_dependents();
   int rows_valid = rows;
@@ -23,9 +26,25 @@ __global__ void embed_rows_kernel(const int* __restrict__ tokens, int pos0, cons
   }
   const __nv_bfloat16* src = table + static_cast<size_t>(tok) * H;
   float* dst = h + static_cast<size_t>(r) * H;
-  for (int k = threadIdx.x * 2; k < H; k += blockDim.x * 2) {
-    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(src + k);
-    *reinterpret_cast<float2*>(dst + k) = make_float2(__low2float(v), __high2float(v));
+  if (ss == nullptr) {
+    for (int k = threadIdx.x * 2; k < H; k += blockDim.x * 2) {
+      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(src + k);
+      *reinterpret_cast<float2*>(dst + k) = make_float2(__low2float(v), __high2float(v));
+    }
+    return;
+  }
+  __shared__ float part[4];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  for (int g = 0; g < H / 128; ++g) {
+    const float x = __bfloat162float(src[g * 128 + t]);
+    dst[g * 128 + t] = x;
+    float q = __fmul_rn(x, x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if (lane == 0) part[warp] = q;
+    __syncthreads();
+    if (t == 0) ss[static_cast<size_t>(r) * (H / 128) + g] = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
+    __syncthreads();
   }
 }
 
@@ -33,6 +52,9 @@ __global__ void embed_rows_kernel(const int* __restrict__ tokens, int pos0, cons
 // The reference rms_norm (mlx_ops.py:21-35) keeps the f32 residual dtype and multiplies the
 // weight in f32; the bf16 cast is the one the following linear applies (mlx_ops.py:122-125).
 // src_row(r) = row_index[r] when row_index is given (the frontier gather before lm_head).
+// Every thread issues all of its loads (up to kNormVec float4 of x and of w) before the first use,
+// so a row costs one memory round trip. Requires H % 4 == 0 and H <= 4 * kNormVec * blockDim.x.
+constexpr int kNormVec = 4;
 __global__ void rmsnorm_bf16_kernel(const float* __restrict__ h, int ld_h, const int* row_index, int rows,
                                     const int* rows_dev, const float* __restrict__ w, float eps, int H,
                                     __nv_bfloat16* __restrict__ out, int ld_out) {
@@ -43,10 +65,29 @@ __global__ void rmsnorm_bf16_kernel(const float* __restrict__ h, int ld_h, const
   const int r = blockIdx.x;
   if (r >= rows_valid) return;
   const int src = row_index != nullptr ? row_index[r] : r;
-  const float* x = h + static_cast<size_t>(src) * ld_h;
-  __shared__ float red[32];
+  const float4* x4 = reinterpret_cast<const float4*>(h + static_cast<size_t>(src) * ld_h);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const int nv = H >> 2;
+  float4 xv[kNormVec], wv[kNormVec];
+#pragma unroll
+  for (int i = 0; i < kNormVec; ++i) {
+    const int k = threadIdx.x + i * blockDim.x;
+    if (k < nv) {
+      xv[i] = __ldcg(x4 + k);
+      wv[i] = __ldg(w4 + k);
+    } else {
+      xv[i] = wv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   float ss = 0.0f;
-  for (int k = threadIdx.x; k < H; k += blockDim.x) ss = __fmaf_rn(x[k], x[k], ss);
+#pragma unroll
+  for (int i = 0; i < kNormVec; ++i) {
+    ss = __fmaf_rn(xv[i].x, xv[i].x, ss);
+    ss = __fmaf_rn(xv[i].y, xv[i].y, ss);
+    ss = __fmaf_rn(xv[i].z, xv[i].z, ss);
+    ss = __fmaf_rn(xv[i].w, xv[i].w, ss);
+  }
+  __shared__ float red[32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -61,8 +102,17 @@ __global__ void rmsnorm_bf16_kernel(const float* __restrict__ h, int ld_h, const
   const float var = __fdiv_rn(red[0], static_cast<float>(H));
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
   __nv_bfloat16* y = out + static_cast<size_t>(r) * ld_out;
-  for (int k = threadIdx.x; k < H; k += blockDim.x) {
-    y[k] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(x[k], scale), w[k]));
+#pragma unroll
+  for (int i = 0; i < kNormVec; ++i) {
+    const int k = threadIdx.x + i * blockDim.x;
+    if (k < nv) {
+      __align__(8) __nv_bfloat16 t[4];
+      t[0] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(xv[i].x, scale), wv[i].x));
+      t[1] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(xv[i].y, scale), wv[i].y));
+      t[2] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(xv[i].z, scale), wv[i].z));
+      t[3] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(xv[i].w, scale), wv[i].w));
+      *reinterpret_cast<uint2*>(y + 4 * k) = *reinterpret_cast<const uint2*>(t);
+    }
   }
 }
 

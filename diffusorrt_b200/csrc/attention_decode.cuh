@@ -5,32 +5,32 @@
 // query heads of one KV head packed with the positions into the M = 128 rows of the UMMA
 // (row r = position r / rep, head g * rep + r % rep).
 //
-// Work split, per KV head g: a cluster of S CTAs (S = 1, 2, 4, 8 or 16) shares the visible keys
-// in balanced runs of 64-key sub-tiles, at most kDaMaxSub sub-tiles per CTA. A CTA
+// Work split, per KV head g: `splits` CTAs share the visible keys in balanced runs of 64-key
+// sub-tiles, at most kDaMaxSub per CTA, so a CTA needs under half of an SM's shared memory and a
+// quarter of its TMEM: CTAs of this kernel pair up on an SM and can sit beside the QKV linear
+// that precedes them. A CTA
 //   1. streams its K and V^T sub-tiles into shared memory with TMA. Sub-tiles that lie wholly
 //      before the first forwarded position hold final K/V from earlier steps and are requested
-//      before the programmatic-dependent-launch wait, so they stream while the QKV linear that
-//      precedes this kernel is still running; the rest (and Q) are requested after it;
+//      before the programmatic-dependent-launch wait, so they stream while the QKV linear is
+//      still running; the rest (and Q) are requested after it;
 //   2. computes S_j = Q K_j^T for every sub-tile into TMEM (one 64-column block each);
-//   3. runs a two-pass softmax over all of its keys with two threads per row (pass 1: row max,
+//   3. runs a two-pass softmax over its keys with two threads per live row (pass 1: row max,
 //      pass 2: exp2, the bf16 P written over the consumed K sub-tile), in the log2 domain;
 //   4. accumulates O = sum_j P_j V_j on the tensor cores into TMEM;
-//   5. merges the S partial (O, m, l) rows: CTA p owns a run of R = ceil(rows / S) rows; every
-//      CTA stages its rows in order and sends run p to CTA p with one bulk shared-to-shared copy
-//      completing on CTA p's receive barrier; the owner rescales by exp2(m_i - max m) and sums in
-//      rank order, then normalises and writes bf16.
+//   5. with one split, normalises and writes bf16; otherwise writes its unnormalised f32 rows
+//      and (m, l) to a partial buffer that attn_merge_kernel combines (rescale by
+//      exp2(m_i - max m), sum in split order, normalise).
 // All waits are bounded (common.cuh); on a timeout the CTA records the error and unwinds.
 #pragma once
 #include "attention.cuh"
 
 namespace drt {
 
-constexpr int kDaMaxSub = 5;                    // 64-key sub-tiles per CTA
+constexpr int kDaMaxSub = 2;                    // 64-key sub-tiles per CTA
 constexpr int kDaQBytes = 2 * 128 * 128;        // Q: two 64-d atoms x 128 rows
 constexpr int kDaKBytes = 2 * 64 * 128;         // K sub-tile: two 64-d atoms x 64 keys
 constexpr int kDaVBytes = 128 * 128;            // V^T sub-tile: 128 d rows x 64 keys
 constexpr int kDaSubBytes = kDaKBytes + kDaVBytes;
-constexpr int kDaRowFloats = 132;               // merge row: 128 d + m + l + 2 pad (528 B)
 constexpr int kDaThreads = 256;
 // Q | sub-tiles | row-statistics exchange | barriers
 constexpr size_t kDaBodyBytes = kDaQBytes + static_cast<size_t>(kDaMaxSub) * kDaSubBytes;
@@ -46,8 +46,10 @@ struct DecAttnArgs {
   const int* kv_len_dev;
   int prompt_len, block_size, bidirectional;
   int kv_plane0;          // first cache plane of this layer
-  int splits;             // CTAs per KV head (= cluster size along x)
+  int splits;             // CTAs per KV head
   __nv_bfloat16* out;     // [rows][nq * 128]
+  float* part_o;          // splits > 1: [nkv][splits][128 rows][128] unnormalised f32 rows
+  float* part_ml;         // splits > 1: [nkv][splits][128 rows][2] (row max in log2 units, row sum)
   int* status;
   float scale_log2;       // log2(e) / sqrt(head_dim)
 };
@@ -60,51 +62,7 @@ __device__ __forceinline__ int da_limit(const DecAttnArgs& a, int q_pos, int kv_
   return min(lim, kv_len);
 }
 
-// Merge of the S staged partials received by this CTA: rows [row0, row0 + R), recv layout
-// [src][R][kDaRowFloats]. Output rows are written as bf16 [position][head * 128 + d].
-template <int S>
-__device__ __forceinline__ void da_merge(const DecAttnArgs& a, const float* recv, int R, int row0, int rows_total,
-                                         int g, int tid) {
-  for (int it = tid; it < R * 32; it += kDaThreads) {
-    const int i = it >> 5;
-    const int d0 = (it & 31) * 4;
-    const int row = row0 + i;
-    if (row >= rows_total) continue;
-    float m[S], l[S];
-#pragma unroll
-    for (int p = 0; p < S; ++p) {
-      m[p] = recv[(p * R + i) * kDaRowFloats + 128];
-      l[p] = recv[(p * R + i) * kDaRowFloats + 129];
-    }
-    float mx = -INFINITY;
-#pragma unroll
-    for (int p = 0; p < S; ++p)
-      if (l[p] > 0.0f) mx = fmaxf(mx, m[p]);
-    float L = 0.0f;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int p = 0; p < S; ++p) {
-      const float w = l[p] > 0.0f ? exp2f(m[p] - mx) : 0.0f;
-      const float4 t = *reinterpret_cast<const float4*>(recv + (p * R + i) * kDaRowFloats + d0);
-      L += l[p] * w;
-      o.x += t.x * w;
-      o.y += t.y * w;
-      o.z += t.z * w;
-      o.w += t.w * w;
-    }
-    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-    const int pos = row / a.rep;
-    const int head = g * a.rep + (row - pos * a.rep);
-    __align__(8) __nv_bfloat16 t4[4];
-    t4[0] = __float2bfloat16_rn(o.x * inv);
-    t4[1] = __float2bfloat16_rn(o.y * inv);
-    t4[2] = __float2bfloat16_rn(o.z * inv);
-    t4[3] = __float2bfloat16_rn(o.w * inv);
-    *reinterpret_cast<uint2*>(a.out + (static_cast<size_t>(pos) * a.nq + head) * 128 + d0) = *reinterpret_cast<const uint2*>(t4);
-  }
-}
-
-__global__ void __launch_bounds__(kDaThreads, 1)
+__global__ void __launch_bounds__(kDaThreads, 2)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK64,
                        const __grid_constant__ CUtensorMap tmV, const DecAttnArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -117,8 +75,7 @@ __global__ void __launch_bounds__(kDaThreads, 1)
   uint64_t* barKV = bars + 1;                 // [kDaMaxSub]
   uint64_t* barS = bars + 1 + kDaMaxSub;
   uint64_t* barO = barS + 1;
-  uint64_t* xbar = barS + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(barS + 3);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(barS + 2);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x;
@@ -133,7 +90,6 @@ __global__ void __launch_bounds__(kDaThreads, 1)
     for (int j = 0; j < kDaMaxSub; ++j) mbar_init(&barKV[j], 1);
     mbar_init(barS, 1);
     mbar_init(barO, 1);
-    mbar_init(xbar, 1);
     flags[0] = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -161,7 +117,7 @@ __global__ void __launch_bounds__(kDaThreads, 1)
   if (tid == 0)
     for (int j = 0; j < n_final; ++j) load_sub(j);
   if (warp == 0) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, 128);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -279,8 +235,8 @@ __global__ void __launch_bounds__(kDaThreads, 1)
   const float m_out = nt > 0 ? m : -INFINITY;
   const float l_out = nt > 0 ? l : 0.0f;
 
-  if (S == 1) {
-    if (row_ok && flags[0] == 0) {
+  if (row_ok && flags[0] == 0) {
+    if (S == 1) {
       const float inv = l_out > 0.0f ? 1.0f / l_out : 0.0f;
       const int head = g * a.rep + (r - pos * a.rep);
       __nv_bfloat16* dst = a.out + (static_cast<size_t>(pos) * a.nq + head) * 128 + half * 64;
@@ -291,48 +247,13 @@ __global__ void __launch_bounds__(kDaThreads, 1)
         for (int e = 0; e < 8; ++e) t[e] = __float2bfloat16_rn(o[d + e] * inv);
         *reinterpret_cast<uint4*>(dst + d) = *reinterpret_cast<const uint4*>(t);
       }
-    }
-  } else {
-    // Stage rows in order ([row][kDaRowFloats], over Q and the first sub-tiles) and receive into
-    // the next region; both overlay operands that every CTA of the cluster has finished with once
-    // it passes the barrier below.
-    const int R = (rows_total + S - 1) / S;
-    float* stage = reinterpret_cast<float*>(smem);
-    float* recv = stage + 128 * kDaRowFloats;
-    tc_fence_before();
-    __syncthreads();  // all TMEM reads of this CTA done; Q and sub-tiles are free
-    if (r < S * R) {
-      float* row = stage + r * kDaRowFloats + half * 64;
+    } else {
+      const size_t prow = (static_cast<size_t>(g) * S + split) * 128 + r;
+      float* dst = a.part_o + prow * 128 + half * 64;
 #pragma unroll
-      for (int d = 0; d < 64; d += 4) *reinterpret_cast<float4*>(row + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
-      if (half == 0) {
-        stage[r * kDaRowFloats + 128] = m_out;
-        stage[r * kDaRowFloats + 129] = l_out;
-      }
+      for (int d = 0; d < 64; d += 4) *reinterpret_cast<float4*>(dst + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+      if (half == 0) *reinterpret_cast<float2*>(a.part_ml + prow * 2) = make_float2(m_out, l_out);
     }
-    if (tid == 0) mbar_expect_tx(xbar, static_cast<uint32_t>(S * R * kDaRowFloats * 4));
-    fence_proxy_async_smem();
-    cluster_sync();
-    const uint32_t rank = cluster_ctarank();
-    const uint32_t run_bytes = static_cast<uint32_t>(R * kDaRowFloats * 4);
-    if (tid < S && R > 0) {
-      const uint32_t dst = cluster_map(smem_u32(recv) + rank * run_bytes, static_cast<uint32_t>(tid));
-      const uint32_t bar = cluster_map(smem_u32(xbar), static_cast<uint32_t>(tid));
-      asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                   "r"(smem_u32(stage) + tid * run_bytes), "r"(run_bytes), "r"(bar)
-                   : "memory");
-    }
-    if (R > 0 && !mbar_wait(xbar, 0)) { record_error(a.status, DEV_TIMEOUT_EPI); flags[0] = 1; }
-    if (flags[0] == 0) {
-      const int row0 = static_cast<int>(rank) * R;
-      switch (S) {
-        case 2: da_merge<2>(a, recv, R, row0, rows_total, g, tid); break;
-        case 4: da_merge<4>(a, recv, R, row0, rows_total, g, tid); break;
-        case 8: da_merge<8>(a, recv, R, row0, rows_total, g, tid); break;
-        default: da_merge<16>(a, recv, R, row0, rows_total, g, tid); break;
-      }
-    }
-    cluster_sync();  // every CTA has received, so every copy out of this CTA's stage is complete
   }
   if (flags[0] != 0 && tid == 0) {
     if (nt > 0) mbar_wait(barQ, 0);
@@ -340,7 +261,50 @@ __global__ void __launch_bounds__(kDaThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 512);
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
+// Combine the split partials of attn_decode_kernel: one CTA per (live row, KV head), thread d
+// owns output column d. Thread s < splits fetches split s's (m, l) into shared memory while every
+// thread fetches its column of all splits, so the merge costs one round trip.
+constexpr int kDaMaxSplits = 64;
+__global__ void __launch_bounds__(128)
+    attn_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits, int rep, int nq,
+                      int rows, const int* rows_dev, __nv_bfloat16* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
+  int rows_valid = rows;
+  if (rows_dev != nullptr) rows_valid = min(rows_valid, *rows_dev);
+  const int r = blockIdx.x;
+  const int g = blockIdx.y;
+  if (r >= rows_valid * rep) return;
+  const int d = threadIdx.x;
+  __shared__ float sm[kDaMaxSplits], sl[kDaMaxSplits];
+  const size_t base = static_cast<size_t>(g) * splits * 128 + r;  // row index of split 0
+  if (d < splits) {
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(part_ml + (base + static_cast<size_t>(d) * 128) * 2));
+    sm[d] = ml.x;
+    sl[d] = ml.y;
+  }
+  float o[kDaMaxSplits];
+#pragma unroll
+  for (int s = 0; s < kDaMaxSplits; ++s) o[s] = s < splits ? __ldcg(part_o + (base + static_cast<size_t>(s) * 128) * 128 + d) : 0.0f;
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s)
+    if (sl[s] > 0.0f) mx = fmaxf(mx, sm[s]);
+  float L = 0.0f, acc = 0.0f;
+#pragma unroll
+  for (int s = 0; s < kDaMaxSplits; ++s) {
+    if (s < splits) {
+      const float w = sl[s] > 0.0f ? exp2f(sm[s] - mx) : 0.0f;
+      L += sl[s] * w;
+      acc += o[s] * w;
+    }
+  }
+  const int pos = r / rep;
+  const int head = g * rep + (r - pos * rep);
+  out[(static_cast<size_t>(pos) * nq + head) * 128 + d] = __float2bfloat16_rn(L > 0.0f ? acc / L : 0.0f);
 }
 
 }  // namespace drt

@@ -193,7 +193,6 @@ int configure_kernels() {
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDaSmemBytes)) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       result = DRT_INTERNAL_ERROR;
   });
@@ -611,6 +610,8 @@ struct drt_session {
   CUtensorMap m_xn64, m_xn128, m_attn64, m_attn128, m_act64, m_act128, m_xf64, m_q, m_k, m_v;
   CUtensorMap m_k64;                  // K cache with 64-key boxes (decode attention)
   int da_splits = 0;                  // decode attention CTAs per KV head (0: use attn_prefix_kernel)
+  float* da_part_o = nullptr;         // decode attention split partials
+  float* da_part_ml = nullptr;
   // graphs
   int g_step_kernels = 0;             // kernels in one replay of g_step
   cudaGraphExec_t g_step = nullptr;   // plan + forward + score + commit
@@ -803,10 +804,16 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
       da.kv_plane0 = l * m->nkv;
       da.splits = s->da_splits;
       da.out = s->attn;
+      da.part_o = s->da_part_o;
+      da.part_ml = s->da_part_ml;
       da.status = s->status;
       da.scale_log2 = t.scale_log2;
-      CK(launch_cx(attn_decode_kernel, dim3(s->da_splits, m->nkv), dim3(kDaThreads), kDaSmemBytes, s->stream, s->da_splits,
-                   s->m_q, s->m_k64, s->m_v, da));
+      CK(launch_cx(attn_decode_kernel, dim3(s->da_splits, m->nkv), dim3(kDaThreads), kDaSmemBytes, s->stream, 1, s->m_q,
+                   s->m_k64, s->m_v, da));
+      if (s->da_splits > 1)
+        CK(launch_k(attn_merge_kernel, dim3(128, m->nkv), dim3(128), 0, s->stream, true,
+                    static_cast<const float*>(s->da_part_o), static_cast<const float*>(s->da_part_ml), s->da_splits, m->rep,
+                    m->nq, da.rows, da.rows_dev, s->attn));
     } else {
     if (f.decode && qtiles == 1) {
       t.splits = s->attn_splits;
@@ -1004,13 +1011,17 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if (asp == 2) asp = kv_tiles >= 4 ? 4 : 1;
   s->attn_splits = asp;
   s->attn_tps = (kv_tiles + asp - 1) / asp;
-  // Decode attention: the largest power-of-two cluster (<= max_cluster, <= 64-key sub-tiles, one
-  // CTA per SM over all KV heads) whose runs fit kDaMaxSub sub-tiles; otherwise the general kernel.
+  // Decode attention: enough CTAs per KV head that each covers at most kDaMaxSub 64-key sub-tiles
+  // of the longest canvas; canvases needing more than kDaMaxSplits use the general kernel.
   {
     const int n_sub = s->max_seq / 64;
-    int sp = 1;
-    while (sp * 2 <= s->max_cluster && sp * 2 <= n_sub && m->nkv * sp * 2 <= s->sms) sp *= 2;
-    s->da_splits = (m->rep * (kMaxFwdRows / 2) <= 128 && (n_sub + sp - 1) / sp <= kDaMaxSub) ? sp : 0;
+    const int sp = (n_sub + kDaMaxSub - 1) / kDaMaxSub;
+    s->da_splits = (m->rep * (kMaxFwdRows / 2) <= 128 && sp <= kDaMaxSplits) ? sp : 0;
+    if (s->da_splits > 1) {
+      const size_t rows = static_cast<size_t>(m->nkv) * s->da_splits * 128;
+      if ((rc = salloc(s, &s->da_part_o, rows * 128)) != DRT_OK) return fail(rc);
+      if ((rc = salloc(s, &s->da_part_ml, rows * 2)) != DRT_OK) return fail(rc);
+    }
   }
   // Selector scratch.
   s->sel_chunks = (m->V + kSelChunk - 1) / kSelChunk;

@@ -6,9 +6,7 @@
 // (row r = position r / rep, head g * rep + r % rep).
 //
 // Work split, per KV head g: `splits` CTAs share the visible keys in balanced runs of 64-key
-// sub-tiles, at most kDaMaxSub per CTA, so a CTA needs under half of an SM's shared memory and a
-// quarter of its TMEM: CTAs of this kernel pair up on an SM and can sit beside the QKV linear
-// that precedes them. A CTA
+// sub-tiles, at most kDaMaxSub per CTA (one CTA per SM). A CTA
 //   1. streams its K and V^T sub-tiles into shared memory with TMA. Sub-tiles that lie wholly
 //      before the first forwarded position hold final K/V from earlier steps and are requested
 //      before the programmatic-dependent-launch wait, so they stream while the QKV linear is
@@ -17,16 +15,17 @@
 //   3. runs a two-pass softmax over its keys with two threads per live row (pass 1: row max,
 //      pass 2: exp2, the bf16 P written over the consumed K sub-tile), in the log2 domain;
 //   4. accumulates O = sum_j P_j V_j on the tensor cores into TMEM;
-//   5. with one split, normalises and writes bf16; otherwise writes its unnormalised f32 rows
-//      and (m, l) to a partial buffer that attn_merge_kernel combines (rescale by
-//      exp2(m_i - max m), sum in split order, normalise).
+//   5. with one split, normalises and writes bf16; otherwise writes its unnormalised f32 rows and
+//      (m, l) to a partial buffer that attn_merge_kernel combines (rescale by exp2(m_i - max m),
+//      sum in split order, normalise, write bf16).
 // All waits are bounded (common.cuh); on a timeout the CTA records the error and unwinds.
 #pragma once
 #include "attention.cuh"
 
 namespace drt {
 
-constexpr int kDaMaxSub = 2;                    // 64-key sub-tiles per CTA
+constexpr int kDaMaxSub = 4;                    // 64-key sub-tiles per CTA
+constexpr int kDaMaxSplits = 64;                // CTAs per KV head
 constexpr int kDaQBytes = 2 * 128 * 128;        // Q: two 64-d atoms x 128 rows
 constexpr int kDaKBytes = 2 * 64 * 128;         // K sub-tile: two 64-d atoms x 64 keys
 constexpr int kDaVBytes = 128 * 128;            // V^T sub-tile: 128 d rows x 64 keys
@@ -34,7 +33,8 @@ constexpr int kDaSubBytes = kDaKBytes + kDaVBytes;
 constexpr int kDaThreads = 256;
 // Q | sub-tiles | row-statistics exchange | barriers
 constexpr size_t kDaBodyBytes = kDaQBytes + static_cast<size_t>(kDaMaxSub) * kDaSubBytes;
-constexpr size_t kDaSmemBytes = 1024 + kDaBodyBytes + 4 * 128 * 4 + 256;
+constexpr size_t kDaRedFloats = 4 * 128;        // softmax row-statistics exchange
+constexpr size_t kDaSmemBytes = 1024 + kDaBodyBytes + kDaRedFloats * 4 + 256;
 
 struct DecAttnArgs {
   int nq, nkv, rep;
@@ -62,15 +62,15 @@ __device__ __forceinline__ int da_limit(const DecAttnArgs& a, int q_pos, int kv_
   return min(lim, kv_len);
 }
 
-__global__ void __launch_bounds__(kDaThreads, 2)
+__global__ void __launch_bounds__(kDaThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK64,
                        const __grid_constant__ CUtensorMap tmV, const DecAttnArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* sQ = smem;
   uint8_t* sSub = smem + kDaQBytes;  // [kDaMaxSub][K | V^T]
   float* red = reinterpret_cast<float*>(smem + kDaBodyBytes);  // [4][128]: m halves, l halves
-  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 4 * 128);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + kDaRedFloats);
   uint64_t* barQ = bars;
   uint64_t* barKV = bars + 1;                 // [kDaMaxSub]
   uint64_t* barS = bars + 1 + kDaMaxSub;
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kDaThreads, 2)
   if (tid == 0)
     for (int j = 0; j < n_final; ++j) load_sub(j);
   if (warp == 0) {
-    tmem_alloc(tmem_slot, 128);
+    tmem_alloc(tmem_slot, kDaMaxSub * 64 >= 128 ? kDaMaxSub * 64 : 128);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -261,45 +261,50 @@ __global__ void __launch_bounds__(kDaThreads, 2)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 128);
+  if (warp == 0) tmem_dealloc(tmem, kDaMaxSub * 64 >= 128 ? kDaMaxSub * 64 : 128);
 }
 
-// Combine the split partials of attn_decode_kernel: one CTA per (live row, KV head), thread d
-// owns output column d. Thread s < splits fetches split s's (m, l) into shared memory while every
-// thread fetches its column of all splits, so the merge costs one round trip.
-constexpr int kDaMaxSplits = 64;
-__global__ void __launch_bounds__(128)
+// Combine the split partials of attn_decode_kernel. One CTA per KV head and group of
+// kDaMergeRows live rows; thread (row i, column d). Threads d < splits fetch split d's (m, l) into
+// shared memory while every thread fetches its column of all splits, so the merge costs one
+// round trip.
+constexpr int kDaMergeRows = 4;
+__global__ void __launch_bounds__(128 * kDaMergeRows)
     attn_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits, int rep, int nq,
                       int rows, const int* rows_dev, __nv_bfloat16* __restrict__ out) {
   griddep_wait();
   griddep_launch_dependents();
   int rows_valid = rows;
   if (rows_dev != nullptr) rows_valid = min(rows_valid, *rows_dev);
-  const int r = blockIdx.x;
-  const int g = blockIdx.y;
-  if (r >= rows_valid * rep) return;
-  const int d = threadIdx.x;
-  __shared__ float sm[kDaMaxSplits], sl[kDaMaxSplits];
+  const int g = blockIdx.x;
+  const int i = threadIdx.x >> 7;
+  const int d = threadIdx.x & 127;
+  const int r = blockIdx.y * kDaMergeRows + i;
+  if (blockIdx.y * kDaMergeRows >= rows_valid * rep) return;
+  const bool live = r < rows_valid * rep;
+  __shared__ float sm[kDaMergeRows][kDaMaxSplits], sl[kDaMergeRows][kDaMaxSplits];
   const size_t base = static_cast<size_t>(g) * splits * 128 + r;  // row index of split 0
-  if (d < splits) {
+  if (live && d < splits) {
     const float2 ml = __ldcg(reinterpret_cast<const float2*>(part_ml + (base + static_cast<size_t>(d) * 128) * 2));
-    sm[d] = ml.x;
-    sl[d] = ml.y;
+    sm[i][d] = ml.x;
+    sl[i][d] = ml.y;
   }
   float o[kDaMaxSplits];
 #pragma unroll
-  for (int s = 0; s < kDaMaxSplits; ++s) o[s] = s < splits ? __ldcg(part_o + (base + static_cast<size_t>(s) * 128) * 128 + d) : 0.0f;
+  for (int sp = 0; sp < kDaMaxSplits; ++sp)
+    o[sp] = (live && sp < splits) ? __ldcg(part_o + (base + static_cast<size_t>(sp) * 128) * 128 + d) : 0.0f;
   __syncthreads();
+  if (!live) return;
   float mx = -INFINITY;
-  for (int s = 0; s < splits; ++s)
-    if (sl[s] > 0.0f) mx = fmaxf(mx, sm[s]);
+  for (int sp = 0; sp < splits; ++sp)
+    if (sl[i][sp] > 0.0f) mx = fmaxf(mx, sm[i][sp]);
   float L = 0.0f, acc = 0.0f;
 #pragma unroll
-  for (int s = 0; s < kDaMaxSplits; ++s) {
-    if (s < splits) {
-      const float w = sl[s] > 0.0f ? exp2f(sm[s] - mx) : 0.0f;
-      L += sl[s] * w;
-      acc += o[s] * w;
+  for (int sp = 0; sp < kDaMaxSplits; ++sp) {
+    if (sp < splits) {
+      const float w = sl[i][sp] > 0.0f ? exp2f(sm[i][sp] - mx) : 0.0f;
+      L += sl[i][sp] * w;
+      acc += o[sp] * w;
     }
   }
   const int pos = r / rep;

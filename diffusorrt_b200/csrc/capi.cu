@@ -811,7 +811,7 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
       CK(launch_cx(attn_decode_kernel, dim3(s->da_splits, m->nkv), dim3(kDaThreads), kDaSmemBytes, s->stream, 1, s->m_q,
                    s->m_k64, s->m_v, da));
       if (s->da_splits > 1)
-        CK(launch_k(attn_merge_kernel, dim3(128, m->nkv), dim3(128), 0, s->stream, true,
+        CK(launch_k(attn_merge_kernel, dim3(m->nkv, 128 / kDaMergeRows), dim3(128 * kDaMergeRows), 0, s->stream, true,
                     static_cast<const float*>(s->da_part_o), static_cast<const float*>(s->da_part_ml), s->da_splits, m->rep,
                     m->nq, da.rows, da.rows_dev, s->attn));
     } else {
@@ -1012,11 +1012,12 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   s->attn_splits = asp;
   s->attn_tps = (kv_tiles + asp - 1) / asp;
   // Decode attention: enough CTAs per KV head that each covers at most kDaMaxSub 64-key sub-tiles
-  // of the longest canvas; canvases needing more than kDaMaxSplits use the general kernel.
+  // of the longest canvas, all CTAs resident at once (one per SM); otherwise the general kernel.
   {
     const int n_sub = s->max_seq / 64;
     const int sp = (n_sub + kDaMaxSub - 1) / kDaMaxSub;
-    s->da_splits = (m->rep * (kMaxFwdRows / 2) <= 128 && sp <= kDaMaxSplits) ? sp : 0;
+    const bool fits = m->rep * (kMaxFwdRows / 2) <= 128 && sp <= kDaMaxSplits;
+    s->da_splits = fits ? sp : 0;
     if (s->da_splits > 1) {
       const size_t rows = static_cast<size_t>(m->nkv) * s->da_splits * 128;
       if ((rc = salloc(s, &s->da_part_o, rows * 128)) != DRT_OK) return fail(rc);

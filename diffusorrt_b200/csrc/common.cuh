@@ -27,6 +27,13 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// First 1024-byte aligned address inside a dynamic shared-memory array. The offset is applied as
+// pointer arithmetic on the shared array (not through an integer round trip), so the compiler
+// keeps treating every access through the result as shared memory.
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* smem_raw) {
+  return smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

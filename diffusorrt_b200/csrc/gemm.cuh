@@ -74,7 +74,7 @@ struct GemmCfg {
   // Ring, or (split-K) the receive buffer plus the epilogue exchange buffer, whichever is larger.
   __host__ __device__ static size_t body_bytes(int stages) {
     const size_t ring = static_cast<size_t>(stages) * kStageBytes;
-    const size_t epi = static_cast<size_t>(BN) * 128 * 4 + (32 * 128 + 64) * 4;
+    const size_t epi = static_cast<size_t>(BN) * 128 * 4 + (32 * 128 + 160) * 4;
     return ((ring > epi ? ring : epi) + 1023) & ~size_t(1023);
   }
   __host__ __device__ static size_t smem_bytes(int stages) { return 1024 + body_bytes(stages) + 256; }
@@ -89,8 +89,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Epilogue for up to 32 accumulator columns (activation rows col0 .. col0+ncols-1).
 // v[i] holds this thread's weight row (m0 + tid) for activation row col0 + i. All loops run to
 // 32 with a guard so v stays in registers.
+// rope_c / rope_s: optional RoPE factors for this thread's feature at rows col0 + i, loaded by the
+// caller ahead of time (the decode kernel fetches them before its accumulator is ready); when null
+// the QKV epilogue reads the tables itself.
 __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int col0, int ncols, int m0, int tid,
-                                                    float* xs, int pos0) {
+                                                    float* xs, int pos0, const float* rope_c = nullptr,
+                                                    const float* rope_s = nullptr) {
   const int n = m0 + tid;
   const float b = a.bias != nullptr ? a.bias[n] : 0.0f;
   switch (a.epi) {
@@ -187,19 +191,23 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
         v[i] = val;
         xs[i * 128 + tid] = val;
       }
-      __syncthreads();
       float* rs = xs + 32 * 128;  // 32 per-row scales
+      float* part = rs + 32;        // [4 warps][32 rows] partial sums of squares
       const int warp = tid >> 5, lane = tid & 31;
       if (nw != nullptr) {
-        for (int i = warp * 8; i < warp * 8 + 8; ++i) {
-          float ss = 0.0f;
+        // All rows at once: a warp tree per row over this warp's 32 features, then the four warps
+        // in order; one thread per row finishes its scale.
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float x = xs[i * 128 + lane + 32 * j];
-            ss = __fmaf_rn(x, x, ss);
+        for (int i = 0; i < 32; ++i) {
+          if (i < ncols) {
+            const float t = warp_sum(__fmul_rn(v[i], v[i]));
+            if (lane == 0) part[warp * 32 + i] = t;
           }
-          ss = warp_sum(ss);
-          if (lane == 0) rs[i] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
+        }
+        __syncthreads();
+        if (tid < ncols) {
+          const float ss = __fadd_rn(__fadd_rn(__fadd_rn(part[tid], part[32 + tid]), part[64 + tid]), part[96 + tid]);
+          rs[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
         }
       }
       __syncthreads();
@@ -217,8 +225,8 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
           xp = __fmul_rn(__fmul_rn(xp, rs[i]), w_part);
         }
         const int pos = pos0 + col0 + i;
-        const float c = a.rope_cos[static_cast<size_t>(pos) * 64 + (tid & 63)];
-        const float s = a.rope_sin[static_cast<size_t>(pos) * 64 + (tid & 63)];
+        const float c = rope_c != nullptr ? rope_c[i] : a.rope_cos[static_cast<size_t>(pos) * 64 + (tid & 63)];
+        const float s = rope_s != nullptr ? rope_s[i] : a.rope_sin[static_cast<size_t>(pos) * 64 + (tid & 63)];
         const float rot = tid < 64 ? -xp : xp;
         const float out = __fadd_rn(__fmul_rn(x, c), __fmul_rn(rot, s));
         if (is_q) {
@@ -287,7 +295,7 @@ __global__ void __launch_bounds__(128, 1)
                        const GemmArgs a) {
   using Cfg = GemmCfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   const int stages = a.stages;
   uint8_t* ring = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring + Cfg::body_bytes(stages));

@@ -53,6 +53,151 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t
                : "memory");
 }
 
+// Decode epilogues, written in phases (every shared-memory read of a phase is issued before the
+// first dependent use, and every global store comes last) over a compile-time number of columns
+// CPR with no per-column guards except on the stores, so the few warps of a CTA keep many
+// independent operations in flight; results are those of gemm_epilogue_chunk.
+//
+// QKV tile, columns [c0, c0 + nc) of this CTA's slice (v[i] = accumulator of column c0 + i,
+// nc <= CPR): q / k rows get bias, the per-row RMSNorm over the head (QK-norm) and RoPE; v rows
+// are written transposed into the V^T cache. rope_c / rope_s hold this thread's RoPE factors.
+template <int CPR>
+__device__ __forceinline__ void dec_epilogue_qkv(const GemmArgs& a, const float* v, int c0, int nc, int m0, int tid,
+                                                 float* xs, int pos0, const float* rope_c, const float* rope_s) {
+  const int n = m0 + tid;
+  const float b = a.bias != nullptr ? a.bias[n] : 0.0f;
+  const int tile = m0 >> 7;
+  const bool is_q = tile < a.nq;
+  const bool is_k = !is_q && tile < a.nq + a.nkv;
+  float val[CPR];
+#pragma unroll
+  for (int i = 0; i < CPR; ++i) val[i] = __fadd_rn(bf16_round(v[i]), b);
+  if (!is_q && !is_k) {
+    // V^T[g][d][pos], contiguous along pos: this thread's feature row, nc consecutive positions.
+    const int g = tile - a.nq - a.nkv;
+    __nv_bfloat16* dst = a.vtcache + (static_cast<size_t>(g) * 128 + tid) * a.max_seq + pos0 + c0;
+    if (CPR % 8 == 0 && nc == CPR && ((pos0 + c0) & 7) == 0) {
+#pragma unroll
+      for (int q = 0; q < CPR / 8; ++q) {
+        __align__(16) __nv_bfloat16 t[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) t[e] = __float2bfloat16_rn(val[q * 8 + e]);
+        *reinterpret_cast<uint4*>(dst + q * 8) = *reinterpret_cast<const uint4*>(t);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < CPR; ++i)
+        if (i < nc) dst[i] = __float2bfloat16_rn(val[i]);
+    }
+    return;
+  }
+  const float* nw = is_q ? a.qnorm_w : a.knorm_w;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int partner = tid ^ 64;
+  const float w_self = nw != nullptr ? nw[tid] : 1.0f;
+  const float w_part = nw != nullptr ? nw[partner] : 1.0f;
+  float* rs = xs + 32 * 128;  // per-row scales
+  float* part = rs + 32;        // [4 warps][32 rows]
+#pragma unroll
+  for (int i = 0; i < CPR; ++i) xs[i * 128 + tid] = val[i];
+  if (nw != nullptr) {
+    float sq[CPR];
+#pragma unroll
+    for (int i = 0; i < CPR; ++i) sq[i] = __fmul_rn(val[i], val[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int i = 0; i < CPR; ++i) sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < CPR; ++i) part[warp * 32 + i] = sq[i];
+    }
+  }
+  __syncthreads();
+  if (nw != nullptr && tid < CPR) {
+    const float ss = __fadd_rn(__fadd_rn(__fadd_rn(part[tid], part[32 + tid]), part[64 + tid]), part[96 + tid]);
+    rs[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
+  }
+  __syncthreads();
+  float xp[CPR], sc[CPR];
+#pragma unroll
+  for (int i = 0; i < CPR; ++i) {
+    xp[i] = xs[i * 128 + partner];
+    sc[i] = nw != nullptr ? rs[i] : 1.0f;
+  }
+  __nv_bfloat16 outv[CPR];
+#pragma unroll
+  for (int i = 0; i < CPR; ++i) {
+    float x = val[i], y = xp[i];
+    if (nw != nullptr) {
+      x = __fmul_rn(__fmul_rn(x, sc[i]), w_self);
+      y = __fmul_rn(__fmul_rn(y, sc[i]), w_part);
+    }
+    const float rot = tid < 64 ? -y : y;
+    outv[i] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(x, rope_c[i]), __fmul_rn(rot, rope_s[i])));
+  }
+  const int head = is_q ? tile : tile - a.nq;
+#pragma unroll
+  for (int i = 0; i < CPR; ++i) {
+    if (i < nc) {
+      if (is_q) a.out_bf16[(static_cast<size_t>(c0 + i) * a.nq + head) * 128 + tid] = outv[i];
+      else a.kcache[(static_cast<size_t>(head) * a.max_seq + pos0 + c0 + i) * 128 + tid] = outv[i];
+    }
+  }
+}
+
+// SwiGLU tile (lanes 0..63 gate rows j0 + f, lanes 64..127 up rows j0 + f of the same features):
+// act[c0 + i, j0 + f] = bf16(silu(g) * u). Both halves of the CTA work: thread t takes feature
+// t & 63 for the columns of parity t >> 6.
+template <int CPR>
+__device__ __forceinline__ void dec_epilogue_swiglu(const GemmArgs& a, const float* v, int c0, int nc, int m0, int tid,
+                                                    float* xs) {
+  const float b = a.bias != nullptr ? a.bias[m0 + tid] : 0.0f;
+#pragma unroll
+  for (int i = 0; i < CPR; ++i) xs[i * 128 + tid] = __fadd_rn(bf16_round(v[i]), b);
+  __syncthreads();
+  constexpr int H = CPR / 2;
+  const int f = tid & 63, par = tid >> 6;
+  float g[H], u[H];
+#pragma unroll
+  for (int k = 0; k < H; ++k) {
+    g[k] = xs[(2 * k + par) * 128 + f];
+    u[k] = xs[(2 * k + par) * 128 + 64 + f];
+  }
+  __nv_bfloat16 act[H];
+#pragma unroll
+  for (int k = 0; k < H; ++k) {
+    const float sig = 1.0f / (1.0f + expf(-g[k]));
+    act[k] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(g[k], sig), u[k]));
+  }
+  const int j0 = m0 >> 1;
+#pragma unroll
+  for (int k = 0; k < H; ++k) {
+    const int i = 2 * k + par;
+    if (i < nc) a.out_bf16[static_cast<size_t>(c0 + i) * a.ld_out + j0 + f] = act[k];
+  }
+}
+
+template <int CPR>
+__device__ __forceinline__ void dec_epilogue_t(const GemmArgs& a, const float* v, int c0, int nc, int m0, int tid, float* xs,
+                                               int pos0, const float* rope_c, const float* rope_s) {
+  if (a.epi == EPI_QKV) dec_epilogue_qkv<CPR>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s);
+  else dec_epilogue_swiglu<CPR>(a, v, c0, nc, m0, tid, xs);
+}
+
+// QKV or SwiGLU epilogue for a slice of cpr columns (cpr = 2, 4, 8, 16 or 32).
+__device__ __forceinline__ void dec_epilogue(const GemmArgs& a, const float* v, int cpr, int c0, int nc, int m0, int tid,
+                                             float* xs, int pos0, const float* rope_c, const float* rope_s) {
+  switch (cpr) {
+    case 2: dec_epilogue_t<2>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s); break;
+    case 4: dec_epilogue_t<4>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s); break;
+    case 8: dec_epilogue_t<8>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s); break;
+    case 16: dec_epilogue_t<16>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s); break;
+    default: dec_epilogue_t<32>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s); break;
+  }
+}
+
 // Sum of this CTA's column slice over the S received partials, in rank order. The slice layout is
 // [CPR / W][lane][W] per source (W = min(CPR, 4)); S and the MMA width are compile-time so the
 // loop is fully unrolled with static indices.
@@ -101,7 +246,7 @@ __device__ __forceinline__ void dec_sum_any(int S, const float* recv, int tid, f
 __global__ void __launch_bounds__(128, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   const int stages = a.stages;
   uint8_t* ring = smem;
   uint8_t* sB = ring + dec_ring_bytes(stages);
@@ -168,13 +313,22 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t rank = S > 1 ? cluster_ctarank() : 0u;
   const int c0 = static_cast<int>(rank) * cpr;
   const int nvalid = max(0, min(cpr, rows_valid - c0));
-  // Residual epilogue: fetch the rows this CTA will update now, off the critical path.
-  float pre[32];
+  // Epilogue inputs that do not depend on the accumulator are fetched now, off the critical path:
+  // the residual rows this CTA will update, or the RoPE factors of its Q/K rows.
+  float pre[32], pre2[32];
+  const bool rope_tile = a.epi == EPI_QKV && (m0 >> 7) < a.nq + a.nkv;
   if (S > 1 && a.epi == EPI_RESID) {
     const int n = m0 + tid;
 #pragma unroll
     for (int i = 0; i < 32; ++i)
       pre[i] = i < nvalid ? __ldcg(a.out_f32 + static_cast<size_t>(c0 + i) * a.ld_out + n) : 0.0f;
+  } else if (S > 1 && rope_tile) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const size_t idx = static_cast<size_t>(pos0 + c0 + i) * 64 + (tid & 63);
+      pre[i] = i < nvalid ? __ldg(a.rope_cos + idx) : 0.0f;
+      pre2[i] = i < nvalid ? __ldg(a.rope_sin + idx) : 0.0f;
+    }
   }
   if (tid == 0) {
     if (nkb > 0) {
@@ -291,6 +445,8 @@ __global__ void __launch_bounds__(128, 1)
         for (int i = 0; i < 32; ++i)
           if (i < nvalid)
             a.out_f32[static_cast<size_t>(c0 + i) * a.ld_out + n] = __fadd_rn(pre[i], __fadd_rn(bf16_round(v[i]), b));
+      } else if (a.epi == EPI_QKV || a.epi == EPI_SWIGLU) {
+        dec_epilogue(a, v, cpr, c0, nvalid, m0, tid, xs, pos0, pre, pre2);
       } else {
         gemm_epilogue_chunk(a, v, c0, nvalid, m0, tid, xs, pos0);
       }

@@ -191,10 +191,15 @@ int configure_kernels() {
         cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
-        cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDaSmemBytes)) != cudaSuccess ||
-        cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDaSmemBytes)) != cudaSuccess)
       result = DRT_INTERNAL_ERROR;
+    for (int epi = 0; epi <= EPI_QKV && result == DRT_OK; ++epi)
+      for (int sp = 1; sp <= 16 && result == DRT_OK; sp *= 2) {
+        DecGemmKernel k = dec_gemm_kernel(epi, sp);
+        if (k == nullptr || cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+            cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+          result = DRT_INTERNAL_ERROR;
+      }
   });
   if (result != DRT_OK) return set_error(DRT_INTERNAL_ERROR, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(cudaGetLastError()));
   return DRT_OK;
@@ -721,8 +726,10 @@ int run_dec_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, G
     if (dec_smem_bytes(st, a.kb_per_split) <= kFullSm) s_full = st;
   }
   a.stages = (s_co >= std::min(a.kb_per_split, 4)) ? s_co : s_full;
-  CK(launch_kc(gemm_decode_kernel, dim3(tiles_m, 1, a.splits), dim3(128), dec_smem_bytes(a.stages, a.kb_per_split), s->stream,
-               true, a.splits, mA, mB, a));
+  DecGemmKernel kern = dec_gemm_kernel(a.epi, a.splits);
+  if (kern == nullptr) return set_error(DRT_INTERNAL_ERROR, "no decode linear for epilogue %d, split %d", a.epi, a.splits);
+  CK(launch_kc(kern, dim3(tiles_m, 1, a.splits), dim3(128), dec_smem_bytes(a.stages, a.kb_per_split), s->stream, true,
+               a.splits, mA, mB, a));
   return DRT_OK;
 }
 

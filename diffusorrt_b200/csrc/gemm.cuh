@@ -92,25 +92,23 @@ __device__ __forceinline__ float warp_sum(float v) {
 // rope_c / rope_s: optional RoPE factors for this thread's feature at rows col0 + i, loaded by the
 // caller ahead of time (the decode kernel fetches them before its accumulator is ready); when null
 // the QKV epilogue reads the tables itself.
-__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int col0, int ncols, int m0, int tid,
-                                                    float* xs, int pos0, const float* rope_c = nullptr,
-                                                    const float* rope_s = nullptr) {
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* v, int col0, int ncols, int m0, int tid,
+                                                      float* xs, int pos0, const float* rope_c = nullptr,
+                                                      const float* rope_s = nullptr) {
   const int n = m0 + tid;
   const float b = a.bias != nullptr ? a.bias[n] : 0.0f;
-  switch (a.epi) {
-    case EPI_STORE_RAW: {
+    if constexpr (EPI == EPI_STORE_RAW) {
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = v[i];
-      break;
     }
-    case EPI_STORE_F32: {
+    if constexpr (EPI == EPI_STORE_F32) {
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = __fadd_rn(bf16_round(v[i]), b);
-      break;
     }
-    case EPI_RESID: {
+    if constexpr (EPI == EPI_RESID) {
       float cur[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) cur[i] = i < ncols ? a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] : 0.0f;
@@ -134,9 +132,8 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
               __fadd_rn(__fadd_rn(__fadd_rn(xs[tid], xs[32 + tid]), xs[64 + tid]), xs[96 + tid]);
         __syncthreads();
       }
-      break;
     }
-    case EPI_SWIGLU: {
+    if constexpr (EPI == EPI_SWIGLU) {
       // Tile layout (set by the weight packer): lanes 0..63 = gate rows j0..j0+63,
       // lanes 64..127 = up rows j0..j0+63 of the same intermediate features.
       const int j0 = (m0 >> 1);
@@ -158,9 +155,8 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
         }
       }
       __syncthreads();
-      break;
     }
-    case EPI_QKV: {
+    if constexpr (EPI == EPI_QKV) {
       const int tile = m0 >> 7;
       const bool is_q = tile < a.nq;
       const bool is_k = !is_q && tile < a.nq + a.nkv;
@@ -182,7 +178,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
           for (int i = 0; i < 32; ++i)
             if (i < ncols) dst[i] = __float2bfloat16_rn(__fadd_rn(bf16_round(v[i]), b));
         }
-        break;
+        return;
       }
       const float* nw = is_q ? a.qnorm_w : a.knorm_w;
 #pragma unroll
@@ -236,10 +232,19 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
         }
       }
       __syncthreads();
-      break;
     }
-    default:
-      break;
+}
+
+// Runtime dispatch over the epilogue kinds (the prefill kernel, whose epilogue is a launch argument).
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int col0, int ncols, int m0, int tid,
+                                                    float* xs, int pos0) {
+  switch (a.epi) {
+    case EPI_STORE_RAW: gemm_epilogue_chunk_t<EPI_STORE_RAW>(a, v, col0, ncols, m0, tid, xs, pos0); break;
+    case EPI_STORE_F32: gemm_epilogue_chunk_t<EPI_STORE_F32>(a, v, col0, ncols, m0, tid, xs, pos0); break;
+    case EPI_RESID: gemm_epilogue_chunk_t<EPI_RESID>(a, v, col0, ncols, m0, tid, xs, pos0); break;
+    case EPI_SWIGLU: gemm_epilogue_chunk_t<EPI_SWIGLU>(a, v, col0, ncols, m0, tid, xs, pos0); break;
+    case EPI_QKV: gemm_epilogue_chunk_t<EPI_QKV>(a, v, col0, ncols, m0, tid, xs, pos0); break;
+    default: break;
   }
 }
 

@@ -179,24 +179,7 @@ __device__ __forceinline__ void dec_epilogue_swiglu(const GemmArgs& a, const flo
   }
 }
 
-template <int CPR>
-__device__ __forceinline__ void dec_epilogue_t(const GemmArgs& a, const float* v, int c0, int nc, int m0, int tid, float* xs,
-                                               int pos0, const float* rope_c, const float* rope_s) {
-  if (a.epi == EPI_QKV) dec_epilogue_qkv<CPR>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s);
-  else dec_epilogue_swiglu<CPR>(a, v, c0, nc, m0, tid, xs);
-}
 
-// QKV or SwiGLU epilogue for a slice of cpr columns (cpr = 2, 4, 8, 16 or 32).
-__device__ __forceinline__ void dec_epilogue(const GemmArgs& a, const float* v, int cpr, int c0, int nc, int m0, int tid,
-                                             float* xs, int pos0, const float* rope_c, const float* rope_s) {
-  switch (cpr) {
-    case 2: dec_epilogue_t<2>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s); break;
-    case 4: dec_epilogue_t<4>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s); break;
-    case 8: dec_epilogue_t<8>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s); break;
-    case 16: dec_epilogue_t<16>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s); break;
-    default: dec_epilogue_t<32>(a, v, c0, nc, m0, tid, xs, pos0, rope_c, rope_s); break;
-  }
-}
 
 // Sum of this CTA's column slice over the S received partials, in rank order. The slice layout is
 // [CPR / W][lane][W] per source (W = min(CPR, 4)); S and the MMA width are compile-time so the
@@ -233,53 +216,213 @@ __device__ __forceinline__ void dec_sum_slices(const float* recv, int tid, float
   }
 }
 
-template <int NCOL>
-__device__ __forceinline__ void dec_sum_any(int S, const float* recv, int tid, float* v) {
-  switch (S) {
-    case 2: dec_sum_slices<2, NCOL>(recv, tid, v); break;
-    case 4: dec_sum_slices<4, NCOL>(recv, tid, v); break;
-    case 8: dec_sum_slices<8, NCOL>(recv, tid, v); break;
-    default: dec_sum_slices<16, NCOL>(recv, tid, v); break;
+
+// Shared-memory carve-up of one decode-linear CTA.
+struct DecSmem {
+  uint8_t* ring;
+  uint8_t* sB;
+  float* stage;
+  float* recv;
+  float* xs;
+  uint64_t* fullA;
+  uint64_t* emptyA;
+  uint64_t* fullB;
+  uint64_t* accum;
+  uint64_t* xbar;
+  int* flags;
+};
+
+// Everything after the dependency wait, for a compile-time epilogue EPI, split-K factor S and MMA
+// width NCOL: activation load, weight ring, UMMA, split-K exchange and epilogue.
+template <int EPI, int S, int NCOL>
+__device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMap* tmB, const GemmArgs& a, const DecSmem& sm,
+                                        uint32_t tmem, int m0, int kb0, int nkb, int npre, int stages, uint64_t policy,
+                                        int rows_valid, int pos0) {
+  constexpr int CPR = NCOL / S;  // columns owned by each CTA of the cluster
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = S > 1 ? cluster_ctarank() : 0u;
+  const int c0 = static_cast<int>(rank) * CPR;
+  const int nvalid = max(0, min(CPR, rows_valid - c0));
+  // Epilogue inputs that do not depend on the accumulator are fetched now, off the critical path:
+  // the residual rows this CTA will update, or the RoPE factors of its Q/K rows.
+  float pre[CPR], pre2[CPR];
+  if constexpr (S > 1 && EPI == EPI_RESID) {
+    const int n = m0 + tid;
+#pragma unroll
+    for (int i = 0; i < CPR; ++i) pre[i] = i < nvalid ? __ldcg(a.out_f32 + static_cast<size_t>(c0 + i) * a.ld_out + n) : 0.0f;
+  }
+  if constexpr (S > 1 && EPI == EPI_QKV) {
+    if ((m0 >> 7) < a.nq + a.nkv) {
+#pragma unroll
+      for (int i = 0; i < CPR; ++i) {
+        const size_t idx = static_cast<size_t>(pos0 + c0 + i) * 64 + (tid & 63);
+        pre[i] = i < nvalid ? __ldg(a.rope_cos + idx) : 0.0f;
+        pre2[i] = i < nvalid ? __ldg(a.rope_sin + idx) : 0.0f;
+      }
+    }
+  }
+  if (tid == 0) {
+    if (nkb > 0) {
+      mbar_expect_tx(sm.fullB, static_cast<uint32_t>(nkb * kDecBBytes));
+      for (int i = 0; i < nkb; ++i) tma_load_2d(sm.sB + i * kDecBBytes, tmB, sm.fullB, (kb0 + i) * 64, 0);
+    }
+    if constexpr (S > 1) mbar_expect_tx(sm.xbar, static_cast<uint32_t>(S * 128 * CPR * 4));
+  }
+  griddep_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = npre; i < nkb; ++i) {
+        const int s = i % stages;
+        if (!mbar_wait(&sm.emptyA[s], ((i / stages) - 1) & 1)) { ok = false; break; }
+        mbar_expect_tx(&sm.fullA[s], kDecABytes);
+        tma_load_2d_hint(sm.ring + static_cast<size_t>(s) * kDecABytes, tmA, &sm.fullA[s], (kb0 + i) * 64, m0, policy);
+      }
+      if (!ok) { record_error(a.status, DEV_TIMEOUT_TMA); sm.flags[0] = 1; }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, NCOL);
+      bool ok = nkb == 0 || mbar_wait(sm.fullB, 0);
+      tc_fence_after();
+      for (int i = 0; i < nkb && ok; ++i) {
+        const int s = i % stages;
+        if (!mbar_wait(&sm.fullA[s], (i / stages) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(sm.ring + static_cast<size_t>(s) * kDecABytes);
+        const uint32_t b_addr = smem_u32(sm.sB + i * kDecBBytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16(tmem, sdesc_kmajor_sw128(a_addr + kk * 32), sdesc_kmajor_sw128(b_addr + kk * 32), idesc,
+                    (i | kk) != 0 ? 1u : 0u);
+        umma_commit(&sm.emptyA[s]);
+      }
+      if (!ok) { record_error(a.status, DEV_TIMEOUT_MMA); sm.flags[0] = 1; }
+      umma_commit(sm.accum);
+    }
+    __syncwarp();
+  }
+
+  bool acc_ok = true;
+  if (nkb > 0) acc_ok = mbar_wait(sm.accum, 0);
+  tc_fence_after();
+  if (!acc_ok) { record_error(a.status, DEV_TIMEOUT_EPI); sm.flags[0] = 1; }
+  const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  float acc[NCOL];
+  if (acc_ok && nkb > 0) {
+#pragma unroll
+    for (int cb = 0; cb < NCOL; cb += 32) tmem_ld32(lane_addr + cb, acc + cb);
+  } else {
+#pragma unroll
+    for (int c = 0; c < NCOL; ++c) acc[c] = 0.0f;
+  }
+  if constexpr (S == 1) {
+    __syncthreads();
+    if (sm.flags[0] == 0) {
+      gemm_epilogue_chunk_t<EPI>(a, acc, 0, min(32, rows_valid), m0, tid, sm.xs, pos0);
+      if constexpr (NCOL == 64)
+        if (rows_valid > 32) gemm_epilogue_chunk_t<EPI>(a, acc + 32, 32, rows_valid - 32, m0, tid, sm.xs, pos0);
+    }
+  } else {
+    // Stage the partial as S contiguous slices and send slice p to CTA p. Inside a slice the
+    // columns are grouped in units of W = min(CPR, 4): [CPR / W][lane][W], so both the staging
+    // stores and the receiver's reads are bank-conflict free. The stage overlays this CTA's
+    // drained ring; the receive buffer overlays it too, so nothing is sent before every CTA of the
+    // cluster is past its MMAs (the cluster barrier below).
+    tc_fence_before();
+    __syncthreads();  // every warp is past its TMEM loads
+    if constexpr (CPR >= 4) {
+#pragma unroll
+      for (int j = 0; j < NCOL; j += 4) {
+        const int p = j / CPR, c = j - p * CPR;
+        *reinterpret_cast<float4*>(sm.stage + p * 128 * CPR + ((c >> 2) * 128 + tid) * 4) =
+            make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < NCOL; j += 2)
+        *reinterpret_cast<float2*>(sm.stage + (j >> 1) * 256 + tid * 2) = make_float2(acc[j], acc[j + 1]);
+    }
+    fence_proxy_async_smem();
+    cluster_sync();  // all stages written, every CTA's ring drained and receive barrier armed
+    constexpr uint32_t slice_bytes = static_cast<uint32_t>(128 * CPR * 4);
+    if (tid < S) {
+      const uint32_t dst = cluster_map(smem_u32(sm.recv) + rank * slice_bytes, static_cast<uint32_t>(tid));
+      const uint32_t bar = cluster_map(smem_u32(sm.xbar), static_cast<uint32_t>(tid));
+      bulk_copy_to_peer(dst, smem_u32(sm.stage) + tid * slice_bytes, slice_bytes, bar);
+    }
+    if (!mbar_wait(sm.xbar, 0)) { record_error(a.status, DEV_TIMEOUT_EPI); sm.flags[0] = 1; }
+    float v[CPR];
+    dec_sum_slices<S, NCOL>(sm.recv, tid, v);
+    // Every copy into this CTA has landed; once all CTAs pass the final barrier, every copy out of
+    // this CTA's stage has too.
+    cluster_arrive();
+    __syncthreads();  // all slices summed before the epilogue reuses the receive buffer
+    if (nvalid > 0 && sm.flags[0] == 0) {
+      if constexpr (EPI == EPI_RESID) {
+        const int n = m0 + tid;
+        const float b = a.bias != nullptr ? a.bias[n] : 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPR; ++i)
+          if (i < nvalid)
+            a.out_f32[static_cast<size_t>(c0 + i) * a.ld_out + n] = __fadd_rn(pre[i], __fadd_rn(bf16_round(v[i]), b));
+      } else if constexpr (EPI == EPI_QKV) {
+        dec_epilogue_qkv<CPR>(a, v, c0, nvalid, m0, tid, sm.xs, pos0, pre, pre2);
+      } else if constexpr (EPI == EPI_SWIGLU) {
+        dec_epilogue_swiglu<CPR>(a, v, c0, nvalid, m0, tid, sm.xs);
+      } else {
+        float vv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) vv[i] = i < CPR ? v[i < CPR ? i : 0] : 0.0f;
+        gemm_epilogue_chunk_t<EPI>(a, vv, c0, nvalid, m0, tid, sm.xs, pos0);
+      }
+    }
+    cluster_wait();
   }
 }
 
+// One decode linear: CTA (m-tile, 1, split) of a grid whose z extent is the split-K factor S,
+// launched as clusters of S CTAs along z. Instantiated per epilogue and split factor so that each
+// kernel carries only the code it runs (the instruction cache is cold at every launch).
+template <int EPI, int S>
 __global__ void __launch_bounds__(128, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   const int stages = a.stages;
-  uint8_t* ring = smem;
-  uint8_t* sB = ring + dec_ring_bytes(stages);
-  float* stage = reinterpret_cast<float*>(smem);
-  float* recv = stage + 128 * kDecRows;
-  float* xs = recv;  // epilogue scratch, once the received slices are summed
+  DecSmem sm;
+  sm.ring = smem;
+  sm.sB = smem + dec_ring_bytes(stages);
+  sm.stage = reinterpret_cast<float*>(smem);
+  sm.recv = sm.stage + 128 * kDecRows;
+  sm.xs = sm.recv;  // epilogue scratch, once the received slices are summed
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + dec_body_bytes(stages, a.kb_per_split));
-  uint64_t* fullA = bars;
-  uint64_t* emptyA = bars + stages;
-  uint64_t* fullB = bars + 2 * stages;
-  uint64_t* accum = fullB + 1;
-  uint64_t* xbar = fullB + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fullB + 3);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] error
+  sm.fullA = bars;
+  sm.emptyA = bars + stages;
+  sm.fullB = bars + 2 * stages;
+  sm.accum = sm.fullB + 1;
+  sm.xbar = sm.fullB + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm.fullB + 3);
+  sm.flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] error
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
-  const int lane = tid & 31;
   const int m0 = blockIdx.x * 128;
   const int kb_total = a.K >> 6;
   const int kb0 = blockIdx.z * a.kb_per_split;
   const int nkb = max(0, min(a.kb_per_split, kb_total - kb0));
-  const int S = a.splits;
 
   if (tid == 0) {
-    for (int s = 0; s < stages; ++s) {
-      mbar_init(&fullA[s], 1);
-      mbar_init(&emptyA[s], 1);
+    for (int st = 0; st < stages; ++st) {
+      mbar_init(&sm.fullA[st], 1);
+      mbar_init(&sm.emptyA[st], 1);
     }
-    mbar_init(fullB, 1);
-    mbar_init(accum, 1);
-    mbar_init(xbar, 1);
-    flags[0] = 0;
+    mbar_init(sm.fullB, 1);
+    mbar_init(sm.accum, 1);
+    mbar_init(sm.xbar, 1);
+    sm.flags[0] = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -290,8 +433,8 @@ __global__ void __launch_bounds__(128, 1)
   if (tid == 0) {
     policy = l2_policy_evict_first();
     for (int i = 0; i < npre; ++i) {
-      mbar_expect_tx(&fullA[i], kDecABytes);
-      tma_load_2d_hint(ring + static_cast<size_t>(i) * kDecABytes, &tmA, &fullA[i], (kb0 + i) * 64, m0, policy);
+      mbar_expect_tx(&sm.fullA[i], kDecABytes);
+      tma_load_2d_hint(sm.ring + static_cast<size_t>(i) * kDecABytes, &tmA, &sm.fullA[i], (kb0 + i) * 64, m0, policy);
     }
   }
   if (warp == 0) {
@@ -308,158 +451,31 @@ __global__ void __launch_bounds__(128, 1)
   if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
   rows_valid = max(0, min(rows_valid, kDecRows));
   const int pos0 = a.pos0_dev != nullptr ? *a.pos0_dev : a.pos0;
-  const int ncol = rows_valid <= 32 ? 32 : 64;  // MMA N (uniform across the cluster)
-  const int cpr = ncol / S;                     // columns owned by each CTA of the cluster
-  const uint32_t rank = S > 1 ? cluster_ctarank() : 0u;
-  const int c0 = static_cast<int>(rank) * cpr;
-  const int nvalid = max(0, min(cpr, rows_valid - c0));
-  // Epilogue inputs that do not depend on the accumulator are fetched now, off the critical path:
-  // the residual rows this CTA will update, or the RoPE factors of its Q/K rows.
-  float pre[32], pre2[32];
-  const bool rope_tile = a.epi == EPI_QKV && (m0 >> 7) < a.nq + a.nkv;
-  if (S > 1 && a.epi == EPI_RESID) {
-    const int n = m0 + tid;
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-      pre[i] = i < nvalid ? __ldcg(a.out_f32 + static_cast<size_t>(c0 + i) * a.ld_out + n) : 0.0f;
-  } else if (S > 1 && rope_tile) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const size_t idx = static_cast<size_t>(pos0 + c0 + i) * 64 + (tid & 63);
-      pre[i] = i < nvalid ? __ldg(a.rope_cos + idx) : 0.0f;
-      pre2[i] = i < nvalid ? __ldg(a.rope_sin + idx) : 0.0f;
-    }
-  }
-  if (tid == 0) {
-    if (nkb > 0) {
-      mbar_expect_tx(fullB, static_cast<uint32_t>(nkb * kDecBBytes));
-      for (int i = 0; i < nkb; ++i) tma_load_2d(sB + i * kDecBBytes, &tmB, fullB, (kb0 + i) * 64, 0);
-    }
-    if (S > 1) mbar_expect_tx(xbar, static_cast<uint32_t>(S * 128 * cpr * 4));
-  }
-  griddep_launch_dependents();
+  // MMA width from the live row count, uniform across the cluster.
+  if (rows_valid <= 32) dec_run<EPI, S, 32>(&tmA, &tmB, a, sm, tmem, m0, kb0, nkb, npre, stages, policy, rows_valid, pos0);
+  else dec_run<EPI, S, 64>(&tmA, &tmB, a, sm, tmem, m0, kb0, nkb, npre, stages, policy, rows_valid, pos0);
 
-  if (warp == 0) {
-    if (lane == 0) {
-      bool ok = true;
-      for (int i = npre; i < nkb; ++i) {
-        const int s = i % stages;
-        if (!mbar_wait(&emptyA[s], ((i / stages) - 1) & 1)) { ok = false; break; }
-        mbar_expect_tx(&fullA[s], kDecABytes);
-        tma_load_2d_hint(ring + static_cast<size_t>(s) * kDecABytes, &tmA, &fullA[s], (kb0 + i) * 64, m0, policy);
-      }
-      if (!ok) { record_error(a.status, DEV_TIMEOUT_TMA); flags[0] = 1; }
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(128, ncol);
-      bool ok = nkb == 0 || mbar_wait(fullB, 0);
-      tc_fence_after();
-      for (int i = 0; i < nkb && ok; ++i) {
-        const int s = i % stages;
-        if (!mbar_wait(&fullA[s], (i / stages) & 1)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t a_addr = smem_u32(ring + static_cast<size_t>(s) * kDecABytes);
-        const uint32_t b_addr = smem_u32(sB + i * kDecBBytes);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_bf16(tmem, sdesc_kmajor_sw128(a_addr + kk * 32), sdesc_kmajor_sw128(b_addr + kk * 32), idesc,
-                    (i | kk) != 0 ? 1u : 0u);
-        umma_commit(&emptyA[s]);
-      }
-      if (!ok) { record_error(a.status, DEV_TIMEOUT_MMA); flags[0] = 1; }
-      umma_commit(accum);
-    }
-    __syncwarp();
-  }
-
-  bool acc_ok = true;
-  if (nkb > 0) acc_ok = mbar_wait(accum, 0);
-  tc_fence_after();
-  if (!acc_ok) { record_error(a.status, DEV_TIMEOUT_EPI); flags[0] = 1; }
-  const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  float acc[64];
-  if (acc_ok && nkb > 0) {
-    tmem_ld32(lane_addr, acc);
-    if (ncol == 64) tmem_ld32(lane_addr + 32, acc + 32);
-    else {
-#pragma unroll
-      for (int c = 32; c < 64; ++c) acc[c] = 0.0f;
-    }
-  } else {
-#pragma unroll
-    for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
-  }
-  if (S == 1) {
-    __syncthreads();
-    if (flags[0] == 0) {
-      gemm_epilogue_chunk(a, acc, 0, min(32, rows_valid), m0, tid, xs, pos0);
-      if (rows_valid > 32) gemm_epilogue_chunk(a, acc + 32, 32, rows_valid - 32, m0, tid, xs, pos0);
-    }
-  } else {
-    // Stage the partial as S contiguous slices and send slice p to CTA p. Inside a slice the
-    // columns are grouped in units of W = min(cpr, 4): [cpr / W][lane][W], so both the staging
-    // stores and the receiver's reads are bank-conflict free. The stage overlays this CTA's
-    // drained ring; the receive buffer overlays it too, so nothing is sent before every CTA of the
-    // cluster is past its MMAs (the cluster barrier below).
-    tc_fence_before();
-    __syncthreads();  // every warp is past its TMEM loads
-    if (cpr >= 4) {
-#pragma unroll
-      for (int j = 0; j < 64; j += 4) {
-        if (j < ncol) {
-          const int p = j / cpr, c = j - p * cpr;
-          *reinterpret_cast<float4*>(stage + p * 128 * cpr + ((c >> 2) * 128 + tid) * 4) =
-              make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 64; j += 2) {
-        if (j < ncol) *reinterpret_cast<float2*>(stage + (j >> 1) * 256 + tid * 2) = make_float2(acc[j], acc[j + 1]);
-      }
-    }
-    fence_proxy_async_smem();
-    cluster_sync();  // all stages written, every CTA's ring drained and receive barrier armed
-    const uint32_t slice_bytes = static_cast<uint32_t>(128 * cpr * 4);
-    if (tid < S) {
-      const uint32_t dst = cluster_map(smem_u32(recv) + rank * slice_bytes, static_cast<uint32_t>(tid));
-      const uint32_t bar = cluster_map(smem_u32(xbar), static_cast<uint32_t>(tid));
-      bulk_copy_to_peer(dst, smem_u32(stage) + tid * slice_bytes, slice_bytes, bar);
-    }
-    const bool got = mbar_wait(xbar, 0);
-    if (!got) { record_error(a.status, DEV_TIMEOUT_EPI); flags[0] = 1; }
-    float v[32];
-    if (ncol == 32) dec_sum_any<32>(S, recv, tid, v);
-    else dec_sum_any<64>(S, recv, tid, v);
-    // Every copy into this CTA has landed; once all CTAs pass the final barrier, every copy out of
-    // this CTA's stage has too.
-    cluster_arrive();
-    __syncthreads();  // all slices summed before the epilogue reuses the receive buffer
-    if (nvalid > 0 && flags[0] == 0) {
-      if (a.epi == EPI_RESID) {
-        const int n = m0 + tid;
-        const float b = a.bias != nullptr ? a.bias[n] : 0.0f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nvalid)
-            a.out_f32[static_cast<size_t>(c0 + i) * a.ld_out + n] = __fadd_rn(pre[i], __fadd_rn(bf16_round(v[i]), b));
-      } else if (a.epi == EPI_QKV || a.epi == EPI_SWIGLU) {
-        dec_epilogue(a, v, cpr, c0, nvalid, m0, tid, xs, pos0, pre, pre2);
-      } else {
-        gemm_epilogue_chunk(a, v, c0, nvalid, m0, tid, xs, pos0);
-      }
-    }
-    cluster_wait();
-  }
-  if (flags[0] != 0 && tid == 0) {
-    for (int s = 0; s < npre; ++s) mbar_wait(&fullA[s], 0);
-    if (nkb > 0) mbar_wait(fullB, 0);
+  if (sm.flags[0] != 0 && tid == 0) {
+    for (int st = 0; st < npre; ++st) mbar_wait(&sm.fullA[st], 0);
+    if (nkb > 0) mbar_wait(sm.fullB, 0);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 64);
+}
+
+using DecGemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmArgs);
+
+// The instantiation for an epilogue kind and split factor (nullptr if not instantiated).
+inline DecGemmKernel dec_gemm_kernel(int epi, int S) {
+#define DRT_DEC_ROW(E) \
+  { gemm_decode_kernel<E, 1>, gemm_decode_kernel<E, 2>, gemm_decode_kernel<E, 4>, gemm_decode_kernel<E, 8>, gemm_decode_kernel<E, 16> }
+  static const DecGemmKernel table[4][5] = {DRT_DEC_ROW(EPI_STORE_F32), DRT_DEC_ROW(EPI_RESID), DRT_DEC_ROW(EPI_SWIGLU),
+                                            DRT_DEC_ROW(EPI_QKV)};
+#undef DRT_DEC_ROW
+  const int si = S == 1 ? 0 : S == 2 ? 1 : S == 4 ? 2 : S == 8 ? 3 : S == 16 ? 4 : -1;
+  if (epi < 0 || epi > EPI_QKV || si < 0) return nullptr;
+  return table[epi][si];
 }
 
 }  // namespace drt

@@ -130,6 +130,16 @@ def _algorithmic_bytes(cfg: dict, w: dict, trace_kv: list[int]) -> float:
     return wb + kv + w["block"] * kvp
 
 
+def _measured_traffic(alg_bytes: float) -> float | None:
+    """DRAM bytes per denoising step from the committed ncu capture (profiles/), scaled from the
+    captured K/V length to this run's algorithmic bytes (traffic grows with the bytes streamed)."""
+    p = ROOT / "profiles" / "decode_step_cfg1_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return float(d["dram_bytes_per_step"]) * alg_bytes / float(d["algorithmic_bytes_per_step"])
+
+
 def _run_ours(args, world, rank, local) -> dict | None:
     import torch
 
@@ -220,7 +230,9 @@ def _run_ours(args, world, rank, local) -> dict | None:
         "roofline": {"bound": "hbm", "kernel": "one denoising step (CUDA graph of the step's kernels)",
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
-                     "algorithmic_bytes_per_step": int(alg), "traffic": None},
+                     "algorithmic_bytes_per_step": int(alg),
+                     "traffic": (int(_measured_traffic(alg)) if _measured_traffic(alg) else None),
+                     "traffic_note": "DRAM bytes per step from profiles/decode_step_cfg1_traffic.json scaled to this K/V length"},
         "e2e": {"value": round(world * committed / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
                 "h2d_bytes_per_step": 4 * (w["prompt"] + w["gen"]),
                 "d2h_bytes_per_step": 4 * (w["prompt"] + w["gen"]) + 512},
@@ -231,7 +243,7 @@ def _run_ours(args, world, rank, local) -> dict | None:
     return line
 
 
-def _cpu_baseline(args, sample_layers: int = 2) -> dict:
+def _cpu_baseline(args, sample_layers: int = 1) -> dict:
     """The reference's CPU algorithm (float64 executable-spec forward over the whole window,
     float64 max-prob selector) for one denoising step of the workload, timed on this host."""
     from oracle import forward as ofwd

@@ -10,7 +10,12 @@ seeded requests run one per GPU (request-parallel, weak scaling, no collective o
 One bench step = one complete request: prompt upload, prefill, every denoising step (forward,
 selector, policy, commit on the GPU), canvas download.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg0]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg0|cfg4]
+
+--workload cfg4 is the isolated unmask-selector microbenchmark: fp32 logits
+[B, L, 151936] ~ N(0, 3^2) from a seed, a Bernoulli(0.5) mask of masked positions, max-prob and
+entropy confidence over the masked rows, then top-k (k = 1, 4, 8) and threshold-0.9 choices per
+batch item; reported as HBM GB/s of the logits the selector must read (the masked rows once).
 """
 from __future__ import annotations
 
@@ -298,17 +303,167 @@ def _cpu_baseline(args, sample_layers: int = 1) -> dict:
                        f"{w['block']} frontier rows); measured {t_fwd + t_sel + t_head:.1f} s")}
 
 
+SEL_V = 151936
+SEL_SHAPES = [(1, 32), (1, 256), (8, 32), (8, 256)]
+
+
+def _selector_case(B: int, L: int, seed: int, device):
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    logits = torch.randn(B * L, SEL_V, generator=g, device=device, dtype=torch.float32) * 3.0
+    mask = torch.rand(B, L, generator=g, device=device) < 0.5
+    rows = torch.nonzero(mask.reshape(-1)).reshape(-1).to(torch.int32)
+    counts = mask.sum(1).tolist()
+    offsets = torch.tensor(np.concatenate([[0], np.cumsum(counts)]), dtype=torch.int32, device=device)
+    return logits, mask, rows, offsets
+
+
+def _run_selector(args, world, rank, local) -> dict | None:
+    """cfg4: selector + choices over the masked rows; CUDA-event time per step, L2 flushed between
+    steps (a 256 MB write) so every variant reads its logits from HBM."""
+    import torch
+
+    from diffusorrt_b200 import _lib, build, kernels
+
+    if rank == 0:
+        build.build()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        build.build()
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    variants = {}
+    launches = 0
+    headline = None
+    for B, L in SEL_SHAPES:
+        logits, mask, rows, offsets = _selector_case(B, L, 1000 * B + L + rank, dev)
+        n = rows.numel()
+        scratch = kernels.selector_scratch(n, SEL_V, dev)
+        conf = torch.empty(n, dtype=torch.float64, device=dev)
+        tok = torch.empty(n, dtype=torch.int32, device=dev)
+        chosen = torch.empty(n, dtype=torch.int32, device=dev)
+        tie = torch.empty(B, dtype=torch.int32, device=dev)
+        for mode_name, mode in (("max_prob", _lib.SELECT_MAX_PROB), ("entropy", _lib.SELECT_NEG_ENTROPY)):
+            def step():
+                kernels.select_gather(logits, rows, mode=mode, temperature=1.0, scratch=scratch, conf=conf, token=tok)
+                for k in (1, 4, 8):
+                    kernels.select_choices(conf, offsets, mode=kernels.CHOICE_TOPK, k=k, chosen=chosen, tie=tie)
+                kernels.select_choices(conf, offsets, mode=kernels.CHOICE_THRESHOLD, tau=0.9, chosen=chosen, tie=tie)
+            for _ in range(args.warmup):
+                step()
+            torch.cuda.synchronize()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+            for e0, e1 in ev:
+                flush.fill_(1)
+                e0.record()
+                step()
+                e1.record()
+            torch.cuda.synchronize()
+            ms = float(np.mean([e0.elapsed_time(e1) for e0, e1 in ev]))
+            alg = n * SEL_V * 4
+            gbs = alg / (ms * 1e-3) / 1e9
+            launches += args.steps * (5 + (1 if mode == _lib.SELECT_NEG_ENTROPY else 0))
+            variants[f"B{B}_L{L}_{mode_name}"] = {"masked_rows": n, "us_per_step": round(ms * 1e3, 2),
+                                                   "GB_per_s": round(gbs, 1)}
+            if (B, L, mode_name) == (8, 256, "max_prob"):
+                headline = (ms, alg, n, logits, rows, offsets, mask)
+    ms, alg, n, logits, rows, offsets, mask = headline
+    # End to end through the C ABI from pinned host memory: the [B, L, V] logits and the masked-row
+    # list go up, the choices come back.
+    host_logits = logits.cpu().pin_memory()
+    host_rows = rows.cpu().pin_memory()
+    host_off = offsets.cpu().pin_memory()
+    d_logits = torch.empty_like(logits)
+    d_rows = torch.empty_like(rows)
+    d_off = torch.empty_like(offsets)
+    scratch = kernels.selector_scratch(n, SEL_V, dev)
+    conf = torch.empty(n, dtype=torch.float64, device=dev)
+    tok = torch.empty(n, dtype=torch.int32, device=dev)
+    chosen = torch.empty(n, dtype=torch.int32, device=dev)
+    tie = torch.empty(8, dtype=torch.int32, device=dev)
+    host_chosen = torch.empty(n, dtype=torch.int32).pin_memory()
+    e2e = []
+    for i in range(args.warmup + args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        d_logits.copy_(host_logits, non_blocking=True)
+        d_rows.copy_(host_rows, non_blocking=True)
+        d_off.copy_(host_off, non_blocking=True)
+        kernels.select_gather(d_logits, d_rows, mode=_lib.SELECT_MAX_PROB, scratch=scratch, conf=conf, token=tok)
+        kernels.select_choices(conf, d_off, mode=kernels.CHOICE_TOPK, k=1, chosen=chosen, tie=tie)
+        host_chosen.copy_(chosen, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            e2e.append(e0.elapsed_time(e1))
+    e2e_ms = float(np.mean(e2e))
+    if rank != 0:
+        return None
+    peaks = _peaks()
+    gbs = alg / (ms * 1e-3) / 1e9
+    return {
+        "metric": "unmask selector throughput (cfg4: fp32 [B, L, 151936] logits, 50% masked, softmax confidence + "
+                  "top-k/threshold choices)",
+        "value": round(world * gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0, 3^2) logits, Bernoulli(0.5) mask)",
+        "config": {"workload": "cfg4: B 8, L 256, V 151936, max-prob, top-k 1/4/8 + threshold 0.9 per step",
+                   "masked_rows": n, "l2": "flushed before every timed step (256 MB write)", "variants": variants},
+        "roofline": {"bound": "hbm", "kernel": "sel_pass1_kernel + sel_choose_kernel (one step)",
+                     "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                     "algorithmic_bytes_per_step": int(alg), "traffic": None},
+        "e2e": {"value": round(world * alg / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": int(logits.numel() * 4 + rows.numel() * 4 + offsets.numel() * 4),
+                "d2h_bytes_per_step": int(n * 4)},
+        "gpu_launches": launches,
+    }
+
+
+def _cpu_selector_baseline(sample_rows: int = 48) -> dict:
+    """The reference selector restated (float64 NumPy, one thread) on a sample of cfg4 rows."""
+    from oracle import selector as osel
+
+    rng = np.random.default_rng(7)
+    rows = (rng.standard_normal((sample_rows, SEL_V), dtype=np.float32) * np.float32(3.0)).astype(np.float32)
+    t0 = time.perf_counter()
+    conf, _ = osel.max_prob_rows(rows)
+    for k in (1, 4, 8):
+        osel.topk_choices(conf, k)
+    osel.threshold_choices(conf, 0.9)
+    dt = time.perf_counter() - t0
+    return {"GB_per_s": sample_rows * SEL_V * 4 / dt / 1e9, "seconds": dt,
+            "sample": f"{sample_rows} rows of 151936 fp32 logits: max-prob confidence, top-k 1/4/8 and threshold choices"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cfg1", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="cfg1", choices=sorted(WORKLOADS) + ["cfg4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world, rank, local = _dist()
+    if args.impl == "reference" and args.workload == "cfg4":
+        if rank != 0:
+            return
+        samples = [_cpu_selector_baseline() for _ in range(max(1, min(args.steps, 3)))]
+        gbs = float(np.mean([x["GB_per_s"] for x in samples]))
+        cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+        print(json.dumps({"metric": "unmask selector throughput (cfg4)", "impl": "reference", "value": round(gbs, 3),
+                          "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+                          "data": "synthetic", "config": {"workload": "cfg4"},
+                          "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                                           "sample": samples[0]["sample"]},
+                          "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
     if args.impl == "reference":
         if rank != 0:
             return
@@ -335,6 +490,18 @@ def main():
 
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
+    if args.workload == "cfg4":
+        line = _run_selector(args, world, rank, local)
+        if rank == 0 and line is not None:
+            if not args.no_cpu_baseline and world == 1:
+                cb = _cpu_selector_baseline()
+                line["cpu_baseline"] = {"value": round(cb["GB_per_s"], 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                                        "sample": cb["sample"]}
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
     line = _run_ours(args, world, rank, local)
     if rank == 0 and line is not None:
         if not args.no_cpu_baseline and world == 1:

@@ -117,6 +117,10 @@ SIGNATURES = {
                                          ctypes.c_double, _P, _P, _P, _P]),
     "drt_selector_rows_noalloc": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                                  ctypes.c_double, _P, _P, _P]),
+    "drt_selector_gather": (ctypes.c_int, [_P, ctypes.c_int64, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                           ctypes.c_double, _P, _P, _P, _P]),
+    "drt_select_choices": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
+                                          ctypes.c_double, _P, _P, _P]),
     "drt_linear_scratch_bytes": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     "drt_linear_bf16": (ctypes.c_int, [_P, _P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.c_int32, _P, _P]),

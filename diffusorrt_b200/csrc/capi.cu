@@ -1468,6 +1468,57 @@ extern "C" int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows
   return DRT_OK;
 }
 
+extern "C" int drt_selector_gather(const float* logits, int64_t ld, const int32_t* row_index, int32_t n_rows, int32_t vocab,
+                                   int32_t mode, double temperature, void* scratch, double* conf, int32_t* token, void* stream) {
+  REQUIRE(logits && row_index && scratch && conf && token, "null argument");
+  REQUIRE(n_rows >= 0 && vocab >= 1 && ld >= vocab, "bad selector geometry");
+  REQUIRE(mode == DRT_SELECT_MAX_PROB || mode == DRT_SELECT_NEG_ENTROPY, "unknown selector mode %d", mode);
+  if (n_rows == 0) return DRT_OK;
+  REQUIRE(n_rows <= 65535, "at most 65535 rows per call");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int chunks = (vocab + kSelChunk - 1) / kSelChunk;
+  const size_t np = static_cast<size_t>(n_rows) * chunks;
+  uint8_t* p = static_cast<uint8_t*>(scratch);
+  auto take = [&](size_t bytes) { uint8_t* q = p; p += (bytes + 255) & ~size_t(255); return q; };
+  SelArgs a;
+  memset(&a, 0, sizeof(a));
+  a.part_sum = reinterpret_cast<double*>(take(np * 8));
+  a.row_amax = reinterpret_cast<double*>(take(static_cast<size_t>(n_rows) * 8));
+  a.row_sum = reinterpret_cast<double*>(take(static_cast<size_t>(n_rows) * 8));
+  a.part_max = reinterpret_cast<float*>(take(np * 4));
+  a.part_idx = reinterpret_cast<int*>(take(np * 4));
+  a.counters = reinterpret_cast<int*>(take(static_cast<size_t>(n_rows) * 4));
+  CK(cudaMemsetAsync(a.counters, 0, sizeof(int) * n_rows, st));
+  a.logits = logits;
+  a.ld = ld;
+  a.row_index = row_index;
+  a.rows = n_rows;
+  a.vocab = vocab;
+  a.chunk = kSelChunk;
+  a.nchunks = chunks;
+  a.mode = mode;
+  a.temperature = mode == DRT_SELECT_NEG_ENTROPY ? temperature : 0.0;
+  a.exclude = -1;
+  a.conf = conf;
+  a.token = token;
+  CK(launch_k(sel_pass1_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  if (mode == DRT_SELECT_NEG_ENTROPY) CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  return DRT_OK;
+}
+
+extern "C" int drt_select_choices(const double* conf, const int32_t* offsets, int32_t n_items, int32_t mode, int32_t k,
+                                  double tau, double tie_rel, int32_t* chosen, int32_t* tie, void* stream) {
+  REQUIRE(conf && offsets && chosen && tie, "null argument");
+  REQUIRE(n_items >= 0 && n_items <= 65535, "n_items outside [0, 65535]");
+  REQUIRE(mode == CHOICE_TOPK || mode == CHOICE_THRESHOLD, "unknown choice mode %d", mode);
+  REQUIRE(mode != CHOICE_TOPK || k >= 0, "k must be >= 0");
+  REQUIRE(tie_rel >= 0.0, "tie_rel must be >= 0");
+  if (n_items == 0) return DRT_OK;
+  CK(launch_k(sel_choose_kernel, dim3(n_items), dim3(32), 0, static_cast<cudaStream_t>(stream), false, conf, offsets, mode, k, tau,
+              tie_rel, chosen, tie));
+  return DRT_OK;
+}
+
 extern "C" size_t drt_linear_scratch_bytes(int32_t rows, int32_t n, int32_t K, int32_t splits) {
   (void)rows;
   (void)n;

@@ -207,4 +207,108 @@ __global__ void __launch_bounds__(kSelThreads) sel_entropy_kernel(const SelArgs 
   a.counters[r] = 0;
 }
 
+// Batched choice over per-item confidence runs (the selector's output for each batch item's
+// masked positions, row offsets[b] .. offsets[b + 1]). One warp per item.
+//   top-k (_topk_count_choices, python/src/edllm/backends/diffusion_runtime.py:290-299): the k
+//     highest confidences, the lowest row first among equal values;
+//   threshold (_threshold_choices, :302-314): every row with conf >= tau, else the first argmax.
+// chosen[row] = 1 for committed rows, 0 otherwise. tie[b] certifies the decision like the device
+// decode policy: TIE bit 1 (near) when the k-th / (k+1)-th gap, or any |conf - tau| (and, without a
+// hit, the top-1 / top-2 gap), is within tie_rel relative; bit 2 (exact) when those values are
+// equal. Those are the only items where NumPy's unstable argsort or its own last-bit rounding of
+// the confidence may decide differently.
+enum ChoiceMode : int { CHOICE_TOPK = 0, CHOICE_THRESHOLD = 1 };
+
+__device__ __forceinline__ void warp_best(double v, int i, double& bv, int& bi) {
+  bv = v;
+  bi = i;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (v2 > bv || (v2 == bv && i2 < bi)) {
+      bv = v2;
+      bi = i2;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(32) sel_choose_kernel(const double* __restrict__ conf, const int* __restrict__ offsets,
+                                                        int mode, int k, double tau, double tie_rel, int* chosen, int* tie) {
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x;
+  const int r0 = offsets[b], r1 = offsets[b + 1];
+  const int n = r1 - r0;
+  for (int i = lane; i < n; i += 32) chosen[r0 + i] = 0;
+  __syncwarp();
+  int flag = 0;
+  if (n <= 0) {
+    if (lane == 0) tie[b] = 0;
+    return;
+  }
+  if (mode == CHOICE_TOPK) {
+    const int kk = min(k, n);
+    double prev = 0.0;
+    for (int round = 0; round <= kk && round < n; ++round) {
+      // best remaining row: lane-local scan, then warp reduction (lowest index among equals)
+      double bv = -INFINITY;
+      int bi = INT_MAX;
+      for (int i = lane; i < n; i += 32) {
+        if (chosen[r0 + i]) continue;
+        const double v = conf[r0 + i];
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+      }
+      double wv;
+      int wi;
+      warp_best(bv, bi, wv, wi);
+      if (round < kk) {
+        if (lane == 0) chosen[r0 + wi] = 1;
+        __syncwarp();
+        prev = wv;
+      } else {
+        // rank k + 1: certify the cut
+        if (wv == prev) flag |= 2;
+        else if (!(prev - wv > tie_rel * fabs(prev))) flag |= 1;
+      }
+    }
+  } else {
+    int hits = 0;
+    for (int i = lane; i < n; i += 32) {
+      const double v = conf[r0 + i];
+      if (v >= tau) {
+        chosen[r0 + i] = 1;
+        ++hits;
+      }
+      if (!(fabs(v - tau) > tie_rel * fabs(tau))) flag |= (v == tau) ? 2 : 1;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      hits += __shfl_xor_sync(0xffffffffu, hits, o);
+      flag |= __shfl_xor_sync(0xffffffffu, flag, o);
+    }
+    if (hits == 0) {
+      double bv = -INFINITY, sv = -INFINITY;
+      int bi = INT_MAX;
+      for (int i = lane; i < n; i += 32) {
+        const double v = conf[r0 + i];
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+      }
+      double wv;
+      int wi;
+      warp_best(bv, bi, wv, wi);
+      // second best (excluding the winner's row)
+      for (int i = lane; i < n; i += 32)
+        if (i != wi) sv = fmax(sv, conf[r0 + i]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sv = fmax(sv, __shfl_xor_sync(0xffffffffu, sv, o));
+      if (lane == 0) chosen[r0 + wi] = 1;
+      if (n > 1) {
+        if (sv == wv) flag |= 2;
+        else if (!(wv - sv > tie_rel * fabs(wv))) flag |= 1;
+      }
+    }
+  }
+  if (lane == 0) tie[b] = flag;
+}
+
 }  // namespace drt

@@ -40,6 +40,51 @@ def select_rows(logits: torch.Tensor, *, mode: int = _lib.SELECT_MAX_PROB, tempe
     return conf, token
 
 
+CHOICE_TOPK = 0
+CHOICE_THRESHOLD = 1
+
+
+def select_gather(logits: torch.Tensor, row_index: torch.Tensor, *, mode: int = _lib.SELECT_MAX_PROB,
+                  temperature: float = 0.0, scratch: torch.Tensor | None = None, conf: torch.Tensor | None = None,
+                  token: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None):
+    """(confidence f64, token i32) for the rows row_index (int32 CUDA) of f32 logits [rows, vocab]."""
+    if logits.dtype != torch.float32 or not logits.is_cuda or logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a row-major CUDA float32 [rows, vocab] tensor")
+    if row_index.dtype != torch.int32 or not row_index.is_cuda or not row_index.is_contiguous():
+        raise ValueError("row_index must be a contiguous CUDA int32 tensor")
+    n = row_index.numel()
+    vocab = logits.shape[1]
+    dev = logits.device
+    if scratch is None:
+        scratch = selector_scratch(n, vocab, dev)
+    if conf is None:
+        conf = torch.empty(n, dtype=torch.float64, device=dev)
+    if token is None:
+        token = torch.empty(n, dtype=torch.int32, device=dev)
+    _lib.check(_lib.load().drt_selector_gather(logits.data_ptr(), logits.stride(0), row_index.data_ptr(), n, vocab,
+                                               int(mode), float(temperature), scratch.data_ptr(), conf.data_ptr(),
+                                               token.data_ptr(), _stream_ptr(stream)))
+    return conf, token
+
+
+def select_choices(conf: torch.Tensor, offsets: torch.Tensor, *, mode: int, k: int = 1, tau: float = 0.9,
+                   tie_rel: float = 2.0 ** -40, chosen: torch.Tensor | None = None, tie: torch.Tensor | None = None,
+                   stream: torch.cuda.Stream | None = None):
+    """Top-k (mode CHOICE_TOPK) or threshold (CHOICE_THRESHOLD) choices per confidence run
+    offsets[b] .. offsets[b + 1]: chosen[row] in {0, 1} (int32) and tie[b] certification bits."""
+    if conf.dtype != torch.float64 or offsets.dtype != torch.int32:
+        raise ValueError("conf must be float64 and offsets int32 CUDA tensors")
+    n_items = offsets.numel() - 1
+    if chosen is None:
+        chosen = torch.empty(conf.numel(), dtype=torch.int32, device=conf.device)
+    if tie is None:
+        tie = torch.empty(max(1, n_items), dtype=torch.int32, device=conf.device)
+    _lib.check(_lib.load().drt_select_choices(conf.data_ptr(), offsets.data_ptr(), n_items, int(mode), int(k),
+                                              float(tau), float(tie_rel), chosen.data_ptr(), tie.data_ptr(),
+                                              _stream_ptr(stream)))
+    return chosen, tie
+
+
 def linear_bf16(x: torch.Tensor, w: torch.Tensor, *, splits: int = 1, round_bf16: bool = True,
                 out: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
                 stream: torch.cuda.Stream | None = None) -> torch.Tensor:

@@ -209,6 +209,20 @@ void drt_session_close(drt_session* s);
 size_t drt_selector_scratch_bytes(int32_t n_rows, int32_t vocab);
 int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows, int32_t vocab, int32_t mode,
                       double temperature, void* scratch, double* conf, int32_t* token, void* stream);
+/* The selector over gathered rows: row r reads logits row row_index[r] (device int32), the way the
+ * reference scores only the masked frontier (diffusion_runtime.py:1946-1949 gathers the masked
+ * rows, then _raw_max_prob_confidence :136-165 / _entropy_confidence :90-114 score them).
+ * Same scratch, modes and outputs as drt_selector_rows. */
+int drt_selector_gather(const float* logits, int64_t ld, const int32_t* row_index, int32_t n_rows, int32_t vocab,
+                        int32_t mode, double temperature, void* scratch, double* conf, int32_t* token, void* stream);
+/* Commit choices for a batch of confidence runs: item b owns rows offsets[b] .. offsets[b + 1]
+ * (device int32, n_items + 1 entries). mode 0 = top-k (_topk_count_choices,
+ * diffusion_runtime.py:290-299: the k highest, lowest row first among equals), mode 1 =
+ * threshold (_threshold_choices, :302-314: conf >= tau, else the first argmax). Writes
+ * chosen[row] in {0, 1} and tie[b]: bit 1 when the deciding gap (k-th vs (k+1)-th, |conf - tau|,
+ * or top-1 vs top-2 without a hit) is within tie_rel relative, bit 2 when it is an exact tie. */
+int drt_select_choices(const double* conf, const int32_t* offsets, int32_t n_items, int32_t mode, int32_t k, double tau,
+                       double tie_rel, int32_t* chosen, int32_t* tie, void* stream);
 /* The same selector without any device allocation, for callers that may not allocate device
  * memory: a host whose GPU memory is owned by its own pool or fixed budget (outside of which it
  * may not cudaMalloc), or a latency-critical caller that cannot afford cudaMalloc's implicit

@@ -40,6 +40,9 @@ WORKLOADS = {
     "cfg1": dict(prompt=4096, gen=512, block=32, strategy="block_threshold", steps=128, rounds=8, tau=0.9),
     # prompt 64, 128 new tokens, 32 rounds per block, top-1 fixed quota.
     "cfg0": dict(prompt=64, gen=128, block=32, strategy="bd3_fixed_quota", steps=128, rounds=0, tau=0.9),
+    # the cfg0 model with 4-bit affine (group 64) layer linears and lm_head,
+    # prompt 512, 256 new tokens, 128 steps = 8 blocks x 16 rounds, 2 commits per round.
+    "cfg3": dict(prompt=512, gen=256, block=32, strategy="bd3_fixed_quota", steps=128, rounds=0, tau=0.9, quant=True),
 }
 
 
@@ -113,11 +116,16 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def _weight_bytes(cfg: dict) -> int:
+def _weight_bytes(cfg: dict, quant: bool = False) -> int:
+    """Weight bytes one denoising step streams: bf16 linears and lm_head, or (quant) their 4-bit
+    nibbles plus a bf16 scale and bias per group of 64 inputs."""
     H, I, V = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
     qd, kd = cfg["attention_heads"] * cfg["head_dim"], cfg["num_kv_heads"] * cfg["head_dim"]
     per_layer = H * (qd + 2 * kd) + qd * H + 2 * I * H + I * H
-    return 2 * (cfg["layer_count"] * per_layer + V * H)
+    params = cfg["layer_count"] * per_layer + V * H
+    if quant:
+        return params // 2 + (params // 64) * 4
+    return 2 * params
 
 
 def _kv_bytes_per_pos(cfg: dict) -> int:
@@ -127,7 +135,7 @@ def _kv_bytes_per_pos(cfg: dict) -> int:
 def _algorithmic_bytes(cfg: dict, w: dict, trace_kv: list[int]) -> float:
     """Average HBM bytes one denoising step must move: every weight once, the visible K/V of
     the forwarded rows once, the active block's K/V written once."""
-    wb = _weight_bytes(cfg)
+    wb = _weight_bytes(cfg, bool(w.get("quant")))
     kvp = _kv_bytes_per_pos(cfg)
     if not trace_kv:
         return float(wb)
@@ -161,8 +169,9 @@ def _run_ours(args, world, rank, local) -> dict | None:
     w = WORKLOADS[args.workload]
     cfg = dict(QWEN3_06B_BD3LM)
     max_seq = ((w["prompt"] + w["gen"] + 127) // 128) * 128
+    engine = {"linear_quant_bits": 4, "linear_quant_group_size": 64} if w.get("quant") else None
     rt = Runtime(model_config=cfg, synthetic_seed=0, device_ordinal=local, max_seq=max_seq,
-                 max_prefill_rows=min(4096, ((w["prompt"] + 127) // 128) * 128))
+                 max_prefill_rows=min(4096, ((w["prompt"] + 127) // 128) * 128), engine_config=engine)
     sess = rt.session({"decode_strategy": w["strategy"], "block_size": w["block"]})
     prompt = [int(t) for t in np.random.default_rng(rank).integers(0, 151643, size=w["prompt"])]
 
@@ -225,18 +234,20 @@ def _run_ours(args, world, rank, local) -> dict | None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded random-init weights and prompts)",
-        "config": {"workload": f"{args.workload}: Qwen3-0.6B-arch BD3LM, prompt {w['prompt']}, gen {w['gen']}, "
-                               f"block {w['block']}, {w['strategy']}"
+        "config": {"workload": f"{args.workload}: Qwen3-0.6B-arch BD3LM{' (4-bit affine g64 linears + lm_head)' if w.get('quant') else ''}, "
+                               f"prompt {w['prompt']}, gen {w['gen']}, block {w['block']}, {w['strategy']}"
                                + (f" tau {w['tau']} rounds/block {w['rounds']}" if w["strategy"] == "block_threshold" else
                                   f" steps {w['steps']}"),
                    "requests_per_gpu": 1, "parallelism": f"request-parallel x{world}",
                    "committed_tokens_per_request": committed, "denoising_steps_per_request": forwards,
-                   "l2": "inputs larger than L2: 1.19 GB of weights streamed every denoising step"},
+                   "l2": (f"inputs larger than L2: {_weight_bytes(cfg, bool(w.get('quant'))) / 1e9:.2f} GB of weights "
+                          "streamed every denoising step")},
         "roofline": {"bound": "hbm", "kernel": "one denoising step (CUDA graph of the step's kernels)",
+                     "weights": "4-bit affine" if w.get("quant") else "bf16",
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
                      "algorithmic_bytes_per_step": int(alg),
-                     "traffic": (int(_measured_traffic(alg)) if _measured_traffic(alg) else None),
+                     "traffic": (int(_measured_traffic(alg)) if _measured_traffic(alg) and not w.get("quant") else None),
                      "traffic_note": "DRAM bytes per step from profiles/decode_step_cfg1_traffic.json scaled to this K/V length"},
         "e2e": {"value": round(world * committed / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
                 "h2d_bytes_per_step": 4 * (w["prompt"] + w["gen"]),
@@ -471,7 +482,7 @@ def main():
         samples = [_cpu_baseline(args) for _ in range(max(1, min(args.steps, 2)))]
         step_s = float(np.mean([s["step_s"] for s in samples]))
         steps_per_request = 16 * 8 if args.workload == "cfg1" else 128
-        tokens_per_request = 16 * 8 if args.workload == "cfg1" else 128
+        tokens_per_request = {"cfg1": 16 * 8, "cfg3": 256}.get(args.workload, 128)
         value = tokens_per_request / (step_s * steps_per_request)
         line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * steps_per_request * 1e3,

@@ -98,6 +98,7 @@ SIGNATURES = {
     "drt_model_set_rope": (ctypes.c_int, [_P, _P, _P, ctypes.c_int32]),
     "drt_model_device_bytes": (ctypes.c_int64, [_P]),
     "drt_model_destroy": (None, [_P]),
+    "drt_model_quantize": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32]),
     "drt_session_open": (ctypes.c_int, [_P, ctypes.POINTER(SessionConfig), ctypes.POINTER(_P)]),
     "drt_session_start": (ctypes.c_int, [_P, _I32P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                          ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_double,
@@ -121,6 +122,9 @@ SIGNATURES = {
                                            ctypes.c_double, _P, _P, _P, _P]),
     "drt_select_choices": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
                                           ctypes.c_double, _P, _P, _P]),
+    "drt_quantize_q4": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int32, _P, _P, _P, _P]),
+    "drt_linear_q4": (ctypes.c_int, [_P, _P, _P, _P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                     _P]),
     "drt_linear_scratch_bytes": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     "drt_linear_bf16": (ctypes.c_int, [_P, _P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.c_int32, _P, _P]),

@@ -24,6 +24,7 @@
 #include "gemm.cuh"
 #include "gemm_decode.cuh"
 #include "policy.cuh"
+#include "quant.cuh"
 #include "rowops.cuh"
 #include "selector.cuh"
 
@@ -106,6 +107,22 @@ int map_matrix(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, i
   const uint64_t strides[1] = {static_cast<uint64_t>(cols) * 2};
   const uint32_t box[2] = {64, static_cast<uint32_t>(box_rows)};
   return make_map(map, base, 2, dims, strides, box);
+}
+
+// Row-major uint8 matrix [rows][cols_bytes] (packed 4-bit weights), box {box_cols bytes, box_rows},
+// no swizzle: a box lands as box_rows contiguous rows of box_cols bytes.
+int map_u8(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_bytes, int box_cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return set_error(DRT_INTERNAL_ERROR, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || cols_bytes % 16 != 0 || box_cols % 16 != 0)
+    return set_error(DRT_INTERNAL_ERROR, "packed weight map alignment");
+  cuuint64_t d[2] = {static_cast<cuuint64_t>(cols_bytes), static_cast<cuuint64_t>(rows)};
+  cuuint64_t st[1] = {static_cast<cuuint64_t>(cols_bytes)};
+  cuuint32_t b[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)}, e[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(DRT_INTERNAL_ERROR, "cuTensorMapEncodeTiled (u8) failed (%d)", static_cast<int>(r));
+  return DRT_OK;
 }
 
 thread_local int64_t g_launches = 0;  // kernels enqueued by this thread (launch accounting)
@@ -193,9 +210,10 @@ int configure_kernels() {
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDaSmemBytes)) != cudaSuccess)
       result = DRT_INTERNAL_ERROR;
+    for (int qi = 0; qi < 2 && result == DRT_OK; ++qi)
     for (int epi = 0; epi <= EPI_QKV && result == DRT_OK; ++epi)
       for (int sp = 1; sp <= 16 && result == DRT_OK; sp *= 2) {
-        DecGemmKernel k = dec_gemm_kernel(epi, sp);
+        DecGemmKernel k = dec_gemm_kernel(epi, sp, qi == 1);
         if (k == nullptr || cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
             cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
           result = DRT_INTERNAL_ERROR;
@@ -218,10 +236,20 @@ constexpr double kTieRel = 9.094947017729282e-13;  // 2^-40
 }  // namespace
 
 // ======================================================================= model
+// 4-bit affine copy of one linear weight [n][K] (quant.cuh): packed nibbles [n][K / 2], bf16 scale
+// and bias [n][K / 64], and the TMA map over the packed bytes (box: 64 inputs x 128 rows).
+struct QuantW {
+  uint8_t* q = nullptr;
+  __nv_bfloat16* scale = nullptr;
+  __nv_bfloat16* bias = nullptr;
+  CUtensorMap map;
+};
+
 struct LayerW {
   __nv_bfloat16 *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr;
   float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *bqkv = nullptr;
   CUtensorMap m_qkv, m_o, m_gu, m_down;
+  QuantW q_qkv, q_o, q_gu, q_down;
 };
 
 struct drt_model {
@@ -235,6 +263,8 @@ struct drt_model {
   float* final_norm = nullptr;
   std::vector<LayerW> layers;
   CUtensorMap m_lm;
+  bool quantized = false;   // layer linears and lm_head run from their 4-bit copies
+  QuantW q_lm;
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
   int rope_pos = 0;
@@ -563,6 +593,44 @@ extern "C" int drt_model_get_tensor(drt_model* m, const char* key, void* data, i
   return DRT_OK;
 }
 
+namespace {
+// (Re)build the 4-bit copy of the bf16 weight w [n][K].
+int quantize_into(drt_model* m, QuantW* qw, const __nv_bfloat16* w, int64_t n, int64_t K) {
+  if (qw->q == nullptr) {
+    TRY(dalloc(m, &qw->q, static_cast<size_t>(n) * (K / 2)));
+    TRY(dalloc(m, &qw->scale, static_cast<size_t>(n) * (K / 64)));
+    TRY(dalloc(m, &qw->bias, static_cast<size_t>(n) * (K / 64)));
+    TRY(map_u8(&qw->map, qw->q, n, K / 2, 32, 128));
+  }
+  const int64_t total = n * (K / 64);
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 65535));
+  quantize_q4_kernel<<<blocks, 256>>>(w, n, static_cast<int>(K), qw->q, qw->scale, qw->bias);
+  CK(cudaGetLastError());
+  return DRT_OK;
+}
+}  // namespace
+
+extern "C" int drt_model_quantize(drt_model* m, int32_t bits, int32_t group_size) {
+  REQUIRE(m, "null model");
+  if (bits != 4 || group_size != 64)
+    return set_error(DRT_UNSUPPORTED, "linear quantization serves bits 4 with group size 64 (got bits %d, group %d)", bits,
+                     group_size);
+  REQUIRE(m->H % 64 == 0 && m->I % 64 == 0, "linear in-dims must be multiples of the group size");
+  CK(cudaSetDevice(m->device));
+  const int64_t H = m->H, I = m->I, qd = static_cast<int64_t>(m->nq) * 128;
+  for (int l = 0; l < m->L; ++l) {
+    LayerW& w = m->layers[l];
+    TRY(quantize_into(m, &w.q_qkv, w.wqkv, m->qkv_rows, H));
+    TRY(quantize_into(m, &w.q_o, w.wo, H, qd));
+    TRY(quantize_into(m, &w.q_gu, w.wgu, m->gu_rows, H));
+    TRY(quantize_into(m, &w.q_down, w.wdown, H, I));
+  }
+  TRY(quantize_into(m, &m->q_lm, m->lm_head, m->V, H));
+  CK(cudaDeviceSynchronize());
+  m->quantized = true;
+  return DRT_OK;
+}
+
 extern "C" int64_t drt_model_device_bytes(const drt_model* m) { return m ? m->bytes : 0; }
 
 extern "C" void drt_model_destroy(drt_model* m) {
@@ -709,11 +777,29 @@ void dec_split(int tiles, int kb, int sms, int max_split, int* splits, int* kbps
   *kbps = best_kb;
 }
 
-// Decode linear over at most kDecRows activation rows (mB: the bf16 activation map, box 64 rows).
-int run_dec_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a) {
+// Decode linear over at most kDecRows activation rows (mB: the bf16 activation map, box 64 rows);
+// q: the weight's 4-bit copy when the model is quantized (tmA then maps the packed nibbles).
+int run_dec_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a, const QuantW* q = nullptr) {
   const int tiles_m = a.n_out / 128;
   const int kb = a.K / 64;
   dec_split(tiles_m, kb, s->sms, s->max_cluster, &a.splits, &a.kb_per_split);
+  if (q != nullptr) {
+    // every packed tile of a CTA's K slice stays resident: at most kDecQMaxKb blocks per CTA
+    while (a.kb_per_split > kDecQMaxKb && a.splits < std::min(16, s->max_cluster)) {
+      a.splits *= 2;
+      a.kb_per_split = (kb + a.splits - 1) / a.splits;
+    }
+    if (a.kb_per_split > kDecQMaxKb) return set_error(DRT_UNSUPPORTED, "quantized linear with %d K blocks per CTA", a.kb_per_split);
+    a.q_scale = q->scale;
+    a.q_bias = q->bias;
+    a.q_groups = kb;
+    a.stages = kDecQStages;
+    DecGemmKernel kern = dec_gemm_kernel(a.epi, a.splits, true);
+    if (kern == nullptr) return set_error(DRT_INTERNAL_ERROR, "no quantized decode linear for epilogue %d, split %d", a.epi, a.splits);
+    CK(launch_kc(kern, dim3(tiles_m, 1, a.splits), dim3(128), dec_q_smem_bytes(a.kb_per_split), s->stream, true, a.splits,
+                 q->map, mB, a));
+    return DRT_OK;
+  }
   if (a.kb_per_split > kDecMaxKb) return set_error(DRT_UNSUPPORTED, "decode linear with %d K blocks per CTA", a.kb_per_split);
   // Ring depth: the deepest ring (up to the whole K slice) that still lets two CTAs share an SM,
   // so the next kernel's CTAs can stream their weights beside this one; when that leaves fewer
@@ -768,7 +854,7 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     a.max_seq = s->max_seq;
     a.eps = m->cfg.rms_norm_eps;
     if (f.decode) {
-      TRY(run_dec_gemm(s, w.m_qkv, s->m_xn64, a));
+      TRY(run_dec_gemm(s, w.m_qkv, s->m_xn64, a, m->quantized ? &w.q_qkv : nullptr));
     } else {
       TRY(run_gemm<128>(s, w.m_qkv, s->m_xn128, a, false));
     }
@@ -837,7 +923,7 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     o.epi = EPI_RESID;
     o.out_f32 = s->h;
     o.ld_out = H;
-    if (f.decode) TRY(run_dec_gemm(s, w.m_o, s->m_attn64, o));
+    if (f.decode) TRY(run_dec_gemm(s, w.m_o, s->m_attn64, o, m->quantized ? &w.q_o : nullptr));
     else TRY(run_gemm<128>(s, w.m_o, s->m_attn128, o, false));
     TRY(run_rmsnorm(s, s->h, nullptr, f.rows, f.rows_dev, w.post_norm, s->xn));
     // gate/up + SwiGLU.
@@ -845,14 +931,14 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     g.epi = EPI_SWIGLU;
     g.out_bf16 = s->act;
     g.ld_out = m->I;
-    if (f.decode) TRY(run_dec_gemm(s, w.m_gu, s->m_xn64, g));
+    if (f.decode) TRY(run_dec_gemm(s, w.m_gu, s->m_xn64, g, m->quantized ? &w.q_gu : nullptr));
     else TRY(run_gemm<128>(s, w.m_gu, s->m_xn128, g, false));
     // down + residual.
     GemmArgs d = base_args(s, H, m->I, f);
     d.epi = EPI_RESID;
     d.out_f32 = s->h;
     d.ld_out = H;
-    if (f.decode) TRY(run_dec_gemm(s, w.m_down, s->m_act64, d));
+    if (f.decode) TRY(run_dec_gemm(s, w.m_down, s->m_act64, d, m->quantized ? &w.q_down : nullptr));
     else TRY(run_gemm<128>(s, w.m_down, s->m_act128, d, false));
   }
   return DRT_OK;
@@ -869,7 +955,7 @@ int enqueue_head(drt_session* s, const int* row_index, int rows, const int* rows
   a.epi = EPI_STORE_F32;
   a.out_f32 = s->logits;
   a.ld_out = m->V;
-  TRY(run_dec_gemm(s, m->m_lm, s->m_xf64, a));
+  TRY(run_dec_gemm(s, m->m_lm, s->m_xf64, a, m->quantized ? &m->q_lm : nullptr));
   if (with_selector) {
     SelArgs sa;
     memset(&sa, 0, sizeof(sa));
@@ -939,11 +1025,16 @@ int capture(drt_session* s, bool with_policy, cudaGraphExec_t* out) {
 }
 
 // Prefill rows [p0, p1) (positions whose tokens are final) into the K/V cache, in chunks.
+// A quantized model runs every forward through the decode linears (the 4-bit weights have no wide
+// prefill kernel), in chunks of at most kMaxFwdRows rows.
+int forward_chunk_rows(const drt_session* s) { return s->m->quantized ? kMaxFwdRows : s->rows_cap; }
+
 int prefill(drt_session* s, int p0, int p1, int prompt_len, int block_size, int bidirectional) {
-  for (int c0 = p0; c0 < p1; c0 += s->rows_cap) {
+  const int step = forward_chunk_rows(s);
+  for (int c0 = p0; c0 < p1; c0 += step) {
     Fwd f = {};
-    f.decode = false;
-    f.rows = std::min(s->rows_cap, p1 - c0);
+    f.decode = s->m->quantized;
+    f.rows = std::min(step, p1 - c0);
     f.pos0 = c0;
     f.kv_len = c0 + f.rows;
     f.prompt_len = prompt_len;
@@ -1221,9 +1312,11 @@ extern "C" int drt_session_execute_window(drt_session* s, const int32_t* token_i
   drt_model* m = s->m;
   CK(cudaMemcpyAsync(s->canvas, token_ids, sizeof(int) * n_tokens, cudaMemcpyHostToDevice, s->stream));
   std::vector<int> rows;
-  for (int c0 = 0; c0 < n_tokens; c0 += s->rows_cap) {
+  const int step = forward_chunk_rows(s);
+  for (int c0 = 0; c0 < n_tokens; c0 += step) {
     Fwd f = {};
-    f.rows = std::min(s->rows_cap, n_tokens - c0);
+    f.decode = m->quantized;
+    f.rows = std::min(step, n_tokens - c0);
     f.pos0 = c0;
     f.kv_len = c0 + f.rows;
     f.prompt_len = prompt_len;
@@ -1554,6 +1647,51 @@ extern "C" int drt_linear_bf16(const void* x, const void* w, float* y, int32_t r
   a.ld_out = n;
   CK(launch_kc(gemm_swapab_kernel<64>, dim3(tiles_m, tiles_n, splits), dim3(128), GemmCfg<64>::smem_bytes(a.stages), st,
                false, splits, ma, mb, a));
+  return DRT_OK;
+}
+
+extern "C" int drt_linear_q4(const void* x, const void* q, const void* scale, const void* bias, float* y, int32_t rows,
+                             int32_t n, int32_t K, int32_t splits, void* stream) {
+  REQUIRE(x && q && scale && bias && y, "null argument");
+  REQUIRE(rows >= 1 && rows <= kDecRows, "rows must be in [1, %d]", kDecRows);
+  REQUIRE(n >= 128 && n % 128 == 0 && K >= 64 && K % 64 == 0, "quantized linear needs n %% 128 == 0 and K %% 64 == 0");
+  REQUIRE(splits == 1 || splits == 2 || splits == 4 || splits == 8 || splits == 16, "splits must be 1, 2, 4, 8 or 16");
+  const int kb = K / 64;
+  const int kbps = (kb + splits - 1) / splits;
+  REQUIRE(splits <= kb && kbps <= kDecQMaxKb, "K blocks per split must be in [1, %d]", kDecQMaxKb);
+  TRY(configure_kernels());
+  CUtensorMap mq, mb;
+  TRY(map_u8(&mq, q, n, K / 2, 32, 128));
+  TRY(map_matrix(&mb, x, rows, K, 64));
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.n_out = n;
+  a.K = K;
+  a.rows = rows;
+  a.splits = splits;
+  a.kb_per_split = kbps;
+  a.stages = kDecQStages;
+  a.epi = EPI_STORE_F32;
+  a.out_f32 = y;
+  a.ld_out = n;
+  a.q_scale = static_cast<const __nv_bfloat16*>(scale);
+  a.q_bias = static_cast<const __nv_bfloat16*>(bias);
+  a.q_groups = kb;
+  DecGemmKernel kern = dec_gemm_kernel(EPI_STORE_F32, splits, true);
+  CK(launch_kc(kern, dim3(n / 128, 1, splits), dim3(128), dec_q_smem_bytes(kbps), static_cast<cudaStream_t>(stream), false,
+               splits, mq, mb, a));
+  return DRT_OK;
+}
+
+extern "C" int drt_quantize_q4(const void* w, int64_t rows, int32_t K, void* q, void* scale, void* bias, void* stream) {
+  REQUIRE(w && q && scale && bias, "null argument");
+  REQUIRE(rows >= 1 && K >= 64 && K % 64 == 0, "quantization needs K %% 64 == 0");
+  const int64_t total = rows * (K / 64);
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 65535));
+  quantize_q4_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(w), rows, K, static_cast<uint8_t*>(q), static_cast<__nv_bfloat16*>(scale),
+      static_cast<__nv_bfloat16*>(bias));
+  CK(cudaGetLastError());
   return DRT_OK;
 }
 

@@ -63,6 +63,11 @@ struct GemmArgs {
   // the next linear fuses into its activation load: ss_out[row * ss_ld + m0 / 128].
   float* ss_out;
   int ss_ld;
+  // 4-bit affine weights (decode linear, quantized instantiation): per (row, group of 64 inputs)
+  // bf16 scale and bias, [n_out][q_groups] with q_groups = K / 64; the packed nibbles come from tmA.
+  const __nv_bfloat16* q_scale;
+  const __nv_bfloat16* q_bias;
+  int q_groups;
 };
 
 template <int BN>
@@ -80,6 +85,15 @@ struct GemmCfg {
   __host__ __device__ static size_t smem_bytes(int stages) { return 1024 + body_bytes(stages) + 256; }
 };
 
+// Linear output rounding: the bf16-weight contract rounds the matmul output to bf16
+// (mlx_ops.py:122-125); the quantized-weight contract (mx.quantized_matmul, mlx_ops.py:108-117)
+// keeps the f32 result.
+template <bool RND>
+__device__ __forceinline__ float out_round(float x) {
+  if constexpr (RND) return bf16_round(x);
+  else return x;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -92,7 +106,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 // rope_c / rope_s: optional RoPE factors for this thread's feature at rows col0 + i, loaded by the
 // caller ahead of time (the decode kernel fetches them before its accumulator is ready); when null
 // the QKV epilogue reads the tables itself.
-template <int EPI>
+template <int EPI, bool RND = true>
 __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* v, int col0, int ncols, int m0, int tid,
                                                       float* xs, int pos0, const float* rope_c = nullptr,
                                                       const float* rope_s = nullptr) {
@@ -106,7 +120,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
     if constexpr (EPI == EPI_STORE_F32) {
 #pragma unroll
       for (int i = 0; i < 32; ++i)
-        if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = __fadd_rn(bf16_round(v[i]), b);
+        if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = __fadd_rn(out_round<RND>(v[i]), b);
     }
     if constexpr (EPI == EPI_RESID) {
       float cur[32];
@@ -114,7 +128,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
       for (int i = 0; i < 32; ++i) cur[i] = i < ncols ? a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] : 0.0f;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        cur[i] = __fadd_rn(cur[i], __fadd_rn(bf16_round(v[i]), b));
+        cur[i] = __fadd_rn(cur[i], __fadd_rn(out_round<RND>(v[i]), b));
         if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = cur[i];
       }
       if (a.ss_out != nullptr) {
@@ -139,14 +153,14 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
       const int j0 = (m0 >> 1);
       if (tid >= 64) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) xs[i * 64 + (tid - 64)] = __fadd_rn(bf16_round(v[i]), b);
+        for (int i = 0; i < 32; ++i) xs[i * 64 + (tid - 64)] = __fadd_rn(out_round<RND>(v[i]), b);
       }
       __syncthreads();
       if (tid < 64) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           if (i < ncols) {
-            const float g = __fadd_rn(bf16_round(v[i]), b);
+            const float g = __fadd_rn(out_round<RND>(v[i]), b);
             const float u = xs[i * 64 + tid];
             const float sig = 1.0f / (1.0f + expf(-g));
             const float act = __fmul_rn(__fmul_rn(g, sig), u);
@@ -170,20 +184,20 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
           for (int q = 0; q < 4; ++q) {
             __align__(16) __nv_bfloat16 t[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) t[e] = __float2bfloat16_rn(__fadd_rn(bf16_round(v[q * 8 + e]), b));
+            for (int e = 0; e < 8; ++e) t[e] = __float2bfloat16_rn(__fadd_rn(out_round<RND>(v[q * 8 + e]), b));
             *reinterpret_cast<uint4*>(dst + q * 8) = *reinterpret_cast<const uint4*>(t);
           }
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (i < ncols) dst[i] = __float2bfloat16_rn(__fadd_rn(bf16_round(v[i]), b));
+            if (i < ncols) dst[i] = __float2bfloat16_rn(__fadd_rn(out_round<RND>(v[i]), b));
         }
         return;
       }
       const float* nw = is_q ? a.qnorm_w : a.knorm_w;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float val = __fadd_rn(bf16_round(v[i]), b);
+        const float val = __fadd_rn(out_round<RND>(v[i]), b);
         v[i] = val;
         xs[i * 128 + tid] = val;
       }

@@ -32,6 +32,12 @@ constexpr int kDecBBytes = kDecRows * 128;   // one K block of the activation ti
 constexpr int kDecMaxKb = 16;                // K blocks of B kept resident per CTA
 constexpr int kDecXBytes = 128 * kDecRows * 4;        // one f32 partial tile (receive or stage)
 
+// Quantized instantiation: every packed tile of the CTA's K slice is resident (kDecPBytes each), the
+// dequantized bf16 weight tiles go through a ring of kDecQStages A blocks.
+constexpr int kDecPBytes = 128 * 32;  // 128 rows x 64 nibbles
+constexpr int kDecQStages = 3;
+constexpr int kDecQMaxKb = 8;         // K blocks per CTA for the quantized instantiation
+
 __host__ __device__ inline bool dec_split_supported(int S) { return S == 1 || S == 2 || S == 4 || S == 8 || S == 16; }
 
 // Shared memory: [ring: stages x A block][B: kb_per_split x B block], at least two partial tiles
@@ -45,6 +51,16 @@ __host__ __device__ inline size_t dec_body_bytes(int stages, int kb_per_split) {
 __host__ __device__ inline size_t dec_smem_bytes(int stages, int kb_per_split) {
   // alignment slack + body + barriers (2 * stages + 3), TMEM slot and flags
   return 1024 + dec_body_bytes(stages, kb_per_split) + static_cast<size_t>(2 * stages + 3) * 8 + 32;
+}
+// Quantized: [A ring kDecQStages][B kb][packed kb][scale kb x 128 f32][bias kb x 128 f32], at least two
+// partial tiles long (stage and receive overlays).
+__host__ __device__ inline size_t dec_q_body_bytes(int kb_per_split) {
+  const size_t m = static_cast<size_t>(kDecQStages) * kDecABytes +
+                   static_cast<size_t>(kb_per_split) * (kDecBBytes + kDecPBytes + 2 * 128 * 4);
+  return m > static_cast<size_t>(2 * kDecXBytes) ? m : static_cast<size_t>(2 * kDecXBytes);
+}
+__host__ __device__ inline size_t dec_q_smem_bytes(int kb_per_split) {
+  return 1024 + dec_q_body_bytes(kb_per_split) + static_cast<size_t>(2 * kDecQStages + 4) * 8 + 32;
 }
 
 __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes, uint32_t bar_cluster) {
@@ -61,7 +77,7 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t
 // QKV tile, columns [c0, c0 + nc) of this CTA's slice (v[i] = accumulator of column c0 + i,
 // nc <= CPR): q / k rows get bias, the per-row RMSNorm over the head (QK-norm) and RoPE; v rows
 // are written transposed into the V^T cache. rope_c / rope_s hold this thread's RoPE factors.
-template <int CPR>
+template <int CPR, bool RND>
 __device__ __forceinline__ void dec_epilogue_qkv(const GemmArgs& a, const float* v, int c0, int nc, int m0, int tid,
                                                  float* xs, int pos0, const float* rope_c, const float* rope_s) {
   const int n = m0 + tid;
@@ -71,7 +87,7 @@ __device__ __forceinline__ void dec_epilogue_qkv(const GemmArgs& a, const float*
   const bool is_k = !is_q && tile < a.nq + a.nkv;
   float val[CPR];
 #pragma unroll
-  for (int i = 0; i < CPR; ++i) val[i] = __fadd_rn(bf16_round(v[i]), b);
+  for (int i = 0; i < CPR; ++i) val[i] = __fadd_rn(out_round<RND>(v[i]), b);
   if (!is_q && !is_k) {
     // V^T[g][d][pos], contiguous along pos: this thread's feature row, nc consecutive positions.
     const int g = tile - a.nq - a.nkv;
@@ -150,12 +166,12 @@ __device__ __forceinline__ void dec_epilogue_qkv(const GemmArgs& a, const float*
 // SwiGLU tile (lanes 0..63 gate rows j0 + f, lanes 64..127 up rows j0 + f of the same features):
 // act[c0 + i, j0 + f] = bf16(silu(g) * u). Both halves of the CTA work: thread t takes feature
 // t & 63 for the columns of parity t >> 6.
-template <int CPR>
+template <int CPR, bool RND>
 __device__ __forceinline__ void dec_epilogue_swiglu(const GemmArgs& a, const float* v, int c0, int nc, int m0, int tid,
                                                     float* xs) {
   const float b = a.bias != nullptr ? a.bias[m0 + tid] : 0.0f;
 #pragma unroll
-  for (int i = 0; i < CPR; ++i) xs[i * 128 + tid] = __fadd_rn(bf16_round(v[i]), b);
+  for (int i = 0; i < CPR; ++i) xs[i * 128 + tid] = __fadd_rn(out_round<RND>(v[i]), b);
   __syncthreads();
   constexpr int H = CPR / 2;
   const int f = tid & 63, par = tid >> 6;
@@ -221,6 +237,10 @@ __device__ __forceinline__ void dec_sum_slices(const float* recv, int tid, float
 struct DecSmem {
   uint8_t* ring;
   uint8_t* sB;
+  uint8_t* sP;      // quantized: packed tiles [kb][128 rows][32 bytes]
+  float* qsc;       // quantized: [kb][128] scales of this CTA's rows
+  float* qbi;       // quantized: [kb][128] biases
+  uint64_t* fullP;  // quantized: all packed tiles landed
   float* stage;
   float* recv;
   float* xs;
@@ -234,7 +254,7 @@ struct DecSmem {
 
 // Everything after the dependency wait, for a compile-time epilogue EPI, split-K factor S and MMA
 // width NCOL: activation load, weight ring, UMMA, split-K exchange and epilogue.
-template <int EPI, int S, int NCOL>
+template <int EPI, int S, int NCOL, bool QUANT>
 __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMap* tmB, const GemmArgs& a, const DecSmem& sm,
                                         uint32_t tmem, int m0, int kb0, int nkb, int npre, int stages, uint64_t policy,
                                         int rows_valid, int pos0) {
@@ -270,6 +290,49 @@ __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMa
   }
   griddep_launch_dependents();
 
+  if constexpr (QUANT) {
+    // Dequantize group g of this CTA's rows into ring slot g % kDecQStages (thread t: row t), then one
+    // lane issues its UMMAs; the next group's dequantization overlaps them.
+    bool ok = nkb == 0 || (mbar_wait(sm.fullP, 0) && mbar_wait(sm.fullB, 0));
+    ok = __syncthreads_and(ok) != 0;  // uniform across the CTA, so every barrier below is reached by all
+    for (int g = 0; g < nkb && ok; ++g) {
+      const int slot = g % kDecQStages;
+      bool ready = g < kDecQStages || mbar_wait(&sm.emptyA[slot], ((g / kDecQStages) - 1) & 1);
+      const uint8_t* prow = sm.sP + g * kDecPBytes + tid * 32;
+      const uint4 p0 = *reinterpret_cast<const uint4*>(prow);
+      const uint4 p1 = *reinterpret_cast<const uint4*>(prow + 16);
+      const uint32_t pw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+      const float sc = sm.qsc[g * 128 + tid], bi = sm.qbi[g * 128 + tid];
+      uint8_t* arow = sm.ring + static_cast<size_t>(slot) * kDecABytes + tid * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 8 inputs per 16-byte chunk, 4 packed bytes
+        __align__(16) __nv_bfloat16 t[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float qv = static_cast<float>((pw[c] >> (4 * e)) & 15u);
+          t[e] = __float2bfloat16_rn(__fmaf_rn(sc, qv, bi));
+        }
+        *reinterpret_cast<uint4*>(arow + ((c ^ (tid & 7)) * 16)) = *reinterpret_cast<const uint4*>(t);
+      }
+      fence_proxy_async_smem();
+      ok = __syncthreads_and(ready) != 0;
+      if (!ok) break;
+      if (warp == 1 && lane == 0) {
+        tc_fence_after();
+        constexpr uint32_t idesc = idesc_bf16_f32(128, NCOL);
+        const uint32_t a_addr = smem_u32(sm.ring + static_cast<size_t>(slot) * kDecABytes);
+        const uint32_t b_addr = smem_u32(sm.sB + g * kDecBBytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16(tmem, sdesc_kmajor_sw128(a_addr + kk * 32), sdesc_kmajor_sw128(b_addr + kk * 32), idesc,
+                    (g | kk) != 0 ? 1u : 0u);
+        umma_commit(&sm.emptyA[slot]);
+      }
+    }
+    if (!ok) { record_error(a.status, DEV_TIMEOUT_MMA); sm.flags[0] = 1; }
+    if (warp == 1 && lane == 0) umma_commit(sm.accum);
+    __syncwarp();
+  } else {
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
@@ -304,6 +367,7 @@ __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMa
     }
     __syncwarp();
   }
+  }
 
   bool acc_ok = true;
   if (nkb > 0) acc_ok = mbar_wait(sm.accum, 0);
@@ -321,9 +385,9 @@ __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMa
   if constexpr (S == 1) {
     __syncthreads();
     if (sm.flags[0] == 0) {
-      gemm_epilogue_chunk_t<EPI>(a, acc, 0, min(32, rows_valid), m0, tid, sm.xs, pos0);
+      gemm_epilogue_chunk_t<EPI, !QUANT>(a, acc, 0, min(32, rows_valid), m0, tid, sm.xs, pos0);
       if constexpr (NCOL == 64)
-        if (rows_valid > 32) gemm_epilogue_chunk_t<EPI>(a, acc + 32, 32, rows_valid - 32, m0, tid, sm.xs, pos0);
+        if (rows_valid > 32) gemm_epilogue_chunk_t<EPI, !QUANT>(a, acc + 32, 32, rows_valid - 32, m0, tid, sm.xs, pos0);
     }
   } else {
     // Stage the partial as S contiguous slices and send slice p to CTA p. Inside a slice the
@@ -367,16 +431,16 @@ __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMa
 #pragma unroll
         for (int i = 0; i < CPR; ++i)
           if (i < nvalid)
-            a.out_f32[static_cast<size_t>(c0 + i) * a.ld_out + n] = __fadd_rn(pre[i], __fadd_rn(bf16_round(v[i]), b));
+            a.out_f32[static_cast<size_t>(c0 + i) * a.ld_out + n] = __fadd_rn(pre[i], __fadd_rn(out_round<!QUANT>(v[i]), b));
       } else if constexpr (EPI == EPI_QKV) {
-        dec_epilogue_qkv<CPR>(a, v, c0, nvalid, m0, tid, sm.xs, pos0, pre, pre2);
+        dec_epilogue_qkv<CPR, !QUANT>(a, v, c0, nvalid, m0, tid, sm.xs, pos0, pre, pre2);
       } else if constexpr (EPI == EPI_SWIGLU) {
-        dec_epilogue_swiglu<CPR>(a, v, c0, nvalid, m0, tid, sm.xs);
+        dec_epilogue_swiglu<CPR, !QUANT>(a, v, c0, nvalid, m0, tid, sm.xs);
       } else {
         float vv[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) vv[i] = i < CPR ? v[i < CPR ? i : 0] : 0.0f;
-        gemm_epilogue_chunk_t<EPI>(a, vv, c0, nvalid, m0, tid, sm.xs, pos0);
+        gemm_epilogue_chunk_t<EPI, !QUANT>(a, vv, c0, nvalid, m0, tid, sm.xs, pos0);
       }
     }
     cluster_wait();
@@ -384,35 +448,41 @@ __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMa
 }
 
 // One decode linear: CTA (m-tile, 1, split) of a grid whose z extent is the split-K factor S,
-// launched as clusters of S CTAs along z. Instantiated per epilogue and split factor so that each
-// kernel carries only the code it runs (the instruction cache is cold at every launch).
-template <int EPI, int S>
+// launched as clusters of S CTAs along z. Instantiated per epilogue, split factor and weight format
+// (bf16, or 4-bit affine with tmA over the packed nibbles) so that each kernel carries only the
+// code it runs (the instruction cache is cold at every launch).
+template <int EPI, int S, bool QUANT>
 __global__ void __launch_bounds__(128, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
-  const int stages = a.stages;
+  const int stages = QUANT ? kDecQStages : a.stages;
+  const int kbs = a.kb_per_split;
   DecSmem sm;
   sm.ring = smem;
   sm.sB = smem + dec_ring_bytes(stages);
+  sm.sP = sm.sB + static_cast<size_t>(kbs) * kDecBBytes;
+  sm.qsc = reinterpret_cast<float*>(sm.sP + static_cast<size_t>(kbs) * kDecPBytes);
+  sm.qbi = sm.qsc + kbs * 128;
   sm.stage = reinterpret_cast<float*>(smem);
   sm.recv = sm.stage + 128 * kDecRows;
   sm.xs = sm.recv;  // epilogue scratch, once the received slices are summed
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + dec_body_bytes(stages, a.kb_per_split));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (QUANT ? dec_q_body_bytes(kbs) : dec_body_bytes(stages, kbs)));
   sm.fullA = bars;
   sm.emptyA = bars + stages;
   sm.fullB = bars + 2 * stages;
   sm.accum = sm.fullB + 1;
   sm.xbar = sm.fullB + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm.fullB + 3);
+  sm.fullP = sm.fullB + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm.fullB + 4);
   sm.flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] error
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int m0 = blockIdx.x * 128;
   const int kb_total = a.K >> 6;
-  const int kb0 = blockIdx.z * a.kb_per_split;
-  const int nkb = max(0, min(a.kb_per_split, kb_total - kb0));
+  const int kb0 = blockIdx.z * kbs;
+  const int nkb = max(0, min(kbs, kb_total - kb0));
 
   if (tid == 0) {
     for (int st = 0; st < stages; ++st) {
@@ -422,19 +492,35 @@ __global__ void __launch_bounds__(128, 1)
     mbar_init(sm.fullB, 1);
     mbar_init(sm.accum, 1);
     mbar_init(sm.xbar, 1);
+    mbar_init(sm.fullP, 1);
     sm.flags[0] = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
   // Weight prefetch first: it depends on nothing the producer kernel writes.
-  const int npre = min(stages, nkb);
+  const int npre = QUANT ? 0 : min(stages, nkb);
   uint64_t policy = 0;
   if (tid == 0) {
     policy = l2_policy_evict_first();
-    for (int i = 0; i < npre; ++i) {
-      mbar_expect_tx(&sm.fullA[i], kDecABytes);
-      tma_load_2d_hint(sm.ring + static_cast<size_t>(i) * kDecABytes, &tmA, &sm.fullA[i], (kb0 + i) * 64, m0, policy);
+    if constexpr (QUANT) {
+      if (nkb > 0) {
+        mbar_expect_tx(sm.fullP, static_cast<uint32_t>(nkb * kDecPBytes));
+        for (int g = 0; g < nkb; ++g) tma_load_2d_hint(sm.sP + g * kDecPBytes, &tmA, sm.fullP, (kb0 + g) * 32, m0, policy);
+      }
+    } else {
+      for (int i = 0; i < npre; ++i) {
+        mbar_expect_tx(&sm.fullA[i], kDecABytes);
+        tma_load_2d_hint(sm.ring + static_cast<size_t>(i) * kDecABytes, &tmA, &sm.fullA[i], (kb0 + i) * 64, m0, policy);
+      }
+    }
+  }
+  if constexpr (QUANT) {
+    // This thread's row: its scale and bias for every group of the K slice.
+    const size_t base = static_cast<size_t>(m0 + tid) * a.q_groups + kb0;
+    for (int g = 0; g < nkb; ++g) {
+      sm.qsc[g * 128 + tid] = __bfloat162float(a.q_scale[base + g]);
+      sm.qbi[g * 128 + tid] = __bfloat162float(a.q_bias[base + g]);
     }
   }
   if (warp == 0) {
@@ -452,11 +538,14 @@ __global__ void __launch_bounds__(128, 1)
   rows_valid = max(0, min(rows_valid, kDecRows));
   const int pos0 = a.pos0_dev != nullptr ? *a.pos0_dev : a.pos0;
   // MMA width from the live row count, uniform across the cluster.
-  if (rows_valid <= 32) dec_run<EPI, S, 32>(&tmA, &tmB, a, sm, tmem, m0, kb0, nkb, npre, stages, policy, rows_valid, pos0);
-  else dec_run<EPI, S, 64>(&tmA, &tmB, a, sm, tmem, m0, kb0, nkb, npre, stages, policy, rows_valid, pos0);
+  if (rows_valid <= 32)
+    dec_run<EPI, S, 32, QUANT>(&tmA, &tmB, a, sm, tmem, m0, kb0, nkb, npre, stages, policy, rows_valid, pos0);
+  else
+    dec_run<EPI, S, 64, QUANT>(&tmA, &tmB, a, sm, tmem, m0, kb0, nkb, npre, stages, policy, rows_valid, pos0);
 
   if (sm.flags[0] != 0 && tid == 0) {
     for (int st = 0; st < npre; ++st) mbar_wait(&sm.fullA[st], 0);
+    if (QUANT && nkb > 0) mbar_wait(sm.fullP, 0);
     if (nkb > 0) mbar_wait(sm.fullB, 0);
   }
   tc_fence_before();
@@ -466,16 +555,22 @@ __global__ void __launch_bounds__(128, 1)
 
 using DecGemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmArgs);
 
-// The instantiation for an epilogue kind and split factor (nullptr if not instantiated).
-inline DecGemmKernel dec_gemm_kernel(int epi, int S) {
-#define DRT_DEC_ROW(E) \
-  { gemm_decode_kernel<E, 1>, gemm_decode_kernel<E, 2>, gemm_decode_kernel<E, 4>, gemm_decode_kernel<E, 8>, gemm_decode_kernel<E, 16> }
-  static const DecGemmKernel table[4][5] = {DRT_DEC_ROW(EPI_STORE_F32), DRT_DEC_ROW(EPI_RESID), DRT_DEC_ROW(EPI_SWIGLU),
-                                            DRT_DEC_ROW(EPI_QKV)};
+// The instantiation for an epilogue kind, split factor and weight format (nullptr if none).
+inline DecGemmKernel dec_gemm_kernel(int epi, int S, bool quant = false) {
+#define DRT_DEC_ROW(E, Q)                                                                                              \
+  {                                                                                                                    \
+    gemm_decode_kernel<E, 1, Q>, gemm_decode_kernel<E, 2, Q>, gemm_decode_kernel<E, 4, Q>, gemm_decode_kernel<E, 8, Q>, \
+        gemm_decode_kernel<E, 16, Q>                                                                                   \
+  }
+  static const DecGemmKernel table[2][4][5] = {
+      {DRT_DEC_ROW(EPI_STORE_F32, false), DRT_DEC_ROW(EPI_RESID, false), DRT_DEC_ROW(EPI_SWIGLU, false),
+       DRT_DEC_ROW(EPI_QKV, false)},
+      {DRT_DEC_ROW(EPI_STORE_F32, true), DRT_DEC_ROW(EPI_RESID, true), DRT_DEC_ROW(EPI_SWIGLU, true),
+       DRT_DEC_ROW(EPI_QKV, true)}};
 #undef DRT_DEC_ROW
   const int si = S == 1 ? 0 : S == 2 ? 1 : S == 4 ? 2 : S == 8 ? 3 : S == 16 ? 4 : -1;
   if (epi < 0 || epi > EPI_QKV || si < 0) return nullptr;
-  return table[epi][si];
+  return table[quant ? 1 : 0][epi][si];
 }
 
 }  // namespace drt

@@ -101,8 +101,10 @@ class Runtime:
         engine_config = dict(engine_config or {})
         if engine_config.get("compute_dtype", 0) not in (0, "bf16", "bfloat16"):
             raise NotImplementedError("the B200 engine computes with bf16 weights (compute_dtype 0)")
-        if engine_config.get("linear_quant_bits"):
-            raise NotImplementedError("quantized linear weights are not served by this build")
+        quant_bits = engine_config.get("linear_quant_bits")
+        quant_group = int(engine_config.get("linear_quant_group_size", 64) or 64)
+        if quant_bits and (int(quant_bits), quant_group) != (4, 64):
+            raise NotImplementedError("linear quantization is served as 4-bit affine, group size 64")
         if precision is not None and precision.get("weight_type", "bf16") != "bf16":
             raise NotImplementedError(f"precision {precision.get('scheme')!r} is not served by this build")
         cfg = dict(QWEN3_06B_BD3LM)
@@ -130,10 +132,13 @@ class Runtime:
         self.max_seq = int(max_seq)
         cos, sin = rope_half_tables(self.max_seq, cfg["head_dim"], float(cfg["rope_theta"]))
         _call(self._lib.drt_model_set_rope(self._model, cos.ctypes.data, sin.ctypes.data, self.max_seq))
+        self.quantized = False
         if synthetic_seed is not None:
             self.init_synthetic(synthetic_seed)
         if weights is not None:
             self.load_weights(weights)
+        if quant_bits:
+            self.quantize(int(quant_bits), quant_group)
         if creation_memory_budget_bytes and self.device_bytes > int(creation_memory_budget_bytes):
             self.close()
             raise ValueError("model weights exceed creation_memory_budget_bytes")
@@ -147,6 +152,8 @@ class Runtime:
                 std[k] = v
         _call(self._lib.drt_model_init_synthetic(self._model, int(seed) & (2**64 - 1), std["linear_std"],
                                                  std["embed_std"], std["bias_std"]))
+        if getattr(self, "quantized", False):
+            self.quantize()
 
     def load_weights(self, weights: Mapping[str, Any]) -> None:
         """Install tensors by package key (``model.layers.N.self_attn.q_proj.weight`` ...)."""
@@ -162,6 +169,14 @@ class Runtime:
             else:
                 data = _bf16_bits(arr)
                 _call(self._lib.drt_model_set_tensor(self._model, key.encode(), data.ctypes.data, 0, rows, cols))
+        if getattr(self, "quantized", False):
+            self.quantize()
+
+    def quantize(self, bits: int = 4, group_size: int = 64) -> None:
+        """4-bit affine copies of every layer linear and lm_head (the reference's load-time
+        ``_quantize_linear_weights``, mlx_dream.py:2090-2108); later forwards use them."""
+        _call(self._lib.drt_model_quantize(self._model, int(bits), int(group_size)))
+        self.quantized = True
 
     def get_tensor(self, key: str, shape: tuple[int, int]) -> np.ndarray:
         """A resident tensor as float32 (bf16 values widened)."""

@@ -166,6 +166,13 @@ int drt_model_get_tensor(drt_model* model, const char* key, void* data, int32_t 
  * (python/src/edllm/backends/mlx_forward.py:1566-1595). */
 int drt_model_set_rope(drt_model* model, const float* cos_half, const float* sin_half, int32_t n_pos);
 int64_t drt_model_device_bytes(const drt_model* model);
+/* Quantize every layer linear (q/k/v/o, gate/up, down) and lm_head to 4-bit affine groups of 64
+ * inputs (reference _quantize_linear_weights, mlx_dream.py:2090-2108, keys :2033-2087; the
+ * quantizer's rounding rules are defined in diffusorrt_b200/csrc/quant.cuh). The embedding stays
+ * bf16. Later forwards of every session run from the 4-bit copies with the quantized-matmul output
+ * contract (no bf16 rounding of linear outputs, mlx_ops.py:108-117). Call again after
+ * drt_model_set_tensor to refresh the copies. Only bits 4, group_size 64 (else DRT_UNSUPPORTED). */
+int drt_model_quantize(drt_model* model, int32_t bits, int32_t group_size);
 void drt_model_destroy(drt_model* model);
 
 /* ------------------------------------------------------------------ session */
@@ -239,6 +246,14 @@ int drt_selector_rows_noalloc(const float* logits, int64_t ld, int32_t n_rows, i
  * K % 64 == 0; splits in {1, 2, 4, 8, 16} (split-K CTAs of a tile form one thread-block cluster
  * and reduce through distributed shared memory, so scratch may be NULL and
  * drt_linear_scratch_bytes returns 0). */
+/* 4-bit affine quantization of a bf16 weight w [rows x K] (device pointers): q [rows x K/2] packed
+ * nibbles (input 2j in the low nibble of byte j), scale / bias [rows x K/64] bf16 (quant.cuh). */
+int drt_quantize_q4(const void* w, int64_t rows, int32_t K, void* q, void* scale, void* bias, void* stream);
+/* y = x @ dequant(q, scale, bias)^T for rows <= 64: x bf16 [rows x K], y f32 [rows x n] (no output
+ * rounding, the quantized-matmul contract); n % 128 == 0, K % 64 == 0, splits in {1, 2, 4, 8, 16}
+ * with at most 8 groups of 64 inputs per split. The decode linear's quantized instantiation. */
+int drt_linear_q4(const void* x, const void* q, const void* scale, const void* bias, float* y, int32_t rows, int32_t n,
+                  int32_t K, int32_t splits, void* stream);
 size_t drt_linear_scratch_bytes(int32_t rows, int32_t n, int32_t K, int32_t splits);
 int drt_linear_bf16(const void* x, const void* w, float* y, int32_t rows, int32_t n, int32_t K, int32_t splits,
                     int32_t round_bf16, void* scratch, void* stream);

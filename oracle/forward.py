@@ -21,6 +21,7 @@ import math
 import numpy as np
 
 from .numerics import bf16_round, rope_half_tables
+from .quant import dequantize, quantize_q4
 
 
 def visible_mask(q_pos: np.ndarray, kv_len: int, *, prompt_len: int, block_size: int, bidirectional: bool) -> np.ndarray:
@@ -50,6 +51,29 @@ def _lin32(x: np.ndarray, w: np.ndarray, b=None) -> np.ndarray:
     return y
 
 
+def _lin32q(x: np.ndarray, wq, b=None) -> np.ndarray:
+    """Quantized linear (mx.quantized_matmul, mlx_ops.py:108-117): f32 activations times the f32
+    dequantized weights, f32 result with no bf16 rounding, bias added in f32."""
+    y = (np.asarray(x, dtype=np.float32) @ wq.T).astype(np.float32)
+    if b is not None:
+        y = (y + np.asarray(b, dtype=np.float32)).astype(np.float32)
+    return y
+
+
+def quantized_weights(weights: dict, cfg: dict) -> dict:
+    """The dequantized f32 copies of every quantized linear (layer q/k/v/o, gate/up, down and
+    lm_head; reference keys mlx_dream.py:2033-2087), keyed like ``weights``."""
+    out = {}
+    keys = [k for k in weights if k.startswith("model.layers.") and k.endswith(
+        (".q_proj.weight", ".k_proj.weight", ".v_proj.weight", ".o_proj.weight", ".gate_proj.weight",
+         ".up_proj.weight", ".down_proj.weight"))]
+    lm = weights.get("lm_head.weight", weights["model.embed_tokens.weight"])
+    for k in keys:
+        out[k] = dequantize(*quantize_q4(weights[k]))
+    out["lm_head.weight"] = dequantize(*quantize_q4(lm))
+    return out
+
+
 def _rope32(x: np.ndarray, cos_h: np.ndarray, sin_h: np.ndarray) -> np.ndarray:
     # x [S, heads, d]; cos_h/sin_h [S, d/2] -> full tables [S, 1, d]
     cos = np.concatenate([cos_h, cos_h], axis=-1)[:, None, :]
@@ -76,8 +100,9 @@ def _sdpa32(q, k, v, visible):
 
 
 def forward_mlx(weights: dict, cfg: dict, token_ids, *, prompt_len: int = 0, block_size: int = 32,
-                bidirectional: bool = False, output_rows=None, rope=None) -> np.ndarray:
-    """Logits [len(output_rows) (or S), V] f32 of a full-window forward (no cache)."""
+                bidirectional: bool = False, output_rows=None, rope=None, quant: dict | None = None) -> np.ndarray:
+    """Logits [len(output_rows) (or S), V] f32 of a full-window forward (no cache). With ``quant``
+    (``quantized_weights``), every quantized linear follows the quantized-matmul contract."""
     ids = np.asarray(token_ids, dtype=np.int64)
     S = len(ids)
     H, nq, nkv, d = cfg["hidden_size"], cfg["attention_heads"], cfg["num_kv_heads"], cfg["head_dim"]
@@ -90,24 +115,33 @@ def forward_mlx(weights: dict, cfg: dict, token_ids, *, prompt_len: int = 0, blo
     for layer in range(cfg["layer_count"]):
         p = f"model.layers.{layer}."
         g = lambda key: weights.get(p + key)  # noqa: E731
+
+        def lin(x, key, bias_key=None):
+            b = g(bias_key) if bias_key else None
+            if quant is not None:
+                return _lin32q(x, quant[p + key], b)
+            return _lin32(x, g(key), b)
+
         n = _rms32(h, g("input_layernorm.weight"), eps)
-        q = _lin32(n, g("self_attn.q_proj.weight"), g("self_attn.q_proj.bias")).reshape(S, nq, d)
-        k = _lin32(n, g("self_attn.k_proj.weight"), g("self_attn.k_proj.bias")).reshape(S, nkv, d)
-        v = _lin32(n, g("self_attn.v_proj.weight"), g("self_attn.v_proj.bias")).reshape(S, nkv, d)
+        q = lin(n, "self_attn.q_proj.weight", "self_attn.q_proj.bias").reshape(S, nq, d)
+        k = lin(n, "self_attn.k_proj.weight", "self_attn.k_proj.bias").reshape(S, nkv, d)
+        v = lin(n, "self_attn.v_proj.weight", "self_attn.v_proj.bias").reshape(S, nkv, d)
         if g("self_attn.q_norm.weight") is not None:
             q = _rms32(q, g("self_attn.q_norm.weight"), eps)
             k = _rms32(k, g("self_attn.k_norm.weight"), eps)
         q = _rope32(q, cos_h, sin_h)
         k = _rope32(k, cos_h, sin_h)
         attn = _sdpa32(q, k, v, vis)
-        h = (h + _lin32(attn, g("self_attn.o_proj.weight"))).astype(np.float32)
+        h = (h + lin(attn, "self_attn.o_proj.weight")).astype(np.float32)
         n2 = _rms32(h, g("post_attention_layernorm.weight"), eps)
-        gate = _lin32(n2, g("mlp.gate_proj.weight"))
-        up = _lin32(n2, g("mlp.up_proj.weight"))
+        gate = lin(n2, "mlp.gate_proj.weight")
+        up = lin(n2, "mlp.up_proj.weight")
         act = (gate * (np.float32(1.0) / (np.float32(1.0) + np.exp(-gate))) * up).astype(np.float32)
-        h = (h + _lin32(act, g("mlp.down_proj.weight"))).astype(np.float32)
+        h = (h + lin(act, "mlp.down_proj.weight")).astype(np.float32)
     rows = np.arange(S) if output_rows is None else np.asarray(output_rows, dtype=np.int64)
     hn = _rms32(h[rows], weights["model.norm.weight"], eps)
+    if quant is not None:
+        return _lin32q(hn, quant["lm_head.weight"])
     return _lin32(hn, weights["lm_head.weight"])
 
 

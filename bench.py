@@ -259,6 +259,163 @@ def _run_ours(args, world, rank, local) -> dict | None:
     return line
 
 
+DREAM = dict(prompt=256, gen=256, steps=256, temperature=0.2, top_p=0.95, eps=1e-3)
+
+
+def _dream_flops(cfg: dict, canvas: int, n_frontier: float) -> float:
+    """Algorithmic FLOPs of one full-canvas step: every layer linear over the canvas, QK^T and PV
+    over the canvas (bidirectional), lm_head over the frontier rows."""
+    H, I, V, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"], cfg["layer_count"]
+    qd, kd = cfg["attention_heads"] * cfg["head_dim"], cfg["num_kv_heads"] * cfg["head_dim"]
+    per_layer = H * (qd + 2 * kd) + qd * H + 3 * I * H
+    lin = 2.0 * canvas * per_layer * L
+    attn = 2.0 * 2.0 * canvas * canvas * qd * L
+    head = 2.0 * n_frontier * V * H
+    return lin + attn + head
+
+
+def _run_dream(args, world, rank, local) -> dict | None:
+    """cfg2: Dream-7B-architecture full-canvas entropy_count decode, one request per GPU."""
+    import torch
+
+    from diffusorrt_b200 import Runtime, _lib, build
+    from diffusorrt_b200.config import DREAM_7B
+
+    if rank == 0:
+        build.build()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        build.build()
+    torch.cuda.set_device(local)
+    cfg = dict(DREAM_7B)
+    d = DREAM
+    canvas = d["prompt"] + d["gen"]
+    rt = Runtime(model_config=cfg, synthetic_seed=0, device_ordinal=local, max_seq=canvas, max_prefill_rows=canvas)
+    sess = rt.session({"decode_strategy": "entropy_count"})
+    prompt = [int(t) for t in np.random.default_rng(rank).integers(0, 151643, size=d["prompt"])]
+
+    def request():
+        return sess.generate(prompt, max_tokens=d["gen"], steps=d["steps"], temperature=d["temperature"],
+                             top_p=d["top_p"], eps=d["eps"])
+
+    for _ in range(args.warmup):
+        request()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    results = []
+    with ClockSampler(local) as clocks:
+        wall0 = time.perf_counter()
+        for _ in range(args.steps):
+            results.append(request())
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    dev_ms = float(np.mean([r["decode_ms"] for r in results]))
+    e2e_ms = float(np.mean([r["total_ms"] for r in results]))
+    forwards = float(np.mean([r["forward_count"] for r in results]))
+    committed = float(np.mean([r["committed_token_count"] for r in results]))
+    stats = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    dev_ms, e2e_ms = (float(v) for v in stats.tolist())
+    sess.close()
+    rt.close()
+    if rank != 0:
+        return None
+    # frontier sizes of the proceeding steps, from the host schedule the device follows
+    import ctypes
+    sched = (ctypes.c_int32 * d["steps"])()
+    _lib.check(_lib.load().drt_entropy_count_schedule(d["gen"], d["steps"], d["eps"], sched))
+    left, fronts = d["gen"], []
+    for k in sched:
+        if k > 0:
+            fronts.append(left)
+            left -= k
+    flops = _dream_flops(cfg, canvas, float(np.mean(fronts)))
+    ms_step = dev_ms / max(1.0, forwards)
+    achieved = flops / (ms_step * 1e-3) / 1e12
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(pk.get("bf16_tflops_sustained", 1400.0))
+    return {
+        "metric": METRIC,
+        "value": round(world * committed / (dev_ms * 1e-3), 3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dev_ms, 3),
+        "ms_per_denoising_step": round(ms_step, 4),
+        "tokens_per_s_per_request": round(committed / (dev_ms * 1e-3), 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights and prompts)",
+        "config": {"workload": (f"cfg2: Dream-7B-arch full-canvas masked diffusion, prompt {d['prompt']} + canvas "
+                                f"{d['gen']}, {d['steps']} steps, entropy_count (NegEntropy T {d['temperature']}, "
+                                f"top_p {d['top_p']}, eps {d['eps']}), MASK excluded, argmax tokens"),
+                   "requests_per_gpu": 1, "parallelism": f"request-parallel x{world}",
+                   "committed_tokens_per_request": committed, "denoising_steps_per_request": forwards,
+                   "l2": "inputs larger than L2: 15.2 GB of weights streamed every denoising step"},
+        "roofline": {"bound": "tensor", "kernel": "one full-canvas denoising step (CUDA graph of the step's kernels)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4),
+                     "peak_source": "measured (sustained)" if pk else "fallback",
+                     "algorithmic_flops_per_step": int(flops), "traffic": None},
+        "e2e": {"value": round(world * committed / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
+                "h2d_bytes_per_step": 4 * canvas, "d2h_bytes_per_step": 4 * canvas + 64},
+        "gpu_launches": int(results[-1]["kernel_launches"]) * args.steps,
+        "clocks": clocks.summary(),
+        "wall_s": round(wall, 3),
+    }
+
+
+def _cpu_dream_baseline(sample_rows: int = 4) -> dict:
+    """The reference's CPU algorithm for one cfg2 step, timed in pieces on this host: the float64
+    spec forward of one Dream-7B layer over the 512-row canvas (scaled to 28 layers), the float64
+    lm_head over a vocabulary slice (scaled to the full vocabulary and the mean frontier), and the
+    top-p NegEntropy selector on a few rows (scaled to the frontier)."""
+    from oracle import forward as ofwd
+    from oracle import selector as osel
+    from oracle.numerics import synth_weights
+
+    from diffusorrt_b200.config import DREAM_7B
+
+    cfg = dict(DREAM_7B)
+    canvas, front = DREAM["prompt"] + DREAM["gen"], DREAM["gen"] / 2.0
+    small_v = 2048
+    sub = dict(cfg, layer_count=1, vocab_size=small_v)
+    wts = synth_weights(sub, 0, linear_std=0.02, embed_std=0.02, bias_std=0.02)
+    cache = {k: np.asarray(v, dtype=np.float64) for k, v in wts.items()}
+    ids = [int(t) for t in np.random.default_rng(0).integers(0, small_v, size=canvas)]
+    t0 = time.perf_counter()
+    ofwd.forward_fp64(wts, sub, ids, bidirectional=True, output_rows=[0], cast=lambda k: cache.get(k))
+    t_layer = time.perf_counter() - t0
+    H, V = cfg["hidden_size"], cfg["vocab_size"]
+    rng = np.random.default_rng(1)
+    w_slice = rng.standard_normal((V // 16, H))
+    x = rng.standard_normal((16, H))
+    t1 = time.perf_counter()
+    _ = x @ w_slice.T
+    t_head = (time.perf_counter() - t1) * 16 * (front / 16)
+    logits = (rng.standard_normal((sample_rows, V)) * 3).astype(np.float32)
+    t2 = time.perf_counter()
+    osel.neg_entropy_rows(logits, temperature=DREAM["temperature"], top_p=DREAM["top_p"])
+    t_sel = (time.perf_counter() - t2) * front / sample_rows
+    step_s = t_layer * cfg["layer_count"] + t_head + t_sel
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"step_s": step_s, "ms_per_denoising_step": step_s * 1e3, "cores": cores,
+            "sample": (f"one cfg2 step: 1 of 28 Dream-7B layers (float64 spec forward, {canvas} rows, bidirectional) "
+                       f"scaled to 28; lm_head on 16 rows x V/16 scaled to {front:.0f} rows x V; top-p NegEntropy on "
+                       f"{sample_rows} rows scaled to {front:.0f}; measured {t_layer + (t_head + t_sel) / 16:.1f} s")}
+
+
 def _cpu_baseline(args, sample_layers: int = 1) -> dict:
     """The reference's CPU algorithm (float64 executable-spec forward over the whole window,
     float64 max-prob selector) for one denoising step of the workload, timed on this host."""
@@ -455,7 +612,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cfg1", choices=sorted(WORKLOADS) + ["cfg4"])
+    ap.add_argument("--workload", default="cfg1", choices=sorted(WORKLOADS) + ["cfg2", "cfg4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -473,6 +630,23 @@ def main():
                           "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
                                            "sample": samples[0]["sample"]},
                           "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    if args.impl == "reference" and args.workload == "cfg2":
+        if rank != 0:
+            return
+        cb = _cpu_dream_baseline()
+        tokens = DREAM["gen"]
+        sched_steps = DREAM["steps"]
+        value = tokens / (cb["step_s"] * sched_steps)
+        print(json.dumps({"metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["step_s"] * sched_steps * 1e3,
+                          "ms_per_denoising_step": cb["ms_per_denoising_step"], "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+                          "config": {"workload": "cfg2", "prompt": DREAM["prompt"], "gen": DREAM["gen"]},
+                          "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cb["cores"], "kind": "port",
+                                           "sample": cb["sample"]},
+                          "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}), flush=True)
         return
     if args.impl == "reference":
@@ -508,6 +682,21 @@ def main():
                 cb = _cpu_selector_baseline()
                 line["cpu_baseline"] = {"value": round(cb["GB_per_s"], 3), "unit": "GB/s", "cores": 1, "kind": "port",
                                         "sample": cb["sample"]}
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+    if args.workload == "cfg2":
+        line = _run_dream(args, world, rank, local)
+        if rank == 0 and line is not None:
+            if not args.no_cpu_baseline and world == 1:
+                cb = _cpu_dream_baseline()
+                steps = line["config"]["denoising_steps_per_request"]
+                tokens = line["config"]["committed_tokens_per_request"]
+                line["cpu_baseline"] = {"value": round(tokens / (cb["step_s"] * steps), 6), "unit": "tokens/s",
+                                        "cores": cb["cores"], "kind": "port", "sample": cb["sample"],
+                                        "ms_per_denoising_step": round(cb["ms_per_denoising_step"], 1)}
             print(json.dumps(line), flush=True)
         if world > 1:
             import torch.distributed as dist

@@ -23,6 +23,7 @@ STATUS_NAMES = {0: "OK", 1: "VERSION_MISMATCH", 2: "INVALID_ARGUMENT", 3: "UNSUP
                 5: "DEVICE_TIMEOUT"}
 
 STRATEGY_BLOCK_THRESHOLD = 0
+STRATEGY_ENTROPY_COUNT = 5
 STRATEGY_BD3_FIXED_QUOTA = 7
 COMMIT_THRESHOLD = 2
 COMMIT_FIXED_QUOTA = 3
@@ -58,7 +59,8 @@ class GenerateParams(ctypes.Structure):
     _fields_ = [("decode_strategy", ctypes.c_int32), ("steps", ctypes.c_int32), ("block_size", ctypes.c_int32),
                 ("max_tokens", ctypes.c_int32), ("mask_token_id", ctypes.c_int32), ("eos_token_id", ctypes.c_int32),
                 ("confidence_threshold", ctypes.c_double), ("rounds_per_block", ctypes.c_int32),
-                ("trace_steps", ctypes.c_int32)]
+                ("trace_steps", ctypes.c_int32), ("temperature", ctypes.c_double), ("top_p", ctypes.c_double),
+                ("eps", ctypes.c_double)]
 
 
 class GenerateResult(ctypes.Structure):
@@ -111,6 +113,7 @@ SIGNATURES = {
     "drt_session_generate": (ctypes.c_int, [_P, ctypes.POINTER(GenerateParams), _I32P, ctypes.c_int32, _I32P,
                                             ctypes.POINTER(GenerateResult), ctypes.POINTER(StepTrace)]),
     "drt_session_metrics": (ctypes.c_int, [_P, ctypes.POINTER(Metrics)]),
+    "drt_entropy_count_schedule": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_double, _I32P]),
     "drt_session_kv_pointers": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
     "drt_session_close": (None, [_P]),
     "drt_selector_scratch_bytes": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32]),
@@ -120,6 +123,8 @@ SIGNATURES = {
                                                  ctypes.c_double, _P, _P, _P]),
     "drt_selector_gather": (ctypes.c_int, [_P, ctypes.c_int64, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                            ctypes.c_double, _P, _P, _P, _P]),
+    "drt_selector_topp": (ctypes.c_int, [_P, ctypes.c_int64, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
+                                         ctypes.c_double, ctypes.c_int32, ctypes.c_double, _P, _P, _P, _P]),
     "drt_select_choices": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
                                           ctypes.c_double, _P, _P, _P]),
     "drt_quantize_q4": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int32, _P, _P, _P, _P]),

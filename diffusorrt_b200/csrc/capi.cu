@@ -21,6 +21,7 @@
 #include "attention.cuh"
 #include "attention_decode.cuh"
 #include "common.cuh"
+#include "dream.cuh"
 #include "gemm.cuh"
 #include "gemm_decode.cuh"
 #include "policy.cuh"
@@ -692,6 +693,24 @@ struct drt_session {
   int g_step_geom[2] = {-1, -1};      // (mask origin, block size) baked into each graph
   int g_fwd_geom[2] = {-1, -1};
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  // full-canvas (entropy_count) sessions
+  bool dream = false;
+  int head_cap = kMaxFrontier;        // rows the final-norm / lm_head / selector buffers hold
+  int* row_tie = nullptr;             // [head_cap] per-row certification bits (top-p selector)
+  DreamState* dstate = nullptr;
+  DreamState* hdstate = nullptr;      // pinned
+  int* d_fpos = nullptr;              // [head_cap] frontier positions
+  int* d_klist = nullptr;             // transfer count per proceeding step
+  int* d_stepof = nullptr;            // loop step of each proceeding step
+  int d_steps_cap = 0;
+  CUtensorMap m_xf128;
+  cudaGraphExec_t g_dream = nullptr;  // plan + full-canvas forward + head + top-p score + commit
+  int g_dream_kernels = 0;
+  struct DreamKey {
+    int canvas_len, prompt_len, mask_id;
+    double temperature, top_p;
+    StepTrace* trace;
+  } g_dream_key = {-1, -1, -1, 0.0, 0.0, nullptr};
   // metrics
   int64_t m_forwards = 0, m_rows = 0, m_prefill_rows = 0, m_committed = 0, m_near = 0, m_exact = 0;
   double m_ms = 0.0;
@@ -1045,15 +1064,263 @@ int prefill(drt_session* s, int p0, int p1, int prompt_len, int block_size, int 
   }
   return DRT_OK;
 }
+
+constexpr double kToppTieRel = 9.313225746154785e-10;  // 2^-30: nucleus-mass certification bound
+
+// One entropy_count step as a graph: plan (frontier, transfer), the whole canvas forwarded with
+// bidirectional attention, final norm over the shifted rows of the frontier, lm_head, top-p
+// entropy selector and the top-k commit. Shapes are static; the frontier count lives on the device.
+int capture_dream(drt_session* s, const DreamState& g, double temperature, double top_p, cudaGraphExec_t* out) {
+  drt_model* m = s->m;
+  const int gen_cap = g.canvas_len - g.prompt_len;
+  cudaGraph_t graph = nullptr;
+  CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = DRT_OK;
+  if (launch_k(dream_plan_kernel, dim3(1), dim3(kDreamThreads), 0, s->stream, true, s->dstate,
+               static_cast<const int*>(s->canvas), s->d_fpos, s->scope_rows, static_cast<const int*>(s->d_klist)) != cudaSuccess)
+    rc = set_error(DRT_INTERNAL_ERROR, "plan launch failed");
+  if (rc == DRT_OK) {
+    Fwd f = {};
+    f.rows = g.canvas_len;
+    f.pos0 = 0;
+    f.kv_len = g.canvas_len;
+    f.prompt_len = 0;
+    f.block_size = 1;
+    f.bidirectional = 1;
+    rc = enqueue_layers(s, f);
+  }
+  const int* n_dev = &s->dstate->n_frontier;
+  if (rc == DRT_OK) rc = run_rmsnorm(s, s->h, s->scope_rows, gen_cap, n_dev, m->final_norm, s->xf);
+  if (rc == DRT_OK) {
+    Fwd f = {};
+    f.rows = gen_cap;
+    f.rows_dev = n_dev;
+    GemmArgs a = base_args(s, m->V, m->H, f);
+    a.epi = EPI_STORE_F32;
+    a.out_f32 = s->logits;
+    a.ld_out = m->V;
+    rc = run_gemm<128>(s, m->m_lm, s->m_xf128, a, false);
+  }
+  if (rc == DRT_OK) {
+    ToppArgs t;
+    memset(&t, 0, sizeof(t));
+    t.logits = s->logits;
+    t.ld = m->V;
+    t.rows = gen_cap;
+    t.rows_dev = n_dev;
+    t.vocab = m->V;
+    t.temperature = temperature;
+    t.top_p = top_p;
+    t.exclude = (g.mask_id >= 0 && g.mask_id < m->V) ? g.mask_id : -1;
+    t.tie_rel = kToppTieRel;
+    t.conf = s->conf;
+    t.token = s->token;
+    t.tie = s->row_tie;
+    if (launch_k(sel_topp_entropy_kernel, dim3(gen_cap), dim3(kToppThreads), 0, s->stream, true, t) != cudaSuccess)
+      rc = set_error(DRT_INTERNAL_ERROR, "selector launch failed");
+  }
+  if (rc == DRT_OK &&
+      launch_k(dream_commit_kernel, dim3(1), dim3(kDreamThreads), 0, s->stream, true, s->dstate, s->canvas,
+               static_cast<const int*>(s->d_fpos), static_cast<const double*>(s->conf), static_cast<const int*>(s->token),
+               static_cast<const int*>(s->row_tie), kTieRel, static_cast<const int*>(s->d_stepof), s->trace) != cudaSuccess)
+    rc = set_error(DRT_INTERNAL_ERROR, "commit launch failed");
+  cudaError_t e = cudaStreamEndCapture(s->stream, &graph);
+  if (rc != DRT_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return set_error(DRT_INTERNAL_ERROR, "graph capture failed: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(out, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return set_error(DRT_INTERNAL_ERROR, "graph instantiate failed: %s", cudaGetErrorString(e));
+  return DRT_OK;
+}
+
+// linspace(1, eps, steps + 1) in float64 cast to float32, as NumPy computes it: y = i * step,
+// y += 1, the last entry set to eps (numpy/_core/function_base.py linspace).
+void entropy_count_timesteps(int steps, double eps, std::vector<float>* ts) {
+  ts->assign(steps + 1, 0.0f);
+  const double step = (eps - 1.0) / static_cast<double>(steps);
+  for (int i = 0; i <= steps; ++i) {
+    volatile double y = static_cast<double>(i) * step;  // two roundings, as NumPy's two array ops
+    (*ts)[i] = static_cast<float>(y + 1.0);
+  }
+  (*ts)[steps] = static_cast<float>(eps);
+}
+
+void entropy_count_plan(int n_masked, int steps, double eps, int* transfer) {
+  std::vector<float> ts;
+  entropy_count_timesteps(steps, eps, &ts);
+  int n = n_masked;
+  for (int i = 0; i < steps; ++i) {
+    int k = 0;
+    if (n > 0) {
+      if (i < steps - 1) {
+        const double t = static_cast<double>(ts[i]), u = static_cast<double>(ts[i + 1]);
+        const double want = static_cast<double>(n) * (1.0 - u / t);
+        k = want >= static_cast<double>(n) ? n : static_cast<int>(want);
+      } else {
+        k = n;
+      }
+      if (k < 0) k = 0;
+      n -= k;
+    }
+    transfer[i] = k;
+  }
+}
+
+int dream_generate(drt_session* s, const drt_generate_params* p, const int32_t* prompt, int32_t prompt_len, int32_t* out,
+                   drt_generate_result* result, drt_step_trace* trace) {
+  drt_model* m = s->m;
+  REQUIRE(p->steps >= 1, "steps must be >= 1");
+  REQUIRE(p->max_tokens >= 1, "max_tokens must be >= 1");
+  REQUIRE(prompt_len >= 1, "device generation requires a non-empty prompt");
+  const int canvas_len = prompt_len + p->max_tokens;
+  REQUIRE(canvas_len <= s->rows_cap && canvas_len <= s->max_seq,
+          "full-canvas forward of %d positions exceeds the session capacity (%d rows, %d positions)", canvas_len,
+          s->rows_cap, s->max_seq);
+  REQUIRE(p->max_tokens <= s->head_cap, "canvas of %d masked positions exceeds the frontier capacity %d", p->max_tokens,
+          s->head_cap);
+  REQUIRE(std::isfinite(p->temperature) && std::isfinite(p->top_p) && p->top_p > 0.0, "temperature / top_p invalid");
+  REQUIRE(std::isfinite(p->eps) && p->eps >= 0.0 && p->eps <= 1.0, "eps must be in [0, 1]");
+  REQUIRE(p->mask_token_id >= 0 && p->mask_token_id < m->V, "mask token outside the vocabulary");
+  for (int i = 0; i < prompt_len; ++i) {
+    REQUIRE(prompt[i] >= 0 && prompt[i] < m->V, "prompt token %d outside the vocabulary", prompt[i]);
+    REQUIRE(prompt[i] != p->mask_token_id, "device generation cannot carry MASK in its prompt");
+  }
+  CK(cudaSetDevice(s->device));
+  // schedule: the proceeding steps and their transfer counts
+  std::vector<int> transfer(p->steps);
+  entropy_count_plan(p->max_tokens, p->steps, p->eps, transfer.data());
+  std::vector<int> klist, stepof;
+  int iterations = 0, left = p->max_tokens;
+  for (int i = 0; i < p->steps && left > 0; ++i) {
+    ++iterations;
+    if (transfer[i] > 0) {
+      klist.push_back(transfer[i]);
+      stepof.push_back(i);
+      left -= transfer[i];
+    }
+  }
+  const int n_proceed = static_cast<int>(klist.size());
+  if (n_proceed > s->d_steps_cap) {
+    if (s->d_klist) cudaFree(s->d_klist);
+    if (s->d_stepof) cudaFree(s->d_stepof);
+    s->d_klist = s->d_stepof = nullptr;
+    CK(cudaMalloc(&s->d_klist, sizeof(int) * n_proceed));
+    CK(cudaMalloc(&s->d_stepof, sizeof(int) * n_proceed));
+    s->d_steps_cap = n_proceed;
+    if (s->g_dream) { cudaGraphExecDestroy(s->g_dream); s->g_dream = nullptr; }
+  }
+  if (p->trace_steps > s->trace_cap) {
+    if (s->trace) cudaFree(s->trace);
+    s->trace = nullptr;
+    CK(cudaMalloc(&s->trace, sizeof(StepTrace) * p->trace_steps));
+    s->trace_cap = p->trace_steps;
+    if (s->g_dream) { cudaGraphExecDestroy(s->g_dream); s->g_dream = nullptr; }
+  }
+  DreamState* hs = s->hdstate;
+  memset(hs, 0, sizeof(DreamState));
+  hs->canvas_len = canvas_len;
+  hs->prompt_len = prompt_len;
+  hs->mask_id = p->mask_token_id;
+  hs->n_proceed = n_proceed;
+  hs->trace_cap = std::min(p->trace_steps, s->trace_cap);
+  auto& key = s->g_dream_key;
+  if (s->g_dream != nullptr && (key.canvas_len != canvas_len || key.prompt_len != prompt_len ||
+                                key.mask_id != p->mask_token_id || key.temperature != p->temperature ||
+                                key.top_p != p->top_p || key.trace != s->trace)) {
+    cudaGraphExecDestroy(s->g_dream);
+    s->g_dream = nullptr;
+  }
+  if (s->g_dream == nullptr) {
+    const int64_t before = g_launches;
+    TRY(capture_dream(s, *hs, p->temperature, p->top_p, &s->g_dream));
+    s->g_dream_kernels = static_cast<int>(g_launches - before);
+    key = {canvas_len, prompt_len, p->mask_token_id, p->temperature, p->top_p, s->trace};
+  }
+  std::vector<int> canvas(canvas_len, p->mask_token_id);
+  std::copy(prompt, prompt + prompt_len, canvas.begin());
+  cudaEvent_t e_total0 = nullptr, e_total1 = nullptr, e_dec0 = nullptr, e_dec1 = nullptr;
+  CK(cudaEventCreate(&e_total0));
+  CK(cudaEventCreate(&e_total1));
+  CK(cudaEventCreate(&e_dec0));
+  CK(cudaEventCreate(&e_dec1));
+  CK(cudaEventRecord(e_total0, s->stream));
+  CK(cudaMemcpyAsync(s->canvas, canvas.data(), sizeof(int) * canvas_len, cudaMemcpyHostToDevice, s->stream));
+  if (n_proceed > 0) {
+    CK(cudaMemcpyAsync(s->d_klist, klist.data(), sizeof(int) * n_proceed, cudaMemcpyHostToDevice, s->stream));
+    CK(cudaMemcpyAsync(s->d_stepof, stepof.data(), sizeof(int) * n_proceed, cudaMemcpyHostToDevice, s->stream));
+  }
+  CK(cudaMemcpyAsync(s->dstate, hs, sizeof(DreamState), cudaMemcpyHostToDevice, s->stream));
+  CK(cudaEventRecord(e_dec0, s->stream));
+  int rc = DRT_OK;
+  const auto host0 = std::chrono::steady_clock::now();
+  for (int i = 0; i < n_proceed; ++i) {
+    if (cudaGraphLaunch(s->g_dream, s->stream) != cudaSuccess) {
+      rc = set_error(DRT_INTERNAL_ERROR, "graph launch failed");
+      break;
+    }
+  }
+  const float host_ms = std::chrono::duration<float, std::milli>(std::chrono::steady_clock::now() - host0).count();
+  cudaEventRecord(e_dec1, s->stream);
+  cudaMemcpyAsync(hs, s->dstate, sizeof(DreamState), cudaMemcpyDeviceToHost, s->stream);
+  cudaMemcpyAsync(out, s->canvas, sizeof(int) * canvas_len, cudaMemcpyDeviceToHost, s->stream);
+  cudaEventRecord(e_total1, s->stream);
+  cudaError_t se = cudaStreamSynchronize(s->stream);
+  if (rc == DRT_OK && se != cudaSuccess) rc = set_error(DRT_INTERNAL_ERROR, "decode failed: %s", cudaGetErrorString(se));
+  float dec_ms = 0.f, tot_ms = 0.f;
+  cudaEventElapsedTime(&dec_ms, e_dec0, e_dec1);
+  cudaEventElapsedTime(&tot_ms, e_total0, e_total1);
+  cudaEventDestroy(e_dec0);
+  cudaEventDestroy(e_dec1);
+  cudaEventDestroy(e_total0);
+  cudaEventDestroy(e_total1);
+  TRY(rc);
+  TRY(check_status(s));
+  if (trace != nullptr && p->trace_steps > 0) {
+    const int nt = std::min(hs->forward_count, std::min(p->trace_steps, s->trace_cap));
+    CK(cudaMemcpy(trace, s->trace, sizeof(StepTrace) * nt, cudaMemcpyDeviceToHost));
+  }
+  if (result) {
+    result->forward_count = hs->forward_count;
+    result->iteration_count = iterations;
+    result->committed_token_count = hs->committed_count;
+    result->near_tie_steps = hs->near_tie_steps;
+    result->exact_tie_steps = hs->exact_tie_steps;
+    result->stopped = left == 0 ? 1 : 0;
+    result->canvas_len = canvas_len;
+    result->prefill_ms = 0.f;
+    result->decode_ms = dec_ms;
+    result->total_ms = tot_ms;
+    result->kernel_launches = n_proceed * s->g_dream_kernels;
+    result->host_enqueue_ms = host_ms;
+  }
+  s->m_forwards += hs->forward_count;
+  s->m_rows += static_cast<int64_t>(hs->forward_count) * canvas_len;
+  s->m_committed += hs->committed_count;
+  s->m_near += hs->near_tie_steps;
+  s->m_exact += hs->exact_tie_steps;
+  s->m_ms += dec_ms;
+  s->started = false;
+  return DRT_OK;
+}
 }  // namespace
 
 extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt_session** out) {
   REQUIRE(m && cfg && out, "null argument");
   *out = nullptr;
-  REQUIRE(cfg->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA || cfg->decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD,
-          "device sessions run only block_threshold and bd3_fixed_quota (got strategy %d)", cfg->decode_strategy);
-  REQUIRE(cfg->attention_mask_kind == DRT_MASK_D2F_HYBRID, "this device session serves the d2f_hybrid graph only");
-  REQUIRE(cfg->block_size >= 1 && cfg->block_size <= 32, "block_size must be in [1, 32]");
+  const bool dream = cfg->decode_strategy == DRT_STRATEGY_ENTROPY_COUNT;
+  REQUIRE(dream || cfg->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA || cfg->decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD,
+          "device sessions run only block_threshold, bd3_fixed_quota and entropy_count (got strategy %d)",
+          cfg->decode_strategy);
+  if (dream) {
+    REQUIRE(cfg->attention_mask_kind == DRT_MASK_BIDIRECTIONAL, "entropy_count sessions serve the bidirectional graph only");
+    REQUIRE(!m->quantized, "entropy_count sessions need bf16 linears (the 4-bit path forwards at most %d rows)", kMaxFwdRows);
+  } else {
+    REQUIRE(cfg->attention_mask_kind == DRT_MASK_D2F_HYBRID, "this device session serves the d2f_hybrid graph only");
+    REQUIRE(cfg->block_size >= 1 && cfg->block_size <= 32, "block_size must be in [1, 32]");
+  }
   CK(cudaSetDevice(m->device));
   drt_session* s = new drt_session();
   s->m = m;
@@ -1063,6 +1330,8 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   s->rows_cap = std::max(64, ((std::max(m->cfg.max_prefill_rows, 64) + 127) / 128) * 128);
   s->planes = m->L * m->nkv;
   s->sms = num_sms(m->device);
+  s->dream = dream;
+  s->head_cap = dream ? std::min(s->rows_cap, kDreamMaxFrontier) : kMaxFrontier;
   auto fail = [&](int rc) { drt_session_close(s); return rc; };
   int rc;
   if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "stream create failed"));
@@ -1074,8 +1343,8 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = salloc(s, &s->q, static_cast<size_t>(R) * qd)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->attn, static_cast<size_t>(R) * qd)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->act, static_cast<size_t>(R) * m->I)) != DRT_OK) return fail(rc);
-  if ((rc = salloc(s, &s->xf, static_cast<size_t>(kMaxFrontier) * H)) != DRT_OK) return fail(rc);
-  if ((rc = salloc(s, &s->logits, static_cast<size_t>(kMaxFrontier) * m->V)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->xf, static_cast<size_t>(s->head_cap) * H)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->logits, static_cast<size_t>(s->head_cap) * m->V)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->ss, static_cast<size_t>(kMaxFwdRows) * (H / 128))) != DRT_OK) return fail(rc);
   const size_t kv = static_cast<size_t>(s->planes) * s->max_seq * 128;
   if ((rc = salloc(s, &s->kcache, kv)) != DRT_OK) return fail(rc);
@@ -1131,10 +1400,17 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = salloc(s, &s->sel_cnt, kMaxFrontier)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->sel_amax, kMaxFrontier)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->sel_sum, kMaxFrontier)) != DRT_OK) return fail(rc);
-  if ((rc = salloc(s, &s->conf, kMaxFrontier)) != DRT_OK) return fail(rc);
-  if ((rc = salloc(s, &s->token, kMaxFrontier)) != DRT_OK) return fail(rc);
-  if ((rc = salloc(s, &s->scope_rows, kMaxFrontier)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->conf, s->head_cap)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->token, s->head_cap)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->scope_rows, s->head_cap)) != DRT_OK) return fail(rc);
   if (cudaMemset(s->sel_cnt, 0, sizeof(int) * kMaxFrontier) != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "memset failed"));
+  if (dream) {
+    if ((rc = salloc(s, &s->row_tie, s->head_cap)) != DRT_OK) return fail(rc);
+    if ((rc = salloc(s, &s->d_fpos, s->head_cap)) != DRT_OK) return fail(rc);
+    if ((rc = salloc(s, &s->dstate, 1)) != DRT_OK) return fail(rc);
+    if (cudaMallocHost(&s->hdstate, sizeof(DreamState)) != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "pinned alloc failed"));
+    if ((rc = map_matrix(&s->m_xf128, s->xf, s->head_cap, H, 128)) != DRT_OK) return fail(rc);
+  }
   if ((rc = salloc(s, &s->status, 1)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->state, 1)) != DRT_OK) return fail(rc);
   if (cudaMemset(s->status, 0, sizeof(int)) != cudaSuccess || cudaMemset(s->state, 0, sizeof(DecodeState)) != cudaSuccess)
@@ -1149,7 +1425,7 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = map_matrix(&s->m_attn128, s->attn, R, qd, 128)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_act64, s->act, R, m->I, 64)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_act128, s->act, R, m->I, 128)) != DRT_OK) return fail(rc);
-  if ((rc = map_matrix(&s->m_xf64, s->xf, kMaxFrontier, H, 64)) != DRT_OK) return fail(rc);
+  if ((rc = map_matrix(&s->m_xf64, s->xf, s->head_cap, H, 64)) != DRT_OK) return fail(rc);
   {
     const uint64_t dq[3] = {128, static_cast<uint64_t>(m->nq), static_cast<uint64_t>(R)};
     const uint64_t sq[2] = {256, static_cast<uint64_t>(qd) * 2};
@@ -1177,7 +1453,11 @@ extern "C" void drt_session_close(drt_session* s) {
   if (s->stream) cudaStreamSynchronize(s->stream);
   if (s->g_step) cudaGraphExecDestroy(s->g_step);
   if (s->g_fwd) cudaGraphExecDestroy(s->g_fwd);
+  if (s->g_dream) cudaGraphExecDestroy(s->g_dream);
   for (void* p : s->allocs) cudaFree(p);
+  if (s->d_klist) cudaFree(s->d_klist);
+  if (s->d_stepof) cudaFree(s->d_stepof);
+  if (s->hdstate) cudaFreeHost(s->hdstate);
   if (s->trace) cudaFree(s->trace);
   if (s->hstate) cudaFreeHost(s->hstate);
   if (s->hflags) cudaFreeHost(s->hflags);
@@ -1308,6 +1588,11 @@ extern "C" int drt_session_execute_window(drt_session* s, const int32_t* token_i
   REQUIRE(prompt_len >= 0 && prompt_len <= n_tokens && block_size >= 1, "bad mask geometry");
   for (int i = 0; i < n_scope; ++i) REQUIRE(scope[i] >= 0 && scope[i] < n_tokens, "scope position %d outside the window", scope[i]);
   for (int i = 0; i < n_tokens; ++i) REQUIRE(token_ids[i] >= 0 && token_ids[i] < s->m->V, "token outside the vocabulary");
+  // A full-canvas (entropy_count) session forwards the window in one bidirectional pass and applies
+  // the Dream logits convention: position p reads raw row max(p - 1, 0).
+  if (s->dream)
+    REQUIRE(n_tokens <= s->rows_cap, "bidirectional window of %d positions exceeds the session's %d rows", n_tokens,
+            s->rows_cap);
   CK(cudaSetDevice(s->device));
   drt_model* m = s->m;
   CK(cudaMemcpyAsync(s->canvas, token_ids, sizeof(int) * n_tokens, cudaMemcpyHostToDevice, s->stream));
@@ -1321,6 +1606,7 @@ extern "C" int drt_session_execute_window(drt_session* s, const int32_t* token_i
     f.kv_len = c0 + f.rows;
     f.prompt_len = prompt_len;
     f.block_size = block_size;
+    f.bidirectional = s->dream ? 1 : 0;
     TRY(enqueue_layers(s, f));
     // Scope rows inside this chunk, in scope order, up to 64 per head pass.
     std::vector<int> idx;
@@ -1329,7 +1615,7 @@ extern "C" int drt_session_execute_window(drt_session* s, const int32_t* token_i
     for (size_t b = 0; b < idx.size(); b += kMaxFrontier) {
       const int cnt = static_cast<int>(std::min<size_t>(kMaxFrontier, idx.size() - b));
       rows.assign(cnt, 0);
-      for (int j = 0; j < cnt; ++j) rows[j] = scope[idx[b + j]] - c0;
+      for (int j = 0; j < cnt; ++j) rows[j] = (s->dream ? std::max(scope[idx[b + j]] - 1, 0) : scope[idx[b + j]]) - c0;
       CK(cudaMemcpyAsync(s->scope_rows, rows.data(), sizeof(int) * cnt, cudaMemcpyHostToDevice, s->stream));
       TRY(enqueue_head(s, s->scope_rows, cnt, nullptr, false));
       for (int j = 0; j < cnt; ++j)
@@ -1352,6 +1638,10 @@ extern "C" int drt_session_execute_window(drt_session* s, const int32_t* token_i
 extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p, const int32_t* prompt, int32_t prompt_len,
                                     int32_t* out, drt_generate_result* result, drt_step_trace* trace) {
   REQUIRE(s && p && prompt && out, "null argument");
+  if (s->dream) {
+    REQUIRE(p->decode_strategy == DRT_STRATEGY_ENTROPY_COUNT, "an entropy_count session generates with entropy_count only");
+    return dream_generate(s, p, prompt, prompt_len, out, result, trace);
+  }
   REQUIRE(p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA || p->decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD,
           "device generation runs bd3_fixed_quota or block_threshold");
   REQUIRE(p->block_size >= 1 && p->block_size <= 32, "block_size must be in [1, 32]");
@@ -1504,6 +1794,14 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
   return DRT_OK;
 }
 
+extern "C" int drt_entropy_count_schedule(int32_t n_masked, int32_t steps, double eps, int32_t* transfer) {
+  REQUIRE(transfer, "null argument");
+  REQUIRE(n_masked >= 0 && steps >= 1, "n_masked must be >= 0 and steps >= 1");
+  REQUIRE(std::isfinite(eps) && eps >= 0.0 && eps <= 1.0, "eps must be in [0, 1]");
+  entropy_count_plan(n_masked, steps, eps, transfer);
+  return DRT_OK;
+}
+
 extern "C" int drt_session_metrics(drt_session* s, drt_metrics* out) {
   REQUIRE(s && out, "null argument");
   out->forward_count = s->m_forwards;
@@ -1609,6 +1907,34 @@ extern "C" int drt_select_choices(const double* conf, const int32_t* offsets, in
   if (n_items == 0) return DRT_OK;
   CK(launch_k(sel_choose_kernel, dim3(n_items), dim3(32), 0, static_cast<cudaStream_t>(stream), false, conf, offsets, mode, k, tau,
               tie_rel, chosen, tie));
+  return DRT_OK;
+}
+
+extern "C" int drt_selector_topp(const float* logits, int64_t ld, const int32_t* row_index, int32_t n_rows, int32_t vocab,
+                                 double temperature, double top_p, int32_t exclude_token, double tie_rel, double* conf,
+                                 int32_t* token, int32_t* tie, void* stream) {
+  REQUIRE(logits && conf && token, "null argument");
+  REQUIRE(n_rows >= 0 && n_rows <= 65535 * 16, "n_rows outside [0, %d]", 65535 * 16);
+  REQUIRE(vocab >= 1 && ld >= vocab, "vocab must be >= 1 and ld >= vocab");
+  REQUIRE(std::isfinite(temperature) && std::isfinite(top_p) && top_p > 0.0, "temperature / top_p invalid");
+  REQUIRE(tie_rel >= 0.0, "tie_rel must be >= 0");
+  REQUIRE(exclude_token >= -1 && exclude_token < vocab, "exclude_token outside the vocabulary");
+  if (n_rows == 0) return DRT_OK;
+  ToppArgs t;
+  memset(&t, 0, sizeof(t));
+  t.logits = logits;
+  t.ld = ld;
+  t.row_index = row_index;
+  t.rows = n_rows;
+  t.vocab = vocab;
+  t.temperature = temperature;
+  t.top_p = top_p;
+  t.exclude = exclude_token;
+  t.tie_rel = tie_rel;
+  t.conf = conf;
+  t.token = token;
+  t.tie = tie;
+  CK(launch_k(sel_topp_entropy_kernel, dim3(n_rows), dim3(kToppThreads), 0, static_cast<cudaStream_t>(stream), false, t));
   return DRT_OK;
 }
 

@@ -311,4 +311,198 @@ __global__ void __launch_bounds__(32) sel_choose_kernel(const double* __restrict
   if (lane == 0) tie[b] = flag;
 }
 
+// Negative-entropy confidence with a top-p nucleus (_entropy_confidence with top_p,
+// python/src/edllm/backends/diffusion_runtime.py:90-114, _top_p_filter :358-370, _softmax :373-378),
+// one CTA per row:
+//   a = f64(x) / T (T > 0); the excluded token (MASK) is -inf;
+//   sort a descending, cum = cumsum(softmax(sorted)); drop every entry with cum > top_p except the
+//   first; p' = softmax over the kept entries; conf = f32(sum p' log(p' + 1e-10)); token = argmax p'.
+// The kept set is found without sorting. v_b, the first dropped value, is the largest logit whose
+// inclusive mass (the p of every entry >= v_b) exceeds top_p. Every entry above v_b is kept, and of
+// the m copies of v_b the first c are, c = #{i in 1..m : above + i * p(v_b) <= top_p} (at least one
+// when v_b is the maximum). Which copies the reference's unstable sort puts first does not change
+// the entropy, since the copies are equal, nor the token unless v_b is a tied maximum.
+// v_b is located by a radix search over the order-preserving 32-bit keys of the f32 logits: four
+// passes over the row, each accumulating the unnormalised mass exp(a - max) of the keys under the
+// current prefix into 256 digit buckets and descending into the bucket where the cumulative mass
+// from the top crosses top_p * S. bf16-rounded logits repeat often, so the tie copies are counted.
+// tie[r]: bit 2 when the kept copies are a strict subset of a tied maximum (the reference's sort
+// order picks the token); bit 1 when a cumulative mass at the cut is within tie_rel of top_p (the
+// reference's own summation order may decide the other way there).
+struct ToppArgs {
+  const float* logits;
+  int64_t ld;
+  const int* row_index;  // optional gather
+  int rows;
+  const int* rows_dev;   // optional device-side row count
+  int vocab;
+  double temperature;    // <= 0: no scaling
+  double top_p;          // >= 1: no nucleus
+  int exclude;           // -1 for none
+  double tie_rel;
+  double* conf;
+  int* token;
+  int* tie;              // optional
+};
+
+constexpr int kToppThreads = 512;
+
+__device__ __forceinline__ uint32_t f32_order_key(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ float f32_from_order_key(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+template <typename T>
+__device__ __forceinline__ T topp_block_sum(T v, T* red, int lane, int warp) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  T t = T(0);
+  for (int w = 0; w < kToppThreads / 32; ++w) t += red[w];
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const ToppArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int r = blockIdx.x;
+  const int rows = a.rows_dev != nullptr ? min(a.rows, *a.rows_dev) : a.rows;
+  if (r >= rows) return;
+  const int src = a.row_index != nullptr ? a.row_index[r] : r;
+  const float* x = a.logits + static_cast<int64_t>(src) * a.ld;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = kToppThreads / 32;
+  __shared__ double hist[256];
+  __shared__ int hcnt[256];
+  __shared__ double red_d[NW];
+  __shared__ float red_f[NW];
+  __shared__ int red_i[NW];
+  __shared__ uint32_t s_prefix, s_mask;
+  __shared__ double s_above;
+  __shared__ int s_count;
+  const double T = a.temperature > 0.0 ? a.temperature : 1.0;
+  const bool nucleus = a.top_p < 1.0;
+
+  // max logit and its first index
+  float m = -INFINITY;
+  int mi = INT_MAX;
+  for (int i = tid; i < a.vocab; i += kToppThreads) {
+    const float v = x[i];
+    if (i != a.exclude && v > m) { m = v; mi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, mi, o);
+    argmax_merge(m, mi, m2, i2);
+  }
+  if (lane == 0) { red_f[warp] = m; red_i[warp] = mi; }
+  __syncthreads();
+  float gm = red_f[0];
+  int gmi = red_i[0];
+  for (int w = 1; w < NW; ++w) argmax_merge(gm, gmi, red_f[w], red_i[w]);
+  const double am = static_cast<double>(gm) / T;
+  __syncthreads();
+
+  // S, then the radix search for v_b (the key of the first dropped value)
+  double S = 0.0;
+  uint32_t prefix = 0, pmask = 0;
+  double above = 0.0;
+  int count = 0;
+  if (nucleus) {
+    for (int level = 0; level < 4; ++level) {
+      const int shift = 24 - 8 * level;
+      for (int i = tid; i < 256; i += kToppThreads) { hist[i] = 0.0; hcnt[i] = 0; }
+      __syncthreads();
+      double part = 0.0;
+      for (int i = tid; i < a.vocab; i += kToppThreads) {
+        const float v = x[i];
+        const uint32_t k = f32_order_key(v);
+        if (i == a.exclude || (k & pmask) != prefix) continue;
+        const double e = exp(static_cast<double>(v) / T - am);
+        part += e;
+        const int d = static_cast<int>((k >> shift) & 255u);
+        atomicAdd(&hist[d], e);
+        if (level == 3) atomicAdd(&hcnt[d], 1);
+      }
+      if (level == 0) S = topp_block_sum(part, red_d, lane, warp);
+      else __syncthreads();
+      if (tid == 0) {
+        const double limit = a.top_p * S;
+        double cum = above;
+        int d = 255;
+        for (; d > 0; --d) {
+          if (cum + hist[d] > limit) break;
+          cum += hist[d];
+        }
+        s_above = cum;
+        s_count = hcnt[d];
+        s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+        s_mask = pmask | (0xFFu << shift);
+      }
+      __syncthreads();
+      prefix = s_prefix;
+      pmask = s_mask;
+      above = s_above;
+      count = s_count;
+      __syncthreads();
+    }
+  }
+  const uint32_t vb = prefix;
+  // kept copies of v_b and the certification flags
+  __shared__ int s_c, s_flag;
+  if (tid == 0) {
+    int c = 0, flag = 0;
+    if (nucleus) {
+      const double limit = a.top_p * S;
+      const double e = exp(static_cast<double>(f32_from_order_key(vb)) / T - am);
+      while (c < count && above + static_cast<double>(c + 1) * e <= limit) ++c;
+      if (above == 0.0 && c == 0) c = 1;
+      const double tol = a.tie_rel * limit;
+      if (!(fabs(above + static_cast<double>(c) * e - limit) > tol)) flag |= 1;
+      if (c < count && !(fabs(above + static_cast<double>(c + 1) * e - limit) > tol)) flag |= 1;
+      if (above == 0.0 && c < count) flag |= 2;
+    }
+    s_c = c;
+    s_flag = flag;
+  }
+  __syncthreads();
+  const int c = s_c;
+  const double e_vb = nucleus ? exp(static_cast<double>(f32_from_order_key(vb)) / T - am) : 0.0;
+
+  // normaliser over the kept entries
+  double sk = 0.0;
+  for (int i = tid; i < a.vocab; i += kToppThreads) {
+    const float v = x[i];
+    if (i == a.exclude || (nucleus && f32_order_key(v) <= vb)) continue;
+    sk += exp(static_cast<double>(v) / T - am);
+  }
+  double Sk = topp_block_sum(sk, red_d, lane, warp);
+  Sk += static_cast<double>(c) * e_vb;
+  // entropy sum p' log(p' + 1e-10)
+  double h = 0.0;
+  for (int i = tid; i < a.vocab; i += kToppThreads) {
+    const float v = x[i];
+    if (i == a.exclude || (nucleus && f32_order_key(v) <= vb)) continue;
+    const double pv = exp(static_cast<double>(v) / T - am) / Sk;
+    h += pv * log(pv + 1e-10);
+  }
+  double H = topp_block_sum(h, red_d, lane, warp);
+  if (tid == 0) {
+    if (c > 0) {
+      const double pv = e_vb / Sk;
+      H += static_cast<double>(c) * (pv * log(pv + 1e-10));
+    }
+    a.conf[r] = static_cast<double>(static_cast<float>(H));
+    a.token[r] = gmi;
+    if (a.tie != nullptr) a.tie[r] = s_flag;
+  }
+}
+
 }  // namespace drt

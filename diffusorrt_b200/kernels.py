@@ -67,6 +67,28 @@ def select_gather(logits: torch.Tensor, row_index: torch.Tensor, *, mode: int = 
     return conf, token
 
 
+def select_topp_entropy(logits: torch.Tensor, row_index: torch.Tensor | None = None, *, temperature: float = 0.2,
+                        top_p: float = 0.95, exclude_token: int = -1, tie_rel: float = 2.0 ** -30,
+                        stream: torch.cuda.Stream | None = None):
+    """NegEntropy with a top-p nucleus over rows (row_index, int32 CUDA, or every row) of f32 logits:
+    (confidence f64 holding the f32 value, token i32, tie bits i32)."""
+    if logits.dtype != torch.float32 or not logits.is_cuda or logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a row-major CUDA float32 [rows, vocab] tensor")
+    if row_index is not None and (row_index.dtype != torch.int32 or not row_index.is_contiguous()):
+        raise ValueError("row_index must be a contiguous CUDA int32 tensor")
+    n = row_index.numel() if row_index is not None else logits.shape[0]
+    dev = logits.device
+    conf = torch.empty(n, dtype=torch.float64, device=dev)
+    token = torch.empty(n, dtype=torch.int32, device=dev)
+    tie = torch.empty(max(1, n), dtype=torch.int32, device=dev)
+    _lib.check(_lib.load().drt_selector_topp(logits.data_ptr(), logits.stride(0),
+                                             row_index.data_ptr() if row_index is not None else None, n,
+                                             logits.shape[1], float(temperature), float(top_p), int(exclude_token),
+                                             float(tie_rel), conf.data_ptr(), token.data_ptr(), tie.data_ptr(),
+                                             _stream_ptr(stream)))
+    return conf, token, tie[:n]
+
+
 def select_choices(conf: torch.Tensor, offsets: torch.Tensor, *, mode: int, k: int = 1, tau: float = 0.9,
                    tie_rel: float = 2.0 ** -40, chosen: torch.Tensor | None = None, tie: torch.Tensor | None = None,
                    stream: torch.cuda.Stream | None = None):

@@ -35,7 +35,8 @@ import numpy as np
 from . import _lib
 from .config import QWEN3_06B_BD3LM, SYNTHETIC_STD, rope_half_tables
 
-_STRATEGY_IDS = {"block_threshold": _lib.STRATEGY_BLOCK_THRESHOLD, "bd3_fixed_quota": _lib.STRATEGY_BD3_FIXED_QUOTA}
+_STRATEGY_IDS = {"block_threshold": _lib.STRATEGY_BLOCK_THRESHOLD, "bd3_fixed_quota": _lib.STRATEGY_BD3_FIXED_QUOTA,
+                 "entropy_count": _lib.STRATEGY_ENTROPY_COUNT}
 _COMMIT_IDS = {"threshold": _lib.COMMIT_THRESHOLD, "fixed_quota": _lib.COMMIT_FIXED_QUOTA}
 _MASK_IDS = {"bidirectional": _lib.MASK_BIDIRECTIONAL, "d2f_hybrid": _lib.MASK_D2F_HYBRID}
 
@@ -229,7 +230,8 @@ class Session:
         strategy = _enum(session_config.get("decode_strategy", "bd3_fixed_quota"), _STRATEGY_IDS, "decode_strategy")
         default_commit = "threshold" if strategy == _lib.STRATEGY_BLOCK_THRESHOLD else "fixed_quota"
         commit = _enum(session_config.get("commit_policy", default_commit), _COMMIT_IDS, "commit_policy")
-        mask = _enum(session_config.get("attention_mask_kind", "d2f_hybrid"), _MASK_IDS, "attention_mask_kind")
+        default_mask = "bidirectional" if strategy == _lib.STRATEGY_ENTROPY_COUNT else "d2f_hybrid"
+        mask = _enum(session_config.get("attention_mask_kind", default_mask), _MASK_IDS, "attention_mask_kind")
         self.block_size = int(session_config.get("block_size", runtime.config.get("block_size", 32)))
         sc = _lib.SessionConfig(decode_strategy=strategy, commit_policy=commit, attention_mask_kind=mask,
                                 block_size=self.block_size, steps=int(session_config.get("steps", 128)),
@@ -271,7 +273,9 @@ class Session:
         ids = _as_int_list(token_ids, "token_ids")
         sc = _as_int_list(scope, "scope")
         if mask_geometry is None:
-            raise NotImplementedError("this device session executes d2f_hybrid windows; pass mask_geometry")
+            if self.decode_strategy != _lib.STRATEGY_ENTROPY_COUNT:
+                raise NotImplementedError("this device session executes d2f_hybrid windows; pass mask_geometry")
+            mask_geometry = (0, 1)  # bidirectional: the geometry is unused
         prompt_len, block_size = (int(v) for v in mask_geometry)
         out = np.empty((len(sc), self.vocab), dtype="<f4")
         forwarded = ctypes.c_int32()
@@ -287,18 +291,24 @@ class Session:
 
     # ------------------------------------------------------------------ device-resident request
     def generate(self, prompt: Sequence[int], *, max_tokens: int, steps: int, block_size: int | None = None,
-                 decode_strategy: str = "bd3_fixed_quota", mask_token_id: int | None = None,
+                 decode_strategy: str | None = None, mask_token_id: int | None = None,
                  eos_token_id: int | None = None, confidence_threshold: float = 0.9, rounds_per_block: int = 0,
-                 trace_steps: int = 0) -> dict:
+                 trace_steps: int = 0, temperature: float = 0.2, top_p: float | None = 0.95,
+                 eps: float = 1e-3) -> dict:
+        """Whole request on the device. ``decode_strategy="entropy_count"`` (a session opened with
+        that strategy) runs the Dream full-canvas schedule with NegEntropy(temperature, top_p) and
+        linspace(1, eps, steps + 1) timesteps; the others run the BD3 / block-threshold loops."""
         cfg = self.runtime.config
         ids = _as_int_list(prompt, "prompt")
         params = _lib.GenerateParams(
-            decode_strategy=_enum(decode_strategy, _STRATEGY_IDS, "decode_strategy"), steps=int(steps),
+            decode_strategy=(self.decode_strategy if decode_strategy is None
+                             else _enum(decode_strategy, _STRATEGY_IDS, "decode_strategy")), steps=int(steps),
             block_size=int(block_size or self.block_size), max_tokens=int(max_tokens),
             mask_token_id=int(cfg["mask_token_id"] if mask_token_id is None else mask_token_id),
             eos_token_id=int(cfg["eos_token_id"] if eos_token_id is None else eos_token_id),
             confidence_threshold=float(confidence_threshold), rounds_per_block=int(rounds_per_block),
-            trace_steps=int(trace_steps))
+            trace_steps=int(trace_steps), temperature=float(temperature),
+            top_p=1.0 if top_p is None else float(top_p), eps=float(eps))
         out = (ctypes.c_int32 * (len(ids) + int(max_tokens)))()
         res = _lib.GenerateResult()
         trace = (_lib.StepTrace * max(1, int(trace_steps)))() if trace_steps else None

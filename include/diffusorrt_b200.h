@@ -45,6 +45,7 @@ typedef enum drt_status {
 /* Decode strategies and commit policies: the ABI integers of
  * python/src/edllm/abi/enums.py:14-31. Only these are served by a device session. */
 #define DRT_STRATEGY_BLOCK_THRESHOLD 0
+#define DRT_STRATEGY_ENTROPY_COUNT 5
 #define DRT_STRATEGY_BD3_FIXED_QUOTA 7
 #define DRT_COMMIT_THRESHOLD 2
 #define DRT_COMMIT_FIXED_QUOTA 3
@@ -95,7 +96,7 @@ typedef struct drt_session_config {
 
 /* Device-resident decode request (drt_session_generate). */
 typedef struct drt_generate_params {
-  int32_t decode_strategy;     /* DRT_STRATEGY_BD3_FIXED_QUOTA or DRT_STRATEGY_BLOCK_THRESHOLD */
+  int32_t decode_strategy;     /* DRT_STRATEGY_BD3_FIXED_QUOTA, _BLOCK_THRESHOLD or _ENTROPY_COUNT */
   int32_t steps;               /* requested denoising steps (the loop's iteration limit) */
   int32_t block_size;
   int32_t max_tokens;          /* generated canvas length */
@@ -104,6 +105,11 @@ typedef struct drt_generate_params {
   double confidence_threshold; /* block threshold tau */
   int32_t rounds_per_block;    /* block threshold: per-block round budget, 0 = none */
   int32_t trace_steps;         /* record up to this many drt_step_trace entries */
+  /* entropy_count (full-canvas masked diffusion): EntropyCountStrategy(temperature, top_p, eps),
+   * python/src/edllm/backends/diffusion_runtime.py:2079-2110. */
+  double temperature;          /* NegEntropy logits / T (<= 0: no scaling) */
+  double top_p;                /* nucleus mass (>= 1: no nucleus) */
+  double eps;                  /* last timestep of linspace(1, eps, steps + 1) */
 } drt_generate_params;
 
 typedef struct drt_generate_result {
@@ -202,6 +208,11 @@ int drt_session_execute_window(drt_session* s, const int32_t* token_ids, int32_t
  * canvas (prompt + max_tokens). trace (optional, host) receives params->trace_steps entries. */
 int drt_session_generate(drt_session* s, const drt_generate_params* params, const int32_t* prompt,
                          int32_t prompt_len, int32_t* out, drt_generate_result* result, drt_step_trace* trace);
+/* entropy_count transfer schedule (EntropyCountCommit.plan, diffusion_runtime.py:921-937):
+ * timesteps = linspace(1, eps, steps + 1) in float32, transfer[s] = int(N * (1 - t[s+1] / t[s]))
+ * (all N remaining on the last step) for s < steps, from n_masked masked positions, N falling by
+ * each step's transfer. 0 marks a skipped step and every step after the canvas is full. Host only. */
+int drt_entropy_count_schedule(int32_t n_masked, int32_t steps, double eps, int32_t* transfer);
 /* Reference: session.device_metrics() (python/src/edllm/model.py:1087). */
 int drt_session_metrics(drt_session* s, drt_metrics* out);
 /* Raw device pointers of the session's K/V cache planes (tests): K [L*nkv][max_seq][128],
@@ -222,6 +233,15 @@ int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows, int32_t v
  * Same scratch, modes and outputs as drt_selector_rows. */
 int drt_selector_gather(const float* logits, int64_t ld, const int32_t* row_index, int32_t n_rows, int32_t vocab,
                         int32_t mode, double temperature, void* scratch, double* conf, int32_t* token, void* stream);
+/* NegEntropy confidence with a top-p nucleus (_entropy_confidence, diffusion_runtime.py:90-114, with
+ * _top_p_filter :358-370 and _softmax :373-378) of the rows row_index[r] (NULL: row r) of f32 logits
+ * [.., ld]: conf[r] = f32(sum p' log(p' + 1e-10)) over the nucleus-renormalised softmax of x / T
+ * (stored as f64), token[r] = its argmax. exclude_token (-1: none) is scored as -inf
+ * (_exclude_mask_token, :256-282). tie (optional) gets DRT_TIE_NEAR when a cumulative mass at the
+ * nucleus cut is within tie_rel of top_p, DRT_TIE_EXACT when the cut keeps part of a tied maximum. */
+int drt_selector_topp(const float* logits, int64_t ld, const int32_t* row_index, int32_t n_rows, int32_t vocab,
+                      double temperature, double top_p, int32_t exclude_token, double tie_rel, double* conf,
+                      int32_t* token, int32_t* tie, void* stream);
 /* Commit choices for a batch of confidence runs: item b owns rows offsets[b] .. offsets[b + 1]
  * (device int32, n_items + 1 entries). mode 0 = top-k (_topk_count_choices,
  * diffusion_runtime.py:290-299: the k highest, lowest row first among equals), mode 1 =

@@ -203,3 +203,10 @@ def forward_fp64(weights: dict, cfg: dict, token_ids, *, prompt_len: int = 0, bl
     rows = np.arange(S) if output_rows is None else np.asarray(output_rows, dtype=np.int64)
     hn = rms(h[rows], W("model.norm.weight"))
     return hn @ W("lm_head.weight").T
+
+
+def dream_raw_rows(positions) -> list[int]:
+    """Raw logits row each position reads under dream_ar_shift (shift_logits_for_dream,
+    python/src/edllm/backends/mlx_ops.py:157-159: concatenate(logits[:1], logits[:-1])):
+    position p reads raw row max(p - 1, 0)."""
+    return [max(int(p) - 1, 0) for p in positions]

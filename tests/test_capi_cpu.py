@@ -54,6 +54,7 @@ def test_status_and_enum_values_match_reference(golden_dir):
     defines = dict(re.findall(r"#define (DRT_\w+) (\d+)", text))
     assert int(defines["DRT_STRATEGY_BLOCK_THRESHOLD"]) == meta["decode_strategy"]["block_threshold"]
     assert int(defines["DRT_STRATEGY_BD3_FIXED_QUOTA"]) == meta["decode_strategy"]["bd3_fixed_quota"]
+    assert int(defines["DRT_STRATEGY_ENTROPY_COUNT"]) == meta["decode_strategy"]["entropy_count"]
     assert int(defines["DRT_COMMIT_THRESHOLD"]) == meta["commit_policy"]["threshold"]
     assert int(defines["DRT_COMMIT_FIXED_QUOTA"]) == meta["commit_policy"]["fixed_quota"]
     assert int(defines["DRT_MASK_BIDIRECTIONAL"]) == meta["attention_mask_kind"]["bidirectional"]
@@ -98,3 +99,33 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setenv("DIFFUSORRT_B200_LIB", str(tmp_path / "nope.so"))
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _lib.load()
+
+
+@pytest.mark.parametrize("n_masked,steps,eps", [(256, 256, 1e-3), (256, 64, 1e-3), (64, 256, 1e-3), (7, 3, 0.5),
+                                                (100, 100, 0.0), (33, 17, 1.0), (1, 1, 1e-3), (0, 5, 1e-3),
+                                                (512, 300, 0.01)])
+def test_entropy_count_schedule_matches_oracle(lib, n_masked, steps, eps):
+    """The host schedule of the full-canvas loop (pure host code, no device call) equals the oracle's
+    EntropyCount plan driven by a canvas that loses exactly the transfer count each step."""
+    from oracle import policy as opol
+
+    got = (ctypes.c_int32 * steps)()
+    assert lib.drt_entropy_count_schedule(n_masked, steps, ctypes.c_double(eps), got) == 0
+    mask = -1
+    c = opol.Canvas([5] + [mask] * n_masked, 1, mask, -2)
+    pol = opol.EntropyCount(eps=eps, steps=steps)
+    want = []
+    for step in range(steps):
+        plan = pol.plan(c, step)
+        if plan.action == "stop":
+            want.append(0)
+            continue
+        if plan.action == "skip":
+            want.append(0)
+            continue
+        k = min(pol._k, len(plan.frontier))
+        want.append(k)
+        for p in plan.frontier[:k]:
+            c.x[p] = 1
+    assert list(got) == want
+    assert sum(want) == n_masked

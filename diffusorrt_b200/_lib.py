@@ -49,6 +49,15 @@ class ModelConfig(ctypes.Structure):
                 ("max_seq", ctypes.c_int32), ("max_prefill_rows", ctypes.c_int32)]
 
 
+class TpShard(ctypes.Structure):
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("q_head0", ctypes.c_int32),
+                ("q_heads", ctypes.c_int32), ("kv_head0", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
+                ("inter0", ctypes.c_int32), ("inter", ctypes.c_int32)]
+
+
+TP_ID_BYTES = 128
+
+
 class SessionConfig(ctypes.Structure):
     _fields_ = [("decode_strategy", ctypes.c_int32), ("commit_policy", ctypes.c_int32),
                 ("attention_mask_kind", ctypes.c_int32), ("block_size", ctypes.c_int32), ("steps", ctypes.c_int32),
@@ -100,6 +109,11 @@ SIGNATURES = {
     "drt_model_set_rope": (ctypes.c_int, [_P, _P, _P, ctypes.c_int32]),
     "drt_model_device_bytes": (ctypes.c_int64, [_P]),
     "drt_model_destroy": (None, [_P]),
+    "drt_tp_shard_geometry": (ctypes.c_int, [ctypes.POINTER(ModelConfig), ctypes.c_int32, ctypes.c_int32,
+                                             ctypes.POINTER(TpShard)]),
+    "drt_tp_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
+    "drt_model_create_tp": (ctypes.c_int, [ctypes.POINTER(ModelConfig), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                           ctypes.c_char_p, ctypes.POINTER(_P)]),
     "drt_model_quantize": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32]),
     "drt_session_open": (ctypes.c_int, [_P, ctypes.POINTER(SessionConfig), ctypes.POINTER(_P)]),
     "drt_session_start": (ctypes.c_int, [_P, _I32P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,

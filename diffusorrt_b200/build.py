@@ -32,12 +32,27 @@ def up_to_date() -> bool:
     return all(p.stat().st_mtime <= t for p in SOURCES + HEADERS)
 
 
+def nccl_include() -> list[str]:
+    """Include path of nccl.h (types only: the library resolves NCCL at run time)."""
+    try:
+        import nvidia.nccl  # the NCCL that torch.distributed loads
+
+        for base in nvidia.nccl.__path__:
+            if (Path(base) / "include" / "nccl.h").exists():
+                return ["-I", str(Path(base) / "include")]
+    except ImportError:
+        pass
+    if Path("/usr/include/nccl.h").exists():
+        return []
+    raise RuntimeError("nccl.h not found")
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and up_to_date():
         return OUT
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "-o", str(tmp), *map(str, SOURCES)]
+    cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", *nccl_include(),
+           "-o", str(tmp), *map(str, SOURCES), "-ldl"]
     if verbose:
         cmd.insert(1, "-Xptxas")
         cmd.insert(2, "-v")

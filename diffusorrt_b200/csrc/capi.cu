@@ -6,6 +6,8 @@
 // programmatic dependent launch so each kernel's weight prefetch overlaps its predecessor.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <chrono>
@@ -270,6 +272,10 @@ struct drt_model {
   float* rope_sin = nullptr;
   int rope_pos = 0;
   int64_t bytes = 0;
+  // tensor parallelism: this model holds one rank's shard (nq, nkv, I above are the local counts)
+  drt_tp_shard shard = {0, 1, 0, 0, 0, 0, 0, 0};
+  int nq_full = 0, nkv_full = 0, I_full = 0;
+  ncclComm_t comm = nullptr;
 };
 
 namespace {
@@ -280,6 +286,82 @@ int dalloc(drt_model* m, T** p, size_t count) {
   m->allocs.push_back(q);
   m->bytes += static_cast<int64_t>(count * sizeof(T));
   *p = static_cast<T*>(q);
+  return DRT_OK;
+}
+
+// NCCL, resolved at run time from the process's libnccl.so.2 (the one torch.distributed loaded,
+// when it did), so the library carries no link-time NCCL dependency.
+struct NcclApi {
+  bool ok = false;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+int nccl_api(const NcclApi** out) {
+  static NcclApi api;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!api.ok) {
+    const char* env = getenv("DRT_NCCL_LIBRARY");
+    void* h = nullptr;
+    if (env != nullptr && *env) h = dlopen(env, RTLD_NOW | RTLD_GLOBAL);
+    if (h == nullptr) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+    if (h == nullptr) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h == nullptr) return set_error(DRT_UNSUPPORTED, "NCCL not found (libnccl.so.2): %s", dlerror());
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    if (!api.get_unique_id || !api.comm_init_rank || !api.all_reduce || !api.comm_destroy || !api.error_string)
+      return set_error(DRT_UNSUPPORTED, "NCCL library lacks an entry point");
+    api.ok = true;
+  }
+  *out = &api;
+  return DRT_OK;
+}
+
+#define NCCL_CK(api, call)                                                                                   \
+  do {                                                                                                       \
+    ncclResult_t r_ = (call);                                                                                \
+    if (r_ != ncclSuccess) return set_error(DRT_INTERNAL_ERROR, "NCCL: %s", (api)->error_string(r_));      \
+  } while (0)
+
+// Megatron-style shard of one rank: attention heads grouped by K/V head, MLP intermediate columns
+// in 64-column units (one SwiGLU tile pairs 64 gate and 64 up rows).
+int tp_geometry(const drt_model_config* cfg, int rank, int world, drt_tp_shard* out) {
+  REQUIRE(world >= 1 && rank >= 0 && rank < world, "rank %d outside a group of %d", rank, world);
+  const int nq = cfg->attention_heads, nkv = cfg->num_kv_heads;
+  REQUIRE(nkv > 0 && nq % nkv == 0, "attention_heads must divide by num_kv_heads");
+  const int rep = nq / nkv;
+  drt_tp_shard g;
+  g.rank = rank;
+  g.world = world;
+  if (nkv % world == 0) {
+    g.kv_heads = nkv / world;
+    g.kv_head0 = rank * g.kv_heads;
+    g.q_heads = g.kv_heads * rep;
+    g.q_head0 = g.kv_head0 * rep;
+  } else if (world % nkv == 0 && world / nkv <= rep) {
+    // several ranks per K/V head: each projects that head and takes a share of its query heads
+    const int per = world / nkv, j = rank % per;
+    g.kv_heads = 1;
+    g.kv_head0 = rank / per;
+    g.q_heads = rep / per + (j < rep % per ? 1 : 0);
+    g.q_head0 = g.kv_head0 * rep + j * (rep / per) + std::min(j, rep % per);
+  } else {
+    return set_error(DRT_UNSUPPORTED, "%d ranks do not shard %d K/V heads", world, nkv);
+  }
+  REQUIRE(cfg->intermediate_size % 64 == 0, "intermediate_size must be a multiple of 64");
+  const int units = cfg->intermediate_size / 64;
+  REQUIRE(units >= world, "intermediate_size too small for %d ranks", world);
+  const int u = units / world, extra = units % world;
+  g.inter = 64 * (u + (rank < extra ? 1 : 0));
+  g.inter0 = 64 * (rank * u + std::min(rank, extra));
+  *out = g;
   return DRT_OK;
 }
 
@@ -325,6 +407,8 @@ struct Slot {
   int64_t rows = 0, cols = 0;
   int64_t grp = 1, grp_stride = 1, grp_off = 0;
   int64_t f32_offset = 0;
+  // the slot holds block [r0, r0 + rows) x [c0, c0 + cols) of a full_rows x full_cols logical tensor
+  int64_t r0 = 0, c0 = 0, full_rows = 0, full_cols = 0;
 };
 
 int resolve_slot(drt_model* m, const char* key, Slot* out) {
@@ -343,6 +427,15 @@ int resolve_slot(drt_model* m, const char* key, Slot* out) {
     if (!parse_layer_key(key, &l, &rest) || l < 0 || l >= m->L) return set_error(DRT_INVALID_ARGUMENT, "unknown weight key %s", key);
     LayerW& w = m->layers[l];
     const int64_t qr = static_cast<int64_t>(m->nq) * 128, kr = static_cast<int64_t>(m->nkv) * 128;
+    const int64_t q0 = static_cast<int64_t>(m->shard.q_head0) * 128, k0 = static_cast<int64_t>(m->shard.kv_head0) * 128;
+    const int64_t qf = static_cast<int64_t>(m->nq_full) * 128, kf = static_cast<int64_t>(m->nkv_full) * 128;
+    if (rest == "self_attn.q_proj.weight") { s.r0 = q0; s.full_rows = qf; s.full_cols = H; }
+    else if (rest == "self_attn.k_proj.weight" || rest == "self_attn.v_proj.weight") { s.r0 = k0; s.full_rows = kf; s.full_cols = H; }
+    else if (rest == "self_attn.q_proj.bias") { s.c0 = q0; s.full_rows = 1; s.full_cols = qf; }
+    else if (rest == "self_attn.k_proj.bias" || rest == "self_attn.v_proj.bias") { s.c0 = k0; s.full_rows = 1; s.full_cols = kf; }
+    else if (rest == "self_attn.o_proj.weight") { s.c0 = q0; s.full_rows = H; s.full_cols = qf; }
+    else if (rest == "mlp.gate_proj.weight" || rest == "mlp.up_proj.weight") { s.r0 = m->shard.inter0; s.full_rows = m->I_full; s.full_cols = H; }
+    else if (rest == "mlp.down_proj.weight") { s.c0 = m->shard.inter0; s.full_rows = H; s.full_cols = m->I_full; }
     if (rest == "input_layernorm.weight") { s.dst_f32 = w.in_norm; s.rows = 1; s.cols = H; }
     else if (rest == "post_attention_layernorm.weight") { s.dst_f32 = w.post_norm; s.rows = 1; s.cols = H; }
     else if (rest == "self_attn.q_norm.weight") { if (!w.q_norm) return set_error(DRT_INVALID_ARGUMENT, "model has no QK norm"); s.dst_f32 = w.q_norm; s.rows = 1; s.cols = 128; }
@@ -360,6 +453,7 @@ int resolve_slot(drt_model* m, const char* key, Slot* out) {
     else return set_error(DRT_INVALID_ARGUMENT, "unknown weight key %s", key);
   }
   if (s.grp == 1 && s.grp_stride == 1) { s.grp = s.rows; s.grp_stride = 0; }
+  if (s.full_rows == 0) { s.full_rows = s.rows; s.full_cols = s.cols; }
   *out = s;
   return DRT_OK;
 }
@@ -382,9 +476,59 @@ extern "C" int drt_device_count(int32_t* count) {
   return DRT_OK;
 }
 
+namespace {
+int create_model(const drt_model_config* cfg, int32_t device, const drt_tp_shard* shard, drt_model** out);
+}  // namespace
+
 extern "C" int drt_model_create(const drt_model_config* cfg, int32_t device, drt_model** out) {
   REQUIRE(cfg != nullptr && out != nullptr, "null argument");
   *out = nullptr;
+  drt_tp_shard whole;
+  TRY(tp_geometry(cfg, 0, 1, &whole));
+  return create_model(cfg, device, &whole, out);
+}
+
+extern "C" int drt_tp_shard_geometry(const drt_model_config* cfg, int32_t rank, int32_t world, drt_tp_shard* out) {
+  REQUIRE(cfg != nullptr && out != nullptr, "null argument");
+  return tp_geometry(cfg, rank, world, out);
+}
+
+extern "C" int drt_tp_unique_id(uint8_t* id) {
+  REQUIRE(id != nullptr, "null argument");
+  const NcclApi* nc = nullptr;
+  TRY(nccl_api(&nc));
+  ncclUniqueId u;
+  NCCL_CK(nc, nc->get_unique_id(&u));
+  static_assert(sizeof(u.internal) == DRT_TP_ID_BYTES, "NCCL unique id size");
+  memcpy(id, u.internal, DRT_TP_ID_BYTES);
+  return DRT_OK;
+}
+
+extern "C" int drt_model_create_tp(const drt_model_config* cfg, int32_t device, int32_t rank, int32_t world,
+                                   const uint8_t* nccl_id, drt_model** out) {
+  REQUIRE(cfg != nullptr && out != nullptr && nccl_id != nullptr, "null argument");
+  *out = nullptr;
+  drt_tp_shard g;
+  TRY(tp_geometry(cfg, rank, world, &g));
+  const NcclApi* nc = nullptr;
+  TRY(nccl_api(&nc));
+  drt_model* m = nullptr;
+  TRY(create_model(cfg, device, &g, &m));
+  CK(cudaSetDevice(device));
+  ncclUniqueId u;
+  memcpy(u.internal, nccl_id, DRT_TP_ID_BYTES);
+  ncclResult_t r = nc->comm_init_rank(&m->comm, world, u, rank);
+  if (r != ncclSuccess) {
+    m->comm = nullptr;
+    drt_model_destroy(m);
+    return set_error(DRT_INTERNAL_ERROR, "NCCL communicator: %s", nc->error_string(r));
+  }
+  *out = m;
+  return DRT_OK;
+}
+
+namespace {
+int create_model(const drt_model_config* cfg, int32_t device, const drt_tp_shard* shard, drt_model** out) {
   REQUIRE(cfg->head_dim == 128, "head_dim must be 128 (got %d)", cfg->head_dim);
   REQUIRE(cfg->layer_count > 0 && cfg->hidden_size > 0 && cfg->vocab_size > 0, "bad model geometry");
   REQUIRE(cfg->hidden_size % 128 == 0, "hidden_size must be a multiple of 128");
@@ -399,10 +543,14 @@ extern "C" int drt_model_create(const drt_model_config* cfg, int32_t device, drt
   drt_model* m = new drt_model();
   m->cfg = *cfg;
   m->device = device;
+  m->shard = *shard;
+  m->nq_full = cfg->attention_heads;
+  m->nkv_full = cfg->num_kv_heads;
+  m->I_full = cfg->intermediate_size;
   m->H = cfg->hidden_size;
-  m->nq = cfg->attention_heads;
-  m->nkv = cfg->num_kv_heads;
-  m->I = cfg->intermediate_size;
+  m->nq = shard->q_heads;
+  m->nkv = shard->kv_heads;
+  m->I = shard->inter;
   m->V = cfg->vocab_size;
   m->L = cfg->layer_count;
   m->rep = m->nq / m->nkv;
@@ -453,6 +601,7 @@ extern "C" int drt_model_create(const drt_model_config* cfg, int32_t device, drt
   *out = m;
   return DRT_OK;
 }
+}  // namespace
 
 extern "C" int drt_model_set_rope(drt_model* m, const float* cos_half, const float* sin_half, int32_t n_pos) {
   REQUIRE(m && cos_half && sin_half && n_pos > 0, "null argument");
@@ -475,34 +624,39 @@ extern "C" int drt_model_init_synthetic(drt_model* m, uint64_t seed, float linea
   const float s_lin = static_cast<float>(static_cast<double>(linear_std) / unit);
   const float s_emb = static_cast<float>(static_cast<double>(embed_std) / unit);
   const float s_bias = static_cast<float>(static_cast<double>(bias_std) / unit);
+  // (r0, c0, full_cols): the block of the logical tensor this model holds (tensor-parallel shards)
   auto fill = [&](__nv_bfloat16* dst, int64_t rows, int64_t cols, uint32_t tid, float scale, int64_t grp, int64_t grp_stride,
-                  int64_t grp_off) -> int {
+                  int64_t grp_off, int64_t r0 = 0, int64_t c0 = 0, int64_t full_cols = 0) -> int {
     const int64_t total = rows * cols;
     const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 65535));
-    synth_fill_kernel<<<blocks, 256>>>(dst, rows, cols, seed, tid, scale, grp, grp_stride, grp_off);
+    synth_fill_kernel<<<blocks, 256>>>(dst, rows, cols, seed, tid, scale, grp, grp_stride, grp_off, r0, c0,
+                                       full_cols > 0 ? full_cols : cols);
     CK(cudaGetLastError());
     return DRT_OK;
   };
   const int64_t H = m->H, qr = static_cast<int64_t>(m->nq) * 128, kr = static_cast<int64_t>(m->nkv) * 128;
+  const int64_t q0 = static_cast<int64_t>(m->shard.q_head0) * 128, k0 = static_cast<int64_t>(m->shard.kv_head0) * 128;
+  const int64_t qf = static_cast<int64_t>(m->nq_full) * 128, kf = static_cast<int64_t>(m->nkv_full) * 128;
+  const int64_t i0 = m->shard.inter0;
   TRY(fill(m->embed, m->V, H, 1, s_emb, m->V, 0, 0));
   if (!m->cfg.tied_lm_head) TRY(fill(m->lm_head, m->V, H, 2, s_emb, m->V, 0, 0));
   for (int l = 0; l < m->L; ++l) {
     LayerW& w = m->layers[l];
     const uint32_t b = 16u + static_cast<uint32_t>(l) * 16u;
-    TRY(fill(w.wqkv, qr, H, b + 0, s_lin, qr, 0, 0));
-    TRY(fill(w.wqkv, kr, H, b + 1, s_lin, kr, 0, qr));
-    TRY(fill(w.wqkv, kr, H, b + 2, s_lin, kr, 0, qr + kr));
-    TRY(fill(w.wo, H, qr, b + 3, s_lin, H, 0, 0));
-    TRY(fill(w.wgu, m->I, H, b + 4, s_lin, 64, 128, 0));
-    TRY(fill(w.wgu, m->I, H, b + 5, s_lin, 64, 128, 64));
-    TRY(fill(w.wdown, H, m->I, b + 6, s_lin, H, 0, 0));
+    TRY(fill(w.wqkv, qr, H, b + 0, s_lin, qr, 0, 0, q0, 0, H));
+    TRY(fill(w.wqkv, kr, H, b + 1, s_lin, kr, 0, qr, k0, 0, H));
+    TRY(fill(w.wqkv, kr, H, b + 2, s_lin, kr, 0, qr + kr, k0, 0, H));
+    TRY(fill(w.wo, H, qr, b + 3, s_lin, H, 0, 0, 0, q0, qf));
+    TRY(fill(w.wgu, m->I, H, b + 4, s_lin, 64, 128, 0, i0, 0, H));
+    TRY(fill(w.wgu, m->I, H, b + 5, s_lin, 64, 128, 64, i0, 0, H));
+    TRY(fill(w.wdown, H, m->I, b + 6, s_lin, H, 0, 0, 0, i0, m->I_full));
     if (w.bqkv) {
       // Biases are bf16 values held in f32: generate bf16 into a scratch row, widen.
       __nv_bfloat16* tmp = nullptr;
       CK(cudaMalloc(&tmp, sizeof(__nv_bfloat16) * m->qkv_rows));
-      int rc = fill(tmp, 1, qr, b + 7, s_bias, 1, 0, 0);
-      if (rc == DRT_OK) rc = fill(tmp + qr, 1, kr, b + 8, s_bias, 1, 0, 0);
-      if (rc == DRT_OK) rc = fill(tmp + qr + kr, 1, kr, b + 9, s_bias, 1, 0, 0);
+      int rc = fill(tmp, 1, qr, b + 7, s_bias, 1, 0, 0, 0, q0, qf);
+      if (rc == DRT_OK) rc = fill(tmp + qr, 1, kr, b + 8, s_bias, 1, 0, 0, 0, k0, kf);
+      if (rc == DRT_OK) rc = fill(tmp + qr + kr, 1, kr, b + 9, s_bias, 1, 0, 0, 0, k0, kf);
       if (rc == DRT_OK) {
         bf16_to_f32_kernel<<<64, 256>>>(w.bqkv, tmp, m->qkv_rows);
         if (cudaGetLastError() != cudaSuccess) rc = set_error(DRT_INTERNAL_ERROR, "bias widen failed");
@@ -521,10 +675,22 @@ extern "C" int drt_model_set_tensor(drt_model* m, const char* key, const void* d
   REQUIRE(dtype == 0 || dtype == 1, "dtype must be 0 (bf16) or 1 (f32)");
   Slot s;
   TRY(resolve_slot(m, key, &s));
-  REQUIRE(rows * cols == s.rows * s.cols, "%s: expected %lld x %lld elements, got %lld x %lld", key,
-          static_cast<long long>(s.rows), static_cast<long long>(s.cols), static_cast<long long>(rows), static_cast<long long>(cols));
+  REQUIRE(rows * cols == s.full_rows * s.full_cols, "%s: expected %lld x %lld elements, got %lld x %lld", key,
+          static_cast<long long>(s.full_rows), static_cast<long long>(s.full_cols), static_cast<long long>(rows),
+          static_cast<long long>(cols));
   CK(cudaSetDevice(m->device));
   const int64_t n = s.rows * s.cols;
+  // A tensor-parallel shard takes its block of the full logical tensor.
+  std::vector<uint8_t> block;
+  if (s.rows != s.full_rows || s.cols != s.full_cols) {
+    const size_t es = dtype == 1 ? 4 : 2;
+    block.resize(static_cast<size_t>(n) * es);
+    for (int64_t r = 0; r < s.rows; ++r)
+      memcpy(block.data() + static_cast<size_t>(r * s.cols) * es,
+             static_cast<const uint8_t*>(data) + static_cast<size_t>((s.r0 + r) * s.full_cols + s.c0) * es,
+             static_cast<size_t>(s.cols) * es);
+    data = block.data();
+  }
   if (s.dst_f32 != nullptr) {
     std::vector<float> tmp(n);
     if (dtype == 1) {
@@ -559,7 +725,7 @@ extern "C" int drt_model_get_tensor(drt_model* m, const char* key, void* data, i
   REQUIRE(dtype == 0 || dtype == 1, "dtype must be 0 (bf16) or 1 (f32)");
   Slot s;
   TRY(resolve_slot(m, key, &s));
-  REQUIRE(rows * cols == s.rows * s.cols, "%s: element count mismatch", key);
+  REQUIRE(rows * cols == s.rows * s.cols, "%s: element count mismatch (a tensor-parallel shard returns its own block)", key);
   CK(cudaSetDevice(m->device));
   const int64_t n = s.rows * s.cols;
   if (s.dst_f32 != nullptr) {
@@ -613,6 +779,7 @@ int quantize_into(drt_model* m, QuantW* qw, const __nv_bfloat16* w, int64_t n, i
 
 extern "C" int drt_model_quantize(drt_model* m, int32_t bits, int32_t group_size) {
   REQUIRE(m, "null model");
+  REQUIRE(m->shard.world == 1, "4-bit linears are served on whole (not tensor-parallel) models");
   if (bits != 4 || group_size != 64)
     return set_error(DRT_UNSUPPORTED, "linear quantization serves bits 4 with group size 64 (got bits %d, group %d)", bits,
                      group_size);
@@ -638,6 +805,11 @@ extern "C" void drt_model_destroy(drt_model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
   cudaDeviceSynchronize();
+  if (m->comm != nullptr) {
+    const NcclApi* nc = nullptr;
+    if (nccl_api(&nc) == DRT_OK) nc->comm_destroy(m->comm);
+    m->comm = nullptr;
+  }
   for (void* p : m->allocs) cudaFree(p);
   delete m;
 }
@@ -657,6 +829,7 @@ struct drt_session {
   __nv_bfloat16 *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *xf = nullptr;
   float* logits = nullptr;
   float* ss = nullptr;                // [kMaxFwdRows][H / 128] partial sums of squares of h (decode)
+  float* part = nullptr;              // [rows_cap][H] f32 linear partials (tensor-parallel models)
   __nv_bfloat16 *kcache = nullptr, *vtcache = nullptr;
   int max_cluster = 16;               // largest cluster the GPU schedules for the split kernels
   float* sel_pmax = nullptr;
@@ -846,6 +1019,20 @@ int run_rmsnorm(drt_session* s, const float* h, const int* row_index, int rows, 
   return DRT_OK;
 }
 
+// Tensor parallelism: sum the ranks' f32 linear partials (s->part, rows x H) over the group, then
+// h += bf16(sum), the linear's output rounding applied once to the reduced value.
+int tp_reduce_residual(drt_session* s, int rows) {
+  drt_model* m = s->m;
+  const NcclApi* nc = nullptr;
+  TRY(nccl_api(&nc));
+  const size_t n = static_cast<size_t>(rows) * m->H;
+  NCCL_CK(nc, nc->all_reduce(s->part, s->part, n, ncclFloat32, ncclSum, m->comm, s->stream));
+  const unsigned blocks = static_cast<unsigned>(std::min<size_t>((n / 4 + 255) / 256, static_cast<size_t>(s->sms) * 8));
+  CK(launch_k(resid_add_bf16r_kernel, dim3(std::max(1u, blocks)), dim3(256), 0, s->stream, false, s->h,
+              static_cast<const float*>(s->part), static_cast<int64_t>(n)));
+  return DRT_OK;
+}
+
 // Enqueue the transformer layers for the rows described by f (embedding through the last
 // layer's residual). K/V of every forwarded row is written into the cache.
 int enqueue_layers(drt_session* s, const Fwd& f) {
@@ -937,13 +1124,15 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     CK(launch_kc(attn_prefix_kernel, dim3(qtiles, m->nkv, t.splits), dim3(128), kAttnSmemBytes, s->stream, true, t.splits,
                  s->m_q, s->m_k, s->m_v, t));
     }
-    // o_proj + residual.
+    // o_proj + residual (tensor parallel: f32 partial, all-reduce, residual add).
+    const bool tp = m->shard.world > 1;
     GemmArgs o = base_args(s, H, qd, f);
-    o.epi = EPI_RESID;
-    o.out_f32 = s->h;
+    o.epi = tp ? EPI_STORE_RAW : EPI_RESID;
+    o.out_f32 = tp ? s->part : s->h;
     o.ld_out = H;
     if (f.decode) TRY(run_dec_gemm(s, w.m_o, s->m_attn64, o, m->quantized ? &w.q_o : nullptr));
     else TRY(run_gemm<128>(s, w.m_o, s->m_attn128, o, false));
+    if (tp) TRY(tp_reduce_residual(s, f.rows));
     TRY(run_rmsnorm(s, s->h, nullptr, f.rows, f.rows_dev, w.post_norm, s->xn));
     // gate/up + SwiGLU.
     GemmArgs g = base_args(s, m->gu_rows, H, f);
@@ -954,11 +1143,12 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     else TRY(run_gemm<128>(s, w.m_gu, s->m_xn128, g, false));
     // down + residual.
     GemmArgs d = base_args(s, H, m->I, f);
-    d.epi = EPI_RESID;
-    d.out_f32 = s->h;
+    d.epi = tp ? EPI_STORE_RAW : EPI_RESID;
+    d.out_f32 = tp ? s->part : s->h;
     d.ld_out = H;
     if (f.decode) TRY(run_dec_gemm(s, w.m_down, s->m_act64, d, m->quantized ? &w.q_down : nullptr));
     else TRY(run_gemm<128>(s, w.m_down, s->m_act128, d, false));
+    if (tp) TRY(tp_reduce_residual(s, f.rows));
   }
   return DRT_OK;
 }
@@ -1314,6 +1504,7 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   REQUIRE(dream || cfg->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA || cfg->decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD,
           "device sessions run only block_threshold, bd3_fixed_quota and entropy_count (got strategy %d)",
           cfg->decode_strategy);
+  REQUIRE(dream || m->shard.world == 1, "a tensor-parallel model serves entropy_count sessions only");
   if (dream) {
     REQUIRE(cfg->attention_mask_kind == DRT_MASK_BIDIRECTIONAL, "entropy_count sessions serve the bidirectional graph only");
     REQUIRE(!m->quantized, "entropy_count sessions need bf16 linears (the 4-bit path forwards at most %d rows)", kMaxFwdRows);
@@ -1346,6 +1537,7 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = salloc(s, &s->xf, static_cast<size_t>(s->head_cap) * H)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->logits, static_cast<size_t>(s->head_cap) * m->V)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->ss, static_cast<size_t>(kMaxFwdRows) * (H / 128))) != DRT_OK) return fail(rc);
+  if (m->shard.world > 1 && (rc = salloc(s, &s->part, static_cast<size_t>(R) * H)) != DRT_OK) return fail(rc);
   const size_t kv = static_cast<size_t>(s->planes) * s->max_seq * 128;
   if ((rc = salloc(s, &s->kcache, kv)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->vtcache, kv)) != DRT_OK) return fail(rc);

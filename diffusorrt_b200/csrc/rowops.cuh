@@ -134,17 +134,42 @@ __device__ __forceinline__ float synth_value(uint64_t seed, uint32_t tensor_id, 
   return __fmul_rn(static_cast<float>(u), scale);
 }
 
-// Fill logical rows [0, rows) x cols of tensor `tensor_id` into a packed destination:
-// logical row r lands at dst row (r / grp) * grp_stride + grp_off + r % grp.
+// Fill rows [0, rows) x cols of a block of tensor `tensor_id` into a packed destination: block
+// element (r, c) is logical element (r0 + r, c0 + c) of the full [*, full_cols] tensor (a
+// tensor-parallel shard; r0 = c0 = 0 and full_cols = cols for a whole tensor), and block row r lands
+// at dst row (r / grp) * grp_stride + grp_off + r % grp.
 __global__ void synth_fill_kernel(__nv_bfloat16* dst, int64_t rows, int64_t cols, uint64_t seed, uint32_t tensor_id,
-                                  float scale, int64_t grp, int64_t grp_stride, int64_t grp_off) {
+                                  float scale, int64_t grp, int64_t grp_stride, int64_t grp_off, int64_t r0, int64_t c0,
+                                  int64_t full_cols) {
   const int64_t total = rows * cols;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / cols, c = i - r * cols;
     const int64_t dr = (r / grp) * grp_stride + grp_off + r % grp;
-    dst[dr * cols + c] = __float2bfloat16_rn(synth_value(seed, tensor_id, static_cast<uint64_t>(i), scale));
+    const uint64_t li = static_cast<uint64_t>((r0 + r) * full_cols + c0 + c);
+    dst[dr * cols + c] = __float2bfloat16_rn(synth_value(seed, tensor_id, li, scale));
   }
+}
+
+// h[i] += bf16(part[i]) for i < n: the residual add after a tensor-parallel all-reduce of f32
+// linear partials (the linear's bf16 output rounding applied to the reduced sum).
+__global__ void resid_add_bf16r_kernel(float* __restrict__ h, const float* __restrict__ part, int64_t n) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int64_t n4 = n / 4;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 a = reinterpret_cast<float4*>(h)[i];
+    const float4 b = reinterpret_cast<const float4*>(part)[i];
+    a.x = __fadd_rn(a.x, __bfloat162float(__float2bfloat16_rn(b.x)));
+    a.y = __fadd_rn(a.y, __bfloat162float(__float2bfloat16_rn(b.y)));
+    a.z = __fadd_rn(a.z, __bfloat162float(__float2bfloat16_rn(b.z)));
+    a.w = __fadd_rn(a.w, __bfloat162float(__float2bfloat16_rn(b.w)));
+    reinterpret_cast<float4*>(h)[i] = a;
+  }
+  for (int64_t i = n4 * 4 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    h[i] = __fadd_rn(h[i], __bfloat162float(__float2bfloat16_rn(part[i])));
 }
 
 // Copy logical rows of a host-provided bf16 tensor (already on the device) into the packed

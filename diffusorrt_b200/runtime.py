@@ -89,14 +89,44 @@ def _bf16_bits(array) -> np.ndarray:
     return bits.astype(np.uint16)
 
 
+def _model_config(cfg: Mapping[str, Any], max_seq: int = 128, max_prefill_rows: int = 128) -> _lib.ModelConfig:
+    return _lib.ModelConfig(
+        layer_count=cfg["layer_count"], hidden_size=cfg["hidden_size"], attention_heads=cfg["attention_heads"],
+        num_kv_heads=cfg["num_kv_heads"], head_dim=cfg["head_dim"], intermediate_size=cfg["intermediate_size"],
+        vocab_size=cfg["vocab_size"], qk_norm=int(bool(cfg["qk_norm"])), qkv_bias=int(bool(cfg["qkv_bias"])),
+        tied_lm_head=int(bool(cfg["tied_lm_head"])), rms_norm_eps=float(cfg["rms_norm_eps"]),
+        rope_theta=float(cfg["rope_theta"]), max_seq=int(max_seq), max_prefill_rows=int(max_prefill_rows))
+
+
+def tp_shard(lib, cfg: Mapping[str, Any], rank: int, world: int) -> dict:
+    """Shard geometry of one tensor-parallel rank (host-only call into the library)."""
+    out = _lib.TpShard()
+    _call(lib.drt_tp_shard_geometry(ctypes.byref(_model_config(cfg)), int(rank), int(world), ctypes.byref(out)))
+    return {name: getattr(out, name) for name, _ in _lib.TpShard._fields_}
+
+
+def share_tp_id(rank: int, make_id) -> bytes:
+    """Rank 0 makes the group's NCCL id; torch.distributed broadcasts it to every rank."""
+    import torch.distributed as dist
+
+    box = [make_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    nccl_id = box[0]
+    if not isinstance(nccl_id, bytes) or len(nccl_id) != _lib.TP_ID_BYTES:
+        raise RuntimeError("tensor-parallel id exchange failed")
+    return nccl_id
+
+
 class Runtime:
-    """One model resident on one GPU (``diffusorrt_runtime.Runtime``)."""
+    """One model resident on one GPU (``diffusorrt_runtime.Runtime``); with
+    ``tensor_parallel=True``, one rank's shard of a model split over a torch.distributed group."""
 
     def __init__(self, package_dir: str | Path | None = None, *, device: str = "cuda",
                  engine_config: Mapping[str, Any] | None = None, precision: Mapping[str, Any] | None = None,
                  device_ordinal: int = 0, creation_memory_budget_bytes: int = 0,
                  model_config: Mapping[str, Any] | None = None, weights: Mapping[str, Any] | None = None,
-                 synthetic_seed: int | None = None, max_seq: int = 4608 + 128, max_prefill_rows: int = 4096):
+                 synthetic_seed: int | None = None, max_seq: int = 4608 + 128, max_prefill_rows: int = 4096,
+                 tensor_parallel: bool = False):
         if device != "cuda":
             raise ValueError(f"this runtime serves device='cuda' only, not {device!r}")
         engine_config = dict(engine_config or {})
@@ -121,14 +151,20 @@ class Runtime:
         self.config = cfg
         self.device_ordinal = int(device_ordinal)
         self._lib = _lib.load()
-        mc = _lib.ModelConfig(
-            layer_count=cfg["layer_count"], hidden_size=cfg["hidden_size"], attention_heads=cfg["attention_heads"],
-            num_kv_heads=cfg["num_kv_heads"], head_dim=cfg["head_dim"], intermediate_size=cfg["intermediate_size"],
-            vocab_size=cfg["vocab_size"], qk_norm=int(bool(cfg["qk_norm"])), qkv_bias=int(bool(cfg["qkv_bias"])),
-            tied_lm_head=int(bool(cfg["tied_lm_head"])), rms_norm_eps=float(cfg["rms_norm_eps"]),
-            rope_theta=float(cfg["rope_theta"]), max_seq=int(max_seq), max_prefill_rows=int(max_prefill_rows))
+        mc = _model_config(cfg, max_seq, max_prefill_rows)
         handle = ctypes.c_void_p()
-        _call(self._lib.drt_model_create(ctypes.byref(mc), self.device_ordinal, ctypes.byref(handle)))
+        self.tp_rank, self.tp_world = 0, 1
+        if tensor_parallel:
+            # one rank of a tensor-parallel group: torch.distributed (already initialised, one
+            # process per GPU) carries the NCCL id; the model joins the group's communicator
+            import torch.distributed as dist
+
+            self.tp_rank, self.tp_world = dist.get_rank(), dist.get_world_size()
+            nccl_id = share_tp_id(self.tp_rank, self._make_tp_id)
+            _call(self._lib.drt_model_create_tp(ctypes.byref(mc), self.device_ordinal, self.tp_rank, self.tp_world,
+                                                nccl_id, ctypes.byref(handle)))
+        else:
+            _call(self._lib.drt_model_create(ctypes.byref(mc), self.device_ordinal, ctypes.byref(handle)))
         self._model = handle
         self.max_seq = int(max_seq)
         cos, sin = rope_half_tables(self.max_seq, cfg["head_dim"], float(cfg["rope_theta"]))
@@ -143,6 +179,15 @@ class Runtime:
         if creation_memory_budget_bytes and self.device_bytes > int(creation_memory_budget_bytes):
             self.close()
             raise ValueError("model weights exceed creation_memory_budget_bytes")
+
+    def _make_tp_id(self) -> bytes:
+        buf = ctypes.create_string_buffer(_lib.TP_ID_BYTES)
+        _call(self._lib.drt_tp_unique_id(buf))
+        return buf.raw
+
+    def shard(self) -> dict:
+        """This rank's shard geometry (the whole model for a single GPU)."""
+        return tp_shard(self._lib, self.config, self.tp_rank, self.tp_world)
 
     # ------------------------------------------------------------------ weights
     def init_synthetic(self, seed: int, *, linear_std: float | None = None, embed_std: float | None = None,

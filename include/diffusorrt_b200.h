@@ -61,6 +61,18 @@ typedef enum drt_status {
 #define DRT_TIE_NEAR 1
 #define DRT_TIE_EXACT 2
 
+/* Tensor parallelism (BASELINE configs[2] across 2/4/8 GPUs): one rank's shard of the model.
+ * Attention heads are split by K/V head; when there are more ranks than K/V heads, the ranks
+ * sharing a K/V head each project it and split its query heads. MLP intermediate columns are split
+ * in 64-column units. Embedding, norms and lm_head are replicated. */
+typedef struct drt_tp_shard {
+  int32_t rank, world;
+  int32_t q_head0, q_heads;    /* global query heads [q_head0, q_head0 + q_heads) */
+  int32_t kv_head0, kv_heads;  /* global K/V heads [kv_head0, kv_head0 + kv_heads) */
+  int32_t inter0, inter;       /* intermediate columns [inter0, inter0 + inter) of gate/up/down */
+} drt_tp_shard;
+#define DRT_TP_ID_BYTES 128
+
 typedef struct drt_model drt_model;
 typedef struct drt_session drt_session;
 
@@ -180,6 +192,19 @@ int64_t drt_model_device_bytes(const drt_model* model);
  * drt_model_set_tensor to refresh the copies. Only bits 4, group_size 64 (else DRT_UNSUPPORTED). */
 int drt_model_quantize(drt_model* model, int32_t bits, int32_t group_size);
 void drt_model_destroy(drt_model* model);
+/* Shard of rank `rank` in a group of `world` (host only; no device call). */
+int drt_tp_shard_geometry(const drt_model_config* config, int32_t rank, int32_t world, drt_tp_shard* out);
+/* A new NCCL unique id (DRT_TP_ID_BYTES bytes) for drt_model_create_tp; made by one rank and
+ * shared with the others by the caller (torch.distributed in the Python binding). */
+int drt_tp_unique_id(uint8_t* id);
+/* drt_model_create for one rank's shard, joined to the group's NCCL communicator (blocks until
+ * every rank has joined). Weights: drt_model_init_synthetic fills the shard's block of the same
+ * logical tensors a whole model gets; drt_model_set_tensor takes FULL logical tensors and keeps the
+ * shard's block. Sessions on a sharded model serve entropy_count only: the layer forward
+ * all-reduces the f32 o_proj and down_proj partials over the group, then adds bf16(sum) to the
+ * replicated residual, so every rank holds the same hidden state, logits and selections. */
+int drt_model_create_tp(const drt_model_config* config, int32_t device_ordinal, int32_t rank, int32_t world,
+                        const uint8_t* nccl_id, drt_model** out);
 
 /* ------------------------------------------------------------------ session */
 /* Reference: Runtime.session(session_config) (python/src/edllm/model.py:1055-1067). */

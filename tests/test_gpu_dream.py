@@ -134,9 +134,8 @@ def test_entropy_count_generate_matches_oracle(drt, weights, prompt_len, gen, st
     assert out["forward_count"] == int(np.count_nonzero(sched))
     c = opol.Canvas(list(prompt) + [mask] * gen, prompt_len, mask, eos)
     pol = opol.EntropyCount(eps=EPS, steps=steps)
-    trace = out["trace"]
-    agreed = 0
-    for tr in trace:
+    certified, checked_tokens = 0, 0
+    for tr in out["trace"]:
         plan = pol.plan(c, tr["step"])
         assert plan.action == "proceed"
         assert plan.frontier == tr["frontier"]
@@ -146,15 +145,24 @@ def test_entropy_count_generate_matches_oracle(drt, weights, prompt_len, gen, st
         conf, tok = osel.neg_entropy_rows(logits, temperature=T, top_p=TOP_P)
         rows = pol.select(conf)
         assert len(rows) == len(tr["chosen"])
-        same = sorted(rows) == tr["chosen"] and all(tok[r] == tr["tokens"][r] for r in rows)
-        if not same:
-            # only where the oracle's own decision is close (bf16 forward rounding moves confidences)
-            order = np.sort(np.asarray(conf, np.float64))[::-1]
-            k = len(rows)
-            gap = abs(order[k - 1] - order[k]) / max(abs(order[k - 1]), 1e-30) if k < len(order) else 1.0
-            assert tr["tie"] or gap < 0.05, (tr["step"], gap)
-            break
-        agreed += 1
-        for r in rows:
-            c.x[plan.frontier[r]] = tok[r]
-    assert agreed >= 3
+        # The device forward rounds like the reference's bf16 MLX path but not bit for bit, so a
+        # decision is checked where the oracle's own margin is clear: the k-th vs (k+1)-th
+        # confidence for the chosen set, the top-1 vs top-2 logit for a token.
+        order = np.sort(np.asarray(conf, np.float64))[::-1]
+        k = len(rows)
+        gap = abs(order[k - 1] - order[k]) / max(abs(order[k - 1]), 1e-30) if k < len(order) else 1.0
+        if tr["tie"] == 0 and gap > 0.05:
+            assert sorted(rows) == tr["chosen"], tr["step"]
+            certified += 1
+        top2 = np.sort(logits, axis=1)[:, -2:]
+        for i in tr["chosen"]:
+            scale = float(np.abs(logits[i][np.isfinite(logits[i])]).max())
+            if top2[i, 1] - top2[i, 0] > 0.05 * scale:
+                assert tok[i] == tr["tokens"][i], (tr["step"], i)
+                checked_tokens += 1
+        # follow the device's commits so the next step starts from the same canvas
+        for i in tr["chosen"]:
+            c.x[plan.frontier[i]] = tr["tokens"][i]
+    assert c.x == x
+    assert certified >= len(out["trace"]) // 3, (certified, len(out["trace"]))
+    assert checked_tokens >= gen // 3

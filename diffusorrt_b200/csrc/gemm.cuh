@@ -328,8 +328,12 @@ __global__ void __launch_bounds__(128, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int m0 = blockIdx.x * 128;
-  const int n0 = blockIdx.y * BN;
+  // Tile order: with several row tiles, the CTAs that share a weight tile are consecutive in launch
+  // order (row tile fastest), so the weight tile comes from HBM once and from L2 for the others.
+  const int tiles_n = gridDim.y;
+  const int bid = blockIdx.y * gridDim.x + blockIdx.x;
+  const int m0 = (tiles_n > 1 ? bid / tiles_n : static_cast<int>(blockIdx.x)) * 128;
+  const int n0 = (tiles_n > 1 ? bid % tiles_n : static_cast<int>(blockIdx.y)) * BN;
   const int split = blockIdx.z;
   const int kb_total = a.K >> 6;
   const int kb0 = split * a.kb_per_split;
@@ -361,7 +365,7 @@ __global__ void __launch_bounds__(128, 1)
   const int npre = min(stages, nkb);
   uint64_t policy = 0;
   if (tid == 0) {
-    policy = l2_policy_evict_first();
+    policy = tiles_n > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
     for (int i = 0; i < npre; ++i) {
       mbar_expect_tx(&fullA[i], Cfg::kABytes);
       tma_load_2d_hint(ring + static_cast<size_t>(i) * Cfg::kStageBytes, &tmA, &fullA[i], (kb0 + i) * 64, m0, policy);

@@ -6,6 +6,13 @@ kernels at the same shapes as the benchmark with few launches before them, and t
 about 2 GB (weights 1.19 GB, K/V cache ~0.5 GB).
 
     python -m diffusorrt_b200.profile_case [--prompt 4096] [--gen 32] [--rounds 8]
+    python -m diffusorrt_b200.profile_case --dream [--steps 4]
+
+With --dream: the Dream-7B-architecture full-canvas workload (prompt 256 + canvas 256,
+entropy_count over --steps steps, each a 512-row forward); the model's synthetic weights take
+~15 GB. Per step: dream_plan_kernel, embed_rows_kernel, per layer [rmsnorm, gemm_swapab (QKV),
+attn_prefix, gemm_swapab (o), rmsnorm, gemm_swapab (gate/up), gemm_swapab (down)], rmsnorm,
+gemm_swapab (lm_head), sel_topp_entropy_kernel, dream_commit_kernel.
 
 Prints one JSON line: denoising steps run, kernel launches of the request and ms per step.
 
@@ -29,9 +36,28 @@ def main() -> None:
     ap.add_argument("--prompt", type=int, default=4096)
     ap.add_argument("--gen", type=int, default=32)
     ap.add_argument("--rounds", type=int, default=8)
+    ap.add_argument("--dream", action="store_true", help="Dream-7B full-canvas entropy_count instead")
+    ap.add_argument("--steps", type=int, default=4, help="entropy_count steps (--dream)")
     args = ap.parse_args()
     from diffusorrt_b200 import Runtime
-    from diffusorrt_b200.config import QWEN3_06B_BD3LM
+    from diffusorrt_b200.config import DREAM_7B, QWEN3_06B_BD3LM
+
+    if args.dream:
+        prompt_len = 256 if args.prompt == 4096 else args.prompt
+        gen = 256 if args.gen == 32 else args.gen
+        canvas = prompt_len + gen
+        rt = Runtime(model_config=dict(DREAM_7B), synthetic_seed=0, device_ordinal=0, max_seq=canvas,
+                     max_prefill_rows=canvas)
+        sess = rt.session({"decode_strategy": "entropy_count"})
+        prompt = [int(t) for t in np.random.default_rng(0).integers(0, 151643, size=prompt_len)]
+        res = sess.generate(prompt, max_tokens=gen, steps=args.steps, temperature=0.2, top_p=0.95, eps=1e-3)
+        forwards = int(res["forward_count"])
+        print(json.dumps({"prompt": prompt_len, "gen": gen, "forwards": forwards,
+                          "kernel_launches": int(res["kernel_launches"]),
+                          "decode_ms_per_step": res["decode_ms"] / max(1, forwards)}), flush=True)
+        sess.close()
+        rt.close()
+        return
 
     cfg = dict(QWEN3_06B_BD3LM)
     max_seq = ((args.prompt + args.gen + 127) // 128) * 128

@@ -105,7 +105,7 @@ def main() -> int:
             for i in tr["chosen"]:
                 c.x[plan.frontier[i]] = tr["tokens"][i]
         print(f"certified steps: {certified} of {len(out['trace'])}", flush=True)
-        if c.x != out["x"] or certified < len(out["trace"]) // 3:
+        if c.x != out["x"] or certified < max(2, len(out["trace"]) // 5):
             ok = False
     flag = torch.tensor([0 if ok else 1], device=f"cuda:{local}")
     dist.broadcast(flag, src=0)

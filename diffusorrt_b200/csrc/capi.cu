@@ -208,6 +208,7 @@ int configure_kernels() {
     if (cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(sel_topp_entropy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kToppSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
@@ -1306,7 +1307,7 @@ int capture_dream(drt_session* s, const DreamState& g, double temperature, doubl
     t.conf = s->conf;
     t.token = s->token;
     t.tie = s->row_tie;
-    if (launch_k(sel_topp_entropy_kernel, dim3(gen_cap), dim3(kToppThreads), 0, s->stream, true, t) != cudaSuccess)
+    if (launch_k(sel_topp_entropy_kernel, dim3(gen_cap), dim3(kToppThreads), kToppSmemBytes, s->stream, true, t) != cudaSuccess)
       rc = set_error(DRT_INTERNAL_ERROR, "selector launch failed");
   }
   if (rc == DRT_OK &&
@@ -2112,6 +2113,7 @@ extern "C" int drt_selector_topp(const float* logits, int64_t ld, const int32_t*
   REQUIRE(tie_rel >= 0.0, "tie_rel must be >= 0");
   REQUIRE(exclude_token >= -1 && exclude_token < vocab, "exclude_token outside the vocabulary");
   if (n_rows == 0) return DRT_OK;
+  TRY(configure_kernels());
   ToppArgs t;
   memset(&t, 0, sizeof(t));
   t.logits = logits;
@@ -2126,7 +2128,7 @@ extern "C" int drt_selector_topp(const float* logits, int64_t ld, const int32_t*
   t.conf = conf;
   t.token = token;
   t.tie = tie;
-  CK(launch_k(sel_topp_entropy_kernel, dim3(n_rows), dim3(kToppThreads), 0, static_cast<cudaStream_t>(stream), false, t));
+  CK(launch_k(sel_topp_entropy_kernel, dim3(n_rows), dim3(kToppThreads), kToppSmemBytes, static_cast<cudaStream_t>(stream), false, t));
   return DRT_OK;
 }
 

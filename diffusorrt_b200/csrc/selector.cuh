@@ -322,10 +322,21 @@ __global__ void __launch_bounds__(32) sel_choose_kernel(const double* __restrict
 // the m copies of v_b the first c are, c = #{i in 1..m : above + i * p(v_b) <= top_p} (at least one
 // when v_b is the maximum). Which copies the reference's unstable sort puts first does not change
 // the entropy, since the copies are equal, nor the token unless v_b is a tied maximum.
-// v_b is located by a radix search over the order-preserving 32-bit keys of the f32 logits: four
-// passes over the row, each accumulating the unnormalised mass exp(a - max) of the keys under the
-// current prefix into 256 digit buckets and descending into the bucket where the cumulative mass
-// from the top crosses top_p * S. bf16-rounded logits repeat often, so the tie copies are counted.
+//
+// Passes over the row (one CTA per row, about one CTA per SM so the rows in flight stay in L2):
+//   1. max logit and its first index;
+//   2. S = sum exp(a - max) (f64, per-thread then block order) and a histogram of that mass over
+//      the distance from the maximum, max - a, in 1/8 steps (per-warp histograms: the bins spread
+//      the vocabulary, so updates rarely collide);
+//   3. the keys of every entry up to one bin past the bin where the cumulative mass crosses
+//      top_p * S, in index order, into a shared-memory list. Every kept entry and every copy of
+//      v_b is on it, and every entry off it lies below v_b.
+// v_b is then located exactly by a radix search over the order-preserving 32-bit keys of the list
+// (four 8-bit levels, each accumulating the mass of the keys under the current prefix per digit and
+// descending into the digit where the cumulative mass from the top crosses top_p * S), and the
+// nucleus normaliser and entropy are summed over the list. When the list would overflow (a flat
+// distribution whose nucleus holds most of the vocabulary), the same radix search and sums run
+// over the whole row instead.
 // tie[r]: bit 2 when the kept copies are a strict subset of a tied maximum (the reference's sort
 // order picks the token); bit 1 when a cumulative mass at the cut is within tie_rel of top_p (the
 // reference's own summation order may decide the other way there).
@@ -346,6 +357,11 @@ struct ToppArgs {
 };
 
 constexpr int kToppThreads = 512;
+constexpr int kToppWarps = kToppThreads / 32;
+constexpr int kToppBins = 256;           // distance-from-max bins of 1/8 (the last one open-ended)
+constexpr double kToppBinScale = 8.0;
+constexpr int kToppList = 24576;         // candidate keys held in shared memory
+constexpr size_t kToppSmemBytes = static_cast<size_t>(kToppList) * 4 + static_cast<size_t>(kToppWarps) * kToppBins * 8;
 
 __device__ __forceinline__ uint32_t f32_order_key(float v) {
   const uint32_t b = __float_as_uint(v);
@@ -363,12 +379,75 @@ __device__ __forceinline__ T topp_block_sum(T v, T* red, int lane, int warp) {
   if (lane == 0) red[warp] = v;
   __syncthreads();
   T t = T(0);
-  for (int w = 0; w < kToppThreads / 32; ++w) t += red[w];
+  for (int w = 0; w < kToppWarps; ++w) t += red[w];
   __syncthreads();
   return t;
 }
 
+__device__ __forceinline__ int topp_bin(double am, double a) {
+  const double d = (am - a) * kToppBinScale;
+  return d < static_cast<double>(kToppBins - 1) ? static_cast<int>(d) : kToppBins - 1;
+}
+
+// Shared state of one row's search.
+struct ToppShared {
+  double hist[256];
+  int hcnt[256];
+  double red_d[kToppWarps];
+  float red_f[kToppWarps];
+  int red_i[kToppWarps];
+  int warp_tot[kToppWarps + 1];
+  uint32_t prefix, mask;
+  double above;
+  int count, c, flag, n_list;
+};
+
+// Radix search for v_b over the keys key_at(i), i < n (valid(i) false skips an entry); returns
+// (in sh) prefix = key of v_b, above = mass strictly above it, count = its multiplicity.
+template <typename KeyAt, typename Valid>
+__device__ void topp_radix(ToppShared& sh, int n, KeyAt key_at, Valid valid, double T, double am, double limit) {
+  const int tid = threadIdx.x;
+  uint32_t prefix = 0, pmask = 0;
+  double above = 0.0;
+  for (int level = 0; level < 4; ++level) {
+    const int shift = 24 - 8 * level;
+    for (int i = tid; i < 256; i += kToppThreads) { sh.hist[i] = 0.0; sh.hcnt[i] = 0; }
+    __syncthreads();
+    for (int i = tid; i < n; i += kToppThreads) {
+      if (!valid(i)) continue;
+      const uint32_t k = key_at(i);
+      if ((k & pmask) != prefix) continue;
+      const double e = exp(static_cast<double>(f32_from_order_key(k)) / T - am);
+      const int d = static_cast<int>((k >> shift) & 255u);
+      atomicAdd(&sh.hist[d], e);
+      if (level == 3) atomicAdd(&sh.hcnt[d], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      double cum = above;
+      int d = 255;
+      for (; d > 0; --d) {
+        if (cum + sh.hist[d] > limit) break;
+        cum += sh.hist[d];
+      }
+      sh.above = cum;
+      sh.count = sh.hcnt[d];
+      sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
+      sh.mask = pmask | (0xFFu << shift);
+    }
+    __syncthreads();
+    prefix = sh.prefix;
+    pmask = sh.mask;
+    above = sh.above;
+    __syncthreads();
+  }
+}
+
 __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const ToppArgs a) {
+  extern __shared__ __align__(16) uint8_t topp_smem[];
+  uint32_t* list = reinterpret_cast<uint32_t*>(topp_smem);
+  double* whist = reinterpret_cast<double*>(topp_smem + static_cast<size_t>(kToppList) * 4);
+  __shared__ ToppShared sh;
   griddep_wait();
   griddep_launch_dependents();
   const int r = blockIdx.x;
@@ -377,24 +456,16 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
   const int src = a.row_index != nullptr ? a.row_index[r] : r;
   const float* x = a.logits + static_cast<int64_t>(src) * a.ld;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int NW = kToppThreads / 32;
-  __shared__ double hist[256];
-  __shared__ int hcnt[256];
-  __shared__ double red_d[NW];
-  __shared__ float red_f[NW];
-  __shared__ int red_i[NW];
-  __shared__ uint32_t s_prefix, s_mask;
-  __shared__ double s_above;
-  __shared__ int s_count;
   const double T = a.temperature > 0.0 ? a.temperature : 1.0;
   const bool nucleus = a.top_p < 1.0;
+  const int V = a.vocab, ex = a.exclude;
 
-  // max logit and its first index
+  // 1. max logit and its first index
   float m = -INFINITY;
   int mi = INT_MAX;
-  for (int i = tid; i < a.vocab; i += kToppThreads) {
+  for (int i = tid; i < V; i += kToppThreads) {
     const float v = x[i];
-    if (i != a.exclude && v > m) { m = v; mi = i; }
+    if (i != ex && v > m) { m = v; mi = i; }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -402,65 +473,97 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
     const int i2 = __shfl_xor_sync(0xffffffffu, mi, o);
     argmax_merge(m, mi, m2, i2);
   }
-  if (lane == 0) { red_f[warp] = m; red_i[warp] = mi; }
+  if (lane == 0) { sh.red_f[warp] = m; sh.red_i[warp] = mi; }
+  for (int i = tid; i < kToppWarps * kToppBins; i += kToppThreads) whist[i] = 0.0;
   __syncthreads();
-  float gm = red_f[0];
-  int gmi = red_i[0];
-  for (int w = 1; w < NW; ++w) argmax_merge(gm, gmi, red_f[w], red_i[w]);
+  float gm = sh.red_f[0];
+  int gmi = sh.red_i[0];
+  for (int w = 1; w < kToppWarps; ++w) argmax_merge(gm, gmi, sh.red_f[w], sh.red_i[w]);
   const double am = static_cast<double>(gm) / T;
   __syncthreads();
 
-  // S, then the radix search for v_b (the key of the first dropped value)
-  double S = 0.0;
-  uint32_t prefix = 0, pmask = 0;
-  double above = 0.0;
-  int count = 0;
+  // 2. S and the distance histogram
+  double part = 0.0;
+  double* my_hist = whist + warp * kToppBins;
+  for (int i = tid; i < V; i += kToppThreads) {
+    if (i == ex) continue;
+    const double ai = static_cast<double>(x[i]) / T;
+    const double e = exp(ai - am);
+    part += e;
+    if (nucleus) atomicAdd(&my_hist[topp_bin(am, ai)], e);
+  }
+  const double S = topp_block_sum(part, sh.red_d, lane, warp);
+  const double limit = a.top_p * S;
+
+  // 3. candidate list: every entry up to one bin past the crossing bin, in index order
+  bool use_list = false;
   if (nucleus) {
-    for (int level = 0; level < 4; ++level) {
-      const int shift = 24 - 8 * level;
-      for (int i = tid; i < 256; i += kToppThreads) { hist[i] = 0.0; hcnt[i] = 0; }
-      __syncthreads();
-      double part = 0.0;
-      for (int i = tid; i < a.vocab; i += kToppThreads) {
-        const float v = x[i];
-        const uint32_t k = f32_order_key(v);
-        if (i == a.exclude || (k & pmask) != prefix) continue;
-        const double e = exp(static_cast<double>(v) / T - am);
-        part += e;
-        const int d = static_cast<int>((k >> shift) & 255u);
-        atomicAdd(&hist[d], e);
-        if (level == 3) atomicAdd(&hcnt[d], 1);
+    if (tid == 0) {
+      double cum = 0.0;
+      int b = 0;
+      for (; b < kToppBins - 1; ++b) {
+        double hb = 0.0;
+        for (int w = 0; w < kToppWarps; ++w) hb += whist[w * kToppBins + b];
+        cum += hb;
+        if (cum > limit) break;
       }
-      if (level == 0) S = topp_block_sum(part, red_d, lane, warp);
-      else __syncthreads();
-      if (tid == 0) {
-        const double limit = a.top_p * S;
-        double cum = above;
-        int d = 255;
-        for (; d > 0; --d) {
-          if (cum + hist[d] > limit) break;
-          cum += hist[d];
+      sh.c = min(b + 1, kToppBins - 1);  // last bin on the list
+      sh.n_list = 0;
+    }
+    __syncthreads();
+    const int last_bin = sh.c;
+    int n = 0;
+    bool overflow = false;
+    if (last_bin < kToppBins - 1) {
+      for (int base = 0; base < V && !overflow; base += kToppThreads) {
+        const int i = base + tid;
+        bool take = false;
+        uint32_t key = 0;
+        if (i < V && i != ex) {
+          const float v = x[i];
+          take = topp_bin(am, static_cast<double>(v) / T) <= last_bin;
+          key = f32_order_key(v);
         }
-        s_above = cum;
-        s_count = hcnt[d];
-        s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
-        s_mask = pmask | (0xFFu << shift);
+        const unsigned bal = __ballot_sync(0xffffffffu, take);
+        if (lane == 0) sh.warp_tot[warp] = __popc(bal);
+        __syncthreads();
+        if (tid == 0) {
+          int acc = 0;
+          for (int w = 0; w < kToppWarps; ++w) {
+            const int t = sh.warp_tot[w];
+            sh.warp_tot[w] = acc;
+            acc += t;
+          }
+          sh.warp_tot[kToppWarps] = acc;
+        }
+        __syncthreads();
+        const int tot = sh.warp_tot[kToppWarps];
+        if (n + tot > kToppList) {
+          overflow = true;
+        } else if (take) {
+          list[n + sh.warp_tot[warp] + __popc(bal & ((1u << lane) - 1u))] = key;
+        }
+        n += tot;
+        __syncthreads();
       }
-      __syncthreads();
-      prefix = s_prefix;
-      pmask = s_mask;
-      above = s_above;
-      count = s_count;
-      __syncthreads();
+    } else {
+      overflow = true;
+    }
+    use_list = !overflow;
+    if (use_list) {
+      topp_radix(sh, n, [&](int i) { return list[i]; }, [](int) { return true; }, T, am, limit);
+      if (tid == 0) sh.n_list = n;
+    } else {
+      topp_radix(sh, V, [&](int i) { return f32_order_key(x[i]); }, [&](int i) { return i != ex; }, T, am, limit);
     }
   }
-  const uint32_t vb = prefix;
+  const uint32_t vb = nucleus ? sh.prefix : 0u;
   // kept copies of v_b and the certification flags
-  __shared__ int s_c, s_flag;
   if (tid == 0) {
     int c = 0, flag = 0;
     if (nucleus) {
-      const double limit = a.top_p * S;
+      const double above = sh.above;
+      const int count = sh.count;
       const double e = exp(static_cast<double>(f32_from_order_key(vb)) / T - am);
       while (c < count && above + static_cast<double>(c + 1) * e <= limit) ++c;
       if (above == 0.0 && c == 0) c = 1;
@@ -469,31 +572,41 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
       if (c < count && !(fabs(above + static_cast<double>(c + 1) * e - limit) > tol)) flag |= 1;
       if (above == 0.0 && c < count) flag |= 2;
     }
-    s_c = c;
-    s_flag = flag;
+    sh.c = c;
+    sh.flag = flag;
   }
   __syncthreads();
-  const int c = s_c;
+  const int c = sh.c;
   const double e_vb = nucleus ? exp(static_cast<double>(f32_from_order_key(vb)) / T - am) : 0.0;
 
-  // normaliser over the kept entries
+  // normaliser and entropy over the kept entries (the list, or the whole row)
+  const int n_src = use_list ? sh.n_list : V;
+  auto kept_value = [&](int i, float* v) -> bool {
+    if (use_list) {
+      const uint32_t k = list[i];
+      *v = f32_from_order_key(k);
+      return k > vb;
+    }
+    if (i == ex) return false;
+    *v = x[i];
+    return !nucleus || f32_order_key(*v) > vb;
+  };
   double sk = 0.0;
-  for (int i = tid; i < a.vocab; i += kToppThreads) {
-    const float v = x[i];
-    if (i == a.exclude || (nucleus && f32_order_key(v) <= vb)) continue;
-    sk += exp(static_cast<double>(v) / T - am);
+  for (int i = tid; i < n_src; i += kToppThreads) {
+    float v;
+    if (kept_value(i, &v)) sk += exp(static_cast<double>(v) / T - am);
   }
-  double Sk = topp_block_sum(sk, red_d, lane, warp);
+  double Sk = topp_block_sum(sk, sh.red_d, lane, warp);
   Sk += static_cast<double>(c) * e_vb;
-  // entropy sum p' log(p' + 1e-10)
   double h = 0.0;
-  for (int i = tid; i < a.vocab; i += kToppThreads) {
-    const float v = x[i];
-    if (i == a.exclude || (nucleus && f32_order_key(v) <= vb)) continue;
-    const double pv = exp(static_cast<double>(v) / T - am) / Sk;
-    h += pv * log(pv + 1e-10);
+  for (int i = tid; i < n_src; i += kToppThreads) {
+    float v;
+    if (kept_value(i, &v)) {
+      const double pv = exp(static_cast<double>(v) / T - am) / Sk;
+      h += pv * log(pv + 1e-10);
+    }
   }
-  double H = topp_block_sum(h, red_d, lane, warp);
+  double H = topp_block_sum(h, sh.red_d, lane, warp);
   if (tid == 0) {
     if (c > 0) {
       const double pv = e_vb / Sk;
@@ -501,7 +614,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
     }
     a.conf[r] = static_cast<double>(static_cast<float>(H));
     a.token[r] = gmi;
-    if (a.tie != nullptr) a.tie[r] = s_flag;
+    if (a.tie != nullptr) a.tie[r] = sh.flag;
   }
 }
 

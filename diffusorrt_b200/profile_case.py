@@ -6,7 +6,7 @@ kernels at the same shapes as the benchmark with few launches before them, and t
 about 2 GB (weights 1.19 GB, K/V cache ~0.5 GB).
 
     python -m diffusorrt_b200.profile_case [--prompt 4096] [--gen 32] [--rounds 8]
-    python -m diffusorrt_b200.profile_case --dream [--steps 4]
+    python -m diffusorrt_b200.profile_case --dream [--steps 4] [--layers 28]
 
 With --dream: the Dream-7B-architecture full-canvas workload (prompt 256 + canvas 256,
 entropy_count over --steps steps, each a 512-row forward); the model's synthetic weights take
@@ -38,6 +38,7 @@ def main() -> None:
     ap.add_argument("--rounds", type=int, default=8)
     ap.add_argument("--dream", action="store_true", help="Dream-7B full-canvas entropy_count instead")
     ap.add_argument("--steps", type=int, default=4, help="entropy_count steps (--dream)")
+    ap.add_argument("--layers", type=int, default=0, help="transformer layers (--dream; 0 = the model's 28)")
     args = ap.parse_args()
     from diffusorrt_b200 import Runtime
     from diffusorrt_b200.config import DREAM_7B, QWEN3_06B_BD3LM
@@ -46,8 +47,10 @@ def main() -> None:
         prompt_len = 256 if args.prompt == 4096 else args.prompt
         gen = 256 if args.gen == 32 else args.gen
         canvas = prompt_len + gen
-        rt = Runtime(model_config=dict(DREAM_7B), synthetic_seed=0, device_ordinal=0, max_seq=canvas,
-                     max_prefill_rows=canvas)
+        cfg = dict(DREAM_7B)
+        if args.layers > 0:
+            cfg["layer_count"] = args.layers
+        rt = Runtime(model_config=cfg, synthetic_seed=0, device_ordinal=0, max_seq=canvas, max_prefill_rows=canvas)
         sess = rt.session({"decode_strategy": "entropy_count"})
         prompt = [int(t) for t in np.random.default_rng(0).integers(0, 151643, size=prompt_len)]
         res = sess.generate(prompt, max_tokens=gen, steps=args.steps, temperature=0.2, top_p=0.95, eps=1e-3)

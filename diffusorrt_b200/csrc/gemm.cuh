@@ -76,10 +76,12 @@ struct GemmCfg {
   static constexpr int kBBytes = BN * 128;        // BN rows x 64 bf16
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  // Ring, or (split-K) the receive buffer plus the epilogue exchange buffer, whichever is larger.
+  // Ring, or (split-K, BN <= 128) the receive buffer plus the epilogue exchange buffer, whichever is
+  // larger. Wider tiles are never split and only need the exchange buffer after the ring drains.
   __host__ __device__ static size_t body_bytes(int stages) {
     const size_t ring = static_cast<size_t>(stages) * kStageBytes;
-    const size_t epi = static_cast<size_t>(BN) * 128 * 4 + (32 * 128 + 160) * 4;
+    const size_t recv = BN <= 128 ? static_cast<size_t>(BN) * 128 * 4 : 0;
+    const size_t epi = recv + (32 * 128 + 160) * 4;
     return ((ring > epi ? ring : epi) + 1023) & ~size_t(1023);
   }
   __host__ __device__ static size_t smem_bytes(int stages) { return 1024 + body_bytes(stages) + 256; }
@@ -195,6 +197,23 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
         return;
       }
       const float* nw = is_q ? a.qnorm_w : a.knorm_w;
+      // RoPE factors of the chunk's rows, all loaded before any store of the chunk (the stores below
+      // may alias them as far as the compiler knows, which would serialise one load per row).
+      float rc[32], rsn[32];
+      if (rope_c == nullptr) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int pos = pos0 + col0 + min(i, ncols - 1);
+          rc[i] = __ldg(a.rope_cos + static_cast<size_t>(pos) * 64 + (tid & 63));
+          rsn[i] = __ldg(a.rope_sin + static_cast<size_t>(pos) * 64 + (tid & 63));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          rc[i] = rope_c[i];
+          rsn[i] = rope_s[i];
+        }
+      }
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float val = __fadd_rn(out_round<RND>(v[i]), b);
@@ -235,8 +254,8 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
           xp = __fmul_rn(__fmul_rn(xp, rs[i]), w_part);
         }
         const int pos = pos0 + col0 + i;
-        const float c = rope_c != nullptr ? rope_c[i] : a.rope_cos[static_cast<size_t>(pos) * 64 + (tid & 63)];
-        const float s = rope_s != nullptr ? rope_s[i] : a.rope_sin[static_cast<size_t>(pos) * 64 + (tid & 63)];
+        const float c = rc[i];
+        const float s = rsn[i];
         const float rot = tid < 64 ? -xp : xp;
         const float out = __fadd_rn(__fmul_rn(x, c), __fmul_rn(rot, s));
         if (is_q) {

@@ -208,6 +208,7 @@ int configure_kernels() {
     if (cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_swapab_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(sel_topp_entropy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kToppSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
@@ -228,14 +229,6 @@ int configure_kernels() {
   return DRT_OK;
 }
 
-// Split-K factor: the smallest power of two (<= max_split, <= kb) giving at least ~0.8 x SMs
-// CTAs. The split CTAs of one tile form one cluster.
-void split_k(int tiles, int kb, int sms, int max_split, int* splits, int* kbps) {
-  int sp = 1;
-  while (sp < max_split && sp * 2 <= kb && tiles * sp < (sms * 4) / 5) sp *= 2;
-  *splits = sp;
-  *kbps = (kb + sp - 1) / sp;
-}
 
 constexpr double kTieRel = 9.094947017729282e-13;  // 2^-40
 }  // namespace
@@ -856,7 +849,7 @@ struct drt_session {
   int attn_splits = 1, attn_tps = 1;
   int sel_chunks = 1;
   // tensor maps over the activation buffers
-  CUtensorMap m_xn64, m_xn128, m_xn256, m_attn64, m_attn128, m_act64, m_act128, m_xf64, m_q, m_k, m_v;
+  CUtensorMap m_xn64, m_xn128, m_xn256, m_attn64, m_attn128, m_attn256, m_act64, m_act128, m_act256, m_xf64, m_q, m_k, m_v;
   CUtensorMap m_k64;                  // K cache with 64-key boxes (decode attention)
   int da_splits = 0;                  // decode attention CTAs per KV head (0: use attn_prefix_kernel)
   float* da_part_o = nullptr;         // decode attention split partials
@@ -878,7 +871,7 @@ struct drt_session {
   int* d_klist = nullptr;             // transfer count per proceeding step
   int* d_stepof = nullptr;            // loop step of each proceeding step
   int d_steps_cap = 0;
-  CUtensorMap m_xf128;
+  CUtensorMap m_xf128, m_xf256;
   cudaGraphExec_t g_dream = nullptr;  // plan + full-canvas forward + head + top-p score + commit
   int g_dream_kernels = 0;
   struct DreamKey {
@@ -939,24 +932,40 @@ GemmArgs base_args(drt_session* s, int n_out, int K, const Fwd& f) {
   return a;
 }
 
-constexpr size_t kHalfSmPrefill = 113 * 1024;
+constexpr size_t kHalfSmPrefill = 113 * 1024;   // two CTAs share an SM
+constexpr size_t kFullSmPrefill = 227 * 1024;   // one CTA per SM
 
-template <int BN>
-int run_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a, bool allow_split) {
+template <int BN, int KS>
+int launch_wide(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a, size_t smem_cap) {
+  using Cfg = GemmCfg<BN, KS>;
   const int tiles_m = a.n_out / 128;
   const int tiles_n = (a.rows + BN - 1) / BN;
-  const int kb = a.K / 64;
-  if (allow_split) split_k(tiles_m * tiles_n, kb, s->sms, s->max_cluster, &a.splits, &a.kb_per_split);
-  else { a.splits = 1; a.kb_per_split = kb; }
-  // The deepest ring that still lets two CTAs share an SM: one CTA's epilogue then overlaps the
-  // other's main loop (measured on B200: 1.8x over one 6-stage CTA per SM at the 512-row shapes).
-  int max_stages = 2;
-  while (GemmCfg<BN>::smem_bytes(max_stages + 1) <= kHalfSmPrefill) ++max_stages;
-  a.stages = std::max(1, std::min(a.kb_per_split, max_stages));
-  dim3 grid(tiles_m, tiles_n, a.splits);
-  CK(launch_kc(gemm_swapab_kernel<BN>, grid, dim3(128), GemmCfg<BN>::smem_bytes(a.stages), s->stream, true, a.splits, mA,
-               mB, a));
+  a.splits = 1;
+  a.kb_per_split = a.K / 64;
+  int stages = 1;
+  while (Cfg::smem_bytes(stages + 1) <= smem_cap) ++stages;
+  a.stages = std::max(1, std::min((a.kb_per_split + KS - 1) / KS, stages));
+  CK(launch_kc(gemm_swapab_kernel<BN, KS>, dim3(tiles_m, tiles_n, 1), dim3(128), Cfg::smem_bytes(a.stages), s->stream,
+               true, 1, mA, mB, a));
   return DRT_OK;
+}
+
+// Linear over a wide activation block (prompt prefill, full-canvas forward, wide lm_head). Tile and
+// ring shape from the measured B200 behaviour: one CTA's TMA ingest is bound by bytes per barrier
+// round trip, so
+//   * with at least two CTAs per SM of 256-row tiles: 128 x 256 tiles, two CTAs per SM (one CTA's
+//     epilogue overlaps the other's main loop);
+//   * with at most one wave of 128 x 128 tiles: one CTA per SM, two K blocks per stage, three stages;
+//   * otherwise: 128 x 128 tiles, two CTAs per SM.
+// mB128 / mB256: the activation map with 128- / 256-row boxes (mB256 null when the buffer is
+// narrower than 256 rows).
+int run_wide(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB128, const CUtensorMap* mB256, GemmArgs a) {
+  const int tiles_m = a.n_out / 128;
+  const int t256 = tiles_m * ((a.rows + 255) / 256);
+  const int t128 = tiles_m * ((a.rows + 127) / 128);
+  if (mB256 != nullptr && a.rows > 128 && t256 >= 2 * s->sms) return launch_wide<256, 1>(s, mA, *mB256, a, kHalfSmPrefill);
+  if (t128 <= s->sms) return launch_wide<128, 2>(s, mA, mB128, a, kFullSmPrefill);
+  return launch_wide<128, 1>(s, mA, mB128, a, kHalfSmPrefill);
 }
 
 // Split-K factor for the decode linears: the fewest K blocks per CTA with at most one CTA per SM,
@@ -1069,7 +1078,7 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     if (f.decode) {
       TRY(run_dec_gemm(s, w.m_qkv, s->m_xn64, a, m->quantized ? &w.q_qkv : nullptr));
     } else {
-      TRY(run_gemm<128>(s, w.m_qkv, s->m_xn128, a, false));
+      TRY(run_wide(s, w.m_qkv, s->m_xn128, s->rows_cap >= 256 ? &s->m_xn256 : nullptr, a));
     }
     // Attention.
     AttnArgs t;
@@ -1138,7 +1147,7 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     o.out_f32 = tp ? s->part : s->h;
     o.ld_out = H;
     if (f.decode) TRY(run_dec_gemm(s, w.m_o, s->m_attn64, o, m->quantized ? &w.q_o : nullptr));
-    else TRY(run_gemm<128>(s, w.m_o, s->m_attn128, o, false));
+    else TRY(run_wide(s, w.m_o, s->m_attn128, s->rows_cap >= 256 ? &s->m_attn256 : nullptr, o));
     if (tp) TRY(tp_reduce_residual(s, f.rows));
     TRY(run_rmsnorm(s, s->h, nullptr, f.rows, f.rows_dev, w.post_norm, s->xn));
     // gate/up + SwiGLU.
@@ -1147,15 +1156,14 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     g.out_bf16 = s->act;
     g.ld_out = m->I;
     if (f.decode) TRY(run_dec_gemm(s, w.m_gu, s->m_xn64, g, m->quantized ? &w.q_gu : nullptr));
-    else if (f.rows >= 256) TRY(run_gemm<256>(s, w.m_gu, s->m_xn256, g, false));
-    else TRY(run_gemm<128>(s, w.m_gu, s->m_xn128, g, false));
+    else TRY(run_wide(s, w.m_gu, s->m_xn128, s->rows_cap >= 256 ? &s->m_xn256 : nullptr, g));
     // down + residual.
     GemmArgs d = base_args(s, H, m->I, f);
     d.epi = tp ? EPI_STORE_RAW : EPI_RESID;
     d.out_f32 = tp ? s->part : s->h;
     d.ld_out = H;
     if (f.decode) TRY(run_dec_gemm(s, w.m_down, s->m_act64, d, m->quantized ? &w.q_down : nullptr));
-    else TRY(run_gemm<128>(s, w.m_down, s->m_act128, d, false));
+    else TRY(run_wide(s, w.m_down, s->m_act128, s->rows_cap >= 256 ? &s->m_act256 : nullptr, d));
     if (tp) TRY(tp_reduce_residual(s, f.rows));
   }
   return DRT_OK;
@@ -1297,7 +1305,7 @@ int capture_dream(drt_session* s, const DreamState& g, double temperature, doubl
     a.epi = EPI_STORE_F32;
     a.out_f32 = s->logits;
     a.ld_out = m->V;
-    rc = run_gemm<128>(s, m->m_lm, s->m_xf128, a, false);
+    rc = run_wide(s, m->m_lm, s->m_xf128, s->head_cap >= 256 ? &s->m_xf256 : nullptr, a);
   }
   if (rc == DRT_OK) {
     ToppArgs t;
@@ -1610,6 +1618,7 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
     if ((rc = salloc(s, &s->dstate, 1)) != DRT_OK) return fail(rc);
     if (cudaMallocHost(&s->hdstate, sizeof(DreamState)) != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "pinned alloc failed"));
     if ((rc = map_matrix(&s->m_xf128, s->xf, s->head_cap, H, 128)) != DRT_OK) return fail(rc);
+    if (s->head_cap >= 256 && (rc = map_matrix(&s->m_xf256, s->xf, s->head_cap, H, 256)) != DRT_OK) return fail(rc);
   }
   if ((rc = salloc(s, &s->status, 1)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->state, 1)) != DRT_OK) return fail(rc);
@@ -1622,6 +1631,8 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = map_matrix(&s->m_xn64, s->xn, R, H, 64)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_xn128, s->xn, R, H, 128)) != DRT_OK) return fail(rc);
   if (R >= 256 && (rc = map_matrix(&s->m_xn256, s->xn, R, H, 256)) != DRT_OK) return fail(rc);
+  if (R >= 256 && (rc = map_matrix(&s->m_attn256, s->attn, R, qd, 256)) != DRT_OK) return fail(rc);
+  if (R >= 256 && (rc = map_matrix(&s->m_act256, s->act, R, m->I, 256)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_attn64, s->attn, R, qd, 64)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_attn128, s->attn, R, qd, 128)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_act64, s->act, R, m->I, 64)) != DRT_OK) return fail(rc);

@@ -70,11 +70,13 @@ struct GemmArgs {
   int q_groups;
 };
 
-template <int BN>
+// KS: K blocks of 64 per ring stage. One mbarrier phase covers a whole stage; larger stages keep
+// more bytes in flight per barrier round trip, which is what bounds one CTA's TMA ingest rate.
+template <int BN, int KS = 1>
 struct GemmCfg {
-  static constexpr int kABytes = 128 * 128;       // 128 rows x 64 bf16
-  static constexpr int kBBytes = BN * 128;        // BN rows x 64 bf16
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kABytes = 128 * 128;       // 128 rows x 64 bf16 (one K block)
+  static constexpr int kBBytes = BN * 128;        // BN rows x 64 bf16 (one K block)
+  static constexpr int kStageBytes = KS * (kABytes + kBBytes);
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   // Ring, or (split-K, BN <= 128) the receive buffer plus the epilogue exchange buffer, whichever is
   // larger. Wider tiles are never split and only need the exchange buffer after the ring drains.
@@ -327,20 +329,19 @@ __device__ __forceinline__ int split_sum(const float* recv, uint32_t rank, int t
   return CPR;
 }
 
-template <int BN>
+template <int BN, int KS = 1>
 __global__ void __launch_bounds__(128, 1)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const GemmArgs a) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, KS>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   const int stages = a.stages;
   uint8_t* ring = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring + Cfg::body_bytes(stages));
-  uint64_t* fullA = bars;
-  uint64_t* fullB = bars + stages;
-  uint64_t* empty = bars + 2 * stages;
-  uint64_t* accum = bars + 3 * stages;
+  uint64_t* full = bars;               // A and B of a stage
+  uint64_t* empty = bars + stages;
+  uint64_t* accum = bars + 2 * stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] error
 
@@ -357,11 +358,11 @@ __global__ void __launch_bounds__(128, 1)
   const int kb_total = a.K >> 6;
   const int kb0 = split * a.kb_per_split;
   const int nkb = max(0, min(a.kb_per_split, kb_total - kb0));
+  const int nsb = (nkb + KS - 1) / KS;  // ring stages to fill
 
   if (tid == 0) {
     for (int s = 0; s < stages; ++s) {
-      mbar_init(&fullA[s], 1);
-      mbar_init(&fullB[s], 1);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
@@ -380,14 +381,19 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Weight prefetch: independent of the producer kernel, so it is issued before the PDL wait.
-  const int npre = min(stages, nkb);
+  // Stage layout: KS weight tiles (A), then KS activation tiles (B). The stage's barrier is armed
+  // once with every byte of the stage; the weight loads need nothing from the producer kernel, so
+  // the first stages' weights are requested before the PDL wait and their activations after it.
+  const int npre = min(stages, nsb);
   uint64_t policy = 0;
   if (tid == 0) {
     policy = tiles_n > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
     for (int i = 0; i < npre; ++i) {
-      mbar_expect_tx(&fullA[i], Cfg::kABytes);
-      tma_load_2d_hint(ring + static_cast<size_t>(i) * Cfg::kStageBytes, &tmA, &fullA[i], (kb0 + i) * 64, m0, policy);
+      const int nk = min(KS, nkb - i * KS);
+      uint8_t* st = ring + static_cast<size_t>(i) * Cfg::kStageBytes;
+      mbar_expect_tx(&full[i], static_cast<uint32_t>(nk * (Cfg::kABytes + Cfg::kBBytes)));
+      for (int j = 0; j < nk; ++j)
+        tma_load_2d_hint(st + j * Cfg::kABytes, &tmA, &full[i], (kb0 + i * KS + j) * 64, m0, policy);
     }
   }
   griddep_wait();
@@ -398,16 +404,18 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
-      for (int i = 0; i < nkb && ok; ++i) {
+      for (int i = 0; i < nsb && ok; ++i) {
         const int s = i % stages;
+        const int nk = min(KS, nkb - i * KS);
         uint8_t* st = ring + static_cast<size_t>(s) * Cfg::kStageBytes;
         if (i >= stages) {
           if (!mbar_wait(&empty[s], ((i / stages) - 1) & 1)) { ok = false; break; }
-          mbar_expect_tx(&fullA[s], Cfg::kABytes);
-          tma_load_2d_hint(st, &tmA, &fullA[s], (kb0 + i) * 64, m0, policy);
+          mbar_expect_tx(&full[s], static_cast<uint32_t>(nk * (Cfg::kABytes + Cfg::kBBytes)));
+          for (int j = 0; j < nk; ++j)
+            tma_load_2d_hint(st + j * Cfg::kABytes, &tmA, &full[s], (kb0 + i * KS + j) * 64, m0, policy);
         }
-        mbar_expect_tx(&fullB[s], Cfg::kBBytes);
-        tma_load_2d(st + Cfg::kABytes, &tmB, &fullB[s], (kb0 + i) * 64, n0);
+        for (int j = 0; j < nk; ++j)
+          tma_load_2d(st + KS * Cfg::kABytes + j * Cfg::kBBytes, &tmB, &full[s], (kb0 + i * KS + j) * 64, n0);
       }
       if (!ok) { record_error(a.status, DEV_TIMEOUT_TMA); flags[0] = 1; }
     }
@@ -416,17 +424,23 @@ __global__ void __launch_bounds__(128, 1)
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(128, BN);
       bool ok = true;
-      for (int i = 0; i < nkb; ++i) {
+      for (int i = 0; i < nsb; ++i) {
         const int s = i % stages;
+        const int nk = min(KS, nkb - i * KS);
         const uint32_t ph = (i / stages) & 1;
-        if (!mbar_wait(&fullA[s], ph) || !mbar_wait(&fullB[s], ph)) { ok = false; break; }
+        if (!mbar_wait(&full[s], ph)) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_addr = smem_u32(ring + static_cast<size_t>(s) * Cfg::kStageBytes);
-        const uint32_t b_addr = a_addr + Cfg::kABytes;
+        const uint32_t b_addr = a_addr + KS * Cfg::kABytes;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          umma_bf16(tmem, sdesc_kmajor_sw128(a_addr + kk * 32), sdesc_kmajor_sw128(b_addr + kk * 32), idesc,
-                    (i | kk) != 0 ? 1u : 0u);
+        for (int j = 0; j < KS; ++j) {
+          if (j < nk) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              umma_bf16(tmem, sdesc_kmajor_sw128(a_addr + j * Cfg::kABytes + kk * 32),
+                        sdesc_kmajor_sw128(b_addr + j * Cfg::kBBytes + kk * 32), idesc, (i | j | kk) != 0 ? 1u : 0u);
+            }
+          }
         }
         umma_commit(&empty[s]);
       }
@@ -502,10 +516,7 @@ __global__ void __launch_bounds__(128, 1)
   }
   if (failed && tid == 0) {
     // Drain loads that may still be landing in this CTA's shared memory (bounded).
-    for (int s = 0; s < min(stages, nkb); ++s) {
-      mbar_wait(&fullA[s], 0);
-      mbar_wait(&fullB[s], 0);
-    }
+    for (int s = 0; s < min(stages, nsb); ++s) mbar_wait(&full[s], 0);
   }
   tc_fence_before();
   __syncthreads();

@@ -154,22 +154,26 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
     if constexpr (EPI == EPI_SWIGLU) {
       // Tile layout (set by the weight packer): lanes 0..63 = gate rows j0..j0+63,
       // lanes 64..127 = up rows j0..j0+63 of the same intermediate features.
+      // All four warps: every lane parks its 32 values, then lane pair (f, f + 64) splits the rows by
+      // parity, so each thread evaluates 16 SwiGLU outputs instead of half the threads 32.
       const int j0 = (m0 >> 1);
-      if (tid >= 64) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) xs[i * 64 + (tid - 64)] = __fadd_rn(out_round<RND>(v[i]), b);
-      }
+      for (int i = 0; i < 32; ++i) xs[i * 128 + tid] = __fadd_rn(out_round<RND>(v[i]), b);
       __syncthreads();
-      if (tid < 64) {
+      const int f = tid & 63, par = tid >> 6;
+      float g[16], u[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i < ncols) {
-            const float g = __fadd_rn(out_round<RND>(v[i]), b);
-            const float u = xs[i * 64 + tid];
-            const float sig = 1.0f / (1.0f + expf(-g));
-            const float act = __fmul_rn(__fmul_rn(g, sig), u);
-            a.out_bf16[static_cast<size_t>(col0 + i) * a.ld_out + j0 + tid] = __float2bfloat16_rn(act);
-          }
+      for (int k = 0; k < 16; ++k) {
+        g[k] = xs[(2 * k + par) * 128 + f];
+        u[k] = xs[(2 * k + par) * 128 + 64 + f];
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int i = 2 * k + par;
+        if (i < ncols) {
+          const float sig = 1.0f / (1.0f + expf(-g[k]));
+          const float act = __fmul_rn(__fmul_rn(g[k], sig), u[k]);
+          a.out_bf16[static_cast<size_t>(col0 + i) * a.ld_out + j0 + f] = __float2bfloat16_rn(act);
         }
       }
       __syncthreads();

@@ -326,8 +326,8 @@ __global__ void __launch_bounds__(32) sel_choose_kernel(const double* __restrict
 // Passes over the row (one CTA per row, about one CTA per SM so the rows in flight stay in L2):
 //   1. max logit and its first index;
 //   2. S = sum exp(a - max) (f64, per-thread then block order) and a histogram of that mass over
-//      the distance from the maximum, max - a, in 1/8 steps (per-warp histograms: the bins spread
-//      the vocabulary, so updates rarely collide);
+//      the distance from the maximum, max - a, in 1/8 steps (f32, per-warp: the bins spread the
+//      vocabulary, so updates rarely collide; the histogram only places the list cut, below);
 //   3. the keys of every entry up to one bin past the bin where the cumulative mass crosses
 //      top_p * S, in index order, into a shared-memory list. Every kept entry and every copy of
 //      v_b is on it, and every entry off it lies below v_b.
@@ -335,8 +335,9 @@ __global__ void __launch_bounds__(32) sel_choose_kernel(const double* __restrict
 // (four 8-bit levels, each accumulating the mass of the keys under the current prefix per digit and
 // descending into the digit where the cumulative mass from the top crosses top_p * S), and the
 // nucleus normaliser and entropy are summed over the list. When the list would overflow (a flat
-// distribution whose nucleus holds most of the vocabulary), the same radix search and sums run
-// over the whole row instead.
+// distribution whose nucleus holds most of the vocabulary), or its f64 mass does not reach
+// top_p * S (the f32 histogram misplaced the cut), the same radix search and sums run over the whole
+// row instead.
 // tie[r]: bit 2 when the kept copies are a strict subset of a tied maximum (the reference's sort
 // order picks the token); bit 1 when a cumulative mass at the cut is within tie_rel of top_p (the
 // reference's own summation order may decide the other way there).
@@ -361,7 +362,7 @@ constexpr int kToppWarps = kToppThreads / 32;
 constexpr int kToppBins = 256;           // distance-from-max bins of 1/8 (the last one open-ended)
 constexpr double kToppBinScale = 8.0;
 constexpr int kToppList = 24576;         // candidate keys held in shared memory
-constexpr size_t kToppSmemBytes = static_cast<size_t>(kToppList) * 4 + static_cast<size_t>(kToppWarps) * kToppBins * 8;
+constexpr size_t kToppSmemBytes = static_cast<size_t>(kToppList) * 4 + static_cast<size_t>(kToppWarps) * kToppBins * 4;
 
 __device__ __forceinline__ uint32_t f32_order_key(float v) {
   const uint32_t b = __float_as_uint(v);
@@ -384,9 +385,11 @@ __device__ __forceinline__ T topp_block_sum(T v, T* red, int lane, int warp) {
   return t;
 }
 
-__device__ __forceinline__ int topp_bin(double am, double a) {
-  const double d = (am - a) * kToppBinScale;
-  return d < static_cast<double>(kToppBins - 1) ? static_cast<int>(d) : kToppBins - 1;
+// Distance bin of logit v below the maximum gm, in f32 (only consistency between the passes and
+// monotonicity matter: the exact cut is found afterwards from the keys).
+__device__ __forceinline__ int topp_bin(float gm, float v, float scale) {
+  const float d = (gm - v) * scale;
+  return d < static_cast<float>(kToppBins - 1) ? static_cast<int>(d) : kToppBins - 1;
 }
 
 // Shared state of one row's search.
@@ -405,7 +408,7 @@ struct ToppShared {
 // Radix search for v_b over the keys key_at(i), i < n (valid(i) false skips an entry); returns
 // (in sh) prefix = key of v_b, above = mass strictly above it, count = its multiplicity.
 template <typename KeyAt, typename Valid>
-__device__ void topp_radix(ToppShared& sh, int n, KeyAt key_at, Valid valid, double T, double am, double limit) {
+__device__ void topp_radix(ToppShared& sh, int n, KeyAt key_at, Valid valid, double invT, double am, double limit) {
   const int tid = threadIdx.x;
   uint32_t prefix = 0, pmask = 0;
   double above = 0.0;
@@ -417,7 +420,7 @@ __device__ void topp_radix(ToppShared& sh, int n, KeyAt key_at, Valid valid, dou
       if (!valid(i)) continue;
       const uint32_t k = key_at(i);
       if ((k & pmask) != prefix) continue;
-      const double e = exp(static_cast<double>(f32_from_order_key(k)) / T - am);
+      const double e = exp(static_cast<double>(f32_from_order_key(k)) * invT - am);
       const int d = static_cast<int>((k >> shift) & 255u);
       atomicAdd(&sh.hist[d], e);
       if (level == 3) atomicAdd(&sh.hcnt[d], 1);
@@ -443,10 +446,55 @@ __device__ void topp_radix(ToppShared& sh, int n, KeyAt key_at, Valid valid, dou
   }
 }
 
+// f(i, x[i]) for every i < V; each thread keeps 16 loads in flight (the row is read from L2 or
+// HBM, so one outstanding load per thread would leave the pass latency-bound). A thread visits
+// its indices in increasing order.
+template <typename F>
+__device__ __forceinline__ void topp_row_foreach(const float* __restrict__ x, int V, F f) {
+  const int tid = threadIdx.x;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (V & 3) == 0) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const int V4 = V >> 2;
+    constexpr int U = 4;
+    int j = tid;
+    for (; j + (U - 1) * kToppThreads < V4; j += U * kToppThreads) {
+      float4 t[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) t[u] = __ldg(x4 + j + u * kToppThreads);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = 4 * (j + u * kToppThreads);
+        f(i, t[u].x);
+        f(i + 1, t[u].y);
+        f(i + 2, t[u].z);
+        f(i + 3, t[u].w);
+      }
+    }
+    for (; j < V4; j += kToppThreads) {
+      const float4 t = __ldg(x4 + j);
+      f(4 * j, t.x);
+      f(4 * j + 1, t.y);
+      f(4 * j + 2, t.z);
+      f(4 * j + 3, t.w);
+    }
+  } else {
+    constexpr int U = 8;
+    int i = tid;
+    for (; i + (U - 1) * kToppThreads < V; i += U * kToppThreads) {
+      float t[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) t[u] = __ldg(x + i + u * kToppThreads);
+#pragma unroll
+      for (int u = 0; u < U; ++u) f(i + u * kToppThreads, t[u]);
+    }
+    for (; i < V; i += kToppThreads) f(i, __ldg(x + i));
+  }
+}
+
 __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const ToppArgs a) {
   extern __shared__ __align__(16) uint8_t topp_smem[];
   uint32_t* list = reinterpret_cast<uint32_t*>(topp_smem);
-  double* whist = reinterpret_cast<double*>(topp_smem + static_cast<size_t>(kToppList) * 4);
+  float* whist = reinterpret_cast<float*>(topp_smem + static_cast<size_t>(kToppList) * 4);
   __shared__ ToppShared sh;
   griddep_wait();
   griddep_launch_dependents();
@@ -456,17 +504,17 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
   const int src = a.row_index != nullptr ? a.row_index[r] : r;
   const float* x = a.logits + static_cast<int64_t>(src) * a.ld;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const double T = a.temperature > 0.0 ? a.temperature : 1.0;
+  // x / T taken as x * (1 / T): the two differ in the last f64 bit at most, far below the f32 result
+  const double invT = a.temperature > 0.0 ? 1.0 / a.temperature : 1.0;
   const bool nucleus = a.top_p < 1.0;
   const int V = a.vocab, ex = a.exclude;
 
   // 1. max logit and its first index
   float m = -INFINITY;
   int mi = INT_MAX;
-  for (int i = tid; i < V; i += kToppThreads) {
-    const float v = x[i];
+  topp_row_foreach(x, V, [&](int i, float v) {
     if (i != ex && v > m) { m = v; mi = i; }
-  }
+  });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
@@ -474,24 +522,27 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
     argmax_merge(m, mi, m2, i2);
   }
   if (lane == 0) { sh.red_f[warp] = m; sh.red_i[warp] = mi; }
-  for (int i = tid; i < kToppWarps * kToppBins; i += kToppThreads) whist[i] = 0.0;
+  for (int i = tid; i < kToppWarps * kToppBins; i += kToppThreads) whist[i] = 0.0f;
   __syncthreads();
   float gm = sh.red_f[0];
   int gmi = sh.red_i[0];
   for (int w = 1; w < kToppWarps; ++w) argmax_merge(gm, gmi, sh.red_f[w], sh.red_i[w]);
-  const double am = static_cast<double>(gm) / T;
+  const double am = static_cast<double>(gm) * invT;
+  const float bin_scale = static_cast<float>(kToppBinScale * invT);
   __syncthreads();
 
   // 2. S and the distance histogram
   double part = 0.0;
-  double* my_hist = whist + warp * kToppBins;
-  for (int i = tid; i < V; i += kToppThreads) {
-    if (i == ex) continue;
-    const double ai = static_cast<double>(x[i]) / T;
-    const double e = exp(ai - am);
+  float* my_hist = whist + warp * kToppBins;
+  topp_row_foreach(x, V, [&](int i, float v) {
+    if (i == ex) return;
+    const double e = exp(static_cast<double>(v) * invT - am);
     part += e;
-    if (nucleus) atomicAdd(&my_hist[topp_bin(am, ai)], e);
-  }
+    if (nucleus) {
+      const int bin = topp_bin(gm, v, bin_scale);
+      if (bin < kToppBins - 1) atomicAdd(&my_hist[bin], static_cast<float>(e));  // the open last bin is never read
+    }
+  });
   const double S = topp_block_sum(part, sh.red_d, lane, warp);
   const double limit = a.top_p * S;
 
@@ -503,7 +554,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
       int b = 0;
       for (; b < kToppBins - 1; ++b) {
         double hb = 0.0;
-        for (int w = 0; w < kToppWarps; ++w) hb += whist[w * kToppBins + b];
+        for (int w = 0; w < kToppWarps; ++w) hb += static_cast<double>(whist[w * kToppBins + b]);
         cum += hb;
         if (cum > limit) break;
       }
@@ -515,17 +566,35 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
     int n = 0;
     bool overflow = false;
     if (last_bin < kToppBins - 1) {
-      for (int base = 0; base < V && !overflow; base += kToppThreads) {
-        const int i = base + tid;
-        bool take = false;
-        uint32_t key = 0;
-        if (i < V && i != ex) {
-          const float v = x[i];
-          take = topp_bin(am, static_cast<double>(v) / T) <= last_bin;
-          key = f32_order_key(v);
+      // thread t owns 8 consecutive entries of each 4096-entry chunk; a block scan of the per-thread
+      // counts writes the chunk's keys in index order
+      constexpr int G = 8;
+      for (int base = 0; base < V && !overflow; base += G * kToppThreads) {
+        const int i0 = base + G * tid;
+        float v[G];
+        if (i0 + G <= V && (reinterpret_cast<uintptr_t>(x + i0) & 15) == 0) {
+          const float4 t0 = __ldg(reinterpret_cast<const float4*>(x + i0));
+          const float4 t1 = __ldg(reinterpret_cast<const float4*>(x + i0) + 1);
+          v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w;
+          v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
+        } else {
+#pragma unroll
+          for (int g = 0; g < G; ++g) v[g] = i0 + g < V ? __ldg(x + i0 + g) : -INFINITY;
         }
-        const unsigned bal = __ballot_sync(0xffffffffu, take);
-        if (lane == 0) sh.warp_tot[warp] = __popc(bal);
+        unsigned takes = 0;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const int i = i0 + g;
+          if (i < V && i != ex && topp_bin(gm, v[g], bin_scale) <= last_bin) takes |= 1u << g;
+        }
+        const int cnt = __popc(takes);
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        if (lane == 31) sh.warp_tot[warp] = incl;
         __syncthreads();
         if (tid == 0) {
           int acc = 0;
@@ -540,8 +609,11 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
         const int tot = sh.warp_tot[kToppWarps];
         if (n + tot > kToppList) {
           overflow = true;
-        } else if (take) {
-          list[n + sh.warp_tot[warp] + __popc(bal & ((1u << lane) - 1u))] = key;
+        } else {
+          int pos = n + sh.warp_tot[warp] + incl - cnt;
+#pragma unroll
+          for (int g = 0; g < G; ++g)
+            if (takes & (1u << g)) list[pos++] = f32_order_key(v[g]);
         }
         n += tot;
         __syncthreads();
@@ -551,10 +623,16 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
     }
     use_list = !overflow;
     if (use_list) {
-      topp_radix(sh, n, [&](int i) { return list[i]; }, [](int) { return true; }, T, am, limit);
+      // the list must hold the crossing: its own mass has to exceed the limit
+      double lm = 0.0;
+      for (int i = tid; i < n; i += kToppThreads) lm += exp(static_cast<double>(f32_from_order_key(list[i])) * invT - am);
+      use_list = topp_block_sum(lm, sh.red_d, lane, warp) > limit;
+    }
+    if (use_list) {
+      topp_radix(sh, n, [&](int i) { return list[i]; }, [](int) { return true; }, invT, am, limit);
       if (tid == 0) sh.n_list = n;
     } else {
-      topp_radix(sh, V, [&](int i) { return f32_order_key(x[i]); }, [&](int i) { return i != ex; }, T, am, limit);
+      topp_radix(sh, V, [&](int i) { return f32_order_key(x[i]); }, [&](int i) { return i != ex; }, invT, am, limit);
     }
   }
   const uint32_t vb = nucleus ? sh.prefix : 0u;
@@ -564,7 +642,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
     if (nucleus) {
       const double above = sh.above;
       const int count = sh.count;
-      const double e = exp(static_cast<double>(f32_from_order_key(vb)) / T - am);
+      const double e = exp(static_cast<double>(f32_from_order_key(vb)) * invT - am);
       while (c < count && above + static_cast<double>(c + 1) * e <= limit) ++c;
       if (above == 0.0 && c == 0) c = 1;
       const double tol = a.tie_rel * limit;
@@ -577,7 +655,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
   }
   __syncthreads();
   const int c = sh.c;
-  const double e_vb = nucleus ? exp(static_cast<double>(f32_from_order_key(vb)) / T - am) : 0.0;
+  const double e_vb = nucleus ? exp(static_cast<double>(f32_from_order_key(vb)) * invT - am) : 0.0;
 
   // normaliser and entropy over the kept entries (the list, or the whole row)
   const int n_src = use_list ? sh.n_list : V;
@@ -594,7 +672,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
   double sk = 0.0;
   for (int i = tid; i < n_src; i += kToppThreads) {
     float v;
-    if (kept_value(i, &v)) sk += exp(static_cast<double>(v) / T - am);
+    if (kept_value(i, &v)) sk += exp(static_cast<double>(v) * invT - am);
   }
   double Sk = topp_block_sum(sk, sh.red_d, lane, warp);
   Sk += static_cast<double>(c) * e_vb;
@@ -602,7 +680,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
   for (int i = tid; i < n_src; i += kToppThreads) {
     float v;
     if (kept_value(i, &v)) {
-      const double pv = exp(static_cast<double>(v) / T - am) / Sk;
+      const double pv = exp(static_cast<double>(v) * invT - am) / Sk;
       h += pv * log(pv + 1e-10);
     }
   }

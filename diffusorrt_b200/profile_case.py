@@ -7,6 +7,12 @@ about 2 GB (weights 1.19 GB, K/V cache ~0.5 GB).
 
     python -m diffusorrt_b200.profile_case [--prompt 4096] [--gen 32] [--rounds 8]
     python -m diffusorrt_b200.profile_case --dream [--steps 4] [--layers 28]
+    python -m diffusorrt_b200.profile_case --quant --prompt 512 --gen 32
+
+With --quant: the 4-bit affine model under bd3_fixed_quota, 16 rounds per
+32-token block; every forward, prompt chunks included, runs the quantized decode linear
+(gemm_decode_kernel<EPI, S, true>) in 64-row chunks: a 512-token prompt launches 8 x 28 x 4 of them
+before the first denoising step.
 
 With --dream: the Dream-7B-architecture full-canvas workload (prompt 256 + canvas 256,
 entropy_count over --steps steps, each a 512-row forward); the model's synthetic weights take
@@ -39,6 +45,8 @@ def main() -> None:
     ap.add_argument("--dream", action="store_true", help="Dream-7B full-canvas entropy_count instead")
     ap.add_argument("--steps", type=int, default=4, help="entropy_count steps (--dream)")
     ap.add_argument("--layers", type=int, default=0, help="transformer layers (--dream; 0 = the model's 28)")
+    ap.add_argument("--quant", action="store_true",
+                    help="4-bit affine (group 64) linears and lm_head, bd3_fixed_quota with 16 rounds per block")
     args = ap.parse_args()
     from diffusorrt_b200 import Runtime
     from diffusorrt_b200.config import DREAM_7B, QWEN3_06B_BD3LM
@@ -64,13 +72,15 @@ def main() -> None:
 
     cfg = dict(QWEN3_06B_BD3LM)
     max_seq = ((args.prompt + args.gen + 127) // 128) * 128
+    engine = {"linear_quant_bits": 4, "linear_quant_group_size": 64} if args.quant else None
     rt = Runtime(model_config=cfg, synthetic_seed=0, device_ordinal=0, max_seq=max_seq,
-                 max_prefill_rows=min(4096, ((args.prompt + 127) // 128) * 128))
-    sess = rt.session({"decode_strategy": "block_threshold", "block_size": 32})
+                 max_prefill_rows=min(4096, ((args.prompt + 127) // 128) * 128), engine_config=engine)
+    strategy = "bd3_fixed_quota" if args.quant else "block_threshold"
+    sess = rt.session({"decode_strategy": strategy, "block_size": 32})
     prompt = [int(t) for t in np.random.default_rng(0).integers(0, 151643, size=args.prompt)]
-    steps = (args.gen // 32) * args.rounds
-    res = sess.generate(prompt, max_tokens=args.gen, steps=steps, block_size=32, decode_strategy="block_threshold",
-                        confidence_threshold=0.9, rounds_per_block=args.rounds)
+    steps = (args.gen // 32) * (16 if args.quant else args.rounds)
+    res = sess.generate(prompt, max_tokens=args.gen, steps=steps, block_size=32, decode_strategy=strategy,
+                        confidence_threshold=0.9, rounds_per_block=0 if args.quant else args.rounds)
     forwards = int(res["forward_count"])
     print(json.dumps({"prompt": args.prompt, "gen": args.gen, "forwards": forwards,
                       "kernel_launches": int(res["kernel_launches"]),

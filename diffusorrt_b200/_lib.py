@@ -139,6 +139,7 @@ SIGNATURES = {
                                            ctypes.c_double, _P, _P, _P, _P]),
     "drt_selector_topp": (ctypes.c_int, [_P, ctypes.c_int64, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
                                          ctypes.c_double, ctypes.c_int32, ctypes.c_double, _P, _P, _P, _P]),
+    "drt_exp_nonpos": (ctypes.c_int, [_P, _P, ctypes.c_int64, _P]),
     "drt_select_choices": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
                                           ctypes.c_double, _P, _P, _P]),
     "drt_quantize_q4": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int32, _P, _P, _P, _P]),

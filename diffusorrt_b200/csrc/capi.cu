@@ -2151,6 +2151,23 @@ extern "C" int drt_selector_topp(const float* logits, int64_t ld, const int32_t*
   return DRT_OK;
 }
 
+namespace {
+__global__ void exp_nonpos_kernel(const double* __restrict__ x, double* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    y[i] = exp_nonpos(x[i]);
+}
+}  // namespace
+
+extern "C" int drt_exp_nonpos(const double* x, double* y, int64_t n, void* stream) {
+  REQUIRE(x && y && n >= 0, "null argument");
+  if (n == 0) return DRT_OK;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 4096));
+  exp_nonpos_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
+  CK(cudaGetLastError());
+  return DRT_OK;
+}
+
 extern "C" size_t drt_linear_scratch_bytes(int32_t rows, int32_t n, int32_t K, int32_t splits) {
   (void)rows;
   (void)n;

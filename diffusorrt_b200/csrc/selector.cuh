@@ -15,6 +15,7 @@
 // flags ranking decisions closer than the certified bound (see policy.cuh).
 #pragma once
 #include "common.cuh"
+#include "fastexp.cuh"
 
 namespace drt {
 
@@ -54,7 +55,10 @@ __device__ __forceinline__ void argmax_merge(float& m, int& idx, float m2, int i
   }
 }
 
-__device__ __forceinline__ double sel_adjust(double x, double T) { return T > 0.0 ? x / T : x; }
+// x / T evaluated as x * (1 / T) (1 / T = 1 when T <= 0: no scaling); the product differs from the
+// quotient in the last f64 bit at most and is exact for T = 1.
+__device__ __forceinline__ double sel_inv_t(double T) { return T > 0.0 ? 1.0 / T : 1.0; }
+__device__ __forceinline__ double sel_adjust(double x, double inv_t) { return x * inv_t; }
 
 // Pass 1: chunk max / argmax / sum of exp relative to the chunk's adjusted max.
 __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a) {
@@ -111,11 +115,12 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
   int bi = s_i[0];
   for (int w = 1; w < kSelThreads / 32; ++w) argmax_merge(bm, bi, s_m[w], s_i[w]);
 
-  const double amax = sel_adjust(static_cast<double>(bm), a.temperature);
+  const double inv_t = sel_inv_t(a.temperature);
+  const double amax = sel_adjust(static_cast<double>(bm), inv_t);
   double sum = 0.0;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    if (vals[i] != -INFINITY) sum += exp(sel_adjust(static_cast<double>(vals[i]), a.temperature) - amax);
+    if (vals[i] != -INFINITY) sum += exp_nonpos(sel_adjust(static_cast<double>(vals[i]), inv_t) - amax);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -140,14 +145,14 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
   float gm = -INFINITY;
   int gi = INT_MAX;
   for (int k = 0; k < a.nchunks; ++k) argmax_merge(gm, gi, __ldcg(&a.part_max[r * a.nchunks + k]), __ldcg(&a.part_idx[r * a.nchunks + k]));
-  const double gam = sel_adjust(static_cast<double>(gm), a.temperature);
+  const double gam = sel_adjust(static_cast<double>(gm), inv_t);
   double S = 0.0;
   for (int k = 0; k < a.nchunks; ++k) {
     const float cm = __ldcg(&a.part_max[r * a.nchunks + k]);
     const double cs = __ldcg(&a.part_sum[r * a.nchunks + k]);
     if (cm == -INFINITY) continue;
-    const double cam = sel_adjust(static_cast<double>(cm), a.temperature);
-    S += (cam == gam) ? cs : cs * exp(cam - gam);
+    const double cam = sel_adjust(static_cast<double>(cm), inv_t);
+    S += (cam == gam) ? cs : cs * exp_nonpos(cam - gam);
   }
   a.token[r] = gi;
   if (a.mode == SEL_MAXPROB) {
@@ -176,12 +181,14 @@ __global__ void __launch_bounds__(kSelThreads) sel_entropy_kernel(const SelArgs 
   const double amax = a.row_amax[r];
   const double S = a.row_sum[r];
   const int excl = a.exclude_dev != nullptr ? *a.exclude_dev : a.exclude;
+  const double inv_t = sel_inv_t(a.temperature);
+  const double inv_s = 1.0 / S;  // p = e / S taken as e * (1 / S): last-bit differences only
   double acc = 0.0;
   for (int i = lo + tid; i < hi; i += kSelThreads) {
     const float v = i == excl ? -INFINITY : x[i];
     if (v == -INFINITY) continue;  // p = 0 contributes 0 * log(1e-10) = 0
-    const double e = exp(sel_adjust(static_cast<double>(v), a.temperature) - amax);
-    const double p = __ddiv_rn(e, S);
+    const double e = exp_nonpos(sel_adjust(static_cast<double>(v), inv_t) - amax);
+    const double p = __dmul_rn(e, inv_s);
     acc = __dadd_rn(acc, __dmul_rn(p, log(__dadd_rn(p, 1e-10))));
   }
 #pragma unroll
@@ -420,7 +427,7 @@ __device__ void topp_radix(ToppShared& sh, int n, KeyAt key_at, Valid valid, dou
       if (!valid(i)) continue;
       const uint32_t k = key_at(i);
       if ((k & pmask) != prefix) continue;
-      const double e = exp(static_cast<double>(f32_from_order_key(k)) * invT - am);
+      const double e = exp_nonpos(static_cast<double>(f32_from_order_key(k)) * invT - am);
       const int d = static_cast<int>((k >> shift) & 255u);
       atomicAdd(&sh.hist[d], e);
       if (level == 3) atomicAdd(&sh.hcnt[d], 1);
@@ -536,7 +543,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
   float* my_hist = whist + warp * kToppBins;
   topp_row_foreach(x, V, [&](int i, float v) {
     if (i == ex) return;
-    const double e = exp(static_cast<double>(v) * invT - am);
+    const double e = exp_nonpos(static_cast<double>(v) * invT - am);
     part += e;
     if (nucleus) {
       const int bin = topp_bin(gm, v, bin_scale);
@@ -625,7 +632,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
     if (use_list) {
       // the list must hold the crossing: its own mass has to exceed the limit
       double lm = 0.0;
-      for (int i = tid; i < n; i += kToppThreads) lm += exp(static_cast<double>(f32_from_order_key(list[i])) * invT - am);
+      for (int i = tid; i < n; i += kToppThreads) lm += exp_nonpos(static_cast<double>(f32_from_order_key(list[i])) * invT - am);
       use_list = topp_block_sum(lm, sh.red_d, lane, warp) > limit;
     }
     if (use_list) {
@@ -642,7 +649,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
     if (nucleus) {
       const double above = sh.above;
       const int count = sh.count;
-      const double e = exp(static_cast<double>(f32_from_order_key(vb)) * invT - am);
+      const double e = exp_nonpos(static_cast<double>(f32_from_order_key(vb)) * invT - am);
       while (c < count && above + static_cast<double>(c + 1) * e <= limit) ++c;
       if (above == 0.0 && c == 0) c = 1;
       const double tol = a.tie_rel * limit;
@@ -655,7 +662,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
   }
   __syncthreads();
   const int c = sh.c;
-  const double e_vb = nucleus ? exp(static_cast<double>(f32_from_order_key(vb)) * invT - am) : 0.0;
+  const double e_vb = nucleus ? exp_nonpos(static_cast<double>(f32_from_order_key(vb)) * invT - am) : 0.0;
 
   // normaliser and entropy over the kept entries (the list, or the whole row)
   const int n_src = use_list ? sh.n_list : V;
@@ -672,7 +679,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
   double sk = 0.0;
   for (int i = tid; i < n_src; i += kToppThreads) {
     float v;
-    if (kept_value(i, &v)) sk += exp(static_cast<double>(v) * invT - am);
+    if (kept_value(i, &v)) sk += exp_nonpos(static_cast<double>(v) * invT - am);
   }
   double Sk = topp_block_sum(sk, sh.red_d, lane, warp);
   Sk += static_cast<double>(c) * e_vb;
@@ -680,7 +687,7 @@ __global__ void __launch_bounds__(kToppThreads) sel_topp_entropy_kernel(const To
   for (int i = tid; i < n_src; i += kToppThreads) {
     float v;
     if (kept_value(i, &v)) {
-      const double pv = exp(static_cast<double>(v) * invT - am) / Sk;
+      const double pv = exp_nonpos(static_cast<double>(v) * invT - am) / Sk;
       h += pv * log(pv + 1e-10);
     }
   }

@@ -267,6 +267,9 @@ int drt_selector_gather(const float* logits, int64_t ld, const int32_t* row_inde
 int drt_selector_topp(const float* logits, int64_t ld, const int32_t* row_index, int32_t n_rows, int32_t vocab,
                       double temperature, double top_p, int32_t exclude_token, double tie_rel, double* conf,
                       int32_t* token, int32_t* tie, void* stream);
+/* The selector's exp for non-positive arguments (table-driven, Tang 1989), y[i] = exp(x[i]) for
+ * x[i] <= 0, on device arrays; exposed so its accuracy against CUDA's exp can be tested. */
+int drt_exp_nonpos(const double* x, double* y, int64_t n, void* stream);
 /* Commit choices for a batch of confidence runs: item b owns rows offsets[b] .. offsets[b + 1]
  * (device int32, n_items + 1 entries). mode 0 = top-k (_topk_count_choices,
  * diffusion_runtime.py:290-299: the k highest, lowest row first among equals), mode 1 =

@@ -10,7 +10,17 @@ seeded requests run one per GPU (request-parallel, weak scaling, no collective o
 One bench step = one complete request: prompt upload, prefill, every denoising step (forward,
 selector, policy, commit on the GPU), canvas download.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg0|cfg4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg0|cfg2|cfg3|cfg4]
+
+--workload cfg0 / cfg3: BASELINE configs[0] / [3] (cfg3: the cfg0 model with 4-bit affine, group 64
+linears and lm_head, prompt 512, 256 new tokens, 2 commits per round).
+
+--workload cfg2 is BASELINE configs[2]: Dream-7B architecture (28 layers, hidden 3584, 28/4 heads,
+intermediate 18944, vocab 152064, q/k/v bias, untied lm_head), 256-token prompt plus a 256-token
+all-MASK canvas, entropy_count over 256 steps (NegEntropy T 0.2, top_p 0.95, eps 1e-3, MASK
+excluded): every step forwards the whole 512-row canvas with bidirectional attention. With N > 1
+GPUs the one request runs tensor-parallel over the group (heads and MLP sharded, NCCL all-reduce
+after o_proj and down_proj), strong scaling; its roofline is tensor-core FLOP/s.
 
 --workload cfg4 is the isolated unmask-selector microbenchmark: fp32 logits
 [B, L, 151936] ~ N(0, 3^2) from a seed, a Bernoulli(0.5) mask of masked positions, max-prob and
@@ -508,6 +518,8 @@ def _run_selector(args, world, rank, local) -> dict | None:
     variants = {}
     launches = 0
     headline = None
+    clocks = ClockSampler(local)
+    clocks.__enter__()
     for B, L in SEL_SHAPES:
         logits, mask, rows, offsets = _selector_case(B, L, 1000 * B + L + rank, dev)
         n = rows.numel()
@@ -540,6 +552,7 @@ def _run_selector(args, world, rank, local) -> dict | None:
                                                    "GB_per_s": round(gbs, 1)}
             if (B, L, mode_name) == (8, 256, "max_prob"):
                 headline = (ms, alg, n, logits, rows, offsets, mask)
+    clocks.__exit__(None, None, None)
     ms, alg, n, logits, rows, offsets, mask = headline
     # End to end through the C ABI from pinned host memory: the [B, L, V] logits and the masked-row
     # list go up, the choices come back.
@@ -590,6 +603,7 @@ def _run_selector(args, world, rank, local) -> dict | None:
                 "h2d_bytes_per_step": int(logits.numel() * 4 + rows.numel() * 4 + offsets.numel() * 4),
                 "d2h_bytes_per_step": int(n * 4)},
         "gpu_launches": launches,
+        "clocks": clocks.summary(),
     }
 
 

@@ -56,6 +56,7 @@ class TpShard(ctypes.Structure):
 
 
 TP_ID_BYTES = 128
+TP_HANDLE_BYTES = 64
 
 
 class SessionConfig(ctypes.Structure):
@@ -127,6 +128,8 @@ SIGNATURES = {
     "drt_session_generate": (ctypes.c_int, [_P, ctypes.POINTER(GenerateParams), _I32P, ctypes.c_int32, _I32P,
                                             ctypes.POINTER(GenerateResult), ctypes.POINTER(StepTrace)]),
     "drt_session_metrics": (ctypes.c_int, [_P, ctypes.POINTER(Metrics)]),
+    "drt_session_tp_handle": (ctypes.c_int, [_P, ctypes.c_char_p]),
+    "drt_session_tp_connect": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_int32]),
     "drt_entropy_count_schedule": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_double, _I32P]),
     "drt_session_kv_pointers": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
     "drt_session_close": (None, [_P]),

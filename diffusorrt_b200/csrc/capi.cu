@@ -825,6 +825,13 @@ struct drt_session {
   float* logits = nullptr;
   float* ss = nullptr;                // [kMaxFwdRows][H / 128] partial sums of squares of h (decode)
   float* part = nullptr;              // [rows_cap][H] f32 linear partials (tensor-parallel models)
+  // tensor parallel over peer memory: receive buffers [2][world][rows_cap][H] f32 followed by flags
+  // [2][kTpMaxRanks] u64, in one allocation shared with the peers through CUDA IPC
+  uint8_t* tp_buf = nullptr;
+  uint8_t* tp_peer[kTpMaxRanks] = {};
+  bool tp_p2p = false;
+  int* tp_count = nullptr;            // [2] arrival counters of the pushing linears
+  unsigned long long* tp_epoch = nullptr;
   __nv_bfloat16 *kcache = nullptr, *vtcache = nullptr;
   int max_cluster = 16;               // largest cluster the GPU schedules for the split kernels
   float* sel_pmax = nullptr;
@@ -895,12 +902,18 @@ int salloc(drt_session* s, T** p, size_t count) {
   return DRT_OK;
 }
 
+size_t tp_buf_bytes(const drt_session* s) {
+  const size_t slot = static_cast<size_t>(s->rows_cap) * s->m->H;
+  return 2 * static_cast<size_t>(s->m->shard.world) * slot * sizeof(float) + 2 * kTpMaxRanks * sizeof(unsigned long long);
+}
+
 int check_status(drt_session* s) {
   int code = 0;
   CK(cudaMemcpy(&code, s->status, sizeof(int), cudaMemcpyDeviceToHost));
   if (code != 0) {
     cudaMemset(s->status, 0, sizeof(int));
     if (code == DEV_BAD_SHAPE) return set_error(DRT_INVALID_ARGUMENT, "device rejected an input (token id out of range)");
+    if (code == DEV_TIMEOUT_PEER) return set_error(DRT_DEVICE_TIMEOUT, "a tensor-parallel peer did not deliver its partials in time");
     return set_error(DRT_DEVICE_TIMEOUT, "device wait expired (code %d)", code);
   }
   return DRT_OK;
@@ -1035,6 +1048,44 @@ int run_rmsnorm(drt_session* s, const float* h, const int* row_index, int rows, 
   return DRT_OK;
 }
 
+// Peer-memory layout of one rank's tensor-parallel buffer.
+size_t tp_slot(const drt_session* s) { return static_cast<size_t>(s->rows_cap) * s->m->H; }
+size_t tp_recv_offset(const drt_session* s, int b, int src) {
+  return (static_cast<size_t>(b) * s->m->shard.world + src) * tp_slot(s) * sizeof(float);
+}
+size_t tp_flag_offset(const drt_session* s, int b, int src) {
+  return tp_recv_offset(s, 2, 0) + (static_cast<size_t>(b) * kTpMaxRanks + src) * sizeof(unsigned long long);
+}
+
+// Tensor parallel over peer memory: the linear (EPI_TP_PUSH) stores its f32 partial tile by tile
+// into this rank's slot of every rank's receive buffer b and raises this rank's flag there; the
+// reduction kernel then sums the slots once every flag is up. Buffers alternate between o_proj (0)
+// and down_proj (1): a rank writes buffer b again only after it has seen every peer's flag of the
+// other buffer, which each peer raises after it has finished reading b.
+int tp_push_linear(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB128, const CUtensorMap* mB256, GemmArgs a,
+                   int b, int tag, int rows) {
+  drt_model* m = s->m;
+  const int world = m->shard.world, me = m->shard.rank;
+  a.epi = EPI_TP_PUSH;
+  a.ld_out = m->H;
+  a.tp_world = world;
+  a.tp_tag = tag;
+  a.tp_count = s->tp_count + b;
+  a.tp_epoch = s->tp_epoch;
+  for (int r = 0; r < world; ++r) {
+    a.tp_dst[r] = reinterpret_cast<float*>(s->tp_peer[r] + tp_recv_offset(s, b, me));
+    a.tp_flag[r] = reinterpret_cast<unsigned long long*>(s->tp_peer[r] + tp_flag_offset(s, b, me));
+  }
+  TRY(run_wide(s, mA, mB128, mB256, a));
+  const int64_t n = static_cast<int64_t>(rows) * m->H;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((n / 4 + 255) / 256, static_cast<int64_t>(s->sms) * 4));
+  CK(launch_k(tp_reduce_resid_kernel, dim3(std::max(1u, blocks)), dim3(256), 0, s->stream, true, s->h,
+              reinterpret_cast<const float*>(s->tp_buf + tp_recv_offset(s, b, 0)), static_cast<int64_t>(tp_slot(s)),
+              reinterpret_cast<const unsigned long long*>(s->tp_buf + tp_flag_offset(s, b, 0)),
+              static_cast<const unsigned long long*>(s->tp_epoch), tag, world, n, s->status));
+  return DRT_OK;
+}
+
 // Tensor parallelism: sum the ranks' f32 linear partials (s->part, rows x H) over the group, then
 // h += bf16(sum), the linear's output rounding applied once to the reduced value.
 int tp_reduce_residual(drt_session* s, int rows) {
@@ -1054,6 +1105,7 @@ int tp_reduce_residual(drt_session* s, int rows) {
 int enqueue_layers(drt_session* s, const Fwd& f) {
   drt_model* m = s->m;
   const int H = m->H, qd = m->nq * 128;
+  if (s->tp_p2p) CK(launch_k(tp_tick_kernel, dim3(1), dim3(32), 0, s->stream, true, s->tp_epoch));
   CK(launch_k(embed_rows_kernel, dim3(f.rows), dim3(128), 0, s->stream, true, static_cast<const int*>(s->canvas), f.pos0,
               f.pos0_dev, f.rows, f.rows_dev, static_cast<const __nv_bfloat16*>(m->embed), H, s->h, m->V, s->status,
               static_cast<float*>(nullptr)));
@@ -1146,9 +1198,10 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     o.epi = tp ? EPI_STORE_RAW : EPI_RESID;
     o.out_f32 = tp ? s->part : s->h;
     o.ld_out = H;
-    if (f.decode) TRY(run_dec_gemm(s, w.m_o, s->m_attn64, o, m->quantized ? &w.q_o : nullptr));
+    if (s->tp_p2p) TRY(tp_push_linear(s, w.m_o, s->m_attn128, s->rows_cap >= 256 ? &s->m_attn256 : nullptr, o, 0, 2 * l, f.rows));
+    else if (f.decode) TRY(run_dec_gemm(s, w.m_o, s->m_attn64, o, m->quantized ? &w.q_o : nullptr));
     else TRY(run_wide(s, w.m_o, s->m_attn128, s->rows_cap >= 256 ? &s->m_attn256 : nullptr, o));
-    if (tp) TRY(tp_reduce_residual(s, f.rows));
+    if (tp && !s->tp_p2p) TRY(tp_reduce_residual(s, f.rows));
     TRY(run_rmsnorm(s, s->h, nullptr, f.rows, f.rows_dev, w.post_norm, s->xn));
     // gate/up + SwiGLU.
     GemmArgs g = base_args(s, m->gu_rows, H, f);
@@ -1162,9 +1215,10 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     d.epi = tp ? EPI_STORE_RAW : EPI_RESID;
     d.out_f32 = tp ? s->part : s->h;
     d.ld_out = H;
-    if (f.decode) TRY(run_dec_gemm(s, w.m_down, s->m_act64, d, m->quantized ? &w.q_down : nullptr));
+    if (s->tp_p2p) TRY(tp_push_linear(s, w.m_down, s->m_act128, s->rows_cap >= 256 ? &s->m_act256 : nullptr, d, 1, 2 * l + 1, f.rows));
+    else if (f.decode) TRY(run_dec_gemm(s, w.m_down, s->m_act64, d, m->quantized ? &w.q_down : nullptr));
     else TRY(run_wide(s, w.m_down, s->m_act128, s->rows_cap >= 256 ? &s->m_act256 : nullptr, d));
-    if (tp) TRY(tp_reduce_residual(s, f.rows));
+    if (tp && !s->tp_p2p) TRY(tp_reduce_residual(s, f.rows));
   }
   return DRT_OK;
 }
@@ -1553,7 +1607,16 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = salloc(s, &s->xf, static_cast<size_t>(s->head_cap) * H)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->logits, static_cast<size_t>(s->head_cap) * m->V)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->ss, static_cast<size_t>(kMaxFwdRows) * (H / 128))) != DRT_OK) return fail(rc);
-  if (m->shard.world > 1 && (rc = salloc(s, &s->part, static_cast<size_t>(R) * H)) != DRT_OK) return fail(rc);
+  if (m->shard.world > 1) {
+    if ((rc = salloc(s, &s->part, static_cast<size_t>(R) * H)) != DRT_OK) return fail(rc);
+    const size_t bytes = tp_buf_bytes(s);
+    if ((rc = salloc(s, &s->tp_buf, bytes)) != DRT_OK) return fail(rc);
+    if ((rc = salloc(s, &s->tp_count, 2)) != DRT_OK) return fail(rc);
+    if ((rc = salloc(s, &s->tp_epoch, 1)) != DRT_OK) return fail(rc);
+    if (cudaMemset(s->tp_buf, 0, bytes) != cudaSuccess || cudaMemset(s->tp_count, 0, 2 * sizeof(int)) != cudaSuccess ||
+        cudaMemset(s->tp_epoch, 0, sizeof(unsigned long long)) != cudaSuccess)
+      return fail(set_error(DRT_INTERNAL_ERROR, "memset failed"));
+  }
   const size_t kv = static_cast<size_t>(s->planes) * s->max_seq * 128;
   if ((rc = salloc(s, &s->kcache, kv)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->vtcache, kv)) != DRT_OK) return fail(rc);
@@ -1666,6 +1729,8 @@ extern "C" void drt_session_close(drt_session* s) {
   if (s->g_step) cudaGraphExecDestroy(s->g_step);
   if (s->g_fwd) cudaGraphExecDestroy(s->g_fwd);
   if (s->g_dream) cudaGraphExecDestroy(s->g_dream);
+  for (int r = 0; r < kTpMaxRanks; ++r)
+    if (s->tp_peer[r] != nullptr && s->tp_peer[r] != s->tp_buf) cudaIpcCloseMemHandle(s->tp_peer[r]);
   for (void* p : s->allocs) cudaFree(p);
   if (s->d_klist) cudaFree(s->d_klist);
   if (s->d_stepof) cudaFree(s->d_stepof);
@@ -2003,6 +2068,46 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
   s->m_exact += hs->exact_tie_steps;
   s->m_ms += pre_ms + dec_ms;
   s->started = false;
+  return DRT_OK;
+}
+
+extern "C" int drt_session_tp_handle(drt_session* s, void* handle) {
+  REQUIRE(s && handle, "null argument");
+  REQUIRE(s->tp_buf != nullptr, "the session's model is not tensor-parallel");
+  CK(cudaSetDevice(s->device));
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, s->tp_buf));
+  static_assert(sizeof(h) == DRT_TP_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return DRT_OK;
+}
+
+extern "C" int drt_session_tp_connect(drt_session* s, const void* handles, int32_t world) {
+  REQUIRE(s && handles, "null argument");
+  REQUIRE(s->tp_buf != nullptr, "the session's model is not tensor-parallel");
+  REQUIRE(world == s->m->shard.world, "group of %d ranks, model sharded over %d", world, s->m->shard.world);
+  REQUIRE(!s->tp_p2p, "session already connected");
+  CK(cudaSetDevice(s->device));
+  const int me = s->m->shard.rank;
+  for (int r = 0; r < world; ++r) {
+    if (r == me) {
+      s->tp_peer[r] = s->tp_buf;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const uint8_t*>(handles) + static_cast<size_t>(r) * DRT_TP_HANDLE_BYTES, sizeof(h));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < r; ++q)
+        if (q != me && s->tp_peer[q] != nullptr) cudaIpcCloseMemHandle(s->tp_peer[q]);
+      for (int q = 0; q < kTpMaxRanks; ++q) s->tp_peer[q] = nullptr;
+      return set_error(DRT_UNSUPPORTED, "peer %d buffer not mappable: %s", r, cudaGetErrorString(e));
+    }
+    s->tp_peer[r] = static_cast<uint8_t*>(p);
+  }
+  s->tp_p2p = true;
+  if (s->g_dream) { cudaGraphExecDestroy(s->g_dream); s->g_dream = nullptr; }
   return DRT_OK;
 }
 

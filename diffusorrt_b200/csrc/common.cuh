@@ -21,7 +21,18 @@ enum DeviceError : int {
   DEV_TIMEOUT_MMA = 2,
   DEV_TIMEOUT_EPI = 3,
   DEV_BAD_SHAPE = 4,
+  DEV_TIMEOUT_PEER = 5,  // a tensor-parallel peer's partials did not arrive in time
 };
+
+// System-scope release store / acquire load (flags written over NVLink by another GPU).
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

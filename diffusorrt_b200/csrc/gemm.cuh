@@ -30,7 +30,11 @@ enum GemmEpilogue : int {
   EPI_SWIGLU = 2,     // out_bf16[row, j] = bf16(silu(g) * u)       (gate/up interleaved per tile)
   EPI_QKV = 3,        // q/k RMSNorm + RoPE; q -> q buffer, k -> K cache, v -> V^T cache
   EPI_STORE_RAW = 4,  // out_f32[row, n] = acc (no rounding; tests)
+  EPI_TP_PUSH = 5,    // tensor parallel: acc (f32) into this rank's slot of every rank's receive
+                      // buffer (NVLink peer stores); the last CTA raises this rank's flag everywhere
 };
+
+constexpr int kTpMaxRanks = 8;
 
 struct GemmArgs {
   int n_out;             // rows of W; multiple of 128
@@ -68,6 +72,14 @@ struct GemmArgs {
   const __nv_bfloat16* q_scale;
   const __nv_bfloat16* q_bias;
   int q_groups;
+  // EPI_TP_PUSH: per rank r, this rank's slot of r's receive buffer ([rows][ld_out] f32) and this
+  // rank's flag in r's flag array; a local arrival counter; the forward's epoch and this linear's tag
+  // (the flag value is epoch * 64 + tag).
+  float* tp_dst[kTpMaxRanks];
+  unsigned long long* tp_flag[kTpMaxRanks];
+  int* tp_count;
+  const unsigned long long* tp_epoch;
+  int tp_world, tp_tag;
 };
 
 // KS: K blocks of 64 per ring stage. One mbarrier phase covers a whole stage; larger stages keep
@@ -120,6 +132,14 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = v[i];
+    }
+    if constexpr (EPI == EPI_TP_PUSH) {
+      for (int r = 0; r < a.tp_world; ++r) {
+        float* dst = a.tp_dst[r];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < ncols) dst[static_cast<size_t>(col0 + i) * a.ld_out + n] = v[i];
+      }
     }
     if constexpr (EPI == EPI_STORE_F32) {
 #pragma unroll
@@ -283,6 +303,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
     case EPI_RESID: gemm_epilogue_chunk_t<EPI_RESID>(a, v, col0, ncols, m0, tid, xs, pos0); break;
     case EPI_SWIGLU: gemm_epilogue_chunk_t<EPI_SWIGLU>(a, v, col0, ncols, m0, tid, xs, pos0); break;
     case EPI_QKV: gemm_epilogue_chunk_t<EPI_QKV>(a, v, col0, ncols, m0, tid, xs, pos0); break;
+    case EPI_TP_PUSH: gemm_epilogue_chunk_t<EPI_TP_PUSH>(a, v, col0, ncols, m0, tid, xs, pos0); break;
     default: break;
   }
 }
@@ -474,6 +495,23 @@ __global__ void __launch_bounds__(128, 1)
         float v[32];
         tmem_ld32(lane_addr + cb, v);
         gemm_epilogue_chunk(a, v, n0 + cb, min(32, ncol_valid - cb), m0, tid, xs, pos0);
+      }
+    }
+    if (a.epi == EPI_TP_PUSH) {
+      // Every CTA's peer stores are made visible system-wide before it arrives; the last CTA of the
+      // grid then raises this rank's flag in every rank's flag array (failed CTAs arrive too, so
+      // the peers' waits end; the status word carries the failure).
+      __threadfence_system();
+      __syncthreads();
+      if (tid == 0) {
+        const int total = static_cast<int>(gridDim.x * gridDim.y * gridDim.z);
+        if (atomicAdd(a.tp_count, 1) + 1 == total) {
+          __threadfence_system();
+          const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(a.tp_epoch) * 64ull +
+                                       static_cast<unsigned long long>(a.tp_tag);
+          for (int r = 0; r < a.tp_world; ++r) st_release_sys(a.tp_flag[r], e);
+          *a.tp_count = 0;
+        }
       }
     }
   } else {

@@ -151,6 +151,62 @@ __global__ void synth_fill_kernel(__nv_bfloat16* dst, int64_t rows, int64_t cols
   }
 }
 
+// Tensor parallel, peer-memory form: once every rank's flag for this linear (epoch * 64 + tag) is
+// up, h[i] += bf16(sum over ranks, in rank order, of recv[rank][i]). Every rank sums the same
+// partials in the same order, so the residuals stay bit-identical across the group. The wait is
+// bounded: on timeout the status word records DEV_TIMEOUT_PEER and the CTA returns.
+__global__ void tp_reduce_resid_kernel(float* __restrict__ h, const float* __restrict__ recv, int64_t slot,
+                                       const unsigned long long* flags, const unsigned long long* epoch, int tag,
+                                       int world, int64_t n, int* status) {
+  griddep_wait();
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(epoch) * 64ull +
+                                 static_cast<unsigned long long>(tag);
+    // once one wait has run out, later ones do not wait again (the request is failed already)
+    bool good = *reinterpret_cast<volatile int*>(status) != DEV_TIMEOUT_PEER;
+    const uint64_t t0 = globaltimer_ns();
+    for (int r = 0; r < world && good; ++r) {
+      while (ld_acquire_sys(flags + r) < e) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          good = false;
+          break;
+        }
+      }
+    }
+    if (!good) record_error(status, DEV_TIMEOUT_PEER);
+    ok = good ? 1 : 0;
+  }
+  __syncthreads();
+  griddep_launch_dependents();
+  if (!ok) return;
+  const int64_t n4 = n / 4;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    // L2 reads: the peers' stores land in this GPU's L2, not in this SM's L1
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(recv) + i);
+    for (int r = 1; r < world; ++r) {
+      const float4 t = __ldcg(reinterpret_cast<const float4*>(recv + r * slot) + i);
+      acc.x = __fadd_rn(acc.x, t.x);
+      acc.y = __fadd_rn(acc.y, t.y);
+      acc.z = __fadd_rn(acc.z, t.z);
+      acc.w = __fadd_rn(acc.w, t.w);
+    }
+    float4 x = reinterpret_cast<float4*>(h)[i];
+    x.x = __fadd_rn(x.x, __bfloat162float(__float2bfloat16_rn(acc.x)));
+    x.y = __fadd_rn(x.y, __bfloat162float(__float2bfloat16_rn(acc.y)));
+    x.z = __fadd_rn(x.z, __bfloat162float(__float2bfloat16_rn(acc.z)));
+    x.w = __fadd_rn(x.w, __bfloat162float(__float2bfloat16_rn(acc.w)));
+    reinterpret_cast<float4*>(h)[i] = x;
+  }
+}
+
+__global__ void tp_tick_kernel(unsigned long long* epoch) {
+  griddep_wait();
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) *epoch += 1ull;
+}
+
 // h[i] += bf16(part[i]) for i < n: the residual add after a tensor-parallel all-reduce of f32
 // linear partials (the linear's bf16 output rounding applied to the reduced sum).
 __global__ void resid_add_bf16r_kernel(float* __restrict__ h, const float* __restrict__ part, int64_t n) {

@@ -286,6 +286,15 @@ class Session:
         self._s = handle
         self.decode_strategy = strategy
         self.vocab = int(runtime.config["vocab_size"])
+        if runtime.tp_world > 1 and session_config.get("tp_peer_memory", True):
+            # map every rank's partial-sum buffer (collective: every rank opens its session in turn)
+            import torch.distributed as dist
+
+            buf = ctypes.create_string_buffer(_lib.TP_HANDLE_BYTES)
+            _call(self._lib.drt_session_tp_handle(self._s, buf))
+            handles = [None] * runtime.tp_world
+            dist.all_gather_object(handles, buf.raw)
+            _call(self._lib.drt_session_tp_connect(self._s, b"".join(handles), runtime.tp_world))
 
     # ------------------------------------------------------------------ reference surface
     def start_device(self, x: Sequence[int], *, prompt_len: int, block_size: int, mask_token_id: int,

@@ -72,6 +72,7 @@ typedef struct drt_tp_shard {
   int32_t inter0, inter;       /* intermediate columns [inter0, inter0 + inter) of gate/up/down */
 } drt_tp_shard;
 #define DRT_TP_ID_BYTES 128
+#define DRT_TP_HANDLE_BYTES 64
 
 typedef struct drt_model drt_model;
 typedef struct drt_session drt_session;
@@ -233,6 +234,15 @@ int drt_session_execute_window(drt_session* s, const int32_t* token_ids, int32_t
  * canvas (prompt + max_tokens). trace (optional, host) receives params->trace_steps entries. */
 int drt_session_generate(drt_session* s, const drt_generate_params* params, const int32_t* prompt,
                          int32_t prompt_len, int32_t* out, drt_generate_result* result, drt_step_trace* trace);
+/* Tensor-parallel sessions over peer memory: each rank's session owns a receive buffer for the
+ * o_proj / down_proj partials of every rank. drt_session_tp_handle gives its CUDA IPC handle
+ * (DRT_TP_HANDLE_BYTES); after the caller has gathered every rank's handle (rank order),
+ * drt_session_tp_connect maps the peers' buffers. From then on each such linear stores its f32
+ * partial straight into every rank's buffer over NVLink from its epilogue and a flag-gated kernel
+ * adds bf16(sum) to the residual (no NCCL call on the data path). Without it the session uses the
+ * NCCL all-reduce. Both calls are collective over the group. */
+int drt_session_tp_handle(drt_session* s, void* handle);
+int drt_session_tp_connect(drt_session* s, const void* handles, int32_t world);
 /* entropy_count transfer schedule (EntropyCountCommit.plan, diffusion_runtime.py:921-937):
  * timesteps = linspace(1, eps, steps + 1) in float32, transfer[s] = int(N * (1 - t[s+1] / t[s]))
  * (all N remaining on the last step) for s < steps, from n_masked masked positions, N falling by

@@ -830,7 +830,7 @@ struct drt_session {
   uint8_t* tp_buf = nullptr;
   uint8_t* tp_peer[kTpMaxRanks] = {};
   bool tp_p2p = false;
-  int* tp_count = nullptr;            // [2] arrival counters of the pushing linears
+  int* tp_count = nullptr;            // [4] arrival counters: pushing linears [2], reduce-scatter [2]
   unsigned long long* tp_epoch = nullptr;
   __nv_bfloat16 *kcache = nullptr, *vtcache = nullptr;
   int max_cluster = 16;               // largest cluster the GPU schedules for the split kernels
@@ -902,9 +902,12 @@ int salloc(drt_session* s, T** p, size_t count) {
   return DRT_OK;
 }
 
+// One rank's tensor-parallel buffer: receive [2][world][slot] f32 partials, all-gather [2][slot]
+// bf16 sums, reduce-scatter flags [2][kTpMaxRanks] and all-gather flags [2][kTpMaxRanks] (u64).
 size_t tp_buf_bytes(const drt_session* s) {
   const size_t slot = static_cast<size_t>(s->rows_cap) * s->m->H;
-  return 2 * static_cast<size_t>(s->m->shard.world) * slot * sizeof(float) + 2 * kTpMaxRanks * sizeof(unsigned long long);
+  return 2 * static_cast<size_t>(s->m->shard.world) * slot * sizeof(float) + 2 * slot * sizeof(__nv_bfloat16) +
+         4 * kTpMaxRanks * sizeof(unsigned long long);
 }
 
 int check_status(drt_session* s) {
@@ -1048,20 +1051,33 @@ int run_rmsnorm(drt_session* s, const float* h, const int* row_index, int rows, 
   return DRT_OK;
 }
 
-// Peer-memory layout of one rank's tensor-parallel buffer.
+// Peer-memory layout of one rank's tensor-parallel buffer (see tp_buf_bytes).
 size_t tp_slot(const drt_session* s) { return static_cast<size_t>(s->rows_cap) * s->m->H; }
 size_t tp_recv_offset(const drt_session* s, int b, int src) {
   return (static_cast<size_t>(b) * s->m->shard.world + src) * tp_slot(s) * sizeof(float);
 }
-size_t tp_flag_offset(const drt_session* s, int b, int src) {
-  return tp_recv_offset(s, 2, 0) + (static_cast<size_t>(b) * kTpMaxRanks + src) * sizeof(unsigned long long);
+size_t tp_ag_offset(const drt_session* s, int b) {
+  return tp_recv_offset(s, 2, 0) + static_cast<size_t>(b) * tp_slot(s) * sizeof(__nv_bfloat16);
+}
+size_t tp_flag_offset(const drt_session* s, int kind, int b, int src) {  // kind 0: reduce-scatter, 1: all-gather
+  return tp_ag_offset(s, 2) + ((static_cast<size_t>(kind) * 2 + b) * kTpMaxRanks + src) * sizeof(unsigned long long);
 }
 
-// Tensor parallel over peer memory: the linear (EPI_TP_PUSH) stores its f32 partial tile by tile
-// into this rank's slot of every rank's receive buffer b and raises this rank's flag there; the
-// reduction kernel then sums the slots once every flag is up. Buffers alternate between o_proj (0)
-// and down_proj (1): a rank writes buffer b again only after it has seen every peer's flag of the
-// other buffer, which each peer raises after it has finished reading b.
+// Tensor parallel over peer memory, for one row-split linear (o_proj: buffer 0, down_proj: 1):
+//   1. the linear (EPI_TP_PUSH) stores each f32 partial tile into this rank's slot of the receive
+//      buffer of the rank owning the tile's features and, when all its tiles are out, raises this
+//      rank's reduce-scatter flag on every rank;
+//   2. tp_rs_kernel: once every rank's partials are in, the owner sums them (rank order), adds
+//      bf16(sum) to its residual and stores bf16(sum) into the other ranks' all-gather buffers, then
+//      raises its all-gather flag on every rank;
+//   3. tp_ag_kernel: once every owner's sums are in, each rank adds the sums of the tiles it does
+//      not own.
+// Every rank adds the same bf16 values, so the residuals stay bit-identical. A rank writes a
+// buffer again only after it has seen every peer's flag of a later stage that follows the peer's
+// last read of it (stream order on the peer), so two alternating buffers suffice.
+// With two ranks the exchange is one step instead: each linear stores its whole partial into both
+// ranks' buffers and tp_reduce_all_kernel sums them (the same bytes cross NVLink, with one kernel
+// and one flag round trip fewer; measured 7.9 against 8.5 ms per Dream step).
 int tp_push_linear(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB128, const CUtensorMap* mB256, GemmArgs a,
                    int b, int tag, int rows) {
   drt_model* m = s->m;
@@ -1072,17 +1088,40 @@ int tp_push_linear(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB1
   a.tp_tag = tag;
   a.tp_count = s->tp_count + b;
   a.tp_epoch = s->tp_epoch;
+  a.tp_all = world == 2 ? 1 : 0;
   for (int r = 0; r < world; ++r) {
     a.tp_dst[r] = reinterpret_cast<float*>(s->tp_peer[r] + tp_recv_offset(s, b, me));
-    a.tp_flag[r] = reinterpret_cast<unsigned long long*>(s->tp_peer[r] + tp_flag_offset(s, b, me));
+    a.tp_flag[r] = reinterpret_cast<unsigned long long*>(s->tp_peer[r] + tp_flag_offset(s, 0, b, me));
   }
   TRY(run_wide(s, mA, mB128, mB256, a));
-  const int64_t n = static_cast<int64_t>(rows) * m->H;
-  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((n / 4 + 255) / 256, static_cast<int64_t>(s->sms) * 4));
-  CK(launch_k(tp_reduce_resid_kernel, dim3(std::max(1u, blocks)), dim3(256), 0, s->stream, true, s->h,
-              reinterpret_cast<const float*>(s->tp_buf + tp_recv_offset(s, b, 0)), static_cast<int64_t>(tp_slot(s)),
-              reinterpret_cast<const unsigned long long*>(s->tp_buf + tp_flag_offset(s, b, 0)),
-              static_cast<const unsigned long long*>(s->tp_epoch), tag, world, n, s->status));
+  TpStep t;
+  memset(&t, 0, sizeof(t));
+  t.h = s->h;
+  t.recv = reinterpret_cast<const float*>(s->tp_buf + tp_recv_offset(s, b, 0));
+  t.slot = static_cast<int64_t>(tp_slot(s));
+  for (int r = 0; r < world; ++r) {
+    t.ag_dst[r] = reinterpret_cast<__nv_bfloat16*>(s->tp_peer[r] + tp_ag_offset(s, b));
+    t.ag_flag_of_rank[r] = reinterpret_cast<unsigned long long*>(s->tp_peer[r] + tp_flag_offset(s, 1, b, me));
+  }
+  t.ag = reinterpret_cast<const __nv_bfloat16*>(s->tp_buf + tp_ag_offset(s, b));
+  t.rs_flags = reinterpret_cast<const unsigned long long*>(s->tp_buf + tp_flag_offset(s, 0, b, 0));
+  t.ag_flags = reinterpret_cast<const unsigned long long*>(s->tp_buf + tp_flag_offset(s, 1, b, 0));
+  t.count = s->tp_count + 2 + b;
+  t.epoch = s->tp_epoch;
+  t.tag = tag;
+  t.world = world;
+  t.rank = me;
+  t.rows = rows;
+  t.H = m->H;
+  t.status = s->status;
+  const int64_t groups = static_cast<int64_t>(rows) * m->H / 4;
+  const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((groups + 255) / 256, s->sms * 4)));
+  if (a.tp_all) {
+    CK(launch_k(tp_reduce_all_kernel, dim3(blocks), dim3(256), 0, s->stream, true, t));
+  } else {
+    CK(launch_k(tp_rs_kernel, dim3(blocks), dim3(256), 0, s->stream, true, t));
+    CK(launch_k(tp_ag_kernel, dim3(blocks), dim3(256), 0, s->stream, true, t));
+  }
   return DRT_OK;
 }
 
@@ -1611,9 +1650,9 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
     if ((rc = salloc(s, &s->part, static_cast<size_t>(R) * H)) != DRT_OK) return fail(rc);
     const size_t bytes = tp_buf_bytes(s);
     if ((rc = salloc(s, &s->tp_buf, bytes)) != DRT_OK) return fail(rc);
-    if ((rc = salloc(s, &s->tp_count, 2)) != DRT_OK) return fail(rc);
+    if ((rc = salloc(s, &s->tp_count, 4)) != DRT_OK) return fail(rc);
     if ((rc = salloc(s, &s->tp_epoch, 1)) != DRT_OK) return fail(rc);
-    if (cudaMemset(s->tp_buf, 0, bytes) != cudaSuccess || cudaMemset(s->tp_count, 0, 2 * sizeof(int)) != cudaSuccess ||
+    if (cudaMemset(s->tp_buf, 0, bytes) != cudaSuccess || cudaMemset(s->tp_count, 0, 4 * sizeof(int)) != cudaSuccess ||
         cudaMemset(s->tp_epoch, 0, sizeof(unsigned long long)) != cudaSuccess)
       return fail(set_error(DRT_INTERNAL_ERROR, "memset failed"));
   }

@@ -30,8 +30,9 @@ enum GemmEpilogue : int {
   EPI_SWIGLU = 2,     // out_bf16[row, j] = bf16(silu(g) * u)       (gate/up interleaved per tile)
   EPI_QKV = 3,        // q/k RMSNorm + RoPE; q -> q buffer, k -> K cache, v -> V^T cache
   EPI_STORE_RAW = 4,  // out_f32[row, n] = acc (no rounding; tests)
-  EPI_TP_PUSH = 5,    // tensor parallel: acc (f32) into this rank's slot of every rank's receive
-                      // buffer (NVLink peer stores); the last CTA raises this rank's flag everywhere
+  EPI_TP_PUSH = 5,    // tensor parallel: acc (f32) into this rank's slot of the receive buffer of
+                      // the rank owning the tile's features (NVLink peer store when that is another
+                      // GPU); the last CTA raises this rank's flag on every rank
 };
 
 constexpr int kTpMaxRanks = 8;
@@ -74,12 +75,13 @@ struct GemmArgs {
   int q_groups;
   // EPI_TP_PUSH: per rank r, this rank's slot of r's receive buffer ([rows][ld_out] f32) and this
   // rank's flag in r's flag array; a local arrival counter; the forward's epoch and this linear's tag
-  // (the flag value is epoch * 64 + tag).
+  // (the flag value is epoch * 64 + tag). Feature tile t (128 features) is owned by rank t % world.
   float* tp_dst[kTpMaxRanks];
   unsigned long long* tp_flag[kTpMaxRanks];
   int* tp_count;
   const unsigned long long* tp_epoch;
   int tp_world, tp_tag;
+  int tp_all;  // store to every rank instead of the owner only
 };
 
 // KS: K blocks of 64 per ring stage. One mbarrier phase covers a whole stage; larger stages keep
@@ -134,7 +136,9 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
         if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = v[i];
     }
     if constexpr (EPI == EPI_TP_PUSH) {
-      for (int r = 0; r < a.tp_world; ++r) {
+      // to the owning rank (reduce-scatter), or to every rank when tp_all (each rank reduces all)
+      const int owner = (m0 >> 7) % a.tp_world;
+      for (int r = a.tp_all ? 0 : owner; r < (a.tp_all ? a.tp_world : owner + 1); ++r) {
         float* dst = a.tp_dst[r];
 #pragma unroll
         for (int i = 0; i < 32; ++i)

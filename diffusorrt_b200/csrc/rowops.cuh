@@ -151,19 +151,17 @@ __global__ void synth_fill_kernel(__nv_bfloat16* dst, int64_t rows, int64_t cols
   }
 }
 
-// Tensor parallel, peer-memory form: once every rank's flag for this linear (epoch * 64 + tag) is
-// up, h[i] += bf16(sum over ranks, in rank order, of recv[rank][i]). Every rank sums the same
-// partials in the same order, so the residuals stay bit-identical across the group. The wait is
-// bounded: on timeout the status word records DEV_TIMEOUT_PEER and the CTA returns.
-__global__ void tp_reduce_resid_kernel(float* __restrict__ h, const float* __restrict__ recv, int64_t slot,
-                                       const unsigned long long* flags, const unsigned long long* epoch, int tag,
-                                       int world, int64_t n, int* status) {
-  griddep_wait();
+// Tensor parallel, peer-memory form (reduce-scatter then all-gather, both through NVLink stores).
+// Feature tile t (128 features of H) belongs to rank t % world.
+//
+// Bounded wait (thread 0 of each CTA) until flags[r] >= epoch * 64 + tag for every rank r. Once one
+// wait has run out, later ones do not wait again: the request is failed already (status word).
+__device__ __forceinline__ bool tp_wait_flags(const unsigned long long* flags, const unsigned long long* epoch, int tag,
+                                              int world, int* status) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(epoch) * 64ull +
                                  static_cast<unsigned long long>(tag);
-    // once one wait has run out, later ones do not wait again (the request is failed already)
     bool good = *reinterpret_cast<volatile int*>(status) != DEV_TIMEOUT_PEER;
     const uint64_t t0 = globaltimer_ns();
     for (int r = 0; r < world && good; ++r) {
@@ -178,26 +176,137 @@ __global__ void tp_reduce_resid_kernel(float* __restrict__ h, const float* __res
     ok = good ? 1 : 0;
   }
   __syncthreads();
+  return ok != 0;
+}
+
+// Raise this rank's flag (epoch * 64 + tag) on every rank once all CTAs of the grid have made their
+// peer stores visible (the last CTA to arrive raises it and resets the counter).
+__device__ __forceinline__ void tp_raise_flags(unsigned long long* const* flag_of_rank, int world, int* count,
+                                               const unsigned long long* epoch, int tag) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int total = static_cast<int>(gridDim.x * gridDim.y * gridDim.z);
+    if (atomicAdd(count, 1) + 1 == total) {
+      __threadfence_system();
+      const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(epoch) * 64ull +
+                                   static_cast<unsigned long long>(tag);
+      for (int r = 0; r < world; ++r) st_release_sys(flag_of_rank[r], e);
+      *count = 0;
+    }
+  }
+}
+
+struct TpStep {
+  float* h;                             // [rows][H] residual (f32)
+  const float* recv;                    // this rank's receive buffer: [world][slot] f32 partials
+  int64_t slot;                         // rows_cap * H
+  __nv_bfloat16* ag_dst[8];             // per rank: that rank's all-gather buffer ([rows][H] bf16)
+  const __nv_bfloat16* ag;              // this rank's all-gather buffer
+  const unsigned long long* rs_flags;   // this rank's reduce-scatter flags [world]
+  const unsigned long long* ag_flags;   // this rank's all-gather flags [world]
+  unsigned long long* ag_flag_of_rank[8];  // this rank's all-gather flag on each rank
+  int* count;
+  const unsigned long long* epoch;
+  int tag, world, rank, rows, H;
+  int* status;
+};
+
+// Reduce-scatter half: for the feature tiles this rank owns, sum the ranks' partials in rank order,
+// round to bf16 once (the linear's output rounding), add to the residual and store the rounded sum
+// into every other rank's all-gather buffer; then raise this rank's all-gather flag everywhere.
+__global__ void tp_rs_kernel(const TpStep a) {
+  griddep_wait();
+  const bool ok = tp_wait_flags(a.rs_flags, a.epoch, a.tag, a.world, a.status);
+  griddep_launch_dependents();
+  if (ok) {
+    const int tiles = a.H / 128;
+    const int own = (tiles - a.rank + a.world - 1) / a.world;   // tiles t = rank + k * world
+    const int64_t per_row = static_cast<int64_t>(own) * 32;      // float4 groups per row
+    const int64_t total = per_row * a.rows;
+    for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < total;
+         g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const int64_t row = g / per_row;
+      const int64_t rem = g - row * per_row;
+      const int t = a.rank + static_cast<int>(rem / 32) * a.world;
+      const int64_t off = row * a.H + t * 128 + (rem % 32) * 4;
+      // L2 reads: the peers' stores land in this GPU's L2, not in this SM's L1
+      float4 acc = __ldcg(reinterpret_cast<const float4*>(a.recv + off));
+      for (int r = 1; r < a.world; ++r) {
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(a.recv + r * a.slot + off));
+        acc.x = __fadd_rn(acc.x, x.x);
+        acc.y = __fadd_rn(acc.y, x.y);
+        acc.z = __fadd_rn(acc.z, x.z);
+        acc.w = __fadd_rn(acc.w, x.w);
+      }
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+      const __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+      float4 hv = *reinterpret_cast<float4*>(a.h + off);
+      hv.x = __fadd_rn(hv.x, __low2float(lo));
+      hv.y = __fadd_rn(hv.y, __high2float(lo));
+      hv.z = __fadd_rn(hv.z, __low2float(hi));
+      hv.w = __fadd_rn(hv.w, __high2float(hi));
+      *reinterpret_cast<float4*>(a.h + off) = hv;
+      uint2 packed;
+      packed.x = *reinterpret_cast<const uint32_t*>(&lo);
+      packed.y = *reinterpret_cast<const uint32_t*>(&hi);
+      for (int r = 0; r < a.world; ++r)
+        if (r != a.rank) *reinterpret_cast<uint2*>(a.ag_dst[r] + off) = packed;
+    }
+  }
+  tp_raise_flags(a.ag_flag_of_rank, a.world, a.count, a.epoch, a.tag);
+}
+
+// Two-rank form: every rank has received every rank's whole partial; once all flags are up it sums
+// them in rank order and adds bf16(sum) to its residual (one kernel, no second exchange).
+__global__ void tp_reduce_all_kernel(const TpStep a) {
+  griddep_wait();
+  const bool ok = tp_wait_flags(a.rs_flags, a.epoch, a.tag, a.world, a.status);
   griddep_launch_dependents();
   if (!ok) return;
-  const int64_t n4 = n / 4;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    // L2 reads: the peers' stores land in this GPU's L2, not in this SM's L1
-    float4 acc = __ldcg(reinterpret_cast<const float4*>(recv) + i);
-    for (int r = 1; r < world; ++r) {
-      const float4 t = __ldcg(reinterpret_cast<const float4*>(recv + r * slot) + i);
-      acc.x = __fadd_rn(acc.x, t.x);
-      acc.y = __fadd_rn(acc.y, t.y);
-      acc.z = __fadd_rn(acc.z, t.z);
-      acc.w = __fadd_rn(acc.w, t.w);
+  const int64_t total = static_cast<int64_t>(a.rows) * a.H / 4;
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < total;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(a.recv) + g);
+    for (int r = 1; r < a.world; ++r) {
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(a.recv + r * a.slot) + g);
+      acc.x = __fadd_rn(acc.x, x.x);
+      acc.y = __fadd_rn(acc.y, x.y);
+      acc.z = __fadd_rn(acc.z, x.z);
+      acc.w = __fadd_rn(acc.w, x.w);
     }
-    float4 x = reinterpret_cast<float4*>(h)[i];
-    x.x = __fadd_rn(x.x, __bfloat162float(__float2bfloat16_rn(acc.x)));
-    x.y = __fadd_rn(x.y, __bfloat162float(__float2bfloat16_rn(acc.y)));
-    x.z = __fadd_rn(x.z, __bfloat162float(__float2bfloat16_rn(acc.z)));
-    x.w = __fadd_rn(x.w, __bfloat162float(__float2bfloat16_rn(acc.w)));
-    reinterpret_cast<float4*>(h)[i] = x;
+    float4 hv = reinterpret_cast<float4*>(a.h)[g];
+    hv.x = __fadd_rn(hv.x, __bfloat162float(__float2bfloat16_rn(acc.x)));
+    hv.y = __fadd_rn(hv.y, __bfloat162float(__float2bfloat16_rn(acc.y)));
+    hv.z = __fadd_rn(hv.z, __bfloat162float(__float2bfloat16_rn(acc.z)));
+    hv.w = __fadd_rn(hv.w, __bfloat162float(__float2bfloat16_rn(acc.w)));
+    reinterpret_cast<float4*>(a.h)[g] = hv;
+  }
+}
+
+// All-gather half: add the other ranks' rounded sums for the feature tiles they own.
+__global__ void tp_ag_kernel(const TpStep a) {
+  griddep_wait();
+  const bool ok = tp_wait_flags(a.ag_flags, a.epoch, a.tag, a.world, a.status);
+  griddep_launch_dependents();
+  if (!ok) return;
+  const int64_t per_row = static_cast<int64_t>(a.H) / 4;
+  const int64_t total = per_row * a.rows;
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < total;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = g / per_row;
+    const int f = static_cast<int>(g - row * per_row) * 4;
+    if ((f >> 7) % a.world == a.rank) continue;
+    const int64_t off = row * a.H + f;
+    const uint2 packed = __ldcg(reinterpret_cast<const uint2*>(a.ag + off));
+    const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&packed.x);
+    const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&packed.y);
+    float4 hv = *reinterpret_cast<float4*>(a.h + off);
+    hv.x = __fadd_rn(hv.x, __low2float(lo));
+    hv.y = __fadd_rn(hv.y, __high2float(lo));
+    hv.z = __fadd_rn(hv.z, __low2float(hi));
+    hv.w = __fadd_rn(hv.w, __high2float(hi));
+    *reinterpret_cast<float4*>(a.h + off) = hv;
   }
 }
 

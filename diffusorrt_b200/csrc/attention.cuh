@@ -360,3 +360,243 @@ __global__ void __launch_bounds__(128, 1)
 }
 
 }  // namespace drt
+
+namespace drt {
+
+// Attention over many query tiles (prompt prefill, full-canvas forward): the tiles and math of
+// attn_prefix_kernel without split-KV, on 256 threads. The two threads of a query row (t and
+// t + 128: same TMEM lanes, warps w and w + 4) split the row's 128 key columns for the softmax
+// (row max and row sum exchanged through shared memory) and its 128 head dims for the output
+// accumulator; and the S = Q K^T MMA of key tile j + 1 is issued into the second S buffer before
+// the softmax of tile j, so the tensor cores work while the threads do.
+constexpr int kAttnWThreads = 256;
+
+__global__ void __launch_bounds__(kAttnWThreads, 1)
+    attn_wide_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + kAttnQBytes;
+  uint8_t* sP = sKV + kAttnStages * kAttnStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kAttnPBytes);
+  uint64_t* barQ = bars;
+  uint64_t* fullKV = bars + 1;  // [kAttnStages]
+  uint64_t* barS = bars + 1 + kAttnStages;  // [2]
+  uint64_t* barO = barS + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(barO + 1);
+  int* sflag = reinterpret_cast<int*>(tmem_slot + 1);
+  __shared__ float red_m[kAttnWThreads];
+  __shared__ float red_s[kAttnWThreads];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int half = warp >> 2;              // 0: key columns / dims 0..63, 1: 64..127
+  const int r = (warp & 3) * 32 + lane;     // UMMA row = TMEM lane of this thread
+  const int qt = blockIdx.x;
+  const int g = blockIdx.y;
+
+  if (tid == 0) {
+    mbar_init(barQ, 1);
+    for (int s = 0; s < kAttnStages; ++s) mbar_init(&fullKV[s], 1);
+    mbar_init(&barS[0], 1);
+    mbar_init(&barS[1], 1);
+    mbar_init(barO, 1);
+    sflag[0] = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  __syncwarp();
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_o = tmem + 256;       // S buffers at columns 0 and 128
+
+  griddep_wait();
+  griddep_launch_dependents();
+
+  int rows_valid = a.rows;
+  if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
+  const int q_pos0 = a.q_pos0_dev != nullptr ? *a.q_pos0_dev : a.q_pos0;
+  const int kv_len = a.kv_len_dev != nullptr ? *a.kv_len_dev : a.kv_len;
+  const int row0 = qt * a.tile_pos;
+  const int last_row = min(row0 + a.tile_pos, rows_valid) - 1;
+  const int kv_hi = last_row >= row0 ? attn_limit(a, q_pos0 + last_row, kv_len) : 0;
+  const int ntiles = (kv_hi + 127) / 128;
+
+  const int r_local = r / a.rep;
+  const int h_local = r - r_local * a.rep;
+  const int q_row = row0 + r_local;
+  const bool row_ok = (r_local < a.tile_pos) && (q_row < rows_valid);
+  const int head = g * a.rep + h_local;
+  const int lim = row_ok ? attn_limit(a, q_pos0 + q_row, kv_len) : 0;
+  const int plane = a.kv_plane0 + g;
+  const uint32_t idesc = idesc_bf16_f32(128, 128);
+  const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+
+  auto issue_s = [&](int j) {  // tid 0: S_j = Q K_j^T into S buffer j & 1
+    const uint8_t* st = sKV + (j % kAttnStages) * kAttnStageBytes;
+    bool ok = (j > 0 || mbar_wait(barQ, 0)) && mbar_wait(&fullKV[j % kAttnStages], (j / kAttnStages) & 1);
+    if (!ok) {
+      record_error(a.status, DEV_TIMEOUT_TMA);
+      sflag[0] = 1;
+    } else {
+      tc_fence_after();
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t k_addr = smem_u32(st);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+        umma_bf16(tmem + (j & 1) * 128, sdesc_kmajor_sw128(q_addr + off), sdesc_kmajor_sw128(k_addr + off), idesc,
+                  kk != 0 ? 1u : 0u);
+      }
+    }
+    umma_commit(&barS[j & 1]);
+  };
+
+  if (tid == 0 && ntiles > 0) {
+    const uint32_t qbytes = static_cast<uint32_t>(64 * a.rep * a.tile_pos * 2);
+    mbar_expect_tx(barQ, 2 * qbytes);
+    tma_load_3d(sQ, &tmQ, barQ, 0, g * a.rep, row0);
+    tma_load_3d(sQ + 128 * 128, &tmQ, barQ, 64, g * a.rep, row0);
+    for (int j = 0; j < min(kAttnStages, ntiles); ++j) {
+      uint8_t* st = sKV + j * kAttnStageBytes;
+      const int key0 = j * 128;
+      mbar_expect_tx(&fullKV[j], kAttnStageBytes);
+      tma_load_3d(st, &tmK, &fullKV[j], 0, key0, plane);
+      tma_load_3d(st + 128 * 128, &tmK, &fullKV[j], 64, key0, plane);
+      tma_load_3d(st + kAttnKBytes, &tmV, &fullKV[j], key0, 0, plane);
+      tma_load_3d(st + kAttnKBytes + 128 * 128, &tmV, &fullKV[j], key0 + 64, 0, plane);
+    }
+    issue_s(0);
+  }
+
+  float o_acc[64];
+#pragma unroll
+  for (int d = 0; d < 64; ++d) o_acc[d] = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;
+  bool failed = false;
+  int pend_j = ntiles > 0 ? 0 : -1;  // key tile whose S MMA is issued and not yet waited (tid 0)
+
+  for (int j = 0; j < ntiles; ++j) {
+    const int s = j % kAttnStages;
+    uint8_t* st = sKV + s * kAttnStageBytes;
+    const int key0 = j * 128;
+    if (!mbar_wait(&barS[j & 1], (j >> 1) & 1)) { record_error(a.status, DEV_TIMEOUT_MMA); sflag[0] = 1; }
+    pend_j = -1;
+    tc_fence_after();
+    __syncthreads();
+    if (sflag[0]) { failed = true; break; }
+    // next tile's S on the tensor cores while this tile's softmax runs
+    if (tid == 0 && j + 1 < ntiles) {
+      issue_s(j + 1);
+      pend_j = j + 1;
+    }
+
+    const uint32_t tmem_s = tmem + (j & 1) * 128 + lane_off + half * 64;
+    float tile_max = -INFINITY;
+#pragma unroll
+    for (int cb = 0; cb < 64; cb += 32) {
+      float sv[32];
+      tmem_ld32(tmem_s + cb, sv);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int kp = key0 + half * 64 + cb + i;
+        const float x = (kp < lim) ? sv[i] * a.scale_log2 : -INFINITY;
+        tile_max = fmaxf(tile_max, x);
+      }
+    }
+    red_m[tid] = tile_max;
+    __syncthreads();
+    tile_max = fmaxf(red_m[r], red_m[r + 128]);
+    const float m_new = fmaxf(m_run, tile_max);
+    const float alpha = (m_new == -INFINITY) ? 1.0f : exp2f(m_run - m_new);
+    float psum = 0.0f;
+#pragma unroll
+    for (int cb = 0; cb < 64; cb += 32) {
+      float sv[32];
+      tmem_ld32(tmem_s + cb, sv);
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const int col = half * 64 + cb + i;
+        const int kp = key0 + col;
+        const float p0 = (kp < lim && m_new != -INFINITY) ? exp2f(sv[i] * a.scale_log2 - m_new) : 0.0f;
+        const float p1 = (kp + 1 < lim && m_new != -INFINITY) ? exp2f(sv[i + 1] * a.scale_log2 - m_new) : 0.0f;
+        const __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+        psum += __low2float(pb) + __high2float(pb);
+        *reinterpret_cast<__nv_bfloat162*>(sP + sw128_offset(r, col, 128)) = pb;
+      }
+    }
+    red_s[tid] = psum;
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    l_run = l_run * alpha + (red_s[r] + red_s[r + 128]);
+    m_run = m_new;
+
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t p_addr = smem_u32(sP);
+      const uint32_t v_addr = smem_u32(st + kAttnKBytes);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+        umma_bf16(tmem_o, sdesc_kmajor_sw128(p_addr + off), sdesc_kmajor_sw128(v_addr + off), idesc,
+                  kk != 0 ? 1u : 0u);
+      }
+      umma_commit(barO);
+    }
+    if (!mbar_wait(barO, j & 1)) { record_error(a.status, DEV_TIMEOUT_MMA); sflag[0] = 1; }
+    tc_fence_after();
+#pragma unroll
+    for (int cb = 0; cb < 64; cb += 32) {
+      float ov[32];
+      tmem_ld32(tmem_o + lane_off + half * 64 + cb, ov);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o_acc[cb + i] = o_acc[cb + i] * alpha + ov[i];
+    }
+    // Stage s is free (S_j and PV_j done): refill it with tile j + kAttnStages.
+    if (tid == 0 && j + kAttnStages < ntiles && !sflag[0]) {
+      const int key1 = (j + kAttnStages) * 128;
+      mbar_expect_tx(&fullKV[s], kAttnStageBytes);
+      tma_load_3d(st, &tmK, &fullKV[s], 0, key1, plane);
+      tma_load_3d(st + 128 * 128, &tmK, &fullKV[s], 64, key1, plane);
+      tma_load_3d(st + kAttnKBytes, &tmV, &fullKV[s], key1, 0, plane);
+      tma_load_3d(st + kAttnKBytes + 128 * 128, &tmV, &fullKV[s], key1 + 64, 0, plane);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (sflag[0]) { failed = true; break; }
+  }
+
+  if (!failed && row_ok) {
+    const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+    __nv_bfloat16* dst = a.out + static_cast<size_t>(q_row) * a.nq * 128 + static_cast<size_t>(head) * 128 + half * 64;
+#pragma unroll
+    for (int d = 0; d < 64; d += 8) {
+      __align__(16) __nv_bfloat16 t[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) t[e] = __float2bfloat16_rn(o_acc[d + e] * inv);
+      *reinterpret_cast<uint4*>(dst + d) = *reinterpret_cast<const uint4*>(t);
+    }
+  }
+  if (failed && tid == 0) {
+    // an S MMA may still be in flight, and loads may still be landing (bounded waits)
+    if (pend_j >= 0) mbar_wait(&barS[pend_j & 1], (pend_j >> 1) & 1);
+    mbar_wait(barQ, 0);
+    for (int s = 0; s < min(kAttnStages, ntiles); ++s) mbar_wait(&fullKV[s], 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace drt

@@ -210,6 +210,7 @@ int configure_kernels() {
         cudaFuncSetAttribute(gemm_swapab_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(sel_topp_entropy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kToppSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
@@ -1224,12 +1225,14 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     if (f.decode && qtiles == 1) {
       t.splits = s->attn_splits;
       t.tiles_per_split = s->attn_tps;
+      CK(launch_kc(attn_prefix_kernel, dim3(qtiles, m->nkv, t.splits), dim3(128), kAttnSmemBytes, s->stream, true,
+                   t.splits, s->m_q, s->m_k, s->m_v, t));
     } else {
       t.splits = 1;
       t.tiles_per_split = (s->max_seq + 127) / 128;
+      CK(launch_k(attn_wide_kernel, dim3(qtiles, m->nkv, 1), dim3(kAttnWThreads), kAttnSmemBytes, s->stream, true,
+                  s->m_q, s->m_k, s->m_v, t));
     }
-    CK(launch_kc(attn_prefix_kernel, dim3(qtiles, m->nkv, t.splits), dim3(128), kAttnSmemBytes, s->stream, true, t.splits,
-                 s->m_q, s->m_k, s->m_v, t));
     }
     // o_proj + residual (tensor parallel: f32 partial, all-reduce, residual add).
     const bool tp = m->shard.world > 1;

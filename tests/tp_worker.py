@@ -55,12 +55,21 @@ def main() -> int:
     with rt.session({"decode_strategy": "entropy_count"}) as s:
         win = s.execute_window(ids, scope)
         out = s.generate(prompt, max_tokens=gen, steps=steps, temperature=T, top_p=TOP_P, eps=EPS, trace_steps=steps)
+    # the NCCL all-reduce path (sessions that do not map the peers' buffers) on the same window
+    with rt.session({"decode_strategy": "entropy_count", "tp_peer_memory": False}) as s:
+        win_nccl = s.execute_window(ids, scope)
     rt.close()
     logits = np.frombuffer(win.logits, dtype="<f4").reshape(win.n_rows, win.n_vocab)
+    logits_nccl = np.frombuffer(win_nccl.logits, dtype="<f4").reshape(win.n_rows, win.n_vocab)
     allx = [None] * world
     dist.all_gather_object(allx, (logits.tobytes(), out["x"], out["trace"]))
     ok = True
+    nerr = float(np.abs(logits - logits_nccl).max())
+    if nerr > 5e-3 * float(np.abs(logits).max()):
+        print(f"rank {rank}: peer-memory and NCCL reductions differ by {nerr:.3e}", flush=True)
+        ok = False
     if rank == 0:
+        print(f"max |peer - nccl| = {nerr:.3e}", flush=True)
         for r in range(1, world):
             if allx[r][0] != allx[0][0] or allx[r][1] != allx[0][1]:
                 print(f"rank {r} differs from rank 0", flush=True)
@@ -108,7 +117,7 @@ def main() -> int:
         if c.x != out["x"] or certified < max(2, len(out["trace"]) // 5):
             ok = False
     flag = torch.tensor([0 if ok else 1], device=f"cuda:{local}")
-    dist.broadcast(flag, src=0)
+    dist.all_reduce(flag, op=dist.ReduceOp.MAX)
     dist.destroy_process_group()
     return int(flag.item())
 

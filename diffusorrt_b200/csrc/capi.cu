@@ -215,7 +215,8 @@ int configure_kernels() {
         cudaFuncSetAttribute(gemm_swapab_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDaSmemBytes)) != cudaSuccess)
+        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDaSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       result = DRT_INTERNAL_ERROR;
     for (int qi = 0; qi < 2 && result == DRT_OK; ++qi)
     for (int epi = 0; epi <= EPI_QKV && result == DRT_OK; ++epi)
@@ -860,6 +861,7 @@ struct drt_session {
   CUtensorMap m_xn64, m_xn128, m_xn256, m_attn64, m_attn128, m_attn256, m_act64, m_act128, m_act256, m_xf64, m_q, m_k, m_v;
   CUtensorMap m_k64;                  // K cache with 64-key boxes (decode attention)
   int da_splits = 0;                  // decode attention CTAs per KV head (0: use attn_prefix_kernel)
+  int da_cluster = 0;                 // the splits of a KV head run as one cluster and merge in it
   float* da_part_o = nullptr;         // decode attention split partials
   float* da_part_ml = nullptr;
   // graphs
@@ -1210,14 +1212,16 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
       da.bidirectional = f.bidirectional;
       da.kv_plane0 = l * m->nkv;
       da.splits = s->da_splits;
+      da.cluster_merge = s->da_cluster;
       da.out = s->attn;
       da.part_o = s->da_part_o;
       da.part_ml = s->da_part_ml;
       da.status = s->status;
       da.scale_log2 = t.scale_log2;
-      CK(launch_cx(attn_decode_kernel, dim3(s->da_splits, m->nkv), dim3(kDaThreads), kDaSmemBytes, s->stream, 1, s->m_q,
+      CK(launch_cx(attn_decode_kernel, dim3(s->da_splits, m->nkv), dim3(kDaThreads), kDaSmemBytes, s->stream,
+                   s->da_cluster ? s->da_splits : 1, s->m_q,
                    s->m_k64, s->m_v, da));
-      if (s->da_splits > 1)
+      if (s->da_splits > 1 && !s->da_cluster)
         CK(launch_k(attn_merge_kernel, dim3(m->nkv, 128 / kDaMergeRows), dim3(128 * kDaMergeRows), 0, s->stream, true,
                     static_cast<const float*>(s->da_part_o), static_cast<const float*>(s->da_part_ml), s->da_splits, m->rep,
                     m->nq, da.rows, da.rows_dev, s->attn));
@@ -1698,7 +1702,28 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
     const int sp = (n_sub + kDaMaxSub - 1) / kDaMaxSub;
     const bool fits = m->rep * (kMaxFwdRows / 2) <= 128 && sp <= kDaMaxSplits;
     s->da_splits = fits ? sp : 0;
-    if (s->da_splits > 1) {
+    // One cluster per KV head when every cluster can be resident at once: the split merge then
+    // happens in distributed shared memory instead of a second kernel.
+    if (s->da_splits > 1 && s->da_splits <= 16) {
+      cudaLaunchConfig_t lc = {};
+      lc.gridDim = dim3(s->da_splits, m->nkv);
+      lc.blockDim = dim3(kDaThreads);
+      lc.dynamicSmemBytes = kDaSmemBytes;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = static_cast<unsigned>(s->da_splits);
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      lc.attrs = at;
+      lc.numAttrs = 1;
+      int nc = 0;
+      if (cudaOccupancyMaxActiveClusters(&nc, attn_decode_kernel, &lc) != cudaSuccess) {
+        cudaGetLastError();
+        nc = 0;
+      }
+      s->da_cluster = nc >= m->nkv ? 1 : 0;
+    }
+    if (s->da_splits > 1 && !s->da_cluster) {
       const size_t rows = static_cast<size_t>(m->nkv) * s->da_splits * 128;
       if ((rc = salloc(s, &s->da_part_o, rows * 128)) != DRT_OK) return fail(rc);
       if ((rc = salloc(s, &s->da_part_ml, rows * 2)) != DRT_OK) return fail(rc);

@@ -106,6 +106,36 @@ def test_propose_agrees_with_window_forward(rt):
     np.testing.assert_allclose(scores, want_conf, rtol=0.05)
 
 
+@pytest.mark.parametrize("max_seq", [2048, 6144])
+def test_long_prefix_decode_attention(max_seq):
+    """The decode step's split-KV attention over a long cached prefix (prefilled by the first
+    propose, then the 32 active rows forwarded as a decode step) agrees with the cache-free window
+    forward: at 2048 the splits of a KV head (7) merge inside one thread-block cluster, at 6144
+    (20 splits, more than a cluster holds) through the separate merge kernel."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from diffusorrt_b200 import Runtime
+
+    r = Runtime(model_config=SMALL, max_seq=max_seq, max_prefill_rows=256)
+    try:
+        r.init_synthetic(SEED, **STD)
+        n_prefix = max_seq - 96
+        prompt = _prompt(n_prefix, max_seq)
+        mask = SMALL["mask_token_id"]
+        x = prompt + [mask] * 32
+        with r.session({"decode_strategy": "bd3_fixed_quota", "block_size": 32}) as s:
+            s.start_device(x, prompt_len=0, block_size=32, mask_token_id=mask, exact_kv=False, steps=32)
+            frontier = list(range(n_prefix, n_prefix + 32))
+            scores, tokens, fwd = s.propose_device(frontier, window_end=n_prefix + 32, frozen_prefix=n_prefix)
+            assert fwd == n_prefix + 32
+            ref = _window_logits(s, x, frontier)
+    finally:
+        r.close()
+    want_conf, want_tok = osel.max_prob_rows(ref)
+    assert np.mean(np.asarray(tokens) == np.asarray(want_tok)) >= 0.9
+    np.testing.assert_allclose(scores, want_conf, rtol=0.05)
+
+
 def _host_loop(s, prompt, *, strategy, gen, steps, bs, tau=0.9, cap=0):
     """The reference run_decode_loop over propose_device / commit_device (oracle policy)."""
     mask, eos = SMALL["mask_token_id"], SMALL["eos_token_id"]

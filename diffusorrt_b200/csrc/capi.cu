@@ -1698,7 +1698,7 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   // Decode attention: enough CTAs per KV head that each covers at most kDaMaxSub 64-key sub-tiles
   // of the longest canvas, all CTAs resident at once (one per SM); otherwise the general kernel.
   {
-    const int n_sub = s->max_seq / 64;
+    const int n_sub = (s->max_seq + 63) / 64;  // sub-tiles of the longest canvas, the last one partial
     const int sp = (n_sub + kDaMaxSub - 1) / kDaMaxSub;
     const bool fits = m->rep * (kMaxFwdRows / 2) <= 128 && sp <= kDaMaxSplits;
     s->da_splits = fits ? sp : 0;

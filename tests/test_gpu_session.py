@@ -106,12 +106,13 @@ def test_propose_agrees_with_window_forward(rt):
     np.testing.assert_allclose(scores, want_conf, rtol=0.05)
 
 
-@pytest.mark.parametrize("max_seq", [2048, 6144])
-def test_long_prefix_decode_attention(max_seq):
+@pytest.mark.parametrize("max_seq,n_prefix", [(328, 296), (2048, 1952), (6144, 6048)])
+def test_long_prefix_decode_attention(max_seq, n_prefix):
     """The decode step's split-KV attention over a long cached prefix (prefilled by the first
     propose, then the 32 active rows forwarded as a decode step) agrees with the cache-free window
-    forward: at 2048 the splits of a KV head (7) merge inside one thread-block cluster, at 6144
-    (20 splits, more than a cluster holds) through the separate merge kernel."""
+    forward: at 328 the keys end in a partial sixth sub-tile (two splits), at 2048 the splits of a
+    KV head (7) merge inside one thread-block cluster, at 6144 (20 splits, more than a cluster
+    holds) through the separate merge kernel."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from diffusorrt_b200 import Runtime
@@ -119,7 +120,6 @@ def test_long_prefix_decode_attention(max_seq):
     r = Runtime(model_config=SMALL, max_seq=max_seq, max_prefill_rows=256)
     try:
         r.init_synthetic(SEED, **STD)
-        n_prefix = max_seq - 96
         prompt = _prompt(n_prefix, max_seq)
         mask = SMALL["mask_token_id"]
         x = prompt + [mask] * 32

@@ -216,7 +216,8 @@ int configure_kernels() {
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDaSmemBytes)) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_lm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
       result = DRT_INTERNAL_ERROR;
     for (int qi = 0; qi < 2 && result == DRT_OK; ++qi)
     for (int epi = 0; epi <= EPI_QKV && result == DRT_OK; ++epi)
@@ -1009,6 +1010,20 @@ void dec_split(int tiles, int kb, int sms, int max_split, int* splits, int* kbps
 int run_dec_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a, const QuantW* q = nullptr) {
   const int tiles_m = a.n_out / 128;
   const int kb = a.K / 64;
+  if (q == nullptr && a.epi == EPI_STORE_F32 && tiles_m >= 2 * s->sms && kb <= kLmMaxKb) {
+    // Vocabulary projection: one persistent CTA per SM over a contiguous run of weight tiles, the
+    // deepest weight ring that fits beside the resident activation tile.
+    const size_t budget = 227 * 1024;
+    int stages = 0;
+    while (stages < 8 && lm_smem_bytes(stages + 1, kb) <= budget) ++stages;
+    if (stages < 2) return set_error(DRT_INTERNAL_ERROR, "lm_head ring does not fit (K = %d)", a.K);
+    a.stages = stages;
+    a.splits = 1;
+    a.kb_per_split = kb;
+    CK(launch_k(gemm_lm_kernel, dim3(std::min(tiles_m, s->sms)), dim3(kLmThreads), lm_smem_bytes(stages, kb), s->stream,
+                true, mA, mB, a));
+    return DRT_OK;
+  }
   dec_split(tiles_m, kb, s->sms, s->max_cluster, &a.splits, &a.kb_per_split);
   if (q != nullptr) {
     // every packed tile of a CTA's K slice stays resident: at most kDecQMaxKb blocks per CTA

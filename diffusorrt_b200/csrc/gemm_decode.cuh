@@ -558,6 +558,197 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) tmem_dealloc(tmem, 64);
 }
 
+// ---------------------------------------------------------------- lm_head over the decode rows
+// The vocabulary projection of a decode step (n_out = V, e.g. 151936 = 1187 weight tiles, K = H)
+// as one persistent CTA per SM that walks a contiguous run of weight tiles: the tiles of
+// consecutive vocabulary rows are one contiguous range of HBM (128 rows x K x 2 bytes each), the
+// activation tile is loaded once per CTA instead of once per weight tile, and the weight ring keeps
+// streaming across tile boundaries. Warp-specialised (kLmThreads = 192): warps 0-3 read the f32
+// accumulator (TMEM lane quarter = warp) and store the logits; warp 4 is the TMA producer, warp 5
+// issues the UMMAs. The accumulator is double-buffered in TMEM (two blocks of 64 columns), so the
+// MMAs of tile t + 1 run while the epilogue of tile t stores. Output: f32 logits rounded to bf16
+// (the EPI_STORE_F32 epilogue of the other decode linears, same values). All waits are bounded.
+constexpr int kLmThreads = 192;
+constexpr int kLmMaxKb = 16;   // K <= 1024: the whole activation tile stays resident
+__host__ __device__ inline size_t lm_smem_bytes(int stages, int nkb) {
+  // alignment slack + B tile + ring + barriers (2 stages + fullB + 2 full + 2 empty + drain), TMEM
+  // slot, flags
+  return 1024 + static_cast<size_t>(nkb) * kDecBBytes + static_cast<size_t>(stages) * kDecABytes +
+         static_cast<size_t>(2 * stages + 6) * 8 + 32;
+}
+
+template <int NCOL>
+__device__ __forceinline__ void lm_run(const CUtensorMap* tmA, const CUtensorMap* tmB, const GemmArgs& a, uint8_t* sB,
+                                       uint8_t* ring, uint64_t* fullA, uint64_t* emptyA, uint64_t* fullB, uint64_t* accF,
+                                       uint64_t* accE, uint64_t* drain, volatile int* flags, uint32_t tmem, int tile0,
+                                       int ntiles, int nkb, int stages, int rows_valid) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int total = ntiles * nkb;
+  if (warp == 4) {
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      bool ok = true;
+      // Weight K blocks continue from the ones requested before the dependency wait (kDecPreStages).
+      int g = min(total, min(stages, kDecPreStages));
+      for (; g < total; ++g) {
+        const int s = g % stages;
+        if (g >= stages && !mbar_wait(&emptyA[s], ((g / stages) - 1) & 1)) { ok = false; break; }
+        if (flags[0] != 0) break;
+        mbar_expect_tx(&fullA[s], kDecABytes);
+        tma_load_2d_hint(ring + static_cast<size_t>(s) * kDecABytes, tmA, &fullA[s], (g % nkb) * 64, (tile0 + g / nkb) * 128,
+                         policy);
+      }
+      flags[1] = g;  // weight K blocks requested
+      if (!ok) { record_error(a.status, DEV_TIMEOUT_TMA); flags[0] = 1; }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, NCOL);
+      bool ok = total == 0 || mbar_wait(fullB, 0);
+      int g = 0;
+      for (int t = 0; t < ntiles && ok; ++t) {
+        const int buf = t & 1;
+        if (t >= 2 && !mbar_wait(&accE[buf], ((t >> 1) - 1) & 1)) { ok = false; break; }
+        if (flags[0] != 0) { ok = false; break; }
+        tc_fence_after();
+        for (int i = 0; i < nkb; ++i, ++g) {
+          const int s = g % stages;
+          if (!mbar_wait(&fullA[s], (g / stages) & 1)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(ring + static_cast<size_t>(s) * kDecABytes);
+          const uint32_t b_addr = smem_u32(sB + static_cast<size_t>(i) * kDecBBytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + buf * 64, sdesc_kmajor_sw128(a_addr + kk * 32), sdesc_kmajor_sw128(b_addr + kk * 32), idesc,
+                      (i | kk) != 0 ? 1u : 0u);
+          umma_commit(&emptyA[s]);
+        }
+        if (ok) umma_commit(&accF[buf]);
+      }
+      flags[2] = g;  // weight K blocks whose bytes landed
+      if (!ok) {
+        record_error(a.status, DEV_TIMEOUT_MMA);
+        flags[0] = 1;
+        umma_commit(drain);  // every UMMA issued so far completes before TMEM is released
+        mbar_wait(drain, 0);
+      }
+    }
+    __syncwarp();
+  } else {
+    // Epilogue: thread tid holds vocabulary row m0 + tid of each tile.
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    for (int t = 0; t < ntiles; ++t) {
+      const int buf = t & 1;
+      // Both exits are decided per warp: the TMEM loads below are warp-collective.
+      if (__any_sync(0xffffffffu, flags[0] != 0)) break;
+      const bool ready = __all_sync(0xffffffffu, mbar_wait(&accF[buf], (t >> 1) & 1));
+      if (!ready) {
+        if (lane == 0) { record_error(a.status, DEV_TIMEOUT_EPI); flags[0] = 1; }
+        break;
+      }
+      tc_fence_after();
+      float acc[NCOL];
+#pragma unroll
+      for (int cb = 0; cb < NCOL; cb += 32) tmem_ld32(tmem + lane_off + buf * 64 + cb, acc + cb);
+      tc_fence_before();
+      mbar_arrive(&accE[buf]);  // this thread is done with the buffer: tile t + 2 may overwrite it
+      const int m0 = (tile0 + t) * 128;
+      gemm_epilogue_chunk_t<EPI_STORE_F32, true>(a, acc, 0, min(32, rows_valid), m0, tid, nullptr, 0);
+      if constexpr (NCOL == 64)
+        if (rows_valid > 32) gemm_epilogue_chunk_t<EPI_STORE_F32, true>(a, acc + 32, 32, rows_valid - 32, m0, tid, nullptr, 0);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kLmThreads, 1)
+    gemm_lm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
+  const int stages = a.stages;
+  const int nkb = a.K >> 6;
+  uint8_t* sB = smem;
+  uint8_t* ring = smem + static_cast<size_t>(nkb) * kDecBBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + static_cast<size_t>(stages) * kDecABytes);
+  uint64_t* fullA = bars;
+  uint64_t* emptyA = bars + stages;
+  uint64_t* fullB = bars + 2 * stages;
+  uint64_t* accF = fullB + 1;  // [2]
+  uint64_t* accE = fullB + 3;  // [2]
+  uint64_t* drain = fullB + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fullB + 6);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] error, [1] requested, [2] landed
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  // This CTA's run of consecutive weight tiles (the grid splits the tiles evenly, one CTA per SM).
+  const int tiles_m = a.n_out >> 7;
+  const int tile0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * tiles_m) / gridDim.x);
+  const int ntiles = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * tiles_m) / gridDim.x) - tile0;
+  const int total = ntiles * nkb;
+  const int npre = min(total, min(stages, kDecPreStages));
+  if (tid == 0) {
+    for (int st = 0; st < stages; ++st) {
+      mbar_init(&fullA[st], 1);
+      mbar_init(&emptyA[st], 1);
+    }
+    mbar_init(fullB, 1);
+    mbar_init(&accF[0], 1);
+    mbar_init(&accF[1], 1);
+    mbar_init(&accE[0], 128);
+    mbar_init(&accE[1], 128);
+    mbar_init(drain, 1);
+    flags[0] = 0;
+    flags[1] = 0;
+    flags[2] = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    // The first weight K blocks need nothing from the producer kernel.
+    const uint64_t policy = l2_policy_evict_first();
+    for (int g = 0; g < npre; ++g) {
+      mbar_expect_tx(&fullA[g], kDecABytes);
+      tma_load_2d_hint(ring + static_cast<size_t>(g) * kDecABytes, &tmA, &fullA[g], (g % nkb) * 64, (tile0 + g / nkb) * 128,
+                       policy);
+    }
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  griddep_wait();
+  int rows_valid = a.rows;
+  if (a.rows_dev != nullptr) rows_valid = min(rows_valid, *a.rows_dev);
+  rows_valid = max(0, min(rows_valid, kDecRows));
+  if (tid == 0 && total > 0) {
+    mbar_expect_tx(fullB, static_cast<uint32_t>(nkb * kDecBBytes));
+    for (int i = 0; i < nkb; ++i) tma_load_2d(sB + static_cast<size_t>(i) * kDecBBytes, &tmB, fullB, i * 64, 0);
+  }
+  griddep_launch_dependents();
+  if (rows_valid <= 32)
+    lm_run<32>(&tmA, &tmB, a, sB, ring, fullA, emptyA, fullB, accF, accE, drain, flags, tmem, tile0, ntiles, nkb, stages,
+               rows_valid);
+  else
+    lm_run<64>(&tmA, &tmB, a, sB, ring, fullA, emptyA, fullB, accF, accE, drain, flags, tmem, tile0, ntiles, nkb, stages,
+               rows_valid);
+
+  __syncthreads();
+  if (flags[0] != 0 && tid == 0) {
+    // A wait gave up: let every copy this CTA requested land before the shared memory goes away.
+    // The producer runs at most `stages` blocks ahead of the last block whose bytes landed, so the
+    // blocks in between occupy distinct slots and each is the newest request on its slot.
+    if (total > 0) mbar_wait(fullB, 0);
+    for (int g = flags[2]; g < flags[1]; ++g) mbar_wait(&fullA[g % stages], (g / stages) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
 using DecGemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmArgs);
 
 // The instantiation for an epilogue kind, split factor and weight format (nullptr if none).

@@ -136,6 +136,33 @@ def test_long_prefix_decode_attention(max_seq, n_prefix):
     np.testing.assert_allclose(scores, want_conf, rtol=0.05)
 
 
+def test_large_vocab_head_matches_oracle():
+    """A vocabulary of 320 weight tiles (more than two per SM) takes the persistent lm_head kernel:
+    one CTA per SM over a contiguous run of tiles, activation tile loaded once, TMEM accumulator
+    double-buffered. Its logits match the CPU oracle at both MMA widths (20 and 48 rows)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from diffusorrt_b200 import Runtime
+
+    cfg = dict(SMALL, vocab_size=40960, mask_token_id=40000, eos_token_id=40001)
+    r = Runtime(model_config=cfg, max_seq=256, max_prefill_rows=256)
+    try:
+        r.init_synthetic(SEED, **STD)
+        weights = synth_weights(cfg, SEED, **STD)
+        ids = _prompt(96, 5, vocab=40000)
+        with r.session({"decode_strategy": "bd3_fixed_quota", "block_size": 32}) as s:
+            for scope in (list(range(70, 90)), list(range(0, 96, 2))):
+                got = _window_logits(s, ids, scope)
+                want = ofwd.forward_mlx(weights, cfg, ids, prompt_len=0, block_size=32, output_rows=scope)
+                scale = float(np.abs(want).max())
+                err = np.abs(got - want)
+                assert err.max() <= 0.02 * scale, (len(scope), err.max(), scale)
+                assert float(np.mean(err)) <= 0.002 * scale
+                assert np.mean(np.argmax(got, -1) == np.argmax(want, -1)) >= 0.9
+    finally:
+        r.close()
+
+
 def _host_loop(s, prompt, *, strategy, gen, steps, bs, tau=0.9, cap=0):
     """The reference run_decode_loop over propose_device / commit_device (oracle policy)."""
     mask, eos = SMALL["mask_token_id"], SMALL["eos_token_id"]

@@ -26,8 +26,8 @@ Kernel order, for a profiler's name filter and skip count: the prompt prefill la
 embed_rows_kernel and two rmsnorm_bf16_kernel per layer (with the prefill linears and attention);
 every denoising step then launches plan_kernel, embed_rows_kernel, per layer
 [rmsnorm, gemm_decode (QKV), attn_decode, attn_merge, gemm_decode (o), rmsnorm, gemm_decode
-(gate/up), gemm_decode (down)], then rmsnorm, gemm_decode (lm_head), sel_pass1_kernel and
-commit_kernel.
+(gate/up), gemm_decode (down)], then rmsnorm, gemm_lm_kernel (lm_head; gemm_decode for the
+4-bit model), sel_pass1_kernel and commit_kernel.
 """
 from __future__ import annotations
 

@@ -4,7 +4,7 @@ Runs the reference's own CPU code (importable without MLX) on seeded inputs and 
 fixtures next to this script. The reference tree is only read; nothing here runs on the GPU
 box (the fixtures travel, this script does not need to).
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [--reference /path/to/reference]
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --reference /path/to/reference
 
 Fixtures:
   selector.npz   max-prob / entropy (incl. temperature + top-p) / top-k / threshold / MASK exclusion
@@ -131,8 +131,11 @@ def _tables(mlx_forward, numpyref) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("DIFFUSORRT_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("DIFFUSORRT_REFERENCE"),
+                    help="checkout of the reference project (or set DIFFUSORRT_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference checkout with --reference or DIFFUSORRT_REFERENCE")
     sys.path.insert(0, str(Path(args.reference) / "python" / "src"))
     sys.dont_write_bytecode = True
     from edllm.abi import ABI_VERSION

@@ -56,6 +56,29 @@ constexpr int kAttnStages = 2;
 constexpr int kAttnRowStride = 132;  // floats per received row (conflict-free float4 access)
 constexpr size_t kAttnSmemBytes = 1024 + kAttnQBytes + kAttnStages * kAttnStageBytes + kAttnPBytes + 256;
 
+// 2^x with the PTX approximate instruction (relative error within 2^-22 of the exact power; a
+// subnormal result flushes to zero). P is rounded to bf16 right after, 2^-9 relative.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Columns [c, c + 64) of this thread's TMEM lane (two 32x32b.x32 loads), one wait for both, in the
+// same statement so no use of the registers can be scheduled before the data lands.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t taddr, float* v) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr), "r"(taddr + 32)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Split-KV merge inside one cluster of S CTAs (one KV head). CTA r owns query rows
 // [r*R, (r+1)*R), R = 128 / S. Every thread pushes its row's unnormalized (o, m, l) into the
 // owner's receive buffer recv[src rank * R + row % R] with remote stores; after the cluster
@@ -501,39 +524,47 @@ __global__ void __launch_bounds__(kAttnWThreads, 1)
       pend_j = j + 1;
     }
 
+    // This thread's 64 scores of the tile (keys key0 + 64 half ..), read from TMEM once and kept in
+    // registers for both passes. The row max is taken over the raw scores and scaled once (the
+    // scale is positive and rounding is monotonic, so this is the max of the scaled scores).
     const uint32_t tmem_s = tmem + (j & 1) * 128 + lane_off + half * 64;
+    const int k_lo = key0 + half * 64;
+    const bool full = k_lo + 64 <= lim;  // every key of this thread's half visible to its row
+    float sv[64];
+    tmem_ld32x2(tmem_s, sv);
     float tile_max = -INFINITY;
+    if (full) {
 #pragma unroll
-    for (int cb = 0; cb < 64; cb += 32) {
-      float sv[32];
-      tmem_ld32(tmem_s + cb, sv);
+      for (int i = 0; i < 64; ++i) tile_max = fmaxf(tile_max, sv[i]);
+    } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int kp = key0 + half * 64 + cb + i;
-        const float x = (kp < lim) ? sv[i] * a.scale_log2 : -INFINITY;
-        tile_max = fmaxf(tile_max, x);
-      }
+      for (int i = 0; i < 64; ++i)
+        if (k_lo + i < lim) tile_max = fmaxf(tile_max, sv[i]);
     }
-    red_m[tid] = tile_max;
+    red_m[tid] = tile_max * a.scale_log2;
     __syncthreads();
     tile_max = fmaxf(red_m[r], red_m[r + 128]);
     const float m_new = fmaxf(m_run, tile_max);
     const float alpha = (m_new == -INFINITY) ? 1.0f : exp2f(m_run - m_new);
+    const bool live = m_new != -INFINITY;
     float psum = 0.0f;
 #pragma unroll
-    for (int cb = 0; cb < 64; cb += 32) {
-      float sv[32];
-      tmem_ld32(tmem_s + cb, sv);
+    for (int c8 = 0; c8 < 8; ++c8) {
+      // P = 2^(s scale - m) for 8 keys, packed to bf16 and stored as one 16-byte chunk of the
+      // 128-byte-swizzled P tile
+      float p[8];
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const int col = half * 64 + cb + i;
-        const int kp = key0 + col;
-        const float p0 = (kp < lim && m_new != -INFINITY) ? exp2f(sv[i] * a.scale_log2 - m_new) : 0.0f;
-        const float p1 = (kp + 1 < lim && m_new != -INFINITY) ? exp2f(sv[i + 1] * a.scale_log2 - m_new) : 0.0f;
-        const __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-        psum += __low2float(pb) + __high2float(pb);
-        *reinterpret_cast<__nv_bfloat162*>(sP + sw128_offset(r, col, 128)) = pb;
+      for (int e = 0; e < 8; ++e) {
+        const int i = c8 * 8 + e;
+        p[e] = (live && (full || k_lo + i < lim)) ? ex2_ftz(__fmaf_rn(sv[i], a.scale_log2, -m_new)) : 0.0f;
       }
+      __align__(16) __nv_bfloat162 pb[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        pb[e] = __floats2bfloat162_rn(p[2 * e], p[2 * e + 1]);
+        psum += __low2float(pb[e]) + __high2float(pb[e]);
+      }
+      *reinterpret_cast<uint4*>(sP + sw128_offset(r, half * 64 + c8 * 8, 128)) = *reinterpret_cast<const uint4*>(pb);
     }
     red_s[tid] = psum;
     fence_proxy_async_smem();

@@ -121,13 +121,10 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Epilogue for up to 32 accumulator columns (activation rows col0 .. col0+ncols-1).
 // v[i] holds this thread's weight row (m0 + tid) for activation row col0 + i. All loops run to
 // 32 with a guard so v stays in registers.
-// rope_c / rope_s: optional RoPE factors for this thread's feature at rows col0 + i, loaded by the
-// caller ahead of time (the decode kernel fetches them before its accumulator is ready); when null
-// the QKV epilogue reads the tables itself.
+// xs: shared scratch of at least 32 x 132 floats (SwiGLU, QKV, residual sums of squares).
 template <int EPI, bool RND = true>
 __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* v, int col0, int ncols, int m0, int tid,
-                                                      float* xs, int pos0, const float* rope_c = nullptr,
-                                                      const float* rope_s = nullptr) {
+                                                      float* xs, int pos0) {
   const int n = m0 + tid;
   const float b = a.bias != nullptr ? a.bias[n] : 0.0f;
     if constexpr (EPI == EPI_STORE_RAW) {
@@ -227,74 +224,60 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
         return;
       }
       const float* nw = is_q ? a.qnorm_w : a.knorm_w;
-      // RoPE factors of the chunk's rows, all loaded before any store of the chunk (the stores below
-      // may alias them as far as the compiler knows, which would serialise one load per row).
-      float rc[32], rsn[32];
-      if (rope_c == nullptr) {
+      // The chunk is staged in shared memory and re-read with four threads per row: thread t owns
+      // row i = t / 4 and features [16 q, 16 q + 16) and [64 + 16 q, 80 + 16 q), q = t % 4, so the
+      // RoPE partners (f, f + 64) sit in the same thread, the row's sum of squares takes two
+      // shuffles (no block barrier), and every store is a 32-byte run of the row.
+      constexpr int kLd = 132;  // padded row stride (floats) of the staged chunk
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int pos = pos0 + col0 + min(i, ncols - 1);
-          rc[i] = __ldg(a.rope_cos + static_cast<size_t>(pos) * 64 + (tid & 63));
-          rsn[i] = __ldg(a.rope_sin + static_cast<size_t>(pos) * 64 + (tid & 63));
-        }
-      } else {
+      for (int i = 0; i < 32; ++i) xs[i * kLd + tid] = __fadd_rn(out_round<RND>(v[i]), b);
+      __syncthreads();
+      const int i = tid >> 2, q = tid & 3;
+      const int f0 = q * 16;
+      float lo[16], hi[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          rc[i] = rope_c[i];
-          rsn[i] = rope_s[i];
-        }
+      for (int e = 0; e < 16; e += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(xs + i * kLd + f0 + e);
+        const float4 h4 = *reinterpret_cast<const float4*>(xs + i * kLd + 64 + f0 + e);
+        lo[e] = l4.x; lo[e + 1] = l4.y; lo[e + 2] = l4.z; lo[e + 3] = l4.w;
+        hi[e] = h4.x; hi[e + 1] = h4.y; hi[e + 2] = h4.z; hi[e + 3] = h4.w;
       }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float val = __fadd_rn(out_round<RND>(v[i]), b);
-        v[i] = val;
-        xs[i * 128 + tid] = val;
-      }
-      float* rs = xs + 32 * 128;  // 32 per-row scales
-      float* part = rs + 32;        // [4 warps][32 rows] partial sums of squares
-      const int warp = tid >> 5, lane = tid & 31;
+      __syncthreads();  // the staged chunk is consumed; the caller may stage the next one
+      const int pos = pos0 + col0 + max(0, min(i, ncols - 1));
       if (nw != nullptr) {
-        // All rows at once: a warp tree per row over this warp's 32 features, then the four warps
-        // in order; one thread per row finishes its scale.
+        float ss = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i < ncols) {
-            const float t = warp_sum(__fmul_rn(v[i], v[i]));
-            if (lane == 0) part[warp * 32 + i] = t;
-          }
-        }
-        __syncthreads();
-        if (tid < ncols) {
-          const float ss = __fadd_rn(__fadd_rn(__fadd_rn(part[tid], part[32 + tid]), part[64 + tid]), part[96 + tid]);
-          rs[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
+        for (int e = 0; e < 16; ++e) ss = __fmaf_rn(lo[e], lo[e], ss);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) ss = __fmaf_rn(hi[e], hi[e], ss);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          lo[e] = __fmul_rn(__fmul_rn(lo[e], rs), __ldg(nw + f0 + e));
+          hi[e] = __fmul_rn(__fmul_rn(hi[e], rs), __ldg(nw + 64 + f0 + e));
         }
       }
-      __syncthreads();
-      const int partner = tid ^ 64;
-      const float w_self = nw != nullptr ? nw[tid] : 1.0f;
-      const float w_part = nw != nullptr ? nw[partner] : 1.0f;
-      const int head = is_q ? tile : tile - a.nq;
+      // RoPE: (x_f, x_{f+64}) -> (x_f c - x_{f+64} s, x_{f+64} c + x_f s), c / s of (pos, f)
+      const float* cp = a.rope_cos + static_cast<size_t>(pos) * 64 + f0;
+      const float* sp = a.rope_sin + static_cast<size_t>(pos) * 64 + f0;
+      __align__(16) __nv_bfloat16 olo[16], ohi[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (i >= ncols) continue;
-        float x = v[i];
-        float xp = xs[i * 128 + partner];
-        if (nw != nullptr) {
-          x = __fmul_rn(__fmul_rn(x, rs[i]), w_self);
-          xp = __fmul_rn(__fmul_rn(xp, rs[i]), w_part);
-        }
-        const int pos = pos0 + col0 + i;
-        const float c = rc[i];
-        const float s = rsn[i];
-        const float rot = tid < 64 ? -xp : xp;
-        const float out = __fadd_rn(__fmul_rn(x, c), __fmul_rn(rot, s));
-        if (is_q) {
-          a.out_bf16[(static_cast<size_t>(col0 + i) * a.nq + head) * 128 + tid] = __float2bfloat16_rn(out);
-        } else {
-          a.kcache[(static_cast<size_t>(head) * a.max_seq + pos) * 128 + tid] = __float2bfloat16_rn(out);
-        }
+      for (int e = 0; e < 16; ++e) {
+        const float c = __ldg(cp + e), sn = __ldg(sp + e);
+        olo[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(lo[e], c), __fmul_rn(-hi[e], sn)));
+        ohi[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(hi[e], c), __fmul_rn(lo[e], sn)));
       }
-      __syncthreads();
+      if (i < ncols) {
+        const int head = is_q ? tile : tile - a.nq;
+        __nv_bfloat16* dst = is_q ? a.out_bf16 + (static_cast<size_t>(col0 + i) * a.nq + head) * 128
+                                  : a.kcache + (static_cast<size_t>(head) * a.max_seq + pos) * 128;
+        *reinterpret_cast<uint4*>(dst + f0) = *reinterpret_cast<const uint4*>(olo);
+        *reinterpret_cast<uint4*>(dst + f0 + 8) = *reinterpret_cast<const uint4*>(olo + 8);
+        *reinterpret_cast<uint4*>(dst + 64 + f0) = *reinterpret_cast<const uint4*>(ohi);
+        *reinterpret_cast<uint4*>(dst + 64 + f0 + 8) = *reinterpret_cast<const uint4*>(ohi + 8);
+      }
     }
 }
 

@@ -46,7 +46,7 @@ class ModelConfig(ctypes.Structure):
                 ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("intermediate_size", ctypes.c_int32),
                 ("vocab_size", ctypes.c_int32), ("qk_norm", ctypes.c_int32), ("qkv_bias", ctypes.c_int32),
                 ("tied_lm_head", ctypes.c_int32), ("rms_norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
-                ("max_seq", ctypes.c_int32), ("max_prefill_rows", ctypes.c_int32)]
+                ("max_seq", ctypes.c_int32), ("max_prefill_rows", ctypes.c_int32), ("logits_shift", ctypes.c_int32)]
 
 
 class TpShard(ctypes.Structure):
@@ -70,7 +70,7 @@ class GenerateParams(ctypes.Structure):
                 ("max_tokens", ctypes.c_int32), ("mask_token_id", ctypes.c_int32), ("eos_token_id", ctypes.c_int32),
                 ("confidence_threshold", ctypes.c_double), ("rounds_per_block", ctypes.c_int32),
                 ("trace_steps", ctypes.c_int32), ("temperature", ctypes.c_double), ("top_p", ctypes.c_double),
-                ("eps", ctypes.c_double)]
+                ("eps", ctypes.c_double), ("seed", ctypes.c_uint64), ("mask_origin", ctypes.c_int32)]
 
 
 class GenerateResult(ctypes.Structure):
@@ -113,6 +113,7 @@ SIGNATURES = {
     "drt_tp_shard_geometry": (ctypes.c_int, [ctypes.POINTER(ModelConfig), ctypes.c_int32, ctypes.c_int32,
                                              ctypes.POINTER(TpShard)]),
     "drt_tp_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
+    "drt_tp_flag_value": (ctypes.c_uint64, [ctypes.c_uint64, ctypes.c_int32, ctypes.c_int32]),
     "drt_model_create_tp": (ctypes.c_int, [ctypes.POINTER(ModelConfig), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                            ctypes.c_char_p, ctypes.POINTER(_P)]),
     "drt_model_quantize": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32]),
@@ -130,6 +131,7 @@ SIGNATURES = {
     "drt_session_metrics": (ctypes.c_int, [_P, ctypes.POINTER(Metrics)]),
     "drt_session_tp_handle": (ctypes.c_int, [_P, ctypes.c_char_p]),
     "drt_session_tp_connect": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_int32]),
+    "drt_session_peer_wait_drill": (ctypes.c_int, [_P]),
     "drt_entropy_count_schedule": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_double, _I32P]),
     "drt_session_kv_pointers": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
     "drt_session_close": (None, [_P]),
@@ -142,6 +144,8 @@ SIGNATURES = {
                                            ctypes.c_double, _P, _P, _P, _P]),
     "drt_selector_topp": (ctypes.c_int, [_P, ctypes.c_int64, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
                                          ctypes.c_double, ctypes.c_int32, ctypes.c_double, _P, _P, _P, _P]),
+    "drt_selector_sample": (ctypes.c_int, [_P, ctypes.c_int64, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
+                                           ctypes.c_uint64, ctypes.c_int32, _P, _P, _P, _P, _P, _P]),
     "drt_exp_nonpos": (ctypes.c_int, [_P, _P, ctypes.c_int64, _P]),
     "drt_select_choices": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
                                           ctypes.c_double, _P, _P, _P]),

@@ -13,12 +13,15 @@ QWEN3_06B_BD3LM = dict(
     layer_count=28, hidden_size=1024, attention_heads=16, num_kv_heads=8, head_dim=128,
     intermediate_size=3072, vocab_size=151936, qk_norm=True, qkv_bias=False, tied_lm_head=True,
     rms_norm_eps=1e-6, rope_theta=1e6, mask_token_id=151669, eos_token_id=151645, block_size=32,
+    logits_shift=False, mask_origin=0,
 )
 
 DREAM_7B = dict(
     layer_count=28, hidden_size=3584, attention_heads=28, num_kv_heads=4, head_dim=128,
     intermediate_size=18944, vocab_size=152064, qk_norm=False, qkv_bias=True, tied_lm_head=False,
     rms_norm_eps=1e-6, rope_theta=1e6, mask_token_id=151666, eos_token_id=151643, block_size=8,
+    # Dream's logits convention (dream_ar_shift) and its D2F graph's mask origin (the prompt)
+    logits_shift=True, mask_origin="prompt",
 )
 
 # Seeded synthetic weights: linears and embedding N(0, 0.02^2)-shaped (an Irwin-Hall sum of four

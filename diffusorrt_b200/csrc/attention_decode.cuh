@@ -147,6 +147,9 @@ __global__ void __launch_bounds__(kDaThreads, 1)
   const int n_sub = (kv_len + 63) / 64;
   const int sub0 = static_cast<int>((static_cast<long long>(split) * n_sub) / S);
   const int sub1 = static_cast<int>((static_cast<long long>(split + 1) * n_sub) / S);
+  // The host sizes `splits` so that no CTA gets more than kDaMaxSub sub-tiles; a mismatch is reported
+  // instead of dropping keys (the loads stay within the CTA's kDaMaxSub slots either way).
+  if (sub1 - sub0 > kDaMaxSub && tid == 0) record_error(a.status, DEV_BAD_GEOMETRY);
   const int nt = min(kDaMaxSub, max(0, sub1 - sub0));
   // Sub-tiles wholly before the first forwarded position hold final K/V.
   const int n_final = max(0, min(nt, q_pos0 / 64 - sub0));

@@ -491,6 +491,10 @@ extern "C" int drt_tp_shard_geometry(const drt_model_config* cfg, int32_t rank, 
   return tp_geometry(cfg, rank, world, out);
 }
 
+extern "C" uint64_t drt_tp_flag_value(uint64_t epoch, int32_t layer, int32_t which) {
+  return tp_flag_value(epoch, 2 * layer + which);
+}
+
 extern "C" int drt_tp_unique_id(uint8_t* id) {
   REQUIRE(id != nullptr, "null argument");
   const NcclApi* nc = nullptr;
@@ -841,6 +845,8 @@ struct drt_session {
   int* sel_pidx = nullptr;
   double* sel_psum = nullptr;
   int* sel_cnt = nullptr;
+  double *sel_skey = nullptr, *sel_skey2 = nullptr;  // sampled-key chunk partials (temperature > 0)
+  int* sel_sidx = nullptr;
   double *sel_amax = nullptr, *sel_sum = nullptr, *conf = nullptr;
   int* token = nullptr;
   int* scope_rows = nullptr;
@@ -854,6 +860,8 @@ struct drt_session {
   int canvas_len = 0;
   int origin = 0, block_size = 32, mask_id = 0;
   bool started = false;
+  bool exact_kv = true;               // propose reuses the frozen prefix's K/V (false: recompute it)
+  int propose_count = 0;              // forwards since start_device (keys the sampled draws)
   // launch geometry
   int sms = 148;
   int attn_splits = 1, attn_tps = 1;
@@ -921,6 +929,7 @@ int check_status(drt_session* s) {
     cudaMemset(s->status, 0, sizeof(int));
     if (code == DEV_BAD_SHAPE) return set_error(DRT_INVALID_ARGUMENT, "device rejected an input (token id out of range)");
     if (code == DEV_TIMEOUT_PEER) return set_error(DRT_DEVICE_TIMEOUT, "a tensor-parallel peer did not deliver its partials in time");
+    if (code == DEV_BAD_GEOMETRY) return set_error(DRT_INTERNAL_ERROR, "a kernel's launch geometry did not cover its work");
     return set_error(DRT_DEVICE_TIMEOUT, "device wait expired (code %d)", code);
   }
   return DRT_OK;
@@ -1007,7 +1016,10 @@ void dec_split(int tiles, int kb, int sms, int max_split, int* splits, int* kbps
 
 // Decode linear over at most kDecRows activation rows (mB: the bf16 activation map, box 64 rows);
 // q: the weight's 4-bit copy when the model is quantized (tmA then maps the packed nibbles).
-int run_dec_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a, const QuantW* q = nullptr) {
+// mB128: the same activation with 128-row boxes, for K too long for the decode kernel's resident
+// activation slice even at the largest split (the wide linear then takes the shape).
+int run_dec_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a, const QuantW* q = nullptr,
+                 const CUtensorMap* mB128 = nullptr) {
   const int tiles_m = a.n_out / 128;
   const int kb = a.K / 64;
   if (q == nullptr && a.epi == EPI_STORE_F32 && tiles_m >= 2 * s->sms && kb <= kLmMaxKb) {
@@ -1042,7 +1054,20 @@ int run_dec_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, G
                  q->map, mB, a));
     return DRT_OK;
   }
-  if (a.kb_per_split > kDecMaxKb) return set_error(DRT_UNSUPPORTED, "decode linear with %d K blocks per CTA", a.kb_per_split);
+  if (a.kb_per_split > kDecMaxKb) {
+    // Long K (Dream-7B's MLP): more split-K CTAs than one per SM, in several waves, so that each
+    // CTA's activation slice stays resident; beyond the largest cluster, the wide linear.
+    int sp = a.splits;
+    while (sp < std::min(16, s->max_cluster) && (kb + sp - 1) / sp > kDecMaxKb) sp *= 2;
+    if ((kb + sp - 1) / sp <= kDecMaxKb) {
+      a.splits = sp;
+      a.kb_per_split = (kb + sp - 1) / sp;
+    } else if (mB128 != nullptr) {
+      return run_wide(s, mA, *mB128, nullptr, a);
+    } else {
+      return set_error(DRT_UNSUPPORTED, "decode linear with %d K blocks per CTA", a.kb_per_split);
+    }
+  }
   // Ring depth: the deepest ring (up to the whole K slice) that still lets two CTAs share an SM,
   // so the next kernel's CTAs can stream their weights beside this one; when that leaves fewer
   // than four stages for a longer slice, the whole slice in one CTA per SM instead.
@@ -1185,7 +1210,7 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     a.max_seq = s->max_seq;
     a.eps = m->cfg.rms_norm_eps;
     if (f.decode) {
-      TRY(run_dec_gemm(s, w.m_qkv, s->m_xn64, a, m->quantized ? &w.q_qkv : nullptr));
+      TRY(run_dec_gemm(s, w.m_qkv, s->m_xn64, a, m->quantized ? &w.q_qkv : nullptr, &s->m_xn128));
     } else {
       TRY(run_wide(s, w.m_qkv, s->m_xn128, s->rows_cap >= 256 ? &s->m_xn256 : nullptr, a));
     }
@@ -1260,7 +1285,7 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     o.out_f32 = tp ? s->part : s->h;
     o.ld_out = H;
     if (s->tp_p2p) TRY(tp_push_linear(s, w.m_o, s->m_attn128, s->rows_cap >= 256 ? &s->m_attn256 : nullptr, o, 0, 2 * l, f.rows));
-    else if (f.decode) TRY(run_dec_gemm(s, w.m_o, s->m_attn64, o, m->quantized ? &w.q_o : nullptr));
+    else if (f.decode) TRY(run_dec_gemm(s, w.m_o, s->m_attn64, o, m->quantized ? &w.q_o : nullptr, &s->m_attn128));
     else TRY(run_wide(s, w.m_o, s->m_attn128, s->rows_cap >= 256 ? &s->m_attn256 : nullptr, o));
     if (tp && !s->tp_p2p) TRY(tp_reduce_residual(s, f.rows));
     TRY(run_rmsnorm(s, s->h, nullptr, f.rows, f.rows_dev, w.post_norm, s->xn));
@@ -1269,7 +1294,7 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     g.epi = EPI_SWIGLU;
     g.out_bf16 = s->act;
     g.ld_out = m->I;
-    if (f.decode) TRY(run_dec_gemm(s, w.m_gu, s->m_xn64, g, m->quantized ? &w.q_gu : nullptr));
+    if (f.decode) TRY(run_dec_gemm(s, w.m_gu, s->m_xn64, g, m->quantized ? &w.q_gu : nullptr, &s->m_xn128));
     else TRY(run_wide(s, w.m_gu, s->m_xn128, s->rows_cap >= 256 ? &s->m_xn256 : nullptr, g));
     // down + residual.
     GemmArgs d = base_args(s, H, m->I, f);
@@ -1277,7 +1302,7 @@ int enqueue_layers(drt_session* s, const Fwd& f) {
     d.out_f32 = tp ? s->part : s->h;
     d.ld_out = H;
     if (s->tp_p2p) TRY(tp_push_linear(s, w.m_down, s->m_act128, s->rows_cap >= 256 ? &s->m_act256 : nullptr, d, 1, 2 * l + 1, f.rows));
-    else if (f.decode) TRY(run_dec_gemm(s, w.m_down, s->m_act64, d, m->quantized ? &w.q_down : nullptr));
+    else if (f.decode) TRY(run_dec_gemm(s, w.m_down, s->m_act64, d, m->quantized ? &w.q_down : nullptr, &s->m_act128));
     else TRY(run_wide(s, w.m_down, s->m_act128, s->rows_cap >= 256 ? &s->m_act256 : nullptr, d));
     if (tp && !s->tp_p2p) TRY(tp_reduce_residual(s, f.rows));
   }
@@ -1295,7 +1320,7 @@ int enqueue_head(drt_session* s, const int* row_index, int rows, const int* rows
   a.epi = EPI_STORE_F32;
   a.out_f32 = s->logits;
   a.ld_out = m->V;
-  TRY(run_dec_gemm(s, m->m_lm, s->m_xf64, a, m->quantized ? &m->q_lm : nullptr));
+  TRY(run_dec_gemm(s, m->m_lm, s->m_xf64, a, m->quantized ? &m->q_lm : nullptr, &s->m_xf128));
   if (with_selector) {
     SelArgs sa;
     memset(&sa, 0, sizeof(sa));
@@ -1318,6 +1343,15 @@ int enqueue_head(drt_session* s, const int* row_index, int rows, const int* rows
     sa.conf = s->conf;
     sa.token = s->token;
     sa.status = s->status;
+    // Temperature sampling when the request asks for it (read on the device, so one graph serves both).
+    sa.sample_t_dev = &s->state->sample_t;
+    sa.sample_seed_dev = &s->state->sample_seed;
+    sa.sample_forward_dev = &s->state->forward_count;
+    sa.positions = s->state->frontier_pos;
+    sa.part_skey = s->sel_skey;
+    sa.part_skey2 = s->sel_skey2;
+    sa.part_sidx = s->sel_sidx;
+    sa.row_tie = s->row_tie;
     CK(launch_k(sel_pass1_kernel, dim3(s->sel_chunks, rows), dim3(kSelThreads), 0, s->stream, true, sa));
   }
   return DRT_OK;
@@ -1349,7 +1383,7 @@ int capture(drt_session* s, bool with_policy, cudaGraphExec_t* out) {
   if (rc == DRT_OK) rc = enqueue_head(s, s->state->frontier_row, kMaxFrontier, &s->state->n_frontier, true);
   if (rc == DRT_OK && with_policy) {
     if (launch_k(commit_kernel, dim3(1), dim3(32), 0, s->stream, true, s->state, s->canvas, static_cast<const double*>(s->conf),
-                 static_cast<const int*>(s->token), s->trace) != cudaSuccess)
+                 static_cast<const int*>(s->token), static_cast<const int*>(s->row_tie), s->trace) != cudaSuccess)
       rc = set_error(DRT_INTERNAL_ERROR, "commit launch failed");
   }
   cudaError_t e = cudaStreamEndCapture(s->stream, &graph);
@@ -1545,6 +1579,7 @@ int dream_generate(drt_session* s, const drt_generate_params* p, const int32_t* 
   hs->canvas_len = canvas_len;
   hs->prompt_len = prompt_len;
   hs->mask_id = p->mask_token_id;
+  hs->shift = m->cfg.logits_shift ? 1 : 0;
   hs->n_proceed = n_proceed;
   hs->trace_cap = std::min(p->trace_steps, s->trace_cap);
   auto& key = s->g_dream_key;
@@ -1665,7 +1700,8 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = salloc(s, &s->q, static_cast<size_t>(R) * qd)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->attn, static_cast<size_t>(R) * qd)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->act, static_cast<size_t>(R) * m->I)) != DRT_OK) return fail(rc);
-  if ((rc = salloc(s, &s->xf, static_cast<size_t>(s->head_cap) * H)) != DRT_OK) return fail(rc);
+  const int xf_rows = std::max(s->head_cap, 128);  // the final-norm rows, at least one 128-row box
+  if ((rc = salloc(s, &s->xf, static_cast<size_t>(xf_rows) * H)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->logits, static_cast<size_t>(s->head_cap) * m->V)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->ss, static_cast<size_t>(kMaxFwdRows) * (H / 128))) != DRT_OK) return fail(rc);
   if (m->shard.world > 1) {
@@ -1751,18 +1787,20 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = salloc(s, &s->sel_pidx, np)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->sel_psum, np)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->sel_cnt, kMaxFrontier)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->sel_skey, np)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->sel_skey2, np)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->sel_sidx, np)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->sel_amax, kMaxFrontier)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->sel_sum, kMaxFrontier)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->conf, s->head_cap)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->token, s->head_cap)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->scope_rows, s->head_cap)) != DRT_OK) return fail(rc);
   if (cudaMemset(s->sel_cnt, 0, sizeof(int) * kMaxFrontier) != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "memset failed"));
+  if ((rc = salloc(s, &s->row_tie, s->head_cap)) != DRT_OK) return fail(rc);
   if (dream) {
-    if ((rc = salloc(s, &s->row_tie, s->head_cap)) != DRT_OK) return fail(rc);
     if ((rc = salloc(s, &s->d_fpos, s->head_cap)) != DRT_OK) return fail(rc);
     if ((rc = salloc(s, &s->dstate, 1)) != DRT_OK) return fail(rc);
     if (cudaMallocHost(&s->hdstate, sizeof(DreamState)) != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "pinned alloc failed"));
-    if ((rc = map_matrix(&s->m_xf128, s->xf, s->head_cap, H, 128)) != DRT_OK) return fail(rc);
     if (s->head_cap >= 256 && (rc = map_matrix(&s->m_xf256, s->xf, s->head_cap, H, 256)) != DRT_OK) return fail(rc);
   }
   if ((rc = salloc(s, &s->status, 1)) != DRT_OK) return fail(rc);
@@ -1783,6 +1821,7 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = map_matrix(&s->m_act64, s->act, R, m->I, 64)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_act128, s->act, R, m->I, 128)) != DRT_OK) return fail(rc);
   if ((rc = map_matrix(&s->m_xf64, s->xf, s->head_cap, H, 64)) != DRT_OK) return fail(rc);
+  if ((rc = map_matrix(&s->m_xf128, s->xf, xf_rows, H, 128)) != DRT_OK) return fail(rc);
   {
     const uint64_t dq[3] = {128, static_cast<uint64_t>(m->nq), static_cast<uint64_t>(R)};
     const uint64_t sq[2] = {256, static_cast<uint64_t>(qd) * 2};
@@ -1836,15 +1875,23 @@ extern "C" int drt_session_kv_pointers(drt_session* s, void** k, void** v) {
 extern "C" int drt_session_start(drt_session* s, const int32_t* x, int32_t n, int32_t prompt_len, int32_t block_size,
                                  int32_t mask_token_id, int32_t exact_kv, int32_t steps, int64_t memory_budget_bytes,
                                  double temperature, uint64_t seed) {
-  (void)exact_kv;
-  (void)seed;
   REQUIRE(s && x, "null argument");
+  // The reference refuses exact K/V on a bidirectional canvas (device_runtime.py:125-126); this
+  // build's bidirectional (entropy_count) sessions decode through drt_session_generate only.
+  REQUIRE(!(s->dream && exact_kv), "bidirectional device generation cannot use exact D2F K/V");
+  if (s->dream)
+    return set_error(DRT_UNSUPPORTED, "an entropy_count session decodes through generate; the bidirectional "
+                                      "propose route (fixed_quota) is not served");
   REQUIRE(n > 0 && n <= s->max_seq, "canvas length %d outside [1, %d]", n, s->max_seq);
   REQUIRE(prompt_len >= 0 && prompt_len <= n, "prompt_len outside the canvas");
   REQUIRE(block_size >= 1 && block_size <= 32, "block_size must be in [1, 32]");
   REQUIRE(steps >= 1, "steps must be >= 1");
   REQUIRE(memory_budget_bytes >= 0, "memory_budget_bytes must be >= 0");
-  if (temperature != 0.0) return set_error(DRT_UNSUPPORTED, "this device session scores at temperature 0 only");
+  REQUIRE(std::isfinite(temperature) && temperature >= 0.0, "temperature must be finite and >= 0");
+  // Above temperature 0 the fixed-quota policy draws each row's token (TopConfidence with sampling,
+  // diffusion_runtime.py:796-828); the threshold policy refuses a temperature (device_runtime.py:207-213).
+  REQUIRE(temperature == 0.0 || s->cfg.decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA,
+          "the block_threshold policy scores at temperature 0 only");
   if (memory_budget_bytes > 0 && memory_budget_bytes < s->bytes + s->m->bytes)
     return set_error(DRT_INVALID_ARGUMENT, "memory budget %lld below the session's %lld device bytes",
                      static_cast<long long>(memory_budget_bytes), static_cast<long long>(s->bytes + s->m->bytes));
@@ -1855,12 +1902,16 @@ extern "C" int drt_session_start(drt_session* s, const int32_t* x, int32_t n, in
   s->hstate->canvas_len = n;
   s->hstate->mask_id = mask_token_id;
   s->hstate->active_block = -1;
+  s->hstate->sample_t = temperature;
+  s->hstate->sample_seed = seed;
   CK(cudaMemcpyAsync(s->state, s->hstate, sizeof(DecodeState), cudaMemcpyHostToDevice, s->stream));
   CK(cudaStreamSynchronize(s->stream));
   s->canvas_len = n;
   s->origin = prompt_len;
   s->block_size = block_size;
   s->mask_id = mask_token_id;
+  s->exact_kv = exact_kv != 0;
+  s->propose_count = 0;
   s->started = true;
   return DRT_OK;
 }
@@ -1869,6 +1920,7 @@ extern "C" int drt_session_propose(drt_session* s, const int32_t* frontier, int3
                                    double* scores, int32_t* tokens, int32_t* forwarded) {
   REQUIRE(s && frontier && scores && tokens, "null argument");
   REQUIRE(s->started, "propose_device before start_device");
+  REQUIRE(!s->dream, "an entropy_count session decodes through generate");
   REQUIRE(nf >= 1 && nf <= kMaxFrontier, "frontier size %d outside [1, %d]", nf, kMaxFrontier);
   REQUIRE(window_end >= 1 && window_end <= s->canvas_len, "window_end %d outside [1, %d]", window_end, s->canvas_len);
   REQUIRE(frozen >= 0 && frozen < window_end, "frozen_prefix %d outside [0, window_end)", frozen);
@@ -1885,26 +1937,36 @@ extern "C" int drt_session_propose(drt_session* s, const int32_t* frontier, int3
     s->g_fwd_geom[1] = s->block_size;
   }
   DecodeState* hs = s->hstate;
-  int cache_end = std::min(hs->cache_end, frozen);
+  // exact_kv: the frozen prefix's K/V from earlier forwards is reused (exact under the block-causal
+  // d2f mask, whose frozen rows never attend past the prefix). Without it every forward recomputes
+  // the K/V of the whole window, the reference's cache-off shape.
+  int cache_end = s->exact_kv ? std::min(hs->cache_end, frozen) : 0;
   CK(cudaEventRecord(s->ev0, s->stream));
   int fwd_rows_total = 0;
-  // Final rows that are not cached yet: prefill them when they exceed one block.
-  if (frozen - cache_end > kMaxFwdRows / 2) {
+  // Final rows that are not cached yet: prefill them when they exceed one block, and always on the
+  // first forward (the prompt goes through the prefill path, as in drt_session_generate).
+  if (frozen > cache_end && (cache_end == 0 || frozen - cache_end > kMaxFwdRows / 2)) {
     TRY(prefill(s, cache_end, frozen, s->origin, s->block_size, 0));
     fwd_rows_total += frozen - cache_end;
     cache_end = frozen;
   }
-  hs->fwd_pos0 = cache_end;
-  hs->fwd_rows = window_end - cache_end;
+  // Under dream_ar_shift position p is scored from row p - 1: the row before the frozen boundary
+  // (the shift feeder) is forwarded again when nothing earlier is.
+  const int shift = s->m->cfg.logits_shift ? 1 : 0;
+  const int pos0 = (shift && cache_end > frozen - 1) ? std::max(frozen - 1, 0) : cache_end;
+  hs->shift = shift;
+  hs->fwd_pos0 = pos0;
+  hs->fwd_rows = window_end - pos0;
   hs->kv_len = window_end;
   hs->n_frontier = nf;
   for (int i = 0; i < nf; ++i) {
     hs->frontier_pos[i] = frontier[i];
-    hs->frontier_row[i] = frontier[i] - cache_end;
+    hs->frontier_row[i] = std::max(frontier[i] - shift, 0) - pos0;
   }
   hs->cache_end = frozen;
   hs->action = PLAN_PROCEED;
   hs->exclude_token = s->cfg.decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD ? s->mask_id : -1;
+  hs->forward_count = s->propose_count;  // the sampled draw's forward index
   fwd_rows_total += hs->fwd_rows;
   CK(cudaMemcpyAsync(s->state, hs, sizeof(DecodeState), cudaMemcpyHostToDevice, s->stream));
   CK(cudaGraphLaunch(s->g_fwd, s->stream));
@@ -1918,6 +1980,7 @@ extern "C" int drt_session_propose(drt_session* s, const int32_t* frontier, int3
   s->m_ms += ms;
   s->m_forwards += 1;
   s->m_rows += fwd_rows_total;
+  s->propose_count += 1;
   if (forwarded) *forwarded = fwd_rows_total;
   return DRT_OK;
 }
@@ -1947,8 +2010,9 @@ extern "C" int drt_session_execute_window(drt_session* s, const int32_t* token_i
   REQUIRE(prompt_len >= 0 && prompt_len <= n_tokens && block_size >= 1, "bad mask geometry");
   for (int i = 0; i < n_scope; ++i) REQUIRE(scope[i] >= 0 && scope[i] < n_tokens, "scope position %d outside the window", scope[i]);
   for (int i = 0; i < n_tokens; ++i) REQUIRE(token_ids[i] >= 0 && token_ids[i] < s->m->V, "token outside the vocabulary");
-  // A full-canvas (entropy_count) session forwards the window in one bidirectional pass and applies
-  // the Dream logits convention: position p reads raw row max(p - 1, 0).
+  // A full-canvas (entropy_count) session forwards the window in one bidirectional pass. Under the
+  // Dream logits convention (logits_shift) position p reads raw row max(p - 1, 0).
+  const bool shift = s->m->cfg.logits_shift != 0;
   if (s->dream)
     REQUIRE(n_tokens <= s->rows_cap, "bidirectional window of %d positions exceeds the session's %d rows", n_tokens,
             s->rows_cap);
@@ -1967,14 +2031,15 @@ extern "C" int drt_session_execute_window(drt_session* s, const int32_t* token_i
     f.block_size = block_size;
     f.bidirectional = s->dream ? 1 : 0;
     TRY(enqueue_layers(s, f));
-    // Scope rows inside this chunk, in scope order, up to 64 per head pass.
+    // Scope rows whose raw row lies inside this chunk, in scope order, up to 64 per head pass.
+    auto raw_row = [&](int p) { return shift ? std::max(p - 1, 0) : p; };
     std::vector<int> idx;
     for (int i = 0; i < n_scope; ++i)
-      if (scope[i] >= c0 && scope[i] < c0 + f.rows) idx.push_back(i);
+      if (raw_row(scope[i]) >= c0 && raw_row(scope[i]) < c0 + f.rows) idx.push_back(i);
     for (size_t b = 0; b < idx.size(); b += kMaxFrontier) {
       const int cnt = static_cast<int>(std::min<size_t>(kMaxFrontier, idx.size() - b));
       rows.assign(cnt, 0);
-      for (int j = 0; j < cnt; ++j) rows[j] = (s->dream ? std::max(scope[idx[b + j]] - 1, 0) : scope[idx[b + j]]) - c0;
+      for (int j = 0; j < cnt; ++j) rows[j] = raw_row(scope[idx[b + j]]) - c0;
       CK(cudaMemcpyAsync(s->scope_rows, rows.data(), sizeof(int) * cnt, cudaMemcpyHostToDevice, s->stream));
       TRY(enqueue_head(s, s->scope_rows, cnt, nullptr, false));
       for (int j = 0; j < cnt; ++j)
@@ -2011,6 +2076,9 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
   REQUIRE(canvas_len <= s->max_seq, "canvas of %d positions exceeds the session capacity %d", canvas_len, s->max_seq);
   REQUIRE(std::isfinite(p->confidence_threshold) && p->confidence_threshold >= 0.0 && p->confidence_threshold <= 1.0,
           "confidence_threshold must be finite and in [0, 1]");
+  REQUIRE(std::isfinite(p->temperature) && p->temperature >= 0.0, "temperature must be finite and >= 0");
+  REQUIRE(p->temperature == 0.0 || p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA,
+          "the block_threshold policy scores at temperature 0 only");
   if (p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA)
     REQUIRE(prompt_len % p->block_size == 0, "BD3LM Candidate prompt length must be a multiple of block_size");
   for (int i = 0; i < prompt_len; ++i) {
@@ -2026,7 +2094,9 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
     s->trace_cap = p->trace_steps;
     if (s->g_step) { cudaGraphExecDestroy(s->g_step); s->g_step = nullptr; }
   }
-  s->origin = 0;
+  // d2f mask origin: 0 for the BD3LM graph's absolute blocks, the prompt length for the D2F graph
+  REQUIRE(p->mask_origin >= -1 && p->mask_origin <= prompt_len, "mask_origin outside [-1, prompt_len]");
+  s->origin = p->mask_origin < 0 ? prompt_len : p->mask_origin;
   s->block_size = p->block_size;
   if (s->g_step != nullptr && (s->g_step_geom[0] != s->origin || s->g_step_geom[1] != s->block_size)) {
     cudaGraphExecDestroy(s->g_step);
@@ -2057,6 +2127,9 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
   hs->eos_id = p->eos_token_id;
   hs->threshold = p->confidence_threshold;
   hs->tie_rel = kTieRel;
+  hs->sample_t = p->temperature;
+  hs->sample_seed = p->seed;
+  hs->shift = s->m->cfg.logits_shift ? 1 : 0;
   hs->active_block = -1;
   hs->trace_cap = std::min(p->trace_steps, s->trace_cap);
   if (p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA) {
@@ -2080,10 +2153,10 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
   }
   hs->cache_end = prompt_len;
   CK(cudaMemcpyAsync(s->state, hs, sizeof(DecodeState), cudaMemcpyHostToDevice, s->stream));
-  // Prefill the prompt (block-causal with origin 0).
+  // Prefill the prompt (d2f mask with the request's origin).
   CK(cudaEventRecord(s->ev0, s->stream));
   const int64_t launches0 = g_launches;
-  TRY(prefill(s, 0, prompt_len, 0, p->block_size, 0));
+  TRY(prefill(s, 0, prompt_len, s->origin, p->block_size, 0));
   const int prefill_launches = static_cast<int>(g_launches - launches0);
   CK(cudaEventRecord(s->ev1, s->stream));
   cudaEvent_t e_dec0 = nullptr, e_dec1 = nullptr;
@@ -2169,6 +2242,7 @@ extern "C" int drt_session_tp_connect(drt_session* s, const void* handles, int32
   REQUIRE(s->tp_buf != nullptr, "the session's model is not tensor-parallel");
   REQUIRE(world == s->m->shard.world, "group of %d ranks, model sharded over %d", world, s->m->shard.world);
   REQUIRE(!s->tp_p2p, "session already connected");
+  REQUIRE(2 * static_cast<unsigned long long>(s->m->L) < kTpTagSpan, "%d layers exceed the peer-flag tag span", s->m->L);
   CK(cudaSetDevice(s->device));
   const int me = s->m->shard.rank;
   for (int r = 0; r < world; ++r) {
@@ -2191,6 +2265,23 @@ extern "C" int drt_session_tp_connect(drt_session* s, const void* handles, int32
   s->tp_p2p = true;
   if (s->g_dream) { cudaGraphExecDestroy(s->g_dream); s->g_dream = nullptr; }
   return DRT_OK;
+}
+
+namespace {
+// A flag pair (flag, epoch) that nothing ever raises: the drill's wait can only run out.
+__device__ unsigned long long g_drill_flags[2];
+
+__global__ void peer_wait_drill_kernel(int* status) {
+  tp_wait_flags(&g_drill_flags[0], &g_drill_flags[1], 1, 1, status);
+}
+}  // namespace
+
+extern "C" int drt_session_peer_wait_drill(drt_session* s) {
+  REQUIRE(s, "null session");
+  CK(cudaSetDevice(s->device));
+  CK(launch_k(peer_wait_drill_kernel, dim3(1), dim3(32), 0, s->stream, false, s->status));
+  CK(cudaStreamSynchronize(s->stream));
+  return check_status(s);
 }
 
 extern "C" int drt_entropy_count_schedule(int32_t n_masked, int32_t steps, double eps, int32_t* transfer) {
@@ -2218,7 +2309,9 @@ extern "C" int drt_session_metrics(drt_session* s, drt_metrics* out) {
 extern "C" size_t drt_selector_scratch_bytes(int32_t n_rows, int32_t vocab) {
   const size_t chunks = (static_cast<size_t>(std::max(vocab, 1)) + kSelChunk - 1) / kSelChunk;
   const size_t np = static_cast<size_t>(std::max(n_rows, 1)) * chunks;
-  return 256 + np * (4 + 4 + 8) + static_cast<size_t>(std::max(n_rows, 1)) * (4 + 8 + 8) + 1024;
+  // chunk partials (max, index, sum; sampled key, runner-up, index), row statistics, counters, and
+  // one 256-byte alignment pad per region
+  return np * (4 + 4 + 8 + 8 + 8 + 4) + static_cast<size_t>(std::max(n_rows, 1)) * (4 + 8 + 8) + 10 * 256;
 }
 
 extern "C" int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows, int32_t vocab, int32_t mode, double temperature,
@@ -2293,6 +2386,52 @@ extern "C" int drt_selector_gather(const float* logits, int64_t ld, const int32_
   a.token = token;
   CK(launch_k(sel_pass1_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
   if (mode == DRT_SELECT_NEG_ENTROPY) CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  return DRT_OK;
+}
+
+extern "C" int drt_selector_sample(const float* logits, int64_t ld, const int32_t* row_index, int32_t n_rows, int32_t vocab,
+                                   double temperature, uint64_t seed, int32_t forward, const int32_t* positions,
+                                   void* scratch, double* conf, int32_t* token, int32_t* tie, void* stream) {
+  REQUIRE(logits && positions && scratch && conf && token, "null argument");
+  REQUIRE(n_rows >= 0 && vocab >= 1 && ld >= vocab, "bad selector geometry");
+  REQUIRE(std::isfinite(temperature) && temperature > 0.0, "sampling needs a finite temperature > 0");
+  REQUIRE(forward >= 0, "forward index must be >= 0");
+  if (n_rows == 0) return DRT_OK;
+  REQUIRE(n_rows <= 65535, "at most 65535 rows per call");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int chunks = (vocab + kSelChunk - 1) / kSelChunk;
+  const size_t np = static_cast<size_t>(n_rows) * chunks;
+  uint8_t* p = static_cast<uint8_t*>(scratch);
+  auto take = [&](size_t bytes) { uint8_t* q = p; p += (bytes + 255) & ~size_t(255); return q; };
+  SelArgs a;
+  memset(&a, 0, sizeof(a));
+  a.part_sum = reinterpret_cast<double*>(take(np * 8));
+  a.part_skey = reinterpret_cast<double*>(take(np * 8));
+  a.part_skey2 = reinterpret_cast<double*>(take(np * 8));
+  a.row_amax = reinterpret_cast<double*>(take(static_cast<size_t>(n_rows) * 8));
+  a.row_sum = reinterpret_cast<double*>(take(static_cast<size_t>(n_rows) * 8));
+  a.part_max = reinterpret_cast<float*>(take(np * 4));
+  a.part_idx = reinterpret_cast<int*>(take(np * 4));
+  a.part_sidx = reinterpret_cast<int*>(take(np * 4));
+  a.counters = reinterpret_cast<int*>(take(static_cast<size_t>(n_rows) * 4));
+  CK(cudaMemsetAsync(a.counters, 0, sizeof(int) * n_rows, st));
+  a.logits = logits;
+  a.ld = ld;
+  a.row_index = row_index;
+  a.rows = n_rows;
+  a.vocab = vocab;
+  a.chunk = kSelChunk;
+  a.nchunks = chunks;
+  a.mode = SEL_SAMPLE;
+  a.exclude = -1;
+  a.sample_t = temperature;
+  a.sample_seed = seed;
+  a.sample_forward = forward;
+  a.positions = positions;
+  a.row_tie = tie;
+  a.conf = conf;
+  a.token = token;
+  CK(launch_k(sel_pass1_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
   return DRT_OK;
 }
 
@@ -2453,24 +2592,60 @@ constexpr size_t kNoAllocScratchBytes = kNoAllocMaxParts * (8 + 4 + 4) + static_
 static __device__ __align__(256) uint8_t g_selector_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mutex;
-void* g_noalloc_ptr[64] = {};
+struct NoAllocEntry {
+  unsigned long long ctx_id;  // process-unique id of the CUDA context (cuCtxGetId)
+  void* ptr;
+};
+std::vector<NoAllocEntry> g_noalloc_cache;
 
-// Device address of g_selector_scratch on the current device. In host code the symbol is only a
-// host-side stand-in, so the address is looked up once per device (with that device current) and
-// cached.
-int noalloc_scratch(void** out) {
-  int dev = -1;
-  CK(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return set_error(DRT_UNSUPPORTED, "device ordinal %d outside [0, 64)", dev);
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_ptr[dev] == nullptr) {
+// Id of the calling thread's current CUDA context; false when no context is current yet. Context ids
+// are unique for the life of the process, so a context created after cudaDeviceReset (or another
+// context on the same device) never matches an address cached for an earlier one.
+bool current_ctx_id(unsigned long long* id) {
+  typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+  typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_selector_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return set_error(DRT_INTERNAL_ERROR, "cudaGetSymbolAddress(selector scratch) failed: %s", cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = p;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr) return false;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Device address of g_selector_scratch in the current context. In host code the symbol is only a
+// host-side stand-in, so the address is looked up once per context (with its device current) and
+// cached under the context's id.
+int noalloc_scratch(void** out) {
+  unsigned long long id = 0;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (current_ctx_id(&id)) {
+    for (const NoAllocEntry& e : g_noalloc_cache)
+      if (e.ctx_id == id) {
+        *out = e.ptr;
+        return DRT_OK;
+      }
   }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_selector_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(DRT_INTERNAL_ERROR, "cudaGetSymbolAddress(selector scratch) failed: %s", cudaGetErrorString(e));
+  // The lookup made the device's primary context current if none was.
+  if (!current_ctx_id(&id)) return set_error(DRT_INTERNAL_ERROR, "no current CUDA context after the symbol lookup");
+  if (g_noalloc_cache.size() >= 64) g_noalloc_cache.erase(g_noalloc_cache.begin());
+  g_noalloc_cache.push_back({id, p});
+  *out = p;
   return DRT_OK;
 }
 }  // namespace

@@ -22,6 +22,7 @@ enum DeviceError : int {
   DEV_TIMEOUT_EPI = 3,
   DEV_BAD_SHAPE = 4,
   DEV_TIMEOUT_PEER = 5,  // a tensor-parallel peer's partials did not arrive in time
+  DEV_BAD_GEOMETRY = 6,  // a kernel's launch geometry does not cover its work (host planning bug)
 };
 
 // System-scope release store / acquire load (flags written over NVLink by another GPU).
@@ -53,6 +54,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 __device__ __forceinline__ void record_error(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
+}
+
+// Tensor-parallel flag values. Each forward ticks an epoch; a row-split linear of layer l raises
+// epoch * kTpTagSpan + tag with tag = 2 l (o_proj) or 2 l + 1 (down_proj), and a reducer waits for
+// a value >= that. Tags stay below kTpTagSpan (sessions refuse models with 2 L >= kTpTagSpan), so
+// every flag of epoch E is below every flag of epoch E + 1 and a stale flag never satisfies a
+// later forward's wait.
+constexpr unsigned long long kTpTagSpan = 1ull << 16;
+__host__ __device__ __forceinline__ unsigned long long tp_flag_value(unsigned long long epoch, int tag) {
+  return epoch * kTpTagSpan + static_cast<unsigned long long>(tag);
 }
 
 // ---------------------------------------------------------------- mbarrier

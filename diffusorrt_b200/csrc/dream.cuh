@@ -30,6 +30,7 @@ struct DreamState {
   int k;                // transfer count of this step
   int forward_count, committed_count, near_tie_steps, exact_tie_steps;
   int trace_cap;
+  int shift;            // dream_ar_shift: position p is scored from row max(p - 1, 0), else row p
 };
 
 // Block-wide exclusive prefix of a 0/1 flag per thread; returns the block total.
@@ -71,7 +72,7 @@ __global__ void __launch_bounds__(kDreamThreads) dream_plan_kernel(DreamState* s
     const int tot = dream_block_scan(f, warp_tot, &slot);
     if (f && n + slot < kDreamMaxFrontier) {
       frontier_pos[n + slot] = p;
-      frontier_row[n + slot] = p > 0 ? p - 1 : 0;
+      frontier_row[n + slot] = st->shift ? (p > 0 ? p - 1 : 0) : p;
     }
     n += tot;
   }

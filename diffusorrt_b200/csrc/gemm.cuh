@@ -75,7 +75,7 @@ struct GemmArgs {
   int q_groups;
   // EPI_TP_PUSH: per rank r, this rank's slot of r's receive buffer ([rows][ld_out] f32) and this
   // rank's flag in r's flag array; a local arrival counter; the forward's epoch and this linear's tag
-  // (the flag value is epoch * 64 + tag). Feature tile t (128 features) is owned by rank t % world.
+  // (the flag value is tp_flag_value(epoch, tag)). Feature tile t (128 features) is owned by rank t % world.
   float* tp_dst[kTpMaxRanks];
   unsigned long long* tp_flag[kTpMaxRanks];
   int* tp_count;
@@ -494,8 +494,8 @@ __global__ void __launch_bounds__(128, 1)
         const int total = static_cast<int>(gridDim.x * gridDim.y * gridDim.z);
         if (atomicAdd(a.tp_count, 1) + 1 == total) {
           __threadfence_system();
-          const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(a.tp_epoch) * 64ull +
-                                       static_cast<unsigned long long>(a.tp_tag);
+          const unsigned long long e =
+              tp_flag_value(*reinterpret_cast<const volatile unsigned long long*>(a.tp_epoch), a.tp_tag);
           for (int r = 0; r < a.tp_world; ++r) st_release_sys(a.tp_flag[r], e);
           *a.tp_count = 0;
         }

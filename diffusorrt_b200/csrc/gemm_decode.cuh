@@ -630,8 +630,6 @@ __device__ __forceinline__ void lm_run(const CUtensorMap* tmA, const CUtensorMap
       if (!ok) {
         record_error(a.status, DEV_TIMEOUT_MMA);
         flags[0] = 1;
-        umma_commit(drain);  // every UMMA issued so far completes before TMEM is released
-        mbar_wait(drain, 0);
       }
     }
     __syncwarp();
@@ -737,6 +735,12 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                rows_valid);
 
   __syncthreads();
+  if (flags[0] != 0 && warp == 5 && (tid & 31) == 0) {
+    // A wait gave up (in whichever warp): every UMMA this thread issued completes before TMEM is
+    // released, since the epilogue may have stopped reading while MMAs were still in flight.
+    umma_commit(drain);
+    mbar_wait(drain, 0);
+  }
   if (flags[0] != 0 && tid == 0) {
     // A wait gave up: let every copy this CTA requested land before the shared memory goes away.
     // The producer runs at most `stages` blocks ahead of the last block whose bytes landed, so the

@@ -36,6 +36,9 @@ struct DecodeState {
   int exclude_token;  // scored as -inf by the selector (block threshold excludes MASK), -1 none
   double threshold;
   double tie_rel;
+  double sample_t;                 // fixed quota: Gumbel temperature (0 = argmax), selector.cuh
+  unsigned long long sample_seed;  // keys the draws with forward_count and the row's position
+  int shift;                       // dream_ar_shift: position p is scored from forwarded row p - 1
   // loop state
   int step, stopped, action, error;
   int cache_end;
@@ -171,6 +174,9 @@ __global__ void plan_kernel(DecodeState* st, const int* x) {
   }
   if (lane == 0) {
     int pos0 = st->cache_end < frozen ? st->cache_end : frozen;
+    // Under dream_ar_shift the first frontier row reads the hidden state of the row before it: that
+    // feeder row is forwarded again (its K/V are rewritten from the same final tokens).
+    if (st->shift && pos0 > frozen - 1) pos0 = max(frozen - 1, 0);
     const int rows = window_end - pos0;
     if (rows > kMaxFwdRows || nf > kMaxFrontier) {
       st->error = 1;
@@ -182,13 +188,16 @@ __global__ void plan_kernel(DecodeState* st, const int* x) {
     st->fwd_rows = rows;
     st->kv_len = window_end;
     st->n_frontier = nf;
-    for (int i = 0; i < nf; ++i) st->frontier_row[i] = st->frontier_pos[i] - pos0;
+    for (int i = 0; i < nf; ++i) st->frontier_row[i] = max(st->frontier_pos[i] - st->shift, 0) - pos0;
     st->cache_end = frozen;
   }
 }
 
 // One warp. Chooses rows from the device scores, writes the committed tokens into the canvas.
-__global__ void commit_kernel(DecodeState* st, int* x, const double* conf, const int* token, StepTrace* trace) {
+// row_tie (optional): per-row certification bits of the selector (a sampled token within the noise
+// rounding bound); those of the committed rows join the step's bits.
+__global__ void commit_kernel(DecodeState* st, int* x, const double* conf, const int* token, const int* row_tie,
+                              StepTrace* trace) {
   griddep_wait();
   griddep_launch_dependents();
   const int lane = threadIdx.x;
@@ -268,6 +277,7 @@ __global__ void commit_kernel(DecodeState* st, int* x, const double* conf, const
       if ((chosen >> i) & 1ull) {
         x[st->frontier_pos[i]] = token[i];
         ++nchosen;
+        if (row_tie != nullptr) tie |= row_tie[i] & TIE_NEAR;
       }
     }
     if (trace != nullptr && st->forward_count < st->trace_cap) {

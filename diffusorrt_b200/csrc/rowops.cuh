@@ -154,14 +154,13 @@ __global__ void synth_fill_kernel(__nv_bfloat16* dst, int64_t rows, int64_t cols
 // Tensor parallel, peer-memory form (reduce-scatter then all-gather, both through NVLink stores).
 // Feature tile t (128 features of H) belongs to rank t % world.
 //
-// Bounded wait (thread 0 of each CTA) until flags[r] >= epoch * 64 + tag for every rank r. Once one
+// Bounded wait (thread 0 of each CTA) until flags[r] >= tp_flag_value(epoch, tag) for every rank r. Once one
 // wait has run out, later ones do not wait again: the request is failed already (status word).
 __device__ __forceinline__ bool tp_wait_flags(const unsigned long long* flags, const unsigned long long* epoch, int tag,
                                               int world, int* status) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
-    const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(epoch) * 64ull +
-                                 static_cast<unsigned long long>(tag);
+    const unsigned long long e = tp_flag_value(*reinterpret_cast<const volatile unsigned long long*>(epoch), tag);
     bool good = *reinterpret_cast<volatile int*>(status) != DEV_TIMEOUT_PEER;
     const uint64_t t0 = globaltimer_ns();
     for (int r = 0; r < world && good; ++r) {
@@ -179,7 +178,7 @@ __device__ __forceinline__ bool tp_wait_flags(const unsigned long long* flags, c
   return ok != 0;
 }
 
-// Raise this rank's flag (epoch * 64 + tag) on every rank once all CTAs of the grid have made their
+// Raise this rank's flag (tp_flag_value(epoch, tag)) on every rank once all CTAs of the grid have made their
 // peer stores visible (the last CTA to arrive raises it and resets the counter).
 __device__ __forceinline__ void tp_raise_flags(unsigned long long* const* flag_of_rank, int world, int* count,
                                                const unsigned long long* epoch, int tag) {
@@ -189,8 +188,7 @@ __device__ __forceinline__ void tp_raise_flags(unsigned long long* const* flag_o
     const int total = static_cast<int>(gridDim.x * gridDim.y * gridDim.z);
     if (atomicAdd(count, 1) + 1 == total) {
       __threadfence_system();
-      const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(epoch) * 64ull +
-                                   static_cast<unsigned long long>(tag);
+      const unsigned long long e = tp_flag_value(*reinterpret_cast<const volatile unsigned long long*>(epoch), tag);
       for (int r = 0; r < world; ++r) st_release_sys(flag_of_rank[r], e);
       *count = 0;
     }

@@ -19,7 +19,48 @@
 
 namespace drt {
 
-enum SelMode : int { SEL_MAXPROB = 0, SEL_ENTROPY = 1 };
+enum SelMode : int { SEL_MAXPROB = 0, SEL_ENTROPY = 1, SEL_SAMPLE = 2 };
+
+// Temperature sampling for the fixed-quota policies (TopConfidence at T > 0, sampling_noise and
+// _sampled_max_prob_confidence, python/src/edllm/backends/diffusion_runtime.py:195-253): row r's
+// token is the first argmax of f64(x) + T * f64(g) (product and sum rounded separately), with the
+// float32 Gumbel noise g = -log(-log u) and u = (top 23 bits + 1/2) * 2^-23 of a splitmix64 hash of
+// (seed, forward index, canvas position, token); the row's confidence is the raw softmax
+// probability of that token, exp(x_tok - max) / S. The float32 logs are CUDA's logf, which can
+// differ from the host's in the last bit; that moves a draw only when two keys are within
+// kSampleTieScale * T of each other, and such rows get DRT_TIE_NEAR.
+constexpr unsigned long long kSampleGolden = 0x9E3779B97F4A7C15ull;
+// |g| <= 17 for every u this hash can produce, and one last-bit difference in each f32 log moves g by
+// at most 2^-21 (1 + |g|) < 2^-16: keys closer than 2^-16 T are not certified.
+constexpr double kSampleTieScale = 1.52587890625e-05;  // 2^-16
+
+// splitmix64's output function (Steele, Lea and Flood 2014).
+__device__ __forceinline__ unsigned long long splitmix_mix(unsigned long long z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+// Key of one (seed, forward, position) row: three chained mixes, each adding a golden-ratio step.
+__device__ __forceinline__ unsigned long long sample_row_key(unsigned long long seed, int forward, int position) {
+  unsigned long long k = splitmix_mix(seed + kSampleGolden);
+  k = splitmix_mix(k + static_cast<unsigned long long>(forward + 1) * kSampleGolden);
+  return splitmix_mix(k + static_cast<unsigned long long>(position + 1) * kSampleGolden);
+}
+__device__ __forceinline__ float sample_gumbel(unsigned long long row_key, int token) {
+  const unsigned long long bits = splitmix_mix(row_key + static_cast<unsigned long long>(token + 1) * kSampleGolden);
+  const float u = (static_cast<float>(bits >> 41) + 0.5f) * 1.1920928955078125e-07f;  // 2^-23, exact
+  return -logf(-logf(u));
+}
+// Best key (lowest index among equals) and the runner-up value, merged in a fixed order.
+__device__ __forceinline__ void top2_merge(double& b1, int& i1, double& b2, double v1, int j1, double v2) {
+  if (v1 > b1 || (v1 == b1 && j1 < i1)) {
+    b2 = fmax(b1, v2);
+    b1 = v1;
+    i1 = j1;
+  } else {
+    b2 = fmax(b2, v1);
+  }
+}
 
 struct SelArgs {
   const float* logits;
@@ -43,9 +84,22 @@ struct SelArgs {
   double* conf;           // [rows]
   int* token;             // [rows]
   int* status;
+  // SEL_SAMPLE, or SEL_MAXPROB with *sample_t_dev > 0: the Gumbel draw (see above)
+  double sample_t;              // temperature (mode SEL_SAMPLE)
+  const double* sample_t_dev;   // optional device-side temperature (a graph replays either mode)
+  unsigned long long sample_seed;
+  const unsigned long long* sample_seed_dev;
+  int sample_forward;           // forward index keying the draw
+  const int* sample_forward_dev;
+  const int* positions;         // [rows] canvas position of each row
+  double* part_skey;            // [rows * nchunks] best sampled key of each chunk
+  double* part_skey2;           // runner-up key
+  int* part_sidx;               // index of the best key
+  int* row_tie;                 // optional [rows]: DRT_TIE_NEAR when the sampled argmax is not certified
 };
 
 constexpr int kSelThreads = 256;
+constexpr int TIE_NEAR_BIT = 1;  // DRT_TIE_NEAR
 constexpr int kSelChunk = 8192;  // logits per CTA: 32 per thread
 
 __device__ __forceinline__ void argmax_merge(float& m, int& idx, float m2, int idx2) {
@@ -115,7 +169,43 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
   int bi = s_i[0];
   for (int w = 1; w < kSelThreads / 32; ++w) argmax_merge(bm, bi, s_m[w], s_i[w]);
 
-  const double inv_t = sel_inv_t(a.temperature);
+  const double samp_t = a.sample_t_dev != nullptr ? *a.sample_t_dev : a.sample_t;
+  const bool sample = (a.mode == SEL_SAMPLE || (a.mode == SEL_MAXPROB && a.sample_t_dev != nullptr)) && samp_t > 0.0;
+  __shared__ double s_k1[kSelThreads / 32], s_k2[kSelThreads / 32];
+  __shared__ int s_ki[kSelThreads / 32];
+  double k1 = -INFINITY, k2 = -INFINITY;
+  int ki = INT_MAX;
+  if (sample) {
+    const unsigned long long seed = a.sample_seed_dev != nullptr ? *a.sample_seed_dev : a.sample_seed;
+    const int fwd = a.sample_forward_dev != nullptr ? *a.sample_forward_dev : a.sample_forward;
+    const unsigned long long rk = sample_row_key(seed, fwd, a.positions[r]);
+    // This thread's values in ascending index order: strict > keeps the lowest index among equals.
+#pragma unroll
+    for (int k = 0; k < kSelChunk / (kSelThreads * 4); ++k) {
+      const int base = lo + (k * kSelThreads + tid) * 4;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (base + e >= hi) continue;
+        const double key = __dadd_rn(static_cast<double>(vals[k * 4 + e]),
+                                     __dmul_rn(samp_t, static_cast<double>(sample_gumbel(rk, base + e))));
+        if (key > k1) { k2 = k1; k1 = key; ki = base + e; }
+        else if (key > k2) { k2 = key; }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const double v1 = __shfl_xor_sync(0xffffffffu, k1, o);
+      const int j1 = __shfl_xor_sync(0xffffffffu, ki, o);
+      const double v2 = __shfl_xor_sync(0xffffffffu, k2, o);
+      top2_merge(k1, ki, k2, v1, j1, v2);
+    }
+    if ((tid & 31) == 0) { s_k1[tid >> 5] = k1; s_ki[tid >> 5] = ki; s_k2[tid >> 5] = k2; }
+    __syncthreads();
+    k1 = s_k1[0]; ki = s_ki[0]; k2 = s_k2[0];
+    for (int w = 1; w < kSelThreads / 32; ++w) top2_merge(k1, ki, k2, s_k1[w], s_ki[w], s_k2[w]);
+  }
+
+  const double inv_t = sample ? 1.0 : sel_inv_t(a.temperature);
   const double amax = sel_adjust(static_cast<double>(bm), inv_t);
   double sum = 0.0;
 #pragma unroll
@@ -134,6 +224,11 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
     a.part_max[slot] = bm;
     a.part_idx[slot] = bi;
     a.part_sum[slot] = bs;
+    if (sample) {
+      a.part_skey[slot] = k1;
+      a.part_sidx[slot] = ki;
+      a.part_skey2[slot] = k2;
+    }
     __threadfence();
     const int old = atomicAdd(&a.counters[r], 1);
     s_last = (old == a.nchunks - 1);
@@ -154,8 +249,23 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
     const double cam = sel_adjust(static_cast<double>(cm), inv_t);
     S += (cam == gam) ? cs : cs * exp_nonpos(cam - gam);
   }
+  if (sample) {
+    double g1 = -INFINITY, g2 = -INFINITY;
+    int gj = INT_MAX;
+    for (int k = 0; k < a.nchunks; ++k)
+      top2_merge(g1, gj, g2, __ldcg(&a.part_skey[r * a.nchunks + k]), __ldcg(&a.part_sidx[r * a.nchunks + k]),
+                 __ldcg(&a.part_skey2[r * a.nchunks + k]));
+    if (gj < 0 || gj >= a.vocab) gj = gi;  // every key -inf (an all -inf row): keep the first max
+    a.token[r] = gj;
+    const float xt = (gj == excl) ? -INFINITY : x[gj];
+    a.conf[r] = __ddiv_rn(exp_nonpos(static_cast<double>(xt) - gam), S);
+    if (a.row_tie != nullptr) a.row_tie[r] = (g1 - g2 <= kSampleTieScale * samp_t) ? TIE_NEAR_BIT : 0;
+    a.counters[r] = 0;
+    return;
+  }
+  if (a.row_tie != nullptr) a.row_tie[r] = 0;
   a.token[r] = gi;
-  if (a.mode == SEL_MAXPROB) {
+  if (a.mode == SEL_MAXPROB || a.mode == SEL_SAMPLE) {
     a.conf[r] = 1.0 / S;
   } else {
     a.row_amax[r] = gam;

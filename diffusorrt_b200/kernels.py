@@ -40,6 +40,31 @@ def select_rows(logits: torch.Tensor, *, mode: int = _lib.SELECT_MAX_PROB, tempe
     return conf, token
 
 
+def select_sample(logits: torch.Tensor, positions: torch.Tensor, *, temperature: float, seed: int, forward: int,
+                  row_index: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None):
+    """Temperature-sampled (confidence f64, token i32, tie i32) per row of f32 logits [rows, vocab]
+    (or of the rows row_index), keyed by (seed, forward, positions[r]) as drt_selector_sample."""
+    if logits.dtype != torch.float32 or not logits.is_cuda or logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a row-major CUDA float32 [rows, vocab] tensor")
+    if positions.dtype != torch.int32 or not positions.is_cuda or not positions.is_contiguous():
+        raise ValueError("positions must be a contiguous CUDA int32 tensor")
+    n = positions.numel() if row_index is None else row_index.numel()
+    if row_index is None and n != logits.shape[0]:
+        raise ValueError("one position per logits row")
+    vocab = logits.shape[1]
+    dev = logits.device
+    scratch = selector_scratch(n, vocab, dev)
+    conf = torch.empty(n, dtype=torch.float64, device=dev)
+    token = torch.empty(n, dtype=torch.int32, device=dev)
+    tie = torch.empty(n, dtype=torch.int32, device=dev)
+    _lib.check(_lib.load().drt_selector_sample(logits.data_ptr(), logits.stride(0),
+                                               0 if row_index is None else row_index.data_ptr(), n, vocab,
+                                               float(temperature), int(seed) & (2**64 - 1), int(forward),
+                                               positions.data_ptr(), scratch.data_ptr(), conf.data_ptr(),
+                                               token.data_ptr(), tie.data_ptr(), _stream_ptr(stream)))
+    return conf, token, tie
+
+
 CHOICE_TOPK = 0
 CHOICE_THRESHOLD = 1
 

@@ -41,11 +41,18 @@ _COMMIT_IDS = {"threshold": _lib.COMMIT_THRESHOLD, "fixed_quota": _lib.COMMIT_FI
 _MASK_IDS = {"bidirectional": _lib.MASK_BIDIRECTIONAL, "d2f_hybrid": _lib.MASK_D2F_HYBRID}
 
 
+class DeviceTimeout(RuntimeError):
+    """A bounded device wait ran out (DRT_DEVICE_TIMEOUT): a tensor-parallel peer stopped, or a
+    copy / MMA never completed. The session and the CUDA context stay usable."""
+
+
 def _raise(exc: _lib.DrtError):
     if exc.status == _lib.INVALID_ARGUMENT:
         raise ValueError(str(exc)) from None
     if exc.status == _lib.UNSUPPORTED:
         raise NotImplementedError(str(exc)) from None
+    if exc.status == _lib.DEVICE_TIMEOUT:
+        raise DeviceTimeout(str(exc)) from None
     raise RuntimeError(str(exc)) from None
 
 
@@ -64,6 +71,26 @@ class WindowResult:
     n_rows: int
     n_vocab: int
     forwarded_rows: int
+
+
+def finalize(x: Sequence[int], prompt_len: int, mask_token_id: int, eos_token_id: int) -> dict:
+    """The visible answer of a decoded canvas, as the reference's ``MaskState.finalize``
+    (python/src/edllm/backends/diffusion_runtime.py:526-558): the answer ends at the first EOS of the
+    generated region ("stop"); without EOS, or with masks left in the answer, the reason is
+    "length"; the visible tokens end at the first unresolved (MASK) row."""
+    gen = list(x[prompt_len:])
+    if eos_token_id in gen:
+        answer, hit_eos, reason = gen[:gen.index(eos_token_id)], True, "stop"
+    else:
+        answer, hit_eos, reason = gen, False, "length"
+    remaining = answer.count(mask_token_id)
+    if remaining:
+        reason = "length"
+        visible = answer[:answer.index(mask_token_id)]
+    else:
+        visible = answer
+    return {"visible_token_ids": visible, "hit_eos": hit_eos, "remaining_mask_count": remaining,
+            "finish_reason": reason}
 
 
 def _as_int_list(values, name: str) -> list[int]:
@@ -95,7 +122,8 @@ def _model_config(cfg: Mapping[str, Any], max_seq: int = 128, max_prefill_rows: 
         num_kv_heads=cfg["num_kv_heads"], head_dim=cfg["head_dim"], intermediate_size=cfg["intermediate_size"],
         vocab_size=cfg["vocab_size"], qk_norm=int(bool(cfg["qk_norm"])), qkv_bias=int(bool(cfg["qkv_bias"])),
         tied_lm_head=int(bool(cfg["tied_lm_head"])), rms_norm_eps=float(cfg["rms_norm_eps"]),
-        rope_theta=float(cfg["rope_theta"]), max_seq=int(max_seq), max_prefill_rows=int(max_prefill_rows))
+        rope_theta=float(cfg["rope_theta"]), max_seq=int(max_seq), max_prefill_rows=int(max_prefill_rows),
+        logits_shift=int(bool(cfg.get("logits_shift", False))))
 
 
 def tp_shard(lib, cfg: Mapping[str, Any], rank: int, world: int) -> dict:
@@ -347,22 +375,36 @@ class Session:
     def generate(self, prompt: Sequence[int], *, max_tokens: int, steps: int, block_size: int | None = None,
                  decode_strategy: str | None = None, mask_token_id: int | None = None,
                  eos_token_id: int | None = None, confidence_threshold: float = 0.9, rounds_per_block: int = 0,
-                 trace_steps: int = 0, temperature: float = 0.2, top_p: float | None = 0.95,
-                 eps: float = 1e-3) -> dict:
+                 trace_steps: int = 0, temperature: float | None = None, top_p: float | None = 0.95,
+                 eps: float = 1e-3, seed: int = 0, mask_origin: int | str | None = None) -> dict:
         """Whole request on the device. ``decode_strategy="entropy_count"`` (a session opened with
         that strategy) runs the Dream full-canvas schedule with NegEntropy(temperature, top_p) and
-        linspace(1, eps, steps + 1) timesteps; the others run the BD3 / block-threshold loops."""
+        linspace(1, eps, steps + 1) timesteps (temperature defaults to 0.2); the others run the BD3 /
+        block-threshold loops, where ``temperature`` > 0 (bd3_fixed_quota only) draws each row's token
+        keyed by ``seed`` (default 0: argmax). ``mask_origin`` is the d2f mask geometry's origin: 0
+        for the BD3LM graph's absolute blocks, ``"prompt"`` for the Dream D2F graph (prompt
+        bidirectional, blocks counted from it); by default the model config's ``mask_origin`` (0).
+        The result carries the final canvas ``x`` and the reference's finalize fields
+        (``visible_token_ids``, ``hit_eos``, ``remaining_mask_count``, ``finish_reason``)."""
         cfg = self.runtime.config
         ids = _as_int_list(prompt, "prompt")
+        strategy = self.decode_strategy if decode_strategy is None else _enum(decode_strategy, _STRATEGY_IDS,
+                                                                             "decode_strategy")
+        if temperature is None:
+            temperature = 0.2 if strategy == _lib.STRATEGY_ENTROPY_COUNT else 0.0
+        if mask_origin is None:
+            mask_origin = cfg.get("mask_origin", 0)
+        origin = -1 if mask_origin == "prompt" else int(mask_origin)
+        mask_id = int(cfg["mask_token_id"] if mask_token_id is None else mask_token_id)
+        eos_id = int(cfg["eos_token_id"] if eos_token_id is None else eos_token_id)
         params = _lib.GenerateParams(
-            decode_strategy=(self.decode_strategy if decode_strategy is None
-                             else _enum(decode_strategy, _STRATEGY_IDS, "decode_strategy")), steps=int(steps),
+            decode_strategy=strategy, steps=int(steps),
             block_size=int(block_size or self.block_size), max_tokens=int(max_tokens),
-            mask_token_id=int(cfg["mask_token_id"] if mask_token_id is None else mask_token_id),
-            eos_token_id=int(cfg["eos_token_id"] if eos_token_id is None else eos_token_id),
+            mask_token_id=mask_id, eos_token_id=eos_id,
             confidence_threshold=float(confidence_threshold), rounds_per_block=int(rounds_per_block),
             trace_steps=int(trace_steps), temperature=float(temperature),
-            top_p=1.0 if top_p is None else float(top_p), eps=float(eps))
+            top_p=1.0 if top_p is None else float(top_p), eps=float(eps), seed=int(seed) & (2**64 - 1),
+            mask_origin=origin)
         out = (ctypes.c_int32 * (len(ids) + int(max_tokens)))()
         res = _lib.GenerateResult()
         trace = (_lib.StepTrace * max(1, int(trace_steps)))() if trace_steps else None
@@ -370,6 +412,7 @@ class Session:
                                              ctypes.byref(res), trace))
         result = {name: getattr(res, name) for name, _ in _lib.GenerateResult._fields_}
         result["x"] = list(out)
+        result.update(finalize(result["x"], len(ids), mask_id, eos_id))
         if trace is not None:
             steps_out = []
             for t in trace[: min(res.forward_count, int(trace_steps))]:
@@ -379,6 +422,11 @@ class Session:
                                   "chosen": [i for i in range(n) if (t.chosen_mask >> i) & 1]})
             result["trace"] = steps_out
         return result
+
+    def peer_wait_drill(self) -> None:
+        """Run one bounded peer-flag wait that nothing satisfies (drt_session_peer_wait_drill);
+        raises DeviceTimeout after the wait limit, leaving the session usable."""
+        _call(self._lib.drt_session_peer_wait_drill(self._s))
 
     def kv_pointers(self) -> tuple[int, int]:
         k, v = ctypes.c_void_p(), ctypes.c_void_p()

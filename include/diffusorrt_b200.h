@@ -94,6 +94,8 @@ typedef struct drt_model_config {
   float rope_theta;
   int32_t max_seq;           /* K/V capacity in positions */
   int32_t max_prefill_rows;  /* rows per prefill chunk (activation capacity) */
+  int32_t logits_shift;      /* 1: dream_ar_shift (position p is scored from the logits of row
+                                max(p - 1, 0), mlx_ops.shift_logits_for_dream); 0: row p itself */
 } drt_model_config;
 
 /* Session config: the keys RuntimeHandle._generate_cuda_native passes to
@@ -120,9 +122,15 @@ typedef struct drt_generate_params {
   int32_t trace_steps;         /* record up to this many drt_step_trace entries */
   /* entropy_count (full-canvas masked diffusion): EntropyCountStrategy(temperature, top_p, eps),
    * python/src/edllm/backends/diffusion_runtime.py:2079-2110. */
-  double temperature;          /* NegEntropy logits / T (<= 0: no scaling) */
+  double temperature;          /* entropy_count: NegEntropy logits / T (<= 0: no scaling);
+                                  bd3_fixed_quota: sampling temperature (0: argmax), as drt_selector_sample;
+                                  block_threshold: must be 0 */
   double top_p;                /* nucleus mass (>= 1: no nucleus) */
   double eps;                  /* last timestep of linspace(1, eps, steps + 1) */
+  uint64_t seed;               /* bd3_fixed_quota at temperature > 0: keys the draws */
+  int32_t mask_origin;         /* d2f mask geometry origin: 0 = absolute blocks from position 0 (the
+                                  BD3LM graph), -1 = the prompt length (prompt bidirectional, blocks
+                                  counted from it: the Dream D2F graph), else that position */
 } drt_generate_params;
 
 typedef struct drt_generate_result {
@@ -195,6 +203,11 @@ int drt_model_quantize(drt_model* model, int32_t bits, int32_t group_size);
 void drt_model_destroy(drt_model* model);
 /* Shard of rank `rank` in a group of `world` (host only; no device call). */
 int drt_tp_shard_geometry(const drt_model_config* config, int32_t rank, int32_t world, drt_tp_shard* out);
+/* The value a row-split linear raises in the peers' flag arrays for forward `epoch`, layer `layer`,
+ * which = 0 (o_proj) or 1 (down_proj); reducers wait for a value >= it. Host only: exposed so the
+ * epoch / tag arithmetic can be checked without a GPU (every flag of one epoch lies below every flag
+ * of the next for any layer count a session accepts). */
+uint64_t drt_tp_flag_value(uint64_t epoch, int32_t layer, int32_t which);
 /* A new NCCL unique id (DRT_TP_ID_BYTES bytes) for drt_model_create_tp; made by one rank and
  * shared with the others by the caller (torch.distributed in the Python binding). */
 int drt_tp_unique_id(uint8_t* id);
@@ -212,7 +225,15 @@ int drt_model_create_tp(const drt_model_config* config, int32_t device_ordinal, 
 int drt_session_open(drt_model* model, const drt_session_config* config, drt_session** out);
 /* Reference: session.start_device(x, prompt_len, block_size, mask_token_id, exact_kv, steps,
  * memory_budget_bytes, temperature, seed) (python/src/edllm/backends/device_runtime.py:140-150).
- * `prompt_len` is the mask-geometry origin (0 for BD3's absolute blocks). */
+ * `prompt_len` is the mask-geometry origin (0 for BD3's absolute blocks).
+ * exact_kv != 0: each propose reuses the K/V of the frozen prefix computed by earlier forwards (exact
+ * under the d2f_hybrid mask); exact_kv == 0: each propose recomputes the whole window's K/V (the
+ * reference's cache-off shape; `forwarded` then counts the whole window). A bidirectional
+ * (entropy_count) session refuses exact_kv (DRT_INVALID_ARGUMENT, as device_runtime.py:125-126) and
+ * decodes through drt_session_generate only (start_device returns DRT_UNSUPPORTED).
+ * temperature > 0 (bd3_fixed_quota only; block_threshold refuses it): each propose draws every
+ * frontier row's token as drt_selector_sample does, keyed by `seed`, the propose's index since
+ * start_device and the row's position; the score is the raw probability of the drawn token. */
 int drt_session_start(drt_session* s, const int32_t* x, int32_t n, int32_t prompt_len, int32_t block_size,
                       int32_t mask_token_id, int32_t exact_kv, int32_t steps, int64_t memory_budget_bytes,
                       double temperature, uint64_t seed);
@@ -243,6 +264,12 @@ int drt_session_generate(drt_session* s, const drt_generate_params* params, cons
  * NCCL all-reduce. Both calls are collective over the group. */
 int drt_session_tp_handle(drt_session* s, void* handle);
 int drt_session_tp_connect(drt_session* s, const void* handles, int32_t world);
+/* Failure-handling drill (no counterpart in the reference, whose ABI reports failures as
+ * INTERNAL_ERROR, python/src/edllm/abi/forward.py:20-25): runs, on the session's stream, the bounded
+ * wait a tensor-parallel reducer makes for a peer's partials, on a flag that nothing raises — what a
+ * rank sees when a peer has stopped. It returns DRT_DEVICE_TIMEOUT once the device wait limit (2 s)
+ * has passed; no GPU fault is raised, and the session, its stream and the context stay usable. */
+int drt_session_peer_wait_drill(drt_session* s);
 /* entropy_count transfer schedule (EntropyCountCommit.plan, diffusion_runtime.py:921-937):
  * timesteps = linspace(1, eps, steps + 1) in float32, transfer[s] = int(N * (1 - t[s+1] / t[s]))
  * (all N remaining on the last step) for s < steps, from n_masked masked positions, N falling by
@@ -280,6 +307,15 @@ int drt_selector_topp(const float* logits, int64_t ld, const int32_t* row_index,
 /* The selector's exp for non-positive arguments (table-driven, Tang 1989), y[i] = exp(x[i]) for
  * x[i] <= 0, on device arrays; exposed so its accuracy against CUDA's exp can be tested. */
 int drt_exp_nonpos(const double* x, double* y, int64_t n, void* stream);
+/* Temperature sampling over rows (row_index NULL: row r) of f32 logits, the reference's
+ * _sampled_max_prob_confidence with sampling_noise (diffusion_runtime.py:195-253): token[r] = the
+ * first argmax over v of f64(x_v) + T * f64(g_v), g = -log(-log u) in float32 with u from a splitmix64
+ * hash of (seed, forward, positions[r] (device int32), v); conf[r] = exp(x_tok - max) / S in f64.
+ * tie (optional) gets DRT_TIE_NEAR where the two best keys lie within 2^-16 T, the most a last-bit
+ * difference of the float32 logs can move a key. Scratch: drt_selector_scratch_bytes. */
+int drt_selector_sample(const float* logits, int64_t ld, const int32_t* row_index, int32_t n_rows, int32_t vocab,
+                        double temperature, uint64_t seed, int32_t forward, const int32_t* positions, void* scratch,
+                        double* conf, int32_t* token, int32_t* tie, void* stream);
 /* Commit choices for a batch of confidence runs: item b owns rows offsets[b] .. offsets[b + 1]
  * (device int32, n_items + 1 entries). mode 0 = top-k (_topk_count_choices,
  * diffusion_runtime.py:290-299: the k highest, lowest row first among equals), mode 1 =
@@ -294,9 +330,10 @@ int drt_select_choices(const double* conf, const int32_t* offsets, int32_t n_ite
  * synchronization. No counterpart in the reference. The scratch is one static device array of
  * about 0.53 MB that every GPU loading this library keeps until exit; calls are limited to
  * n_rows <= 1024 and vocab <= 262144 (larger calls fail with DRT_INVALID_ARGUMENT). The first call
- * on a device looks up the array's device address, so make that first call before any stream
- * capture. All calls share the array: calls that overlap on the GPU (other streams, other
- * threads) race and must be serialized by the caller. */
+ * in each CUDA context looks up the array's device address (cached under the context's id, so a
+ * context made after cudaDeviceReset, or a second context on the same device, looks it up again),
+ * so make that first call before any stream capture. All calls share the array: calls that overlap
+ * on the GPU (other streams, other threads) race and must be serialized by the caller. */
 int drt_selector_rows_noalloc(const float* logits, int64_t ld, int32_t n_rows, int32_t vocab, int32_t mode,
                               double temperature, double* conf, int32_t* token, void* stream);
 /* y = x @ W^T on the tensor cores with the MLX rounding contract (bf16 output rounding when

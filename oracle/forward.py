@@ -99,10 +99,37 @@ def _sdpa32(q, k, v, visible):
     return out.reshape(S, nq * d)
 
 
+def _sdpa_bf16_operands(q, k, v, visible):
+    """``_sdpa32`` with the operand roundings of a bf16 tensor-core attention: Q and K (after QK-norm
+    and RoPE) rounded to bf16, scores accumulated in f32, the unnormalised softmax weights
+    P = 2^(s * log2(e) / sqrt(d) - max) rounded to bf16, O = (P @ V) / sum(P) in f32. V rows are
+    bf16-rounded linear outputs already. Everything else is the f32 contract."""
+    S, nq, d = q.shape
+    rep = nq // k.shape[1]
+    qb, kb = bf16_round(q), bf16_round(k)
+    kk = np.repeat(kb, rep, axis=1)
+    vv = np.repeat(v, rep, axis=1)
+    c = np.float32(math.log2(math.e) / math.sqrt(d))
+    scores = np.einsum("shd,thd->hst", qb, kk, optimize=True).astype(np.float32)
+    scores = np.where(visible[None, :, :], scores, np.float32(-np.inf))
+    m = scores.max(axis=-1, keepdims=True) * c
+    p = bf16_round(np.exp2((scores * c - m).astype(np.float32)))
+    l = p.sum(axis=-1, keepdims=True, dtype=np.float32)
+    out = np.einsum("hst,thd->hsd", p, vv, optimize=True).astype(np.float32) / l
+    return np.transpose(out, (1, 0, 2)).reshape(S, nq * d).astype(np.float32)
+
+
+ATTENTION_OPERANDS = {"f32": _sdpa32, "bf16": _sdpa_bf16_operands}
+
+
 def forward_mlx(weights: dict, cfg: dict, token_ids, *, prompt_len: int = 0, block_size: int = 32,
-                bidirectional: bool = False, output_rows=None, rope=None, quant: dict | None = None) -> np.ndarray:
+                bidirectional: bool = False, output_rows=None, rope=None, quant: dict | None = None,
+                attn_operands: str = "f32") -> np.ndarray:
     """Logits [len(output_rows) (or S), V] f32 of a full-window forward (no cache). With ``quant``
-    (``quantized_weights``), every quantized linear follows the quantized-matmul contract."""
+    (``quantized_weights``), every quantized linear follows the quantized-matmul contract.
+    ``attn_operands="bf16"`` rounds the attention's Q, K and softmax weights to bf16 as tensor-core
+    operands (``_sdpa_bf16_operands``); the default is the reference's f32 attention."""
+    sdpa = ATTENTION_OPERANDS[attn_operands]
     ids = np.asarray(token_ids, dtype=np.int64)
     S = len(ids)
     H, nq, nkv, d = cfg["hidden_size"], cfg["attention_heads"], cfg["num_kv_heads"], cfg["head_dim"]
@@ -131,7 +158,7 @@ def forward_mlx(weights: dict, cfg: dict, token_ids, *, prompt_len: int = 0, blo
             k = _rms32(k, g("self_attn.k_norm.weight"), eps)
         q = _rope32(q, cos_h, sin_h)
         k = _rope32(k, cos_h, sin_h)
-        attn = _sdpa32(q, k, v, vis)
+        attn = sdpa(q, k, v, vis)
         h = (h + lin(attn, "self_attn.o_proj.weight")).astype(np.float32)
         n2 = _rms32(h, g("post_attention_layernorm.weight"), eps)
         gate = lin(n2, "mlp.gate_proj.weight")
@@ -210,3 +237,71 @@ def dream_raw_rows(positions) -> list[int]:
     python/src/edllm/backends/mlx_ops.py:157-159: concatenate(logits[:1], logits[:-1])):
     position p reads raw row max(p - 1, 0)."""
     return [max(int(p) - 1, 0) for p in positions]
+
+
+class PrefixKV:
+    """K (after QK-norm and RoPE) and V of canvas positions [0, length) for every layer, float32:
+    the exact prefix K/V of the reference's d2f path (PrefixKVCacheStrategy,
+    python/src/edllm/backends/mlx_state_cache.py:51-515; the exact-D2F pattern of
+    mlx_d2f_forward.py:205-368). Rows enter only once their tokens are final."""
+
+    def __init__(self, cfg: dict):
+        self.k = [None] * cfg["layer_count"]
+        self.v = [None] * cfg["layer_count"]
+        self.length = 0
+
+
+def forward_mlx_cached(weights: dict, cfg: dict, token_ids, cache: PrefixKV, *, frozen: int, output_rows,
+                       prompt_len: int = 0, block_size: int = 32, rope=None, attn_operands: str = "f32") -> np.ndarray:
+    """``forward_mlx`` logits of ``output_rows`` (absolute positions) for the window ``token_ids``,
+    computing only rows [cache.length, len(token_ids)) against the cached K/V, then caching the
+    rows [cache.length, frozen) (final tokens). Under the block-causal d2f mask a cached row never
+    attends past the frozen prefix, so this equals the cache-free forward (up to float32 summation
+    order)."""
+    ids = np.asarray(token_ids, dtype=np.int64)
+    n = len(ids)
+    c0 = cache.length
+    if not c0 <= frozen <= n:
+        raise ValueError("frozen prefix outside [cache length, window]")
+    H, nq, nkv, d = cfg["hidden_size"], cfg["attention_heads"], cfg["num_kv_heads"], cfg["head_dim"]
+    eps = float(cfg.get("rms_norm_eps", 1e-6))
+    if rope is None:
+        rope = rope_half_tables(n, d, float(cfg.get("rope_theta", 1e6)))
+    cos_h, sin_h = rope[0][c0:n], rope[1][c0:n]
+    S = n - c0
+    vis = visible_mask(np.arange(c0, n), n, prompt_len=prompt_len, block_size=block_size, bidirectional=False)
+    h = np.asarray(weights["model.embed_tokens.weight"], dtype=np.float32)[ids[c0:]].copy()
+    for layer in range(cfg["layer_count"]):
+        p = f"model.layers.{layer}."
+        g = lambda key: weights.get(p + key)  # noqa: E731
+
+        def lin(x, key, bias_key=None):
+            return _lin32(x, g(key), g(bias_key) if bias_key else None)
+
+        x1 = _rms32(h, g("input_layernorm.weight"), eps)
+        q = lin(x1, "self_attn.q_proj.weight", "self_attn.q_proj.bias").reshape(S, nq, d)
+        k = lin(x1, "self_attn.k_proj.weight", "self_attn.k_proj.bias").reshape(S, nkv, d)
+        v = lin(x1, "self_attn.v_proj.weight", "self_attn.v_proj.bias").reshape(S, nkv, d)
+        if g("self_attn.q_norm.weight") is not None:
+            q = _rms32(q, g("self_attn.q_norm.weight"), eps)
+            k = _rms32(k, g("self_attn.k_norm.weight"), eps)
+        q = _rope32(q, cos_h, sin_h)
+        k = _rope32(k, cos_h, sin_h)
+        k_all = k if cache.k[layer] is None else np.concatenate([cache.k[layer], k], axis=0)
+        v_all = v if cache.v[layer] is None else np.concatenate([cache.v[layer], v], axis=0)
+        attn = ATTENTION_OPERANDS[attn_operands](q, k_all, v_all, vis)
+        h = (h + lin(attn, "self_attn.o_proj.weight")).astype(np.float32)
+        x2 = _rms32(h, g("post_attention_layernorm.weight"), eps)
+        gate = lin(x2, "mlp.gate_proj.weight")
+        up = lin(x2, "mlp.up_proj.weight")
+        act = (gate * (np.float32(1.0) / (np.float32(1.0) + np.exp(-gate))) * up).astype(np.float32)
+        h = (h + lin(act, "mlp.down_proj.weight")).astype(np.float32)
+        if frozen > c0:
+            cache.k[layer] = k_all[:frozen]
+            cache.v[layer] = v_all[:frozen]
+    cache.length = max(c0, frozen)
+    rows = np.asarray(output_rows, dtype=np.int64) - c0
+    if rows.min(initial=0) < 0:
+        raise ValueError("output rows inside the cached prefix")
+    hn = _rms32(h[rows], weights["model.norm.weight"], eps)
+    return _lin32(hn, weights["lm_head.weight"])

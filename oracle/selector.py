@@ -112,3 +112,50 @@ def threshold_set_certified(confidence, tau: float, rel: float) -> tuple[set[int
         top = np.sort(c)[::-1]
         ok = ok and bool(top[0] - top[1] > rel * abs(top[0]))
     return chosen, ok
+
+
+_SAMPLE_GOLDEN = np.uint64(0x9E3779B97F4A7C15)
+_M1 = np.uint64(0xBF58476D1CE4E5B9)
+_M2 = np.uint64(0x94D049BB133111EB)
+
+
+def _splitmix_mix(z):
+    z = (z ^ (z >> np.uint64(30))) * _M1
+    z = (z ^ (z >> np.uint64(27))) * _M2
+    return z ^ (z >> np.uint64(31))
+
+
+def sampling_noise(seed: int, forward: int, position: int, vocab: int) -> np.ndarray:
+    """float32 Gumbel noise of one row (``sampling_noise``, diffusion_runtime.py:218-231): a
+    splitmix64 key chained over (seed, forward + 1, position + 1), one more mix per token id + 1,
+    u = (top 23 bits + 1/2) * 2^-23, g = -log(-log u) in float32."""
+    with np.errstate(over="ignore"):
+        key = _splitmix_mix(np.uint64(int(seed) & 0xFFFFFFFFFFFFFFFF) + _SAMPLE_GOLDEN)
+        key = _splitmix_mix(key + np.uint64((int(forward) + 1) & 0xFFFFFFFFFFFFFFFF) * _SAMPLE_GOLDEN)
+        key = _splitmix_mix(key + np.uint64((int(position) + 1) & 0xFFFFFFFFFFFFFFFF) * _SAMPLE_GOLDEN)
+        bits = _splitmix_mix(key + np.arange(1, vocab + 1, dtype=np.uint64) * _SAMPLE_GOLDEN)
+    u = ((bits >> np.uint64(41)).astype(np.float32) + np.float32(0.5)) * np.float32(2.0 ** -23)
+    return -np.log(-np.log(u))
+
+
+def sampled_max_prob_rows(logits, *, temperature: float, seed: int, forward: int, positions):
+    """Sampled token and its raw probability per row (``_sampled_max_prob_confidence``,
+    diffusion_runtime.py:234-253): token = first argmax of f64(x) + T * f64(g) (product and sum
+    rounded separately), confidence = exp(x_tok - max) / sum(exp(x - max)) in float64.
+    Also returns each row's gap between the two best keys (the draw's certification margin)."""
+    rows = np.asarray(logits, dtype=np.float32)
+    if rows.ndim != 2 or len(positions) != rows.shape[0]:
+        raise ValueError("sampling needs one position per logits row")
+    scores = np.empty(rows.shape[0], dtype=np.float64)
+    gaps = np.empty(rows.shape[0], dtype=np.float64)
+    tokens = []
+    for r, pos in enumerate(positions):
+        values = rows[r].astype(np.float64)
+        keys = values + float(temperature) * sampling_noise(seed, forward, int(pos), rows.shape[1]).astype(np.float64)
+        tok = int(np.argmax(keys))
+        top2 = np.partition(keys, -2)[-2:] if keys.size > 1 else np.array([-np.inf, keys[0]])
+        gaps[r] = float(top2[1] - top2[0])
+        weights = np.exp(values - values.max())
+        scores[r] = weights[tok] / weights.sum()
+        tokens.append(tok)
+    return scores, tokens, gaps

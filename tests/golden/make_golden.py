@@ -52,6 +52,18 @@ def _selector(dr) -> dict:
             conf, tok = dr._entropy_confidence(arr, temperature=temp, top_p=top_p)
             out[f"{name}_ent_{tag}_conf"] = np.asarray(conf, dtype=np.float32)
             out[f"{name}_ent_{tag}_tok"] = np.asarray(tok, dtype=np.int64)
+    # Temperature sampling (TopConfidence at T > 0): tokens and raw probabilities of the draws.
+    srng = np.random.default_rng(20261202)
+    for name, arr in (("small", small), ("wide", wide), ("sharp", sharp)):
+        positions = [int(p) for p in srng.integers(0, 5000, size=arr.shape[0])]
+        out[f"{name}_sample_pos"] = np.asarray(positions, dtype=np.int64)
+        for tag, temp, seed, fwd in (("a", 0.7, 11, 0), ("b", 2.0, 2**63 + 3, 17)):
+            conf, tok = dr._sampled_max_prob_confidence(arr, temperature=temp, seed=seed, step=fwd, positions=positions)
+            out[f"{name}_sample_{tag}_conf"] = np.asarray(conf, dtype=np.float64)
+            out[f"{name}_sample_{tag}_tok"] = np.asarray(tok, dtype=np.int64)
+            out[f"{name}_sample_{tag}_args"] = np.asarray([temp, float(seed), float(fwd)], dtype=np.float64)
+            out[f"{name}_sample_{tag}_seed"] = np.asarray([seed], dtype=np.uint64)
+    out["noise_row"] = np.asarray(dr.sampling_noise(5, 2, 40, 4096), dtype=np.float32)
     excl = dr._exclude_mask_token(small[:2], mask_token_id=7)
     out["excl_logits"] = np.asarray(excl, dtype=np.float32)
     confs = rng.random(size=(4, 32))
@@ -97,6 +109,8 @@ def _decode(ds) -> dict:
         mask=250, eos=251, scale=3.0)
     run("bd3_eos", "bd3_fixed_quota", prompt_len=32, gen=128, steps=64, block_size=32, vocab=64,
         mask=60, eos=3, scale=3.0)
+    run("bd3_sampled", "bd3_fixed_quota", prompt_len=32, gen=64, steps=32, block_size=32, vocab=512,
+        mask=500, eos=501, scale=3.0, temperature=0.8, seed=1234)
     run("block_threshold", "block_threshold", prompt_len=32, gen=96, steps=200, block_size=32, vocab=512,
         mask=500, eos=501, scale=6.0, confidence_threshold=0.9)
     run("entropy_count", "entropy_count", prompt_len=16, gen=32, steps=24, block_size=8, vocab=256,

@@ -27,7 +27,7 @@ from oracle.numerics import bf16_round, synth_weights  # noqa: E402
 pytestmark = pytest.mark.gpu
 
 DREAM_SMALL = dict(layer_count=2, hidden_size=256, attention_heads=4, num_kv_heads=2, head_dim=128,
-                   intermediate_size=512, vocab_size=4096, qk_norm=False, qkv_bias=True, tied_lm_head=False,
+                   intermediate_size=512, vocab_size=4096, qk_norm=False, qkv_bias=True, tied_lm_head=False, logits_shift=True,
                    rms_norm_eps=1e-6, rope_theta=1e6, mask_token_id=4000, eos_token_id=4001, block_size=8)
 STD = dict(linear_std=0.05, embed_std=0.05, bias_std=0.02)
 SEED = 21

@@ -51,10 +51,10 @@ def dev():
 
 
 @pytest.mark.parametrize("mode", ["max_prob", "entropy"])
-def test_selector_cfg4_matches_oracle(dev, mode):
+@pytest.mark.parametrize("B,L", [(1, 32), (1, 256), (8, 32), (8, 256)])
+def test_selector_cfg4_matches_oracle(dev, mode, B, L):
     from diffusorrt_b200 import _lib, kernels
-    B, L = 2, 32
-    logits, mask = _case(B, L, seed=11)
+    logits, mask = _case(B, L, seed=11 + B * 1000 + L)
     rows, offsets = _device_rows(mask)
     flat = torch.from_numpy(logits.reshape(B * L, V)).to(dev)
     ridx = torch.tensor(rows, dtype=torch.int32, device=dev)
@@ -94,7 +94,8 @@ def test_selector_cfg4_matches_oracle(dev, mode):
             if tie[b] == 0 and ok:
                 assert got_set == want_set == ref_set, (kind, param, b)
                 certified += 1
-    assert certified >= 6
+    # every decision is certified except where the float64 keys of two rows nearly coincide
+    assert certified >= 3 * B
 
 
 def test_selector_cfg4_full_size_properties(dev):

@@ -95,7 +95,7 @@ def test_propose_agrees_with_window_forward(rt):
     mask = SMALL["mask_token_id"]
     x = prompt + [mask] * 64
     with rt.session({"decode_strategy": "bd3_fixed_quota", "block_size": 32}) as s:
-        s.start_device(x, prompt_len=0, block_size=32, mask_token_id=mask, exact_kv=False, steps=64)
+        s.start_device(x, prompt_len=0, block_size=32, mask_token_id=mask, exact_kv=True, steps=64)
         frontier = list(range(64, 96))
         scores, tokens, fwd = s.propose_device(frontier, window_end=96, frozen_prefix=64)
         assert fwd == 96
@@ -124,7 +124,7 @@ def test_long_prefix_decode_attention(max_seq, n_prefix):
         mask = SMALL["mask_token_id"]
         x = prompt + [mask] * 32
         with r.session({"decode_strategy": "bd3_fixed_quota", "block_size": 32}) as s:
-            s.start_device(x, prompt_len=0, block_size=32, mask_token_id=mask, exact_kv=False, steps=32)
+            s.start_device(x, prompt_len=0, block_size=32, mask_token_id=mask, exact_kv=True, steps=32)
             frontier = list(range(n_prefix, n_prefix + 32))
             scores, tokens, fwd = s.propose_device(frontier, window_end=n_prefix + 32, frozen_prefix=n_prefix)
             assert fwd == n_prefix + 32
@@ -167,7 +167,7 @@ def _host_loop(s, prompt, *, strategy, gen, steps, bs, tau=0.9, cap=0):
     """The reference run_decode_loop over propose_device / commit_device (oracle policy)."""
     mask, eos = SMALL["mask_token_id"], SMALL["eos_token_id"]
     x = list(prompt) + [mask] * gen
-    s.start_device(x, prompt_len=0, block_size=bs, mask_token_id=mask, exact_kv=False, steps=steps)
+    s.start_device(x, prompt_len=0, block_size=bs, mask_token_id=mask, exact_kv=True, steps=steps)
     c = opol.Canvas(x, len(prompt), mask, eos)
     if strategy == "bd3_fixed_quota":
         pol = opol.BD3FixedQuota(block_size=bs, steps=steps, prompt_len=len(prompt), gen_len=gen)
@@ -206,7 +206,7 @@ def test_device_loop_equals_host_loop(rt, strategy, gen, steps, cap):
     with rt.session({"decode_strategy": strategy, "block_size": 32}) as s:
         # Host-driven loop: propose on the device, select on the host (oracle), commit on the device.
         x = list(prompt) + [mask] * gen
-        s.start_device(x, prompt_len=0, block_size=32, mask_token_id=mask, exact_kv=False, steps=steps)
+        s.start_device(x, prompt_len=0, block_size=32, mask_token_id=mask, exact_kv=True, steps=steps)
         c = opol.Canvas(list(x), len(prompt), mask, SMALL["eos_token_id"])
         if strategy == "bd3_fixed_quota":
             pol = opol.BD3FixedQuota(block_size=32, steps=steps, prompt_len=len(prompt), gen_len=gen)

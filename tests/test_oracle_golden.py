@@ -57,15 +57,32 @@ def _policy_for(tr):
     bs = tr["block_size"]
     if tr["strategy"] == "bd3_fixed_quota":
         pol = policy.BD3FixedQuota(block_size=bs, steps=tr["steps"], prompt_len=len(tr["prompt"]), gen_len=tr["gen"])
-        return pol, pol.iteration_limit, False, "max"
+        return pol, pol.iteration_limit, False, "sample" if tr["options"].get("temperature", 0) > 0 else "max"
     if tr["strategy"] == "block_threshold":
         return policy.BlockThreshold(block_size=bs, threshold=tr["options"]["confidence_threshold"]), tr["steps"], True, "max"
     opts = tr["options"]
     return policy.EntropyCount(eps=opts["eps"], steps=tr["steps"]), tr["steps"], True, "ent"
 
 
-@pytest.mark.parametrize("name", ["bd3_cfg0_shape", "bd3_k2", "bd3_ragged_quota", "bd3_eos", "block_threshold",
-                                  "entropy_count"])
+@pytest.mark.parametrize("name", ["small", "wide", "sharp"])
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_sampled_rows(sel, name, tag):
+    """Temperature sampling (TopConfidence at T > 0) against the reference's own draws."""
+    temp, _, fwd = (float(v) for v in sel[f"{name}_sample_{tag}_args"])
+    seed = int(sel[f"{name}_sample_{tag}_seed"][0])
+    conf, tok, gaps = selector.sampled_max_prob_rows(sel[f"{name}_logits"], temperature=temp, seed=seed,
+                                                     forward=int(fwd), positions=list(sel[f"{name}_sample_pos"]))
+    assert tok == list(sel[f"{name}_sample_{tag}_tok"])
+    np.testing.assert_allclose(conf, sel[f"{name}_sample_{tag}_conf"], rtol=1e-13, atol=0)
+    assert np.all(gaps >= 0)
+
+
+def test_sampling_noise_row(sel):
+    np.testing.assert_array_equal(selector.sampling_noise(5, 2, 40, 4096), sel["noise_row"])
+
+
+@pytest.mark.parametrize("name", ["bd3_cfg0_shape", "bd3_k2", "bd3_ragged_quota", "bd3_eos", "bd3_sampled",
+                                  "block_threshold", "entropy_count"])
 def test_decode_trajectory(golden_dir, name):
     tr = json.loads((golden_dir / "decode.json").read_text())[name]
     pol, limit, exclude, kind = _policy_for(tr)
@@ -80,6 +97,11 @@ def test_decode_trajectory(golden_dir, name):
             rows = selector.exclude_mask_token(rows, tr["mask"])
         if kind == "max":
             return selector.max_prob_rows(rows)
+        if kind == "sample":
+            o = tr["options"]
+            conf, tok, _ = selector.sampled_max_prob_rows(rows, temperature=o["temperature"], seed=o["seed"],
+                                                          forward=len(windows) - 1, positions=frontier)
+            return conf, tok
         o = tr["options"]
         return selector.neg_entropy_rows(rows, temperature=o["temperature"], top_p=o["top_p"])
 

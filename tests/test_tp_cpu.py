@@ -109,3 +109,17 @@ def test_id_exchange_and_geometry_agree_across_gloo_ranks(lib):
     assert got[0][1] == got[1][1] == bytes(range(128))
     assert got[0][2] == got[1][2]
     assert [g["q_heads"] for g in got[0][2]] == [14, 14]
+
+
+@pytest.mark.parametrize("layers", [28, 32, 33, 36, 64, 4096])
+def test_peer_flag_epochs_never_overlap(lib, layers):
+    """Every flag a forward raises lies above every flag of the forward before it, whatever the
+    layer count: a stale flag from epoch E can never satisfy a wait of epoch E + 1 (at 36 layers a
+    span of 64 tags per epoch would let layer 35's flag of epoch E pass layers 0-3 of epoch E + 1)."""
+    for epoch in (0, 1, 7, 2**20):
+        top = max(lib.drt_tp_flag_value(epoch, layer, which) for layer in range(layers) for which in (0, 1))
+        low_next = min(lib.drt_tp_flag_value(epoch + 1, layer, which) for layer in range(layers) for which in (0, 1))
+        assert top < low_next, (layers, epoch)
+        # within one forward, every linear has its own value
+        vals = {lib.drt_tp_flag_value(epoch, layer, which) for layer in range(layers) for which in (0, 1)}
+        assert len(vals) == 2 * layers

@@ -16,18 +16,22 @@ bf16-rounded linear outputs, f32 norms / RoPE / SwiGLU / residual — with two k
 Each layer adds its update to the residual with an independent error of about 2 u of that update,
 and the residual's norm grows as the root-sum-square of the updates, so the relative error of the
 final hidden state — and of the logits, one bf16 linear further — stays at a few u independently
-of the depth. The stated tolerance is
-    rms(device - oracle) <= 6 u * rms(oracle)              (0.0117 of the logit RMS)
+of the depth, as long as the layers do not amplify perturbations (the seeded N(0, 0.02^2) weights;
+at 0.05 the 28-layer stack amplifies them about fourfold). The stated tolerance is
+    rms(device - oracle) <= 8 u * rms(oracle)              (0.0156 of the logit RMS)
     max |device - oracle| <= 48 u * rms(oracle)            (a Gaussian-like tail over ~10^7 logits)
-against measured 3-4 u and 16-32 u at 2 and 28 layers. A row's argmax must agree wherever its two
-largest oracle logits lie further apart than twice the max bound.
+Measured on a B200 (relative to the logit RMS): Qwen3-0.6B geometry 3.7 u / 18.8 u, Dream-7B
+width with GQA 7:1 (two layers) 5.4 u / 30 u, the two-layer test models 3.0-5.9 u / 16-32 u.
+Rounding Q, K and P to bf16 in the oracle as well (``attn_operands="bf16"``) removes only a third
+of the RMS error: the rest is the accumulation order of item 2. A row's argmax must agree wherever
+its two largest oracle logits lie further apart than twice the max bound.
 """
 from __future__ import annotations
 
 import numpy as np
 
 U_BF16 = 2.0 ** -9
-RMS_FACTOR = 6.0
+RMS_FACTOR = 8.0
 MAX_FACTOR = 48.0
 
 

@@ -21,6 +21,8 @@ from oracle import selector as osel  # noqa: E402
 from oracle.numerics import bf16_round, synth_weights  # noqa: E402
 from oracle.quant import dequantize, pack_q4, quantize_q4  # noqa: E402
 
+from bf16_tolerance import assert_logits_close  # noqa: E402
+
 pytestmark = pytest.mark.gpu
 
 SMALL = dict(layer_count=2, hidden_size=256, attention_heads=4, num_kv_heads=2, head_dim=128,
@@ -107,11 +109,7 @@ def test_quantized_window_forward_matches_oracle(qrt, qweights):
         res = s.execute_window(ids, scope, mask_geometry=(0, 32))
     got = np.frombuffer(res.logits, dtype="<f4").reshape(res.n_rows, res.n_vocab)
     want = ofwd.forward_mlx(w, SMALL, ids, prompt_len=0, block_size=32, output_rows=scope, quant=qw)
-    scale = float(np.abs(want).max())
-    err = np.abs(got - want)
-    assert err.max() <= 0.02 * scale, (err.max(), scale)
-    assert float(np.mean(err)) <= 0.002 * scale
-    assert np.mean(np.argmax(got, -1) == np.argmax(want, -1)) >= 0.75
+    assert_logits_close(got, want)
 
 
 def test_quantized_decode_matches_oracle_on_certified_steps(qrt, qweights):

@@ -6,7 +6,7 @@
 * propose_device (prefix K/V cache) agrees with a cache-free window forward;
 * the device-resident decode loop equals the host-driven loop over the same session calls,
   step for step, for BD3 fixed-quota and block-threshold;
-* the whole decode agrees with the CPU oracle decode on every certified step.
+* the whole decode agrees with the CPU oracle along the device trajectory within the stated tolerance.
 """
 from __future__ import annotations
 
@@ -19,6 +19,8 @@ from oracle import forward as ofwd  # noqa: E402
 from oracle import policy as opol  # noqa: E402
 from oracle import selector as osel  # noqa: E402
 from oracle.numerics import synth_weights  # noqa: E402
+
+from bf16_tolerance import assert_logits_close  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -72,11 +74,7 @@ def test_execute_window_matches_oracle(rt, weights):
     with rt.session({"decode_strategy": "bd3_fixed_quota", "block_size": 32}) as s:
         got = _window_logits(s, ids, scope)
     want = ofwd.forward_mlx(weights, SMALL, ids, prompt_len=0, block_size=32, output_rows=scope)
-    scale = float(np.abs(want).max())
-    err = np.abs(got - want)
-    assert err.max() <= 0.02 * scale, (err.max(), scale)
-    assert float(np.mean(err)) <= 0.002 * scale
-    assert np.mean(np.argmax(got, -1) == np.argmax(want, -1)) >= 0.75
+    assert_logits_close(got, want)
 
 
 def test_execute_window_long_prefix_chunks(rt, weights):
@@ -86,8 +84,7 @@ def test_execute_window_long_prefix_chunks(rt, weights):
     with rt.session({"decode_strategy": "bd3_fixed_quota", "block_size": 32}) as s:
         got = _window_logits(s, ids, scope)
     want = ofwd.forward_mlx(weights, SMALL, ids, prompt_len=0, block_size=32, output_rows=scope)
-    scale = float(np.abs(want).max())
-    assert np.abs(got - want).max() <= 0.02 * scale
+    assert_logits_close(got, want)
 
 
 def test_propose_agrees_with_window_forward(rt):
@@ -154,11 +151,7 @@ def test_large_vocab_head_matches_oracle():
             for scope in (list(range(70, 90)), list(range(0, 96, 2))):
                 got = _window_logits(s, ids, scope)
                 want = ofwd.forward_mlx(weights, cfg, ids, prompt_len=0, block_size=32, output_rows=scope)
-                scale = float(np.abs(want).max())
-                err = np.abs(got - want)
-                assert err.max() <= 0.02 * scale, (len(scope), err.max(), scale)
-                assert float(np.mean(err)) <= 0.002 * scale
-                assert np.mean(np.argmax(got, -1) == np.argmax(want, -1)) >= 0.9
+                assert_logits_close(got, want)
     finally:
         r.close()
 
@@ -260,42 +253,17 @@ def test_device_loop_equals_host_loop(rt, strategy, gen, steps, cap):
     assert out is not None
 
 
-def test_decode_matches_cpu_oracle_on_certified_steps(rt, weights):
-    """Whole BD3 decode vs the CPU oracle (cache-free MLX-contract forward + reference selector
-    and policy). Steps agree until the first decision whose oracle margin is inside the bf16
-    forward tolerance; the test requires most of the decode to be certified and equal."""
+def test_decode_matches_cpu_oracle_along_trajectory(rt, weights):
+    """Whole BD3 decode vs the CPU oracle (MLX-contract forward + reference selector and policy),
+    step by step along the device's trajectory: every step's confidences, chosen rows and tokens
+    are the oracle's within the stated bf16 logit tolerance (tests/decode_check.py)."""
+    from decode_check import check_bd3_trajectory
+
     prompt = _prompt(64, 21)
     gen, steps, bs = 64, 64, 32
-    mask, eos = SMALL["mask_token_id"], SMALL["eos_token_id"]
     with rt.session({"decode_strategy": "bd3_fixed_quota", "block_size": bs}) as s:
         dev = s.generate(prompt, max_tokens=gen, steps=steps, block_size=bs, trace_steps=256)
-    c = opol.Canvas(list(prompt) + [mask] * gen, len(prompt), mask, eos)
-    pol = opol.BD3FixedQuota(block_size=bs, steps=steps, prompt_len=len(prompt), gen_len=gen)
-    agreed = 0
-    diverged = False
-    for i, tr in enumerate(dev["trace"]):
-        plan = pol.plan(c, tr["step"])
-        assert plan.action == "proceed"
-        assert plan.frontier == tr["frontier"]
-        logits = ofwd.forward_mlx(weights, SMALL, c.x[:plan.window_end], prompt_len=0, block_size=bs,
-                                  output_rows=plan.frontier)
-        conf, tok = osel.max_prob_rows(logits)
-        rows = pol.select(conf)
-        dev_rows = tr["chosen"]
-        same = sorted(rows) == dev_rows and all(tok[r] == tr["tokens"][r] for r in rows)
-        if not same:
-            # Divergence is acceptable only where the oracle's own decision is within tolerance.
-            order = np.sort(conf)[::-1]
-            k = len(rows)
-            gap = (order[k - 1] - order[k]) / order[k - 1] if k < len(order) else 1.0
-            top2 = np.sort(logits[rows[0]])[-2:]
-            logit_gap = float(top2[1] - top2[0])
-            assert gap < 0.05 or logit_gap < 0.05 * float(np.abs(logits).max()), (i, gap, logit_gap)
-            diverged = True
-            break
-        agreed += 1
-        for r in rows:
-            c.x[plan.frontier[r]] = tok[r]
-    if not diverged:
-        assert dev["x"] == c.x
-    assert agreed >= 8
+    report = check_bd3_trajectory(dev, weights, SMALL, prompt, gen=gen, steps=steps, block_size=bs)
+    print("toy decode", report)
+    assert report["steps"] == 64
+    assert report["exact_steps"] >= report["steps"] // 4, report

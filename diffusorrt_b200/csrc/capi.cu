@@ -112,7 +112,7 @@ int map_matrix(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, i
   return make_map(map, base, 2, dims, strides, box);
 }
 
-// Row-major uint8 matrix [rows][cols_bytes] (packed 4-bit weights), box {box_cols bytes, box_rows},
+// Row-major uint8 matrix [rows][cols_bytes] (packed quantized weights), box {box_cols bytes, box_rows},
 // no swizzle: a box lands as box_rows contiguous rows of box_cols bytes.
 int map_u8(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_bytes, int box_cols, int box_rows) {
   EncodeTiledFn fn = encode_fn();
@@ -219,10 +219,10 @@ int configure_kernels() {
         cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_lm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
       result = DRT_INTERNAL_ERROR;
-    for (int qi = 0; qi < 2 && result == DRT_OK; ++qi)
+    for (int qb = 0; qb <= 8 && result == DRT_OK; qb += 4)
     for (int epi = 0; epi <= EPI_QKV && result == DRT_OK; ++epi)
       for (int sp = 1; sp <= 16 && result == DRT_OK; sp *= 2) {
-        DecGemmKernel k = dec_gemm_kernel(epi, sp, qi == 1);
+        DecGemmKernel k = dec_gemm_kernel(epi, sp, qb);
         if (k == nullptr || cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
             cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
           result = DRT_INTERNAL_ERROR;
@@ -237,12 +237,14 @@ constexpr double kTieRel = 9.094947017729282e-13;  // 2^-40
 }  // namespace
 
 // ======================================================================= model
-// 4-bit affine copy of one linear weight [n][K] (quant.cuh): packed nibbles [n][K / 2], bf16 scale
-// and bias [n][K / 64], and the TMA map over the packed bytes (box: 64 inputs x 128 rows).
+// Quantized copy of one linear weight [n][K] (quant.cuh): 4-bit affine (packed nibbles [n][K / 2]) or
+// int8 weight-only (bytes [n][K]), bf16 scale and bias [n][K / 64], and the TMA map over the packed
+// bytes (box: 64 inputs x 128 rows).
 struct QuantW {
   uint8_t* q = nullptr;
   __nv_bfloat16* scale = nullptr;
   __nv_bfloat16* bias = nullptr;
+  int bits_cap = 0;  // widest format the packed buffer holds
   CUtensorMap map;
 };
 
@@ -264,7 +266,8 @@ struct drt_model {
   float* final_norm = nullptr;
   std::vector<LayerW> layers;
   CUtensorMap m_lm;
-  bool quantized = false;   // layer linears and lm_head run from their 4-bit copies
+  bool quantized = false;   // layer linears and lm_head run from their quantized copies
+  int qbits = 0;            // 4 (4-bit affine) or 8 (int8 weight-only) when quantized
   QuantW q_lm;
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
@@ -764,16 +767,22 @@ extern "C" int drt_model_get_tensor(drt_model* m, const char* key, void* data, i
 
 namespace {
 // (Re)build the 4-bit copy of the bf16 weight w [n][K].
-int quantize_into(drt_model* m, QuantW* qw, const __nv_bfloat16* w, int64_t n, int64_t K) {
-  if (qw->q == nullptr) {
-    TRY(dalloc(m, &qw->q, static_cast<size_t>(n) * (K / 2)));
+int quantize_into(drt_model* m, QuantW* qw, const __nv_bfloat16* w, int64_t n, int64_t K, int bits) {
+  if (qw->bits_cap < bits) {  // a narrower earlier buffer stays with the model's allocations
+    TRY(dalloc(m, &qw->q, static_cast<size_t>(n) * K * bits / 8));
+    qw->bits_cap = bits;
+  }
+  if (qw->scale == nullptr) {
     TRY(dalloc(m, &qw->scale, static_cast<size_t>(n) * (K / 64)));
     TRY(dalloc(m, &qw->bias, static_cast<size_t>(n) * (K / 64)));
-    TRY(map_u8(&qw->map, qw->q, n, K / 2, 32, 128));
   }
+  TRY(map_u8(&qw->map, qw->q, n, K * bits / 8, 64 * bits / 8, 128));
   const int64_t total = n * (K / 64);
   const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 65535));
-  quantize_q4_kernel<<<blocks, 256>>>(w, n, static_cast<int>(K), qw->q, qw->scale, qw->bias);
+  if (bits == 8)
+    quantize_q8_kernel<<<blocks, 256>>>(w, n, static_cast<int>(K), qw->q, qw->scale, qw->bias);
+  else
+    quantize_q4_kernel<<<blocks, 256>>>(w, n, static_cast<int>(K), qw->q, qw->scale, qw->bias);
   CK(cudaGetLastError());
   return DRT_OK;
 }
@@ -782,22 +791,23 @@ int quantize_into(drt_model* m, QuantW* qw, const __nv_bfloat16* w, int64_t n, i
 extern "C" int drt_model_quantize(drt_model* m, int32_t bits, int32_t group_size) {
   REQUIRE(m, "null model");
   REQUIRE(m->shard.world == 1, "4-bit linears are served on whole (not tensor-parallel) models");
-  if (bits != 4 || group_size != 64)
-    return set_error(DRT_UNSUPPORTED, "linear quantization serves bits 4 with group size 64 (got bits %d, group %d)", bits,
-                     group_size);
+  if ((bits != 4 && bits != 8) || group_size != 64)
+    return set_error(DRT_UNSUPPORTED, "linear quantization serves bits 4 or 8 with group size 64 (got bits %d, group %d)",
+                     bits, group_size);
   REQUIRE(m->H % 64 == 0 && m->I % 64 == 0, "linear in-dims must be multiples of the group size");
   CK(cudaSetDevice(m->device));
   const int64_t H = m->H, I = m->I, qd = static_cast<int64_t>(m->nq) * 128;
   for (int l = 0; l < m->L; ++l) {
     LayerW& w = m->layers[l];
-    TRY(quantize_into(m, &w.q_qkv, w.wqkv, m->qkv_rows, H));
-    TRY(quantize_into(m, &w.q_o, w.wo, H, qd));
-    TRY(quantize_into(m, &w.q_gu, w.wgu, m->gu_rows, H));
-    TRY(quantize_into(m, &w.q_down, w.wdown, H, I));
+    TRY(quantize_into(m, &w.q_qkv, w.wqkv, m->qkv_rows, H, bits));
+    TRY(quantize_into(m, &w.q_o, w.wo, H, qd, bits));
+    TRY(quantize_into(m, &w.q_gu, w.wgu, m->gu_rows, H, bits));
+    TRY(quantize_into(m, &w.q_down, w.wdown, H, I, bits));
   }
-  TRY(quantize_into(m, &m->q_lm, m->lm_head, m->V, H));
+  TRY(quantize_into(m, &m->q_lm, m->lm_head, m->V, H, bits));
   CK(cudaDeviceSynchronize());
   m->quantized = true;
+  m->qbits = bits;
   return DRT_OK;
 }
 
@@ -1048,9 +1058,9 @@ int run_dec_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, G
     a.q_bias = q->bias;
     a.q_groups = kb;
     a.stages = kDecQStages;
-    DecGemmKernel kern = dec_gemm_kernel(a.epi, a.splits, true);
+    DecGemmKernel kern = dec_gemm_kernel(a.epi, a.splits, s->m->qbits);
     if (kern == nullptr) return set_error(DRT_INTERNAL_ERROR, "no quantized decode linear for epilogue %d, split %d", a.epi, a.splits);
-    CK(launch_kc(kern, dim3(tiles_m, 1, a.splits), dim3(128), dec_q_smem_bytes(a.kb_per_split), s->stream, true, a.splits,
+    CK(launch_kc(kern, dim3(tiles_m, 1, a.splits), dim3(128), dec_q_smem_bytes(a.kb_per_split, s->m->qbits), s->stream, true, a.splits,
                  q->map, mB, a));
     return DRT_OK;
   }
@@ -1399,7 +1409,7 @@ int capture(drt_session* s, bool with_policy, cudaGraphExec_t* out) {
 }
 
 // Prefill rows [p0, p1) (positions whose tokens are final) into the K/V cache, in chunks.
-// A quantized model runs every forward through the decode linears (the 4-bit weights have no wide
+// A quantized model runs every forward through the decode linears (the quantized weights have no wide
 // prefill kernel), in chunks of at most kMaxFwdRows rows.
 int forward_chunk_rows(const drt_session* s) { return s->m->quantized ? kMaxFwdRows : s->rows_cap; }
 
@@ -1673,7 +1683,7 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   REQUIRE(dream || m->shard.world == 1, "a tensor-parallel model serves entropy_count sessions only");
   if (dream) {
     REQUIRE(cfg->attention_mask_kind == DRT_MASK_BIDIRECTIONAL, "entropy_count sessions serve the bidirectional graph only");
-    REQUIRE(!m->quantized, "entropy_count sessions need bf16 linears (the 4-bit path forwards at most %d rows)", kMaxFwdRows);
+    REQUIRE(!m->quantized, "entropy_count sessions need bf16 linears (the quantized path forwards at most %d rows)", kMaxFwdRows);
   } else {
     REQUIRE(cfg->attention_mask_kind == DRT_MASK_D2F_HYBRID, "this device session serves the d2f_hybrid graph only");
     REQUIRE(cfg->block_size >= 1 && cfg->block_size <= 32, "block_size must be in [1, 32]");
@@ -2559,9 +2569,54 @@ extern "C" int drt_linear_q4(const void* x, const void* q, const void* scale, co
   a.q_scale = static_cast<const __nv_bfloat16*>(scale);
   a.q_bias = static_cast<const __nv_bfloat16*>(bias);
   a.q_groups = kb;
-  DecGemmKernel kern = dec_gemm_kernel(EPI_STORE_F32, splits, true);
-  CK(launch_kc(kern, dim3(n / 128, 1, splits), dim3(128), dec_q_smem_bytes(kbps), static_cast<cudaStream_t>(stream), false,
+  DecGemmKernel kern = dec_gemm_kernel(EPI_STORE_F32, splits, 4);
+  CK(launch_kc(kern, dim3(n / 128, 1, splits), dim3(128), dec_q_smem_bytes(kbps, 4), static_cast<cudaStream_t>(stream), false,
                splits, mq, mb, a));
+  return DRT_OK;
+}
+
+extern "C" int drt_linear_q8(const void* x, const void* q, const void* scale, const void* bias, float* y, int32_t rows,
+                             int32_t n, int32_t K, int32_t splits, void* stream) {
+  REQUIRE(x && q && scale && bias && y, "null argument");
+  REQUIRE(rows >= 1 && rows <= kDecRows, "rows must be in [1, %d]", kDecRows);
+  REQUIRE(n >= 128 && n % 128 == 0 && K >= 64 && K % 64 == 0, "quantized linear needs n %% 128 == 0 and K %% 64 == 0");
+  REQUIRE(splits == 1 || splits == 2 || splits == 4 || splits == 8 || splits == 16, "splits must be 1, 2, 4, 8 or 16");
+  const int kb = K / 64;
+  const int kbps = (kb + splits - 1) / splits;
+  REQUIRE(splits <= kb && kbps <= kDecQMaxKb, "K blocks per split must be in [1, %d]", kDecQMaxKb);
+  TRY(configure_kernels());
+  CUtensorMap mq, mb;
+  TRY(map_u8(&mq, q, n, K, 64, 128));
+  TRY(map_matrix(&mb, x, rows, K, 64));
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.n_out = n;
+  a.K = K;
+  a.rows = rows;
+  a.splits = splits;
+  a.kb_per_split = kbps;
+  a.stages = kDecQStages;
+  a.epi = EPI_STORE_F32;
+  a.out_f32 = y;
+  a.ld_out = n;
+  a.q_scale = static_cast<const __nv_bfloat16*>(scale);
+  a.q_bias = static_cast<const __nv_bfloat16*>(bias);
+  a.q_groups = kb;
+  DecGemmKernel kern = dec_gemm_kernel(EPI_STORE_F32, splits, 8);
+  CK(launch_kc(kern, dim3(n / 128, 1, splits), dim3(128), dec_q_smem_bytes(kbps, 8), static_cast<cudaStream_t>(stream), false,
+               splits, mq, mb, a));
+  return DRT_OK;
+}
+
+extern "C" int drt_quantize_q8(const void* w, int64_t rows, int32_t K, void* q, void* scale, void* bias, void* stream) {
+  REQUIRE(w && q && scale && bias, "null argument");
+  REQUIRE(rows >= 1 && K >= 64 && K % 64 == 0, "quantization needs K %% 64 == 0");
+  const int64_t total = rows * (K / 64);
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 65535));
+  quantize_q8_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(w), rows, K, static_cast<uint8_t*>(q), static_cast<__nv_bfloat16*>(scale),
+      static_cast<__nv_bfloat16*>(bias));
+  CK(cudaGetLastError());
   return DRT_OK;
 }
 

@@ -33,9 +33,10 @@ constexpr int kDecMaxKb = 16;                // K blocks of B kept resident per 
 constexpr int kDecPreStages = 2;             // weight K blocks requested before the dependency wait
 constexpr int kDecXBytes = 128 * kDecRows * 4;        // one f32 partial tile (receive or stage)
 
-// Quantized instantiation: every packed tile of the CTA's K slice is resident (kDecPBytes each), the
-// dequantized bf16 weight tiles go through a ring of kDecQStages A blocks.
-constexpr int kDecPBytes = 128 * 32;  // 128 rows x 64 nibbles
+// Quantized instantiations (QB = 4: 4-bit affine, QB = 8: int8 weight-only as an affine form): every
+// packed tile of the CTA's K slice is resident (dec_p_bytes(QB) each), the dequantized bf16 weight
+// tiles go through a ring of kDecQStages A blocks.
+__host__ __device__ constexpr int dec_p_bytes(int qb) { return 128 * 64 * qb / 8; }  // 128 rows x 64 packed inputs
 constexpr int kDecQStages = 3;
 constexpr int kDecQMaxKb = 8;         // K blocks per CTA for the quantized instantiation
 
@@ -55,13 +56,13 @@ __host__ __device__ inline size_t dec_smem_bytes(int stages, int kb_per_split) {
 }
 // Quantized: [A ring kDecQStages][B kb][packed kb][scale kb x 128 f32][bias kb x 128 f32], at least two
 // partial tiles long (stage and receive overlays).
-__host__ __device__ inline size_t dec_q_body_bytes(int kb_per_split) {
+__host__ __device__ inline size_t dec_q_body_bytes(int kb_per_split, int qb) {
   const size_t m = static_cast<size_t>(kDecQStages) * kDecABytes +
-                   static_cast<size_t>(kb_per_split) * (kDecBBytes + kDecPBytes + 2 * 128 * 4);
+                   static_cast<size_t>(kb_per_split) * (kDecBBytes + dec_p_bytes(qb) + 2 * 128 * 4);
   return m > static_cast<size_t>(2 * kDecXBytes) ? m : static_cast<size_t>(2 * kDecXBytes);
 }
-__host__ __device__ inline size_t dec_q_smem_bytes(int kb_per_split) {
-  return 1024 + dec_q_body_bytes(kb_per_split) + static_cast<size_t>(2 * kDecQStages + 4) * 8 + 32;
+__host__ __device__ inline size_t dec_q_smem_bytes(int kb_per_split, int qb) {
+  return 1024 + dec_q_body_bytes(kb_per_split, qb) + static_cast<size_t>(2 * kDecQStages + 4) * 8 + 32;
 }
 
 __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes, uint32_t bar_cluster) {
@@ -238,7 +239,7 @@ __device__ __forceinline__ void dec_sum_slices(const float* recv, int tid, float
 struct DecSmem {
   uint8_t* ring;
   uint8_t* sB;
-  uint8_t* sP;      // quantized: packed tiles [kb][128 rows][32 bytes]
+  uint8_t* sP;      // quantized: packed tiles [kb][128 rows][64 * QB / 8 bytes]
   float* qsc;       // quantized: [kb][128] scales of this CTA's rows
   float* qbi;       // quantized: [kb][128] biases
   uint64_t* fullP;  // quantized: all packed tiles landed
@@ -255,11 +256,15 @@ struct DecSmem {
 
 // Everything after the dependency wait, for a compile-time epilogue EPI, split-K factor S and MMA
 // width NCOL: activation load, weight ring, UMMA, split-K exchange and epilogue.
-template <int EPI, int S, int NCOL, bool QUANT>
+template <int EPI, int S, int NCOL, int QB>
 __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMap* tmB, const GemmArgs& a, const DecSmem& sm,
                                         uint32_t tmem, int m0, int kb0, int nkb, int npre, int stages, uint64_t policy,
                                         int rows_valid, int pos0) {
   constexpr int CPR = NCOL / S;  // columns owned by each CTA of the cluster
+  constexpr bool QUANT = QB != 0;
+  // Output rounding: the bf16 contract rounds every linear output to bf16, and so does int8
+  // weight-only (bf16 activations); the 4-bit quantized-matmul contract keeps f32 outputs.
+  constexpr bool RND = QB != 4;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = S > 1 ? cluster_ctarank() : 0u;
   const int c0 = static_cast<int>(rank) * CPR;
@@ -299,19 +304,27 @@ __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMa
     for (int g = 0; g < nkb && ok; ++g) {
       const int slot = g % kDecQStages;
       bool ready = g < kDecQStages || mbar_wait(&sm.emptyA[slot], ((g / kDecQStages) - 1) & 1);
-      const uint8_t* prow = sm.sP + g * kDecPBytes + tid * 32;
-      const uint4 p0 = *reinterpret_cast<const uint4*>(prow);
-      const uint4 p1 = *reinterpret_cast<const uint4*>(prow + 16);
-      const uint32_t pw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+      constexpr int kRowBytes = 64 * QB / 8;  // packed bytes of one row's group
+      const uint8_t* prow = sm.sP + g * dec_p_bytes(QB) + tid * kRowBytes;
+      uint32_t pw[kRowBytes / 4];
+#pragma unroll
+      for (int w4 = 0; w4 < kRowBytes / 16; ++w4) {
+        const uint4 p = *reinterpret_cast<const uint4*>(prow + w4 * 16);
+        pw[w4 * 4] = p.x;
+        pw[w4 * 4 + 1] = p.y;
+        pw[w4 * 4 + 2] = p.z;
+        pw[w4 * 4 + 3] = p.w;
+      }
       const float sc = sm.qsc[g * 128 + tid], bi = sm.qbi[g * 128 + tid];
       uint8_t* arow = sm.ring + static_cast<size_t>(slot) * kDecABytes + tid * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 8 inputs per 16-byte chunk, 4 packed bytes
+      for (int c = 0; c < 8; ++c) {  // 8 inputs per 16-byte chunk
         __align__(16) __nv_bfloat16 t[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float qv = static_cast<float>((pw[c] >> (4 * e)) & 15u);
-          t[e] = __float2bfloat16_rn(__fmaf_rn(sc, qv, bi));
+          // 4-bit: input 8c + e is nibble e of word c; 8-bit: byte e % 4 of word 2c + e / 4
+          const uint32_t qi = QB == 4 ? (pw[c] >> (4 * e)) & 15u : (pw[2 * c + e / 4] >> (8 * (e % 4))) & 255u;
+          t[e] = __float2bfloat16_rn(__fmaf_rn(sc, static_cast<float>(qi), bi));
         }
         *reinterpret_cast<uint4*>(arow + ((c ^ (tid & 7)) * 16)) = *reinterpret_cast<const uint4*>(t);
       }
@@ -386,9 +399,9 @@ __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMa
   if constexpr (S == 1) {
     __syncthreads();
     if (sm.flags[0] == 0) {
-      gemm_epilogue_chunk_t<EPI, !QUANT>(a, acc, 0, min(32, rows_valid), m0, tid, sm.xs, pos0);
+      gemm_epilogue_chunk_t<EPI, RND>(a, acc, 0, min(32, rows_valid), m0, tid, sm.xs, pos0);
       if constexpr (NCOL == 64)
-        if (rows_valid > 32) gemm_epilogue_chunk_t<EPI, !QUANT>(a, acc + 32, 32, rows_valid - 32, m0, tid, sm.xs, pos0);
+        if (rows_valid > 32) gemm_epilogue_chunk_t<EPI, RND>(a, acc + 32, 32, rows_valid - 32, m0, tid, sm.xs, pos0);
     }
   } else {
     // Stage the partial as S contiguous slices and send slice p to CTA p. Inside a slice the
@@ -432,16 +445,16 @@ __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMa
 #pragma unroll
         for (int i = 0; i < CPR; ++i)
           if (i < nvalid)
-            a.out_f32[static_cast<size_t>(c0 + i) * a.ld_out + n] = __fadd_rn(pre[i], __fadd_rn(out_round<!QUANT>(v[i]), b));
+            a.out_f32[static_cast<size_t>(c0 + i) * a.ld_out + n] = __fadd_rn(pre[i], __fadd_rn(out_round<RND>(v[i]), b));
       } else if constexpr (EPI == EPI_QKV) {
-        dec_epilogue_qkv<CPR, !QUANT>(a, v, c0, nvalid, m0, tid, sm.xs, pos0, pre, pre2);
+        dec_epilogue_qkv<CPR, RND>(a, v, c0, nvalid, m0, tid, sm.xs, pos0, pre, pre2);
       } else if constexpr (EPI == EPI_SWIGLU) {
-        dec_epilogue_swiglu<CPR, !QUANT>(a, v, c0, nvalid, m0, tid, sm.xs);
+        dec_epilogue_swiglu<CPR, RND>(a, v, c0, nvalid, m0, tid, sm.xs);
       } else {
         float vv[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) vv[i] = i < CPR ? v[i < CPR ? i : 0] : 0.0f;
-        gemm_epilogue_chunk_t<EPI, !QUANT>(a, vv, c0, nvalid, m0, tid, sm.xs, pos0);
+        gemm_epilogue_chunk_t<EPI, RND>(a, vv, c0, nvalid, m0, tid, sm.xs, pos0);
       }
     }
     cluster_wait();
@@ -452,23 +465,24 @@ __device__ __forceinline__ void dec_run(const CUtensorMap* tmA, const CUtensorMa
 // launched as clusters of S CTAs along z. Instantiated per epilogue, split factor and weight format
 // (bf16, or 4-bit affine with tmA over the packed nibbles) so that each kernel carries only the
 // code it runs (the instruction cache is cold at every launch).
-template <int EPI, int S, bool QUANT>
+template <int EPI, int S, int QB>
 __global__ void __launch_bounds__(128, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
+  constexpr bool QUANT = QB != 0;
   const int stages = QUANT ? kDecQStages : a.stages;
   const int kbs = a.kb_per_split;
   DecSmem sm;
   sm.ring = smem;
   sm.sB = smem + dec_ring_bytes(stages);
   sm.sP = sm.sB + static_cast<size_t>(kbs) * kDecBBytes;
-  sm.qsc = reinterpret_cast<float*>(sm.sP + static_cast<size_t>(kbs) * kDecPBytes);
+  sm.qsc = reinterpret_cast<float*>(sm.sP + static_cast<size_t>(kbs) * dec_p_bytes(QB));
   sm.qbi = sm.qsc + kbs * 128;
   sm.stage = reinterpret_cast<float*>(smem);
   sm.recv = sm.stage + 128 * kDecRows;
   sm.xs = sm.recv;  // epilogue scratch, once the received slices are summed
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (QUANT ? dec_q_body_bytes(kbs) : dec_body_bytes(stages, kbs)));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (QUANT ? dec_q_body_bytes(kbs, QB) : dec_body_bytes(stages, kbs)));
   sm.fullA = bars;
   sm.emptyA = bars + stages;
   sm.fullB = bars + 2 * stages;
@@ -510,8 +524,9 @@ __global__ void __launch_bounds__(128, 1)
     policy = l2_policy_evict_first();
     if constexpr (QUANT) {
       if (nkb > 0) {
-        mbar_expect_tx(sm.fullP, static_cast<uint32_t>(nkb * kDecPBytes));
-        for (int g = 0; g < nkb; ++g) tma_load_2d_hint(sm.sP + g * kDecPBytes, &tmA, sm.fullP, (kb0 + g) * 32, m0, policy);
+        mbar_expect_tx(sm.fullP, static_cast<uint32_t>(nkb * dec_p_bytes(QB)));
+        for (int g = 0; g < nkb; ++g)
+          tma_load_2d_hint(sm.sP + g * dec_p_bytes(QB), &tmA, sm.fullP, (kb0 + g) * (64 * QB / 8), m0, policy);
       }
     } else {
       for (int i = 0; i < npre; ++i) {
@@ -544,9 +559,9 @@ __global__ void __launch_bounds__(128, 1)
   const int pos0 = a.pos0_dev != nullptr ? *a.pos0_dev : a.pos0;
   // MMA width from the live row count, uniform across the cluster.
   if (rows_valid <= 32)
-    dec_run<EPI, S, 32, QUANT>(&tmA, &tmB, a, sm, tmem, m0, kb0, nkb, npre, stages, policy, rows_valid, pos0);
+    dec_run<EPI, S, 32, QB>(&tmA, &tmB, a, sm, tmem, m0, kb0, nkb, npre, stages, policy, rows_valid, pos0);
   else
-    dec_run<EPI, S, 64, QUANT>(&tmA, &tmB, a, sm, tmem, m0, kb0, nkb, npre, stages, policy, rows_valid, pos0);
+    dec_run<EPI, S, 64, QB>(&tmA, &tmB, a, sm, tmem, m0, kb0, nkb, npre, stages, policy, rows_valid, pos0);
 
   if (sm.flags[0] != 0 && tid == 0) {
     for (int st = 0; st < npre; ++st) mbar_wait(&sm.fullA[st], 0);
@@ -755,22 +770,23 @@ __global__ void __launch_bounds__(kLmThreads, 1)
 
 using DecGemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmArgs);
 
-// The instantiation for an epilogue kind, split factor and weight format (nullptr if none).
-inline DecGemmKernel dec_gemm_kernel(int epi, int S, bool quant = false) {
+// The instantiation for an epilogue kind, split factor and weight format (qbits 0: bf16, 4: 4-bit
+// affine, 8: int8 weight-only; nullptr if none).
+inline DecGemmKernel dec_gemm_kernel(int epi, int S, int qbits = 0) {
 #define DRT_DEC_ROW(E, Q)                                                                                              \
   {                                                                                                                    \
     gemm_decode_kernel<E, 1, Q>, gemm_decode_kernel<E, 2, Q>, gemm_decode_kernel<E, 4, Q>, gemm_decode_kernel<E, 8, Q>, \
         gemm_decode_kernel<E, 16, Q>                                                                                   \
   }
-  static const DecGemmKernel table[2][4][5] = {
-      {DRT_DEC_ROW(EPI_STORE_F32, false), DRT_DEC_ROW(EPI_RESID, false), DRT_DEC_ROW(EPI_SWIGLU, false),
-       DRT_DEC_ROW(EPI_QKV, false)},
-      {DRT_DEC_ROW(EPI_STORE_F32, true), DRT_DEC_ROW(EPI_RESID, true), DRT_DEC_ROW(EPI_SWIGLU, true),
-       DRT_DEC_ROW(EPI_QKV, true)}};
+  static const DecGemmKernel table[3][4][5] = {
+      {DRT_DEC_ROW(EPI_STORE_F32, 0), DRT_DEC_ROW(EPI_RESID, 0), DRT_DEC_ROW(EPI_SWIGLU, 0), DRT_DEC_ROW(EPI_QKV, 0)},
+      {DRT_DEC_ROW(EPI_STORE_F32, 4), DRT_DEC_ROW(EPI_RESID, 4), DRT_DEC_ROW(EPI_SWIGLU, 4), DRT_DEC_ROW(EPI_QKV, 4)},
+      {DRT_DEC_ROW(EPI_STORE_F32, 8), DRT_DEC_ROW(EPI_RESID, 8), DRT_DEC_ROW(EPI_SWIGLU, 8), DRT_DEC_ROW(EPI_QKV, 8)}};
 #undef DRT_DEC_ROW
   const int si = S == 1 ? 0 : S == 2 ? 1 : S == 4 ? 2 : S == 8 ? 3 : S == 16 ? 4 : -1;
-  if (epi < 0 || epi > EPI_QKV || si < 0) return nullptr;
-  return table[quant ? 1 : 0][epi][si];
+  const int qi = qbits == 0 ? 0 : qbits == 4 ? 1 : qbits == 8 ? 2 : -1;
+  if (epi < 0 || epi > EPI_QKV || si < 0 || qi < 0) return nullptr;
+  return table[qi][epi][si];
 }
 
 }  // namespace drt

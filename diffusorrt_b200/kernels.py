@@ -164,6 +164,32 @@ def quantize_q4(w: torch.Tensor, *, stream: torch.cuda.Stream | None = None):
     return q, scale, bias
 
 
+def quantize_q8(w: torch.Tensor, *, stream: torch.cuda.Stream | None = None):
+    """int8 weight-only quantization of a bf16 [rows, K] weight: (bytes uint8 [rows, K] = q + 128,
+    scale bf16 [rows, K/64], bias = -128 * scale bf16 [rows, K/64])."""
+    if w.dtype != torch.bfloat16 or not w.is_contiguous() or w.dim() != 2:
+        raise ValueError("w must be a contiguous bf16 CUDA matrix")
+    rows, K = w.shape
+    q = torch.empty(rows, K, dtype=torch.uint8, device=w.device)
+    scale = torch.empty(rows, K // 64, dtype=torch.bfloat16, device=w.device)
+    bias = torch.empty(rows, K // 64, dtype=torch.bfloat16, device=w.device)
+    _lib.check(_lib.load().drt_quantize_q8(w.data_ptr(), rows, K, q.data_ptr(), scale.data_ptr(), bias.data_ptr(),
+                                           _stream_ptr(stream)))
+    return q, scale, bias
+
+
+def linear_q8(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor, *, splits: int = 1,
+              out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """y = bf16(x @ dequant(q, scale, bias)^T) widened to f32 (int8 weight-only): x [rows <= 64, K] bf16."""
+    rows, K = x.shape
+    n = q.shape[0]
+    if out is None:
+        out = torch.empty(rows, n, dtype=torch.float32, device=x.device)
+    _lib.check(_lib.load().drt_linear_q8(x.data_ptr(), q.data_ptr(), scale.data_ptr(), bias.data_ptr(), out.data_ptr(),
+                                         rows, n, K, int(splits), _stream_ptr(stream)))
+    return out
+
+
 def linear_q4(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor, *, splits: int = 1,
               out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
     """y = x @ dequant(q, scale, bias)^T (f32, no output rounding): x [rows <= 64, K] bf16."""

@@ -162,18 +162,37 @@ class Runtime:
             raise NotImplementedError("the B200 engine computes with bf16 weights (compute_dtype 0)")
         quant_bits = engine_config.get("linear_quant_bits")
         quant_group = int(engine_config.get("linear_quant_group_size", 64) or 64)
-        if quant_bits and (int(quant_bits), quant_group) != (4, 64):
-            raise NotImplementedError("linear quantization is served as 4-bit affine, group size 64")
-        if precision is not None and precision.get("weight_type", "bf16") != "bf16":
-            raise NotImplementedError(f"precision {precision.get('scheme')!r} is not served by this build")
+        if quant_bits and (int(quant_bits) not in (4, 8) or quant_group != 64):
+            raise NotImplementedError("linear quantization is served as 4-bit affine or int8, group size 64")
+        if precision is not None:
+            # cuda_precision_descriptor (python/src/edllm/backends/device_runtime.py:19-47): bf16, or the
+            # int8_weight_only scheme (int8 weights, per-group scales of 64 inputs, bf16 activations)
+            scheme = precision.get("scheme", "bf16")
+            if scheme == "int8_weight_only" or precision.get("weight_type") == "int8":
+                if precision.get("activation_type", "bf16") != "bf16" or precision.get("accumulation_type", "fp32") != "fp32":
+                    raise NotImplementedError(f"precision {precision!r} is not served by this build")
+                quant_bits = quant_bits or 8
+                if int(quant_bits) != 8:
+                    raise ValueError("the int8_weight_only precision quantizes linears to 8 bits")
+            elif precision.get("weight_type", "bf16") != "bf16":
+                raise NotImplementedError(f"precision {scheme!r} is not served by this build")
         cfg = dict(QWEN3_06B_BD3LM)
+        package = None
         if package_dir is not None:
             meta = Path(package_dir) / "model.json"
             if meta.exists():
                 doc = json.loads(meta.read_text())
-                cfg.update({k: v for k, v in doc.get("runtime_config", doc).items() if k in cfg})
-                if synthetic_seed is None and "synthetic_seed" in doc:
-                    synthetic_seed = int(doc["synthetic_seed"])
+                if doc.get("package_format") is not None:
+                    # a converted package: geometry from its GraphIR and tensors, weights from its
+                    # verified safetensors shards (package.py)
+                    from .package import read_package
+
+                    package = read_package(package_dir)
+                    cfg.update(package.config)
+                else:
+                    cfg.update({k: v for k, v in doc.get("runtime_config", doc).items() if k in cfg})
+                    if synthetic_seed is None and "synthetic_seed" in doc:
+                        synthetic_seed = int(doc["synthetic_seed"])
         if model_config:
             cfg.update(model_config)
         self.config = cfg
@@ -198,8 +217,11 @@ class Runtime:
         cos, sin = rope_half_tables(self.max_seq, cfg["head_dim"], float(cfg["rope_theta"]))
         _call(self._lib.drt_model_set_rope(self._model, cos.ctypes.data, sin.ctypes.data, self.max_seq))
         self.quantized = False
+        self.package = package
         if synthetic_seed is not None:
             self.init_synthetic(synthetic_seed)
+        if package is not None:
+            self.load_package(package)
         if weights is not None:
             self.load_weights(weights)
         if quant_bits:
@@ -246,11 +268,35 @@ class Runtime:
         if getattr(self, "quantized", False):
             self.quantize()
 
-    def quantize(self, bits: int = 4, group_size: int = 64) -> None:
-        """4-bit affine copies of every layer linear and lm_head (the reference's load-time
-        ``_quantize_linear_weights``, mlx_dream.py:2090-2108); later forwards use them."""
-        _call(self._lib.drt_model_quantize(self._model, int(bits), int(group_size)))
+    def load_package(self, package) -> None:
+        """Install every tensor of a verified package (``package.read_package``) as stored: bf16
+        matrices as their bits, bf16 vectors (norms, biases) widened exactly to float32."""
+        for name, arr in package.items():
+            if name == "lm_head.weight" and self.config["tied_lm_head"]:
+                continue
+            rows = arr.shape[0] if arr.ndim == 2 else 1
+            cols = arr.shape[-1]
+            if arr.dtype == np.uint16:  # bf16 bits
+                data = np.ascontiguousarray(arr)
+                _call(self._lib.drt_model_set_tensor(self._model, name.encode(), data.ctypes.data, 0, rows, cols))
+            elif arr.ndim == 1:
+                data = np.ascontiguousarray(arr, dtype=np.float32)
+                _call(self._lib.drt_model_set_tensor(self._model, name.encode(), data.ctypes.data, 1, rows, cols))
+            else:
+                data = _bf16_bits(np.asarray(arr, dtype=np.float32))
+                _call(self._lib.drt_model_set_tensor(self._model, name.encode(), data.ctypes.data, 0, rows, cols))
+        if getattr(self, "quantized", False):
+            self.quantize()
+
+    def quantize(self, bits: int | None = None, group_size: int = 64) -> None:
+        """Quantized copies of every layer linear and lm_head, later forwards use them: 4-bit affine
+        (the reference's load-time ``_quantize_linear_weights``, mlx_dream.py:2090-2108) or 8 (the
+        CUDA ``int8_weight_only`` precision). By default the width of the model's last quantization
+        (4 for a first one)."""
+        bits = int(bits if bits is not None else getattr(self, "quant_bits", 4))
+        _call(self._lib.drt_model_quantize(self._model, bits, int(group_size)))
         self.quantized = True
+        self.quant_bits = bits
 
     def get_tensor(self, key: str, shape: tuple[int, int]) -> np.ndarray:
         """A resident tensor as float32 (bf16 values widened)."""

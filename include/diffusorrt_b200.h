@@ -193,12 +193,16 @@ int drt_model_get_tensor(drt_model* model, const char* key, void* data, int32_t 
  * (python/src/edllm/backends/mlx_forward.py:1566-1595). */
 int drt_model_set_rope(drt_model* model, const float* cos_half, const float* sin_half, int32_t n_pos);
 int64_t drt_model_device_bytes(const drt_model* model);
-/* Quantize every layer linear (q/k/v/o, gate/up, down) and lm_head to 4-bit affine groups of 64
- * inputs (reference _quantize_linear_weights, mlx_dream.py:2090-2108, keys :2033-2087; the
- * quantizer's rounding rules are defined in diffusorrt_b200/csrc/quant.cuh). The embedding stays
- * bf16. Later forwards of every session run from the 4-bit copies with the quantized-matmul output
- * contract (no bf16 rounding of linear outputs, mlx_ops.py:108-117). Call again after
- * drt_model_set_tensor to refresh the copies. Only bits 4, group_size 64 (else DRT_UNSUPPORTED). */
+/* Quantize every layer linear (q/k/v/o, gate/up, down) and lm_head in groups of 64 inputs; the
+ * embedding stays bf16. Call again after drt_model_set_tensor to refresh the copies. group_size 64
+ * only (else DRT_UNSUPPORTED).
+ *  bits 4: 4-bit affine (reference _quantize_linear_weights, mlx_dream.py:2090-2108, keys
+ *    :2033-2087); later forwards follow the quantized-matmul output contract (no bf16 rounding of
+ *    linear outputs, mlx_ops.py:108-117).
+ *  bits 8: the CUDA int8_weight_only precision (device_runtime.py:19-56, engine_config
+ *    linear_quant_bits 8): int8 weights with one absmax scale per group; bf16 activations, f32
+ *    accumulation and bf16-rounded outputs, as the bf16 linears.
+ * The quantizers' rounding rules are defined in diffusorrt_b200/csrc/quant.cuh. */
 int drt_model_quantize(drt_model* model, int32_t bits, int32_t group_size);
 void drt_model_destroy(drt_model* model);
 /* Shard of rank `rank` in a group of `world` (host only; no device call). */
@@ -348,6 +352,14 @@ int drt_quantize_q4(const void* w, int64_t rows, int32_t K, void* q, void* scale
  * rounding, the quantized-matmul contract); n % 128 == 0, K % 64 == 0, splits in {1, 2, 4, 8, 16}
  * with at most 8 groups of 64 inputs per split. The decode linear's quantized instantiation. */
 int drt_linear_q4(const void* x, const void* q, const void* scale, const void* bias, float* y, int32_t rows, int32_t n,
+                  int32_t K, int32_t splits, void* stream);
+/* int8 weight-only quantization of a bf16 weight w [rows x K] (device pointers): q [rows x K] bytes
+ * holding the signed weight + 128, scale [rows x K/64] bf16 (absmax / 127) and bias = -128 * scale,
+ * the affine form the decode linear dequantizes (quant.cuh). */
+int drt_quantize_q8(const void* w, int64_t rows, int32_t K, void* q, void* scale, void* bias, void* stream);
+/* y = x @ dequant(q, scale, bias)^T for rows <= 64 with the int8 weight-only contract (bf16 dequantized
+ * weights, f32 accumulation, outputs rounded to bf16 and widened to f32); shapes as drt_linear_q4. */
+int drt_linear_q8(const void* x, const void* q, const void* scale, const void* bias, float* y, int32_t rows, int32_t n,
                   int32_t K, int32_t splits, void* stream);
 size_t drt_linear_scratch_bytes(int32_t rows, int32_t n, int32_t K, int32_t splits);
 int drt_linear_bf16(const void* x, const void* w, float* y, int32_t rows, int32_t n, int32_t K, int32_t splits,

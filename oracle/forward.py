@@ -21,7 +21,7 @@ import math
 import numpy as np
 
 from .numerics import bf16_round, rope_half_tables
-from .quant import dequantize, quantize_q4
+from .quant import dequantize, dequantize_q8, quantize_q4, quantize_q8
 
 
 def visible_mask(q_pos: np.ndarray, kv_len: int, *, prompt_len: int, block_size: int, bidirectional: bool) -> np.ndarray:
@@ -60,17 +60,19 @@ def _lin32q(x: np.ndarray, wq, b=None) -> np.ndarray:
     return y
 
 
-def quantized_weights(weights: dict, cfg: dict) -> dict:
+def quantized_weights(weights: dict, cfg: dict, bits: int = 4) -> dict:
     """The dequantized f32 copies of every quantized linear (layer q/k/v/o, gate/up, down and
-    lm_head; reference keys mlx_dream.py:2033-2087), keyed like ``weights``."""
+    lm_head; reference keys mlx_dream.py:2033-2087), keyed like ``weights``; ``bits`` 4 (4-bit affine)
+    or 8 (int8 weight-only, bf16-exact values)."""
     out = {}
     keys = [k for k in weights if k.startswith("model.layers.") and k.endswith(
         (".q_proj.weight", ".k_proj.weight", ".v_proj.weight", ".o_proj.weight", ".gate_proj.weight",
          ".up_proj.weight", ".down_proj.weight"))]
     lm = weights.get("lm_head.weight", weights["model.embed_tokens.weight"])
+    quant, deq = (quantize_q8, dequantize_q8) if bits == 8 else (quantize_q4, dequantize)
     for k in keys:
-        out[k] = dequantize(*quantize_q4(weights[k]))
-    out["lm_head.weight"] = dequantize(*quantize_q4(lm))
+        out[k] = deq(*quant(weights[k]))
+    out["lm_head.weight"] = deq(*quant(lm))
     return out
 
 
@@ -124,7 +126,7 @@ ATTENTION_OPERANDS = {"f32": _sdpa32, "bf16": _sdpa_bf16_operands}
 
 def forward_mlx(weights: dict, cfg: dict, token_ids, *, prompt_len: int = 0, block_size: int = 32,
                 bidirectional: bool = False, output_rows=None, rope=None, quant: dict | None = None,
-                attn_operands: str = "f32") -> np.ndarray:
+                attn_operands: str = "f32", quant_bits: int = 4) -> np.ndarray:
     """Logits [len(output_rows) (or S), V] f32 of a full-window forward (no cache). With ``quant``
     (``quantized_weights``), every quantized linear follows the quantized-matmul contract.
     ``attn_operands="bf16"`` rounds the attention's Q, K and softmax weights to bf16 as tensor-core
@@ -146,7 +148,9 @@ def forward_mlx(weights: dict, cfg: dict, token_ids, *, prompt_len: int = 0, blo
         def lin(x, key, bias_key=None):
             b = g(bias_key) if bias_key else None
             if quant is not None:
-                return _lin32q(x, quant[p + key], b)
+                # 4-bit: the quantized-matmul contract; int8 weight-only: the bf16 linear contract
+                # over the dequantized (bf16-exact) weights
+                return _lin32q(x, quant[p + key], b) if quant_bits == 4 else _lin32(x, quant[p + key], b)
             return _lin32(x, g(key), b)
 
         n = _rms32(h, g("input_layernorm.weight"), eps)
@@ -168,7 +172,7 @@ def forward_mlx(weights: dict, cfg: dict, token_ids, *, prompt_len: int = 0, blo
     rows = np.arange(S) if output_rows is None else np.asarray(output_rows, dtype=np.int64)
     hn = _rms32(h[rows], weights["model.norm.weight"], eps)
     if quant is not None:
-        return _lin32q(hn, quant["lm_head.weight"])
+        return _lin32q(hn, quant["lm_head.weight"]) if quant_bits == 4 else _lin32(hn, quant["lm_head.weight"])
     return _lin32(hn, weights["lm_head.weight"])
 
 
@@ -252,7 +256,8 @@ class PrefixKV:
 
 
 def forward_mlx_cached(weights: dict, cfg: dict, token_ids, cache: PrefixKV, *, frozen: int, output_rows,
-                       prompt_len: int = 0, block_size: int = 32, rope=None, attn_operands: str = "f32") -> np.ndarray:
+                       prompt_len: int = 0, block_size: int = 32, rope=None, attn_operands: str = "f32",
+                       quant: dict | None = None, quant_bits: int = 4) -> np.ndarray:
     """``forward_mlx`` logits of ``output_rows`` (absolute positions) for the window ``token_ids``,
     computing only rows [cache.length, len(token_ids)) against the cached K/V, then caching the
     rows [cache.length, frozen) (final tokens). Under the block-causal d2f mask a cached row never
@@ -276,7 +281,10 @@ def forward_mlx_cached(weights: dict, cfg: dict, token_ids, cache: PrefixKV, *, 
         g = lambda key: weights.get(p + key)  # noqa: E731
 
         def lin(x, key, bias_key=None):
-            return _lin32(x, g(key), g(bias_key) if bias_key else None)
+            b = g(bias_key) if bias_key else None
+            if quant is not None:
+                return _lin32q(x, quant[p + key], b) if quant_bits == 4 else _lin32(x, quant[p + key], b)
+            return _lin32(x, g(key), b)
 
         x1 = _rms32(h, g("input_layernorm.weight"), eps)
         q = lin(x1, "self_attn.q_proj.weight", "self_attn.q_proj.bias").reshape(S, nq, d)
@@ -304,4 +312,6 @@ def forward_mlx_cached(weights: dict, cfg: dict, token_ids, cache: PrefixKV, *, 
     if rows.min(initial=0) < 0:
         raise ValueError("output rows inside the cached prefix")
     hn = _rms32(h[rows], weights["model.norm.weight"], eps)
+    if quant is not None:
+        return _lin32q(hn, quant["lm_head.weight"]) if quant_bits == 4 else _lin32(hn, quant["lm_head.weight"])
     return _lin32(hn, weights["lm_head.weight"])

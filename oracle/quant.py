@@ -51,3 +51,31 @@ def dequantize(q: np.ndarray, scale: np.ndarray, bias: np.ndarray) -> np.ndarray
     s = np.repeat(scale, GROUP, axis=1)
     b = np.repeat(bias, GROUP, axis=1)
     return (s * q.astype(np.float32)).astype(np.float32) + b
+
+
+def quantize_q8(w) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """int8 weight-only quantization (the build's definition, ``quant.cuh``), in float32:
+        amax = max |w| of the 64 bf16 weights of a group;  scale = bf16_round(amax / 127)
+        q = clip(rint(w / scale), -127, 127)                  (q = 0 where scale == 0)
+    returned as the stored bytes q + 128 (uint8 [n, K]), scale and bias = -128 * scale (f32 [n, K // 64]
+    holding bf16 values)."""
+    w = np.asarray(bf16_round(np.asarray(w, dtype=np.float32)), dtype=np.float32)
+    n, K = w.shape
+    if K % GROUP:
+        raise ValueError("in-dim must be a multiple of 64")
+    g = w.reshape(n, K // GROUP, GROUP)
+    amax = np.abs(g).max(axis=-1)
+    scale = bf16_round(amax.astype(np.float32) / np.float32(127.0))
+    with np.errstate(divide="ignore", invalid="ignore"):
+        t = np.rint((g / scale[..., None]).astype(np.float32))
+    t = np.where(scale[..., None] > 0, t, 0.0)
+    q = (np.clip(t, -127, 127) + 128).astype(np.uint8).reshape(n, K)
+    return q, scale.astype(np.float32), (np.float32(-128.0) * scale).astype(np.float32)
+
+
+def dequantize_q8(q: np.ndarray, scale: np.ndarray, bias: np.ndarray) -> np.ndarray:
+    """The int8 weight-only linear's weight values: bf16_round(scale * byte + bias) = bf16_round(scale
+    * (byte - 128)), the bf16 operand the tensor cores take."""
+    s = np.repeat(scale, GROUP, axis=1)
+    b = np.repeat(bias, GROUP, axis=1)
+    return bf16_round((s * q.astype(np.float32)).astype(np.float32) + b)

@@ -27,7 +27,7 @@ from oracle import selector as osel
 
 
 def check_bd3_trajectory(dev: dict, weights: dict, cfg: dict, prompt: list[int], *, gen: int, steps: int,
-                         block_size: int) -> dict:
+                         block_size: int, quant: dict | None = None, quant_bits: int = 4) -> dict:
     mask, eos = cfg["mask_token_id"], cfg["eos_token_id"]
     c = opol.Canvas(list(prompt) + [mask] * gen, len(prompt), mask, eos)
     pol = opol.BD3FixedQuota(block_size=block_size, steps=steps, prompt_len=len(prompt), gen_len=gen)
@@ -48,7 +48,7 @@ def check_bd3_trajectory(dev: dict, weights: dict, cfg: dict, prompt: list[int],
         assert tr["step"] == step and tr["frontier"] == plan.frontier, step
         frozen = (min(plan.frontier) // block_size) * block_size
         logits = ofwd.forward_mlx_cached(weights, cfg, c.x[:plan.window_end], cache, frozen=frozen,
-                                         output_rows=plan.frontier, rope=rope)
+                                         output_rows=plan.frontier, rope=rope, quant=quant, quant_bits=quant_bits)
         conf, tok = osel.max_prob_rows(logits)
         E = MAX_FACTOR * U_BF16 * float(np.sqrt(np.mean(np.square(logits.astype(np.float64)))))
         lc_dev, lc_or = np.log(np.asarray(tr["scores"])), np.log(conf)

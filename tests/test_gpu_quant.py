@@ -5,8 +5,8 @@
 * the quantized decode linear equals y = x @ bf16(scale * q + bias)^T accumulated in f32 (its own
   operand rounding) tightly, and the reference's quantized-matmul contract (f32 activations,
   f32 dequantized weights) within the bf16 operand-rounding tolerance;
-* a quantized model's window forward matches the CPU oracle's quantized forward, and its
-  device decode agrees with the oracle decode on certified steps.
+* a quantized model's window forward matches the CPU oracle's quantized forward within the stated
+  bf16 tolerance, and its device decode is checked step by step along its trajectory.
 """
 from __future__ import annotations
 
@@ -112,33 +112,16 @@ def test_quantized_window_forward_matches_oracle(qrt, qweights):
     assert_logits_close(got, want)
 
 
-def test_quantized_decode_matches_oracle_on_certified_steps(qrt, qweights):
+def test_quantized_decode_along_trajectory(qrt, qweights):
     """BD3 fixed-quota decode with k = 2 commits per step on the quantized model (the cfg3 policy
-    shape) against the oracle decode driven by the oracle's quantized forward."""
+    shape), checked step by step along the device trajectory against the oracle's quantized forward
+    (tests/decode_check.py)."""
+    from decode_check import check_bd3_trajectory
+
     w, qw = qweights
     prompt = _prompt(64, 13)
     gen, steps, bs = 64, 32, 32
-    mask, eos = SMALL["mask_token_id"], SMALL["eos_token_id"]
     with qrt.session({"decode_strategy": "bd3_fixed_quota", "block_size": bs}) as s:
         dev_out = s.generate(prompt, max_tokens=gen, steps=steps, block_size=bs, trace_steps=256)
-    c = opol.Canvas(list(prompt) + [mask] * gen, len(prompt), mask, eos)
-    pol = opol.BD3FixedQuota(block_size=bs, steps=steps, prompt_len=len(prompt), gen_len=gen)
-    agreed = 0
-    for tr in dev_out["trace"]:
-        plan = pol.plan(c, tr["step"])
-        assert plan.action == "proceed"
-        assert plan.frontier == tr["frontier"]
-        logits = ofwd.forward_mlx(w, SMALL, c.x[:plan.window_end], prompt_len=0, block_size=bs,
-                                  output_rows=plan.frontier, quant=qw)
-        conf, tok = osel.max_prob_rows(logits)
-        rows = pol.select(conf)
-        if not (sorted(rows) == tr["chosen"] and all(tok[r] == tr["tokens"][r] for r in rows)):
-            order = np.sort(conf)[::-1]
-            k = len(rows)
-            gap = (order[k - 1] - order[k]) / order[k - 1] if k < len(order) else 1.0
-            assert gap < 0.05, (tr["step"], gap)
-            break
-        agreed += 1
-        for r in rows:
-            c.x[plan.frontier[r]] = tok[r]
-    assert agreed >= 4
+    report = check_bd3_trajectory(dev_out, w, SMALL, prompt, gen=gen, steps=steps, block_size=bs, quant=qw, quant_bits=4)
+    assert report["steps"] == steps, report

@@ -623,6 +623,72 @@ def _cpu_selector_baseline(sample_rows: int = 48) -> dict:
             "sample": f"{sample_rows} rows of 151936 fp32 logits: max-prob confidence, top-k 1/4/8 and threshold choices"}
 
 
+def _profile_case(args) -> None:
+    """A small, self-contained decode run for profilers (``--profile-case``): the bench workload's
+    kernels at the bench's shapes with few launches before them, about 2 GB on the device.
+
+      cfg1:  Qwen3-0.6B-architecture BD3LM, one --pc-prompt (4096) token prompt and one --pc-gen (32)
+             token block under block_threshold with --pc-rounds (8) rounds;
+      quant: the 4-bit affine model (configs[3]) under bd3_fixed_quota, 16 rounds per 32-token block;
+             every forward, prompt chunks included, runs the quantized decode linear in 64-row chunks;
+      dream: Dream-7B full canvas (prompt 256 + canvas 256), entropy_count over --pc-steps (4) steps,
+             --pc-layers layers (0: the model's 28); ~15 GB of synthetic weights.
+
+    Kernel order, for a profiler's name filter and skip count: the prompt prefill launches one
+    embed_rows_kernel and two rmsnorm_bf16_kernel per layer (with the prefill linears and attention);
+    every denoising step then launches plan_kernel, embed_rows_kernel, per layer [rmsnorm, gemm_decode
+    (QKV), attn_decode, attn_merge, gemm_decode (o), rmsnorm, gemm_decode (gate/up), gemm_decode
+    (down)], then rmsnorm, gemm_lm_kernel (lm_head; gemm_decode for the 4-bit model), sel_pass1_kernel
+    and commit_kernel. A Dream step: dream_plan_kernel, embed_rows_kernel, per layer [rmsnorm,
+    gemm_swapab (QKV), attention, gemm_swapab (o), rmsnorm, gemm_swapab (gate/up), gemm_swapab
+    (down)], rmsnorm, gemm_swapab (lm_head), sel_topp_entropy_kernel, dream_commit_kernel.
+
+    Prints one JSON line: denoising steps run, kernel launches of the request and ms per step."""
+    args.dream = args.profile_case == "dream"
+    args.quant = args.profile_case == "quant"
+    args.prompt, args.gen, args.rounds, args.steps, args.layers = (args.pc_prompt, args.pc_gen, args.pc_rounds,
+                                                                    args.pc_steps, args.pc_layers)
+    from diffusorrt_b200 import Runtime
+    from diffusorrt_b200.config import DREAM_7B, QWEN3_06B_BD3LM
+
+    if args.dream:
+        prompt_len = 256 if args.prompt == 4096 else args.prompt
+        gen = 256 if args.gen == 32 else args.gen
+        canvas = prompt_len + gen
+        cfg = dict(DREAM_7B)
+        if args.layers > 0:
+            cfg["layer_count"] = args.layers
+        rt = Runtime(model_config=cfg, synthetic_seed=0, device_ordinal=0, max_seq=canvas, max_prefill_rows=canvas)
+        sess = rt.session({"decode_strategy": "entropy_count"})
+        prompt = [int(t) for t in np.random.default_rng(0).integers(0, 151643, size=prompt_len)]
+        res = sess.generate(prompt, max_tokens=gen, steps=args.steps, temperature=0.2, top_p=0.95, eps=1e-3)
+        forwards = int(res["forward_count"])
+        print(json.dumps({"prompt": prompt_len, "gen": gen, "forwards": forwards,
+                          "kernel_launches": int(res["kernel_launches"]),
+                          "decode_ms_per_step": res["decode_ms"] / max(1, forwards)}), flush=True)
+        sess.close()
+        rt.close()
+        return
+
+    cfg = dict(QWEN3_06B_BD3LM)
+    max_seq = ((args.prompt + args.gen + 127) // 128) * 128
+    engine = {"linear_quant_bits": 4, "linear_quant_group_size": 64} if args.quant else None
+    rt = Runtime(model_config=cfg, synthetic_seed=0, device_ordinal=0, max_seq=max_seq,
+                 max_prefill_rows=min(4096, ((args.prompt + 127) // 128) * 128), engine_config=engine)
+    strategy = "bd3_fixed_quota" if args.quant else "block_threshold"
+    sess = rt.session({"decode_strategy": strategy, "block_size": 32})
+    prompt = [int(t) for t in np.random.default_rng(0).integers(0, 151643, size=args.prompt)]
+    steps = (args.gen // 32) * (16 if args.quant else args.rounds)
+    res = sess.generate(prompt, max_tokens=args.gen, steps=steps, block_size=32, decode_strategy=strategy,
+                        confidence_threshold=0.9, rounds_per_block=0 if args.quant else args.rounds)
+    forwards = int(res["forward_count"])
+    print(json.dumps({"prompt": args.prompt, "gen": args.gen, "forwards": forwards,
+                      "kernel_launches": int(res["kernel_launches"]),
+                      "decode_ms_per_step": res["decode_ms"] / max(1, forwards)}), flush=True)
+    sess.close()
+    rt.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -631,7 +697,17 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="cfg1", choices=sorted(WORKLOADS) + ["cfg2", "cfg4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", choices=["cfg1", "quant", "dream"],
+                    help="run one small decode for a profiler instead of the benchmark (see _profile_case)")
+    ap.add_argument("--pc-prompt", type=int, default=4096)
+    ap.add_argument("--pc-gen", type=int, default=32)
+    ap.add_argument("--pc-rounds", type=int, default=8)
+    ap.add_argument("--pc-steps", type=int, default=4)
+    ap.add_argument("--pc-layers", type=int, default=0)
     args = ap.parse_args()
+    if args.profile_case:
+        _profile_case(args)
+        return
     args.warmup = max(3, args.warmup)
     world, rank, local = _dist()
     if args.impl == "reference" and args.workload == "cfg4":

@@ -163,6 +163,29 @@ def _measured_traffic(alg_bytes: float) -> float | None:
     return float(d["dram_bytes_per_step"]) * alg_bytes / float(d["algorithmic_bytes_per_step"])
 
 
+def _frontier_stats(sess, prompt, w, probe) -> dict:
+    """Logit scale and decision margins at the frontier (outside the timed region): the std of the
+    first block's frontier logits (one window forward), the spread of the rows' max-prob confidences,
+    and per step the gap between the best and second-best frontier confidence (the margin of the
+    block-threshold / top-k choice) over the traced request."""
+    mask = int(sess.runtime.config["mask_token_id"])
+    n = len(prompt)
+    scope = list(range(n, n + w["block"]))
+    res = sess.execute_window(list(prompt) + [mask] * w["block"], scope, mask_geometry=(0, w["block"]))
+    logits = np.frombuffer(res.logits, dtype="<f4").reshape(res.n_rows, res.n_vocab).astype(np.float64)
+    x = logits - logits.max(axis=1, keepdims=True)
+    max_prob = 1.0 / np.exp(x).sum(axis=1)
+    gaps = []
+    for t in probe["trace"]:
+        sc = sorted(t["scores"], reverse=True)
+        if len(sc) >= 2:
+            gaps.append(sc[0] - sc[1])
+    q = lambda a, v: float(np.quantile(a, v)) if len(a) else None  # noqa: E731
+    return {"frontier_logit_std": round(float(logits.std()), 5),
+            "frontier_max_prob": {"p10": q(max_prob, 0.1), "p50": q(max_prob, 0.5), "p90": q(max_prob, 0.9)},
+            "step_conf_gap_top2": {"p10": q(gaps, 0.1), "p50": q(gaps, 0.5), "p90": q(gaps, 0.9), "steps": len(gaps)}}
+
+
 def _run_ours(args, world, rank, local) -> dict | None:
     import torch
 
@@ -220,6 +243,7 @@ def _run_ours(args, world, rank, local) -> dict | None:
         import torch.distributed as dist
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     dev_ms, e2e_ms, dec_ms, pre_ms = (float(v) for v in stats.tolist())
+    margins = _frontier_stats(sess, prompt, w, probe) if rank == 0 else None
     sess.close()
     rt.close()
     if rank != 0:
@@ -251,7 +275,8 @@ def _run_ours(args, world, rank, local) -> dict | None:
                    "requests_per_gpu": 1, "parallelism": f"request-parallel x{world}",
                    "committed_tokens_per_request": committed, "denoising_steps_per_request": forwards,
                    "l2": (f"inputs larger than L2: {_weight_bytes(cfg, bool(w.get('quant'))) / 1e9:.2f} GB of weights "
-                          "streamed every denoising step")},
+                          "streamed every denoising step"),
+                   "frontier": margins},
         "roofline": {"bound": "hbm", "kernel": "one denoising step (CUDA graph of the step's kernels)",
                      "weights": "4-bit affine" if w.get("quant") else "bf16",
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -631,6 +656,9 @@ def _profile_case(args) -> None:
              token block under block_threshold with --pc-rounds (8) rounds;
       quant: the 4-bit affine model (configs[3]) under bd3_fixed_quota, 16 rounds per 32-token block;
              every forward, prompt chunks included, runs the quantized decode linear in 64-row chunks;
+             --pc-bits 8 loads the int8 weight-only model instead;
+      cfg1 with --pc-temperature T > 0: bd3_fixed_quota with 16 rounds per block, each row's token
+             drawn by the sampling selector (Gumbel keys, seed 0);
       dream: Dream-7B full canvas (prompt 256 + canvas 256), entropy_count over --pc-steps (4) steps,
              --pc-layers layers (0: the model's 28); ~15 GB of synthetic weights.
 
@@ -672,15 +700,17 @@ def _profile_case(args) -> None:
 
     cfg = dict(QWEN3_06B_BD3LM)
     max_seq = ((args.prompt + args.gen + 127) // 128) * 128
-    engine = {"linear_quant_bits": 4, "linear_quant_group_size": 64} if args.quant else None
+    engine = {"linear_quant_bits": args.pc_bits, "linear_quant_group_size": 64} if args.quant else None
     rt = Runtime(model_config=cfg, synthetic_seed=0, device_ordinal=0, max_seq=max_seq,
                  max_prefill_rows=min(4096, ((args.prompt + 127) // 128) * 128), engine_config=engine)
-    strategy = "bd3_fixed_quota" if args.quant else "block_threshold"
+    fixed = args.quant or args.pc_temperature > 0
+    strategy = "bd3_fixed_quota" if fixed else "block_threshold"
     sess = rt.session({"decode_strategy": strategy, "block_size": 32})
     prompt = [int(t) for t in np.random.default_rng(0).integers(0, 151643, size=args.prompt)]
-    steps = (args.gen // 32) * (16 if args.quant else args.rounds)
+    steps = (args.gen // 32) * (16 if fixed else args.rounds)
     res = sess.generate(prompt, max_tokens=args.gen, steps=steps, block_size=32, decode_strategy=strategy,
-                        confidence_threshold=0.9, rounds_per_block=0 if args.quant else args.rounds)
+                        confidence_threshold=0.9, rounds_per_block=0 if fixed else args.rounds,
+                        temperature=args.pc_temperature)
     forwards = int(res["forward_count"])
     print(json.dumps({"prompt": args.prompt, "gen": args.gen, "forwards": forwards,
                       "kernel_launches": int(res["kernel_launches"]),
@@ -704,6 +734,9 @@ def main():
     ap.add_argument("--pc-rounds", type=int, default=8)
     ap.add_argument("--pc-steps", type=int, default=4)
     ap.add_argument("--pc-layers", type=int, default=0)
+    ap.add_argument("--pc-bits", type=int, default=4, choices=(4, 8), help="--profile-case quant: weight bits")
+    ap.add_argument("--pc-temperature", type=float, default=0.0,
+                    help="--profile-case cfg1: > 0 samples each row's token (bd3_fixed_quota)")
     args = ap.parse_args()
     if args.profile_case:
         _profile_case(args)

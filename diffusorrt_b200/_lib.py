@@ -131,6 +131,7 @@ SIGNATURES = {
     "drt_session_metrics": (ctypes.c_int, [_P, ctypes.POINTER(Metrics)]),
     "drt_session_tp_handle": (ctypes.c_int, [_P, ctypes.c_char_p]),
     "drt_session_tp_connect": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_int32]),
+    "drt_session_tp_vocab_parallel": (ctypes.c_int, [_P, ctypes.c_int32]),
     "drt_session_peer_wait_drill": (ctypes.c_int, [_P]),
     "drt_entropy_count_schedule": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_double, _I32P]),
     "drt_session_kv_pointers": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P)]),

@@ -842,12 +842,18 @@ struct drt_session {
   float* logits = nullptr;
   float* ss = nullptr;                // [kMaxFwdRows][H / 128] partial sums of squares of h (decode)
   float* part = nullptr;              // [rows_cap][H] f32 linear partials (tensor-parallel models)
-  // tensor parallel over peer memory: receive buffers [2][world][rows_cap][H] f32 followed by flags
-  // [2][kTpMaxRanks] u64, in one allocation shared with the peers through CUDA IPC
+  // tensor parallel over peer memory: receive buffers [2][world][rows_cap][H] f32, all-gather
+  // buffers [2][rows_cap][H] bf16, flags [3][2][kTpMaxRanks] u64 and the logits [head_cap][V] f32,
+  // in one allocation shared with the peers through CUDA IPC
   uint8_t* tp_buf = nullptr;
   uint8_t* tp_peer[kTpMaxRanks] = {};
   bool tp_p2p = false;
-  int* tp_count = nullptr;            // [4] arrival counters: pushing linears [2], reduce-scatter [2]
+  // vocabulary-parallel lm_head (peers mapped): this rank projects vocabulary tiles
+  // [lm_t0, lm_t0 + lm_tiles) and stores them into every rank's logits
+  bool tp_vocab = false;
+  int lm_t0 = 0, lm_tiles = 0;
+  CUtensorMap m_lm_shard;
+  int* tp_count = nullptr;            // [5] arrival counters: pushing linears [2], reduce-scatter [2], lm_head gather
   unsigned long long* tp_epoch = nullptr;
   __nv_bfloat16 *kcache = nullptr, *vtcache = nullptr;
   int max_cluster = 16;               // largest cluster the GPU schedules for the split kernels
@@ -928,8 +934,10 @@ int salloc(drt_session* s, T** p, size_t count) {
 // bf16 sums, reduce-scatter flags [2][kTpMaxRanks] and all-gather flags [2][kTpMaxRanks] (u64).
 size_t tp_buf_bytes(const drt_session* s) {
   const size_t slot = static_cast<size_t>(s->rows_cap) * s->m->H;
-  return 2 * static_cast<size_t>(s->m->shard.world) * slot * sizeof(float) + 2 * slot * sizeof(__nv_bfloat16) +
-         4 * kTpMaxRanks * sizeof(unsigned long long);
+  const size_t flags = 6 * kTpMaxRanks * sizeof(unsigned long long);
+  const size_t head = (2 * static_cast<size_t>(s->m->shard.world) * slot * sizeof(float) + 2 * slot * sizeof(__nv_bfloat16) +
+                       flags + 255) / 256 * 256;
+  return head + static_cast<size_t>(s->head_cap) * s->m->V * sizeof(float);
 }
 
 int check_status(drt_session* s) {
@@ -1112,9 +1120,10 @@ size_t tp_recv_offset(const drt_session* s, int b, int src) {
 size_t tp_ag_offset(const drt_session* s, int b) {
   return tp_recv_offset(s, 2, 0) + static_cast<size_t>(b) * tp_slot(s) * sizeof(__nv_bfloat16);
 }
-size_t tp_flag_offset(const drt_session* s, int kind, int b, int src) {  // kind 0: reduce-scatter, 1: all-gather
+size_t tp_flag_offset(const drt_session* s, int kind, int b, int src) {  // kind 0: reduce-scatter, 1: all-gather, 2: lm_head
   return tp_ag_offset(s, 2) + ((static_cast<size_t>(kind) * 2 + b) * kTpMaxRanks + src) * sizeof(unsigned long long);
 }
+size_t tp_logits_offset(const drt_session* s) { return (tp_flag_offset(s, 3, 0, 0) + 255) / 256 * 256; }
 
 // Tensor parallel over peer memory, for one row-split linear (o_proj: buffer 0, down_proj: 1):
 //   1. the linear (EPI_TP_PUSH) stores each f32 partial tile into this rank's slot of the receive
@@ -1175,6 +1184,44 @@ int tp_push_linear(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB1
     CK(launch_k(tp_rs_kernel, dim3(blocks), dim3(256), 0, s->stream, true, t));
     CK(launch_k(tp_ag_kernel, dim3(blocks), dim3(256), 0, s->stream, true, t));
   }
+  return DRT_OK;
+}
+
+// Vocabulary-parallel lm_head over peer memory: this rank projects its vocabulary tiles of the
+// final-norm rows (s->xf) and the epilogue stores each logit tile, rounded as the single-GPU head
+// rounds it, into every rank's logits at the tile's vocabulary columns (EPI_TP_GATHER); the last
+// CTA raises this rank's lm_head flag on every rank, and tp_gather_wait_kernel holds the selector
+// until every rank's flag is up. Every rank then holds the whole [rows][V] logits, equal bit for
+// bit to one GPU's (each logit is computed once, by the same arithmetic), and runs the selector on
+// them. A rank overwrites a peer's logits only in the next step's head, after the peer's layer
+// reductions of that step, which follow its selector in stream order.
+int tp_gather_head(drt_session* s, int rows, const int* rows_dev) {
+  drt_model* m = s->m;
+  const int world = m->shard.world, me = m->shard.rank;
+  Fwd f = {};
+  f.rows = rows;
+  f.rows_dev = rows_dev;
+  GemmArgs a = base_args(s, s->lm_tiles * 128, m->H, f);
+  a.epi = EPI_TP_GATHER;
+  a.ld_out = m->V;
+  a.tp_world = world;
+  a.tp_tag = 2 * m->L;
+  a.tp_count = s->tp_count + 4;
+  a.tp_epoch = s->tp_epoch;
+  for (int r = 0; r < world; ++r) {
+    a.tp_dst[r] = reinterpret_cast<float*>(s->tp_peer[r] + tp_logits_offset(s)) + static_cast<size_t>(s->lm_t0) * 128;
+    a.tp_flag[r] = reinterpret_cast<unsigned long long*>(s->tp_peer[r] + tp_flag_offset(s, 2, 0, me));
+  }
+  TRY(run_wide(s, s->m_lm_shard, s->m_xf128, s->head_cap >= 256 ? &s->m_xf256 : nullptr, a));
+  TpStep t;
+  memset(&t, 0, sizeof(t));
+  t.rs_flags = reinterpret_cast<const unsigned long long*>(s->tp_buf + tp_flag_offset(s, 2, 0, 0));
+  t.epoch = s->tp_epoch;
+  t.tag = 2 * m->L;
+  t.world = world;
+  t.rank = me;
+  t.status = s->status;
+  CK(launch_k(tp_gather_wait_kernel, dim3(1), dim3(32), 0, s->stream, true, t));
   return DRT_OK;
 }
 
@@ -1460,11 +1507,15 @@ int capture_dream(drt_session* s, const DreamState& g, double temperature, doubl
     Fwd f = {};
     f.rows = gen_cap;
     f.rows_dev = n_dev;
-    GemmArgs a = base_args(s, m->V, m->H, f);
-    a.epi = EPI_STORE_F32;
-    a.out_f32 = s->logits;
-    a.ld_out = m->V;
-    rc = run_wide(s, m->m_lm, s->m_xf128, s->head_cap >= 256 ? &s->m_xf256 : nullptr, a);
+    if (s->tp_p2p && s->tp_vocab) {
+      rc = tp_gather_head(s, gen_cap, n_dev);
+    } else {
+      GemmArgs a = base_args(s, m->V, m->H, f);
+      a.epi = EPI_STORE_F32;
+      a.out_f32 = s->logits;
+      a.ld_out = m->V;
+      rc = run_wide(s, m->m_lm, s->m_xf128, s->head_cap >= 256 ? &s->m_xf256 : nullptr, a);
+    }
   }
   if (rc == DRT_OK) {
     ToppArgs t;
@@ -1712,15 +1763,18 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = salloc(s, &s->act, static_cast<size_t>(R) * m->I)) != DRT_OK) return fail(rc);
   const int xf_rows = std::max(s->head_cap, 128);  // the final-norm rows, at least one 128-row box
   if ((rc = salloc(s, &s->xf, static_cast<size_t>(xf_rows) * H)) != DRT_OK) return fail(rc);
-  if ((rc = salloc(s, &s->logits, static_cast<size_t>(s->head_cap) * m->V)) != DRT_OK) return fail(rc);
+  // a tensor-parallel session's logits live in its peer-mapped buffer (below): with the
+  // vocabulary-parallel lm_head every rank's projection stores its tiles there
+  if (m->shard.world <= 1 && (rc = salloc(s, &s->logits, static_cast<size_t>(s->head_cap) * m->V)) != DRT_OK) return fail(rc);
   if ((rc = salloc(s, &s->ss, static_cast<size_t>(kMaxFwdRows) * (H / 128))) != DRT_OK) return fail(rc);
   if (m->shard.world > 1) {
     if ((rc = salloc(s, &s->part, static_cast<size_t>(R) * H)) != DRT_OK) return fail(rc);
     const size_t bytes = tp_buf_bytes(s);
     if ((rc = salloc(s, &s->tp_buf, bytes)) != DRT_OK) return fail(rc);
-    if ((rc = salloc(s, &s->tp_count, 4)) != DRT_OK) return fail(rc);
+    s->logits = reinterpret_cast<float*>(s->tp_buf + tp_logits_offset(s));
+    if ((rc = salloc(s, &s->tp_count, 5)) != DRT_OK) return fail(rc);
     if ((rc = salloc(s, &s->tp_epoch, 1)) != DRT_OK) return fail(rc);
-    if (cudaMemset(s->tp_buf, 0, bytes) != cudaSuccess || cudaMemset(s->tp_count, 0, 4 * sizeof(int)) != cudaSuccess ||
+    if (cudaMemset(s->tp_buf, 0, bytes) != cudaSuccess || cudaMemset(s->tp_count, 0, 5 * sizeof(int)) != cudaSuccess ||
         cudaMemset(s->tp_epoch, 0, sizeof(unsigned long long)) != cudaSuccess)
       return fail(set_error(DRT_INTERNAL_ERROR, "memset failed"));
   }
@@ -2273,7 +2327,30 @@ extern "C" int drt_session_tp_connect(drt_session* s, const void* handles, int32
     s->tp_peer[r] = static_cast<uint8_t*>(p);
   }
   s->tp_p2p = true;
+  // Vocabulary-parallel lm_head: rank r projects the tiles [r T / w, (r + 1) T / w) of the T
+  // vocabulary tiles (128 rows each), from its replicated copy of the weight.
+  drt_model* m = s->m;
+  const int tiles = m->V / 128;
+  s->tp_vocab = false;
+  if (!m->quantized && m->V % 128 == 0 && tiles >= world) {
+    s->lm_t0 = static_cast<int>((static_cast<long long>(me) * tiles) / world);
+    s->lm_tiles = static_cast<int>((static_cast<long long>(me + 1) * tiles) / world) - s->lm_t0;
+    TRY(map_matrix(&s->m_lm_shard, m->lm_head + static_cast<size_t>(s->lm_t0) * 128 * m->H, s->lm_tiles * 128, m->H, 128));
+    s->tp_vocab = true;
+  }
   if (s->g_dream) { cudaGraphExecDestroy(s->g_dream); s->g_dream = nullptr; }
+  return DRT_OK;
+}
+
+extern "C" int drt_session_tp_vocab_parallel(drt_session* s, int32_t enable) {
+  REQUIRE(s, "null session");
+  REQUIRE(s->tp_p2p, "the session's peers are not mapped (drt_session_tp_connect)");
+  REQUIRE(!enable || s->lm_tiles > 0, "this model's lm_head cannot be split by vocabulary over the group");
+  if (s->tp_vocab != (enable != 0) && s->g_dream) {
+    cudaGraphExecDestroy(s->g_dream);
+    s->g_dream = nullptr;
+  }
+  s->tp_vocab = enable != 0;
   return DRT_OK;
 }
 

@@ -33,6 +33,9 @@ enum GemmEpilogue : int {
   EPI_TP_PUSH = 5,    // tensor parallel: acc (f32) into this rank's slot of the receive buffer of
                       // the rank owning the tile's features (NVLink peer store when that is another
                       // GPU); the last CTA raises this rank's flag on every rank
+  EPI_TP_GATHER = 6,  // vocabulary-parallel lm_head: bf16r(acc) + bias into every rank's logits
+                      // (tp_dst[r] already offset to this rank's first vocabulary column); the last
+                      // CTA raises this rank's flag on every rank
 };
 
 constexpr int kTpMaxRanks = 8;
@@ -146,6 +149,18 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = __fadd_rn(out_round<RND>(v[i]), b);
+    }
+    if constexpr (EPI == EPI_TP_GATHER) {
+      // the single-GPU head's values (EPI_STORE_F32), stored into every rank's logits
+      float o[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = __fadd_rn(out_round<RND>(v[i]), b);
+      for (int r = 0; r < a.tp_world; ++r) {
+        float* dst = a.tp_dst[r];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < ncols) dst[static_cast<size_t>(col0 + i) * a.ld_out + n] = o[i];
+      }
     }
     if constexpr (EPI == EPI_RESID) {
       float cur[32];
@@ -291,6 +306,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
     case EPI_SWIGLU: gemm_epilogue_chunk_t<EPI_SWIGLU>(a, v, col0, ncols, m0, tid, xs, pos0); break;
     case EPI_QKV: gemm_epilogue_chunk_t<EPI_QKV>(a, v, col0, ncols, m0, tid, xs, pos0); break;
     case EPI_TP_PUSH: gemm_epilogue_chunk_t<EPI_TP_PUSH>(a, v, col0, ncols, m0, tid, xs, pos0); break;
+    case EPI_TP_GATHER: gemm_epilogue_chunk_t<EPI_TP_GATHER>(a, v, col0, ncols, m0, tid, xs, pos0); break;
     default: break;
   }
 }
@@ -484,7 +500,7 @@ __global__ void __launch_bounds__(128, 1)
         gemm_epilogue_chunk(a, v, n0 + cb, min(32, ncol_valid - cb), m0, tid, xs, pos0);
       }
     }
-    if (a.epi == EPI_TP_PUSH) {
+    if (a.epi == EPI_TP_PUSH || a.epi == EPI_TP_GATHER) {
       // Every CTA's peer stores are made visible system-wide before it arrives; the last CTA of the
       // grid then raises this rank's flag in every rank's flag array (failed CTAs arrive too, so
       // the peers' waits end; the status word carries the failure).

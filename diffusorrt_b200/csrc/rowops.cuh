@@ -308,6 +308,14 @@ __global__ void tp_ag_kernel(const TpStep a) {
   }
 }
 
+// Holds the kernels after it until every rank's vocabulary-parallel lm_head has stored its logit
+// tiles here (a.rs_flags: this rank's lm_head flag array, a.tag: the head's tag). Bounded.
+__global__ void tp_gather_wait_kernel(const TpStep a) {
+  griddep_wait();
+  tp_wait_flags(a.rs_flags, a.epoch, a.tag, a.world, a.status);
+  griddep_launch_dependents();
+}
+
 __global__ void tp_tick_kernel(unsigned long long* epoch) {
   griddep_wait();
   griddep_launch_dependents();

@@ -369,6 +369,9 @@ class Session:
             handles = [None] * runtime.tp_world
             dist.all_gather_object(handles, buf.raw)
             _call(self._lib.drt_session_tp_connect(self._s, b"".join(handles), runtime.tp_world))
+            if not session_config.get("tp_vocab_parallel", True):
+                # every rank projects the whole vocabulary (the default splits the lm_head by vocabulary)
+                _call(self._lib.drt_session_tp_vocab_parallel(self._s, 0))
 
     # ------------------------------------------------------------------ reference surface
     def start_device(self, x: Sequence[int], *, prompt_len: int, block_size: int, mask_token_id: int,

@@ -268,6 +268,15 @@ int drt_session_generate(drt_session* s, const drt_generate_params* params, cons
  * NCCL all-reduce. Both calls are collective over the group. */
 int drt_session_tp_handle(drt_session* s, void* handle);
 int drt_session_tp_connect(drt_session* s, const void* handles, int32_t world);
+/* Vocabulary-parallel lm_head of a connected tensor-parallel session (no counterpart in the
+ * reference, which runs on one device; the multi-GPU Dream benchmark configuration splits the
+ * lm_head by vocabulary): rank r projects vocabulary tiles [r T / w, (r + 1) T / w) of the T 128-row tiles and its
+ * epilogue stores them into every rank's logits over NVLink, so every rank's selector sees the
+ * whole row, bit-identical to one GPU's. On by default once drt_session_tp_connect has mapped the
+ * peers (for a bf16 model whose vocabulary is a multiple of 128 with at least one tile per rank);
+ * enable = 0 makes every rank project the whole vocabulary again. Collective: every rank passes
+ * the same value before its next request. Used by the entropy_count (Dream) step. */
+int drt_session_tp_vocab_parallel(drt_session* s, int32_t enable);
 /* Failure-handling drill (no counterpart in the reference, whose ABI reports failures as
  * INTERNAL_ERROR, python/src/edllm/abi/forward.py:20-25): runs, on the session's stream, the bounded
  * wait a tensor-parallel reducer makes for a peer's partials, on a flag that nothing raises — what a

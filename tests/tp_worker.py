@@ -6,7 +6,10 @@ Every rank holds a shard of the same seeded Dream-architecture model. Checked:
   replicated, so everything downstream of it is the same computation on every rank);
 * the sharded window logits match the whole model on one GPU within the f32 summation-order and
   bf16 rounding tolerance, and match the CPU oracle forward as the single-GPU path does;
-* entropy_count generation on the group agrees with the oracle loop on certified steps.
+* entropy_count generation on the group agrees with the oracle loop on certified steps;
+* the vocabulary-parallel lm_head (each rank projects its vocabulary tiles and stores them into
+  every rank's logits) gives the same decode, bit for bit, as every rank projecting the whole
+  vocabulary.
 """
 from __future__ import annotations
 
@@ -55,6 +58,10 @@ def main() -> int:
     with rt.session({"decode_strategy": "entropy_count"}) as s:
         win = s.execute_window(ids, scope)
         out = s.generate(prompt, max_tokens=gen, steps=steps, temperature=T, top_p=TOP_P, eps=EPS, trace_steps=steps)
+    # the same request with every rank projecting the whole vocabulary: the vocabulary-parallel
+    # lm_head (the default above) gathers the same logits, so trace and canvas agree bit for bit
+    with rt.session({"decode_strategy": "entropy_count", "tp_vocab_parallel": False}) as s:
+        out_rep = s.generate(prompt, max_tokens=gen, steps=steps, temperature=T, top_p=TOP_P, eps=EPS, trace_steps=steps)
     # the NCCL all-reduce path (sessions that do not map the peers' buffers) on the same window
     with rt.session({"decode_strategy": "entropy_count", "tp_peer_memory": False}) as s:
         win_nccl = s.execute_window(ids, scope)
@@ -64,6 +71,9 @@ def main() -> int:
     allx = [None] * world
     dist.all_gather_object(allx, (logits.tobytes(), out["x"], out["trace"]))
     ok = True
+    if out_rep["x"] != out["x"] or out_rep["trace"] != out["trace"]:
+        print(f"rank {rank}: vocabulary-parallel and replicated lm_head decodes differ", flush=True)
+        ok = False
     nerr = float(np.abs(logits - logits_nccl).max())
     if nerr > 5e-3 * float(np.abs(logits).max()):
         print(f"rank {rank}: peer-memory and NCCL reductions differ by {nerr:.3e}", flush=True)

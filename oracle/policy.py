@@ -7,6 +7,8 @@ Restates from ``python/src/edllm/backends/diffusion_runtime.py``:
   * ``_block_frontier_plan`` + ``BlockThresholdCommit`` (:1023-1095), plus an optional per-block
     round budget (``rounds_cap``) that the reference does not have (0 = reference rule)
   * ``EntropyCountCommit`` (:904-941)
+  * ``D2FBlockPipelineCommit`` (:1416-1694), threshold commit rule, no revision window, no
+    initial frozen blocks
   * ``run_decode_loop`` (:1829-1991): plan -> (forward + score) -> select -> commit.
 """
 from __future__ import annotations
@@ -156,6 +158,81 @@ class EntropyCount:
 
     def select(self, scores) -> list[int]:
         return selector.topk_choices(scores, self._k)
+
+
+class D2FPipeline:
+    """A sliding window of prompt-relative blocks decoded together (D2FBlockPipelineCommit):
+
+    plan, per step: blocks with no mask leave the window oldest-first (frozen); a committed EOS in
+    the appended region stops appending; at most one new block joins when the last appended
+    block's decoded ratio is >= tau_add (the prompt counts as 1.0); block j is fully activated when
+    block j - 1's ratio is >= tau_act (the prompt / a frozen block: 1.0); the frontier is every
+    masked position of the unfrozen appended blocks, the window ends at the last appended block.
+    select: per unfrozen appended block, the rows whose score is strictly > tau_conf, else, for a
+    fully-activated block, its first most-confident row.
+
+    Activation is sticky in the reference; decoded ratios never fall (nothing is remasked), so
+    "block j - 1's ratio is >= tau_act now" is the same set."""
+
+    def __init__(self, *, block_size: int, threshold: float, add_threshold: float = 0.1,
+                 activate_threshold: float = 0.95):
+        self.bs, self.tau = int(block_size), float(threshold)
+        self.tau_add, self.tau_act = float(add_threshold), float(activate_threshold)
+        self._spans = None
+        self._frozen = 0
+        self._appended = 0
+        self._eos = False
+        self._active = []       # (lo, hi, activated) of this step's unfrozen appended blocks
+        self._frontier = []
+
+    def _ratio(self, c: Canvas, j: int) -> float:
+        lo, hi = self._spans[j]
+        masked = sum(1 for p in range(lo, hi) if c.x[p] == c.mask_id)
+        return (hi - lo - masked) / (hi - lo)
+
+    def plan(self, c: Canvas, step: int) -> Plan:
+        if self._spans is None:
+            start, n = c.prompt_len, len(c.x) - c.prompt_len
+            self._spans = [(start + j, min(start + j + self.bs, start + n)) for j in range(0, n, self.bs)]
+        while self._frozen < self._appended:
+            lo, hi = self._spans[self._frozen]
+            if any(c.x[p] == c.mask_id for p in range(lo, hi)):
+                break
+            self._frozen += 1
+        if not self._eos and self._appended:
+            lo, hi = self._spans[0][0], self._spans[self._appended - 1][1]
+            self._eos = any(c.x[p] == c.eos_id for p in range(lo, hi))
+        if self._appended < len(self._spans) and not self._eos:
+            last = 1.0 if self._appended == 0 else self._ratio(c, self._appended - 1)
+            if last >= self.tau_add:
+                self._appended += 1
+        self._active = []
+        for j in range(self._frozen, self._appended):
+            prev = 1.0 if j == 0 else self._ratio(c, j - 1)
+            self._active.append((*self._spans[j], prev >= self.tau_act))
+        if not self._active:
+            return Plan("stop")
+        self._frontier = [p for lo, hi, _ in self._active for p in range(lo, hi) if c.x[p] == c.mask_id]
+        return Plan("proceed", list(self._frontier), self._spans[self._appended - 1][1])
+
+    @property
+    def frozen_end(self) -> int:
+        """First position of the oldest unfrozen block (the exact K/V prefix ends there)."""
+        return self._active[0][0] if self._active else len(self._spans or [])
+
+    def select(self, scores) -> list[int]:
+        conf = np.asarray(scores, dtype=np.float64)
+        chosen = []
+        for lo, hi, activated in self._active:
+            rows = [r for r, p in enumerate(self._frontier) if lo <= p < hi]
+            if not rows:
+                continue
+            clear = [r for r in rows if conf[r] > self.tau]
+            if clear:
+                chosen.extend(clear)
+            elif activated:
+                chosen.append(rows[int(np.argmax(conf[rows]))])
+        return chosen
 
 
 ScoreFn = Callable[[Canvas, list, "int | None", int], tuple]

@@ -113,6 +113,21 @@ def _decode(ds) -> dict:
         mask=500, eos=501, scale=3.0, temperature=0.8, seed=1234)
     run("block_threshold", "block_threshold", prompt_len=32, gen=96, steps=200, block_size=32, vocab=512,
         mask=500, eos=501, scale=6.0, confidence_threshold=0.9)
+    # d2f_block_pipeline: blocks of 8 with the product preset's thresholds; scale 6 gives rows that
+    # clear tau_conf and rows that do not (semi-activated blocks waiting, forced argmax commits,
+    # several blocks in the window); a small vocabulary makes EOS land early in one case
+    run("d2f_pipeline", "d2f_block_pipeline", prompt_len=24, gen=64, steps=200, block_size=8, vocab=512,
+        mask=500, eos=501, scale=6.0, confidence_threshold=0.8, d2f_add_threshold=0.1,
+        d2f_activate_threshold=0.95)
+    run("d2f_pipeline_tau06", "d2f_block_pipeline", prompt_len=16, gen=60, steps=200, block_size=8, vocab=256,
+        mask=250, eos=251, scale=5.0, confidence_threshold=0.6, d2f_add_threshold=0.25,
+        d2f_activate_threshold=0.9)
+    run("d2f_pipeline_eos", "d2f_block_pipeline", prompt_len=16, gen=64, steps=200, block_size=8, vocab=48,
+        mask=40, eos=3, scale=6.0, confidence_threshold=0.8, d2f_add_threshold=0.1,
+        d2f_activate_threshold=0.95)
+    run("d2f_pipeline_capped", "d2f_block_pipeline", prompt_len=24, gen=64, steps=12, block_size=16, vocab=512,
+        mask=500, eos=501, scale=6.0, confidence_threshold=0.9, d2f_add_threshold=0.1,
+        d2f_activate_threshold=0.95)
     run("entropy_count", "entropy_count", prompt_len=16, gen=32, steps=24, block_size=8, vocab=256,
         mask=250, eos=251, scale=3.0, temperature=0.2, top_p=0.95, eps=1e-3)
     return traces

@@ -60,6 +60,11 @@ def _policy_for(tr):
         return pol, pol.iteration_limit, False, "sample" if tr["options"].get("temperature", 0) > 0 else "max"
     if tr["strategy"] == "block_threshold":
         return policy.BlockThreshold(block_size=bs, threshold=tr["options"]["confidence_threshold"]), tr["steps"], True, "max"
+    if tr["strategy"] == "d2f_block_pipeline":
+        o = tr["options"]
+        pol = policy.D2FPipeline(block_size=bs, threshold=o["confidence_threshold"], add_threshold=o["d2f_add_threshold"],
+                                 activate_threshold=o["d2f_activate_threshold"])
+        return pol, tr["steps"], True, "max"
     opts = tr["options"]
     return policy.EntropyCount(eps=opts["eps"], steps=tr["steps"]), tr["steps"], True, "ent"
 
@@ -82,7 +87,8 @@ def test_sampling_noise_row(sel):
 
 
 @pytest.mark.parametrize("name", ["bd3_cfg0_shape", "bd3_k2", "bd3_ragged_quota", "bd3_eos", "bd3_sampled",
-                                  "block_threshold", "entropy_count"])
+                                  "block_threshold", "entropy_count", "d2f_pipeline", "d2f_pipeline_tau06",
+                                  "d2f_pipeline_eos", "d2f_pipeline_capped"])
 def test_decode_trajectory(golden_dir, name):
     tr = json.loads((golden_dir / "decode.json").read_text())[name]
     pol, limit, exclude, kind = _policy_for(tr)

@@ -23,6 +23,7 @@ STATUS_NAMES = {0: "OK", 1: "VERSION_MISMATCH", 2: "INVALID_ARGUMENT", 3: "UNSUP
                 5: "DEVICE_TIMEOUT"}
 
 STRATEGY_BLOCK_THRESHOLD = 0
+STRATEGY_D2F_BLOCK_PIPELINE = 2
 STRATEGY_ENTROPY_COUNT = 5
 STRATEGY_BD3_FIXED_QUOTA = 7
 COMMIT_THRESHOLD = 2
@@ -70,7 +71,8 @@ class GenerateParams(ctypes.Structure):
                 ("max_tokens", ctypes.c_int32), ("mask_token_id", ctypes.c_int32), ("eos_token_id", ctypes.c_int32),
                 ("confidence_threshold", ctypes.c_double), ("rounds_per_block", ctypes.c_int32),
                 ("trace_steps", ctypes.c_int32), ("temperature", ctypes.c_double), ("top_p", ctypes.c_double),
-                ("eps", ctypes.c_double), ("seed", ctypes.c_uint64), ("mask_origin", ctypes.c_int32)]
+                ("eps", ctypes.c_double), ("seed", ctypes.c_uint64), ("mask_origin", ctypes.c_int32),
+                ("add_threshold", ctypes.c_double), ("activate_threshold", ctypes.c_double)]
 
 
 class GenerateResult(ctypes.Structure):

@@ -1728,8 +1728,9 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   REQUIRE(m && cfg && out, "null argument");
   *out = nullptr;
   const bool dream = cfg->decode_strategy == DRT_STRATEGY_ENTROPY_COUNT;
-  REQUIRE(dream || cfg->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA || cfg->decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD,
-          "device sessions run only block_threshold, bd3_fixed_quota and entropy_count (got strategy %d)",
+  REQUIRE(dream || cfg->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA || cfg->decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD ||
+              cfg->decode_strategy == DRT_STRATEGY_D2F_BLOCK_PIPELINE,
+          "device sessions run only block_threshold, d2f_block_pipeline, bd3_fixed_quota and entropy_count (got strategy %d)",
           cfg->decode_strategy);
   REQUIRE(dream || m->shard.world == 1, "a tensor-parallel model serves entropy_count sessions only");
   if (dream) {
@@ -1988,7 +1989,7 @@ extern "C" int drt_session_propose(drt_session* s, const int32_t* frontier, int3
   REQUIRE(nf >= 1 && nf <= kMaxFrontier, "frontier size %d outside [1, %d]", nf, kMaxFrontier);
   REQUIRE(window_end >= 1 && window_end <= s->canvas_len, "window_end %d outside [1, %d]", window_end, s->canvas_len);
   REQUIRE(frozen >= 0 && frozen < window_end, "frozen_prefix %d outside [0, window_end)", frozen);
-  REQUIRE(window_end - frozen <= kMaxFwdRows / 2, "active window of %d rows exceeds %d", window_end - frozen, kMaxFwdRows / 2);
+  REQUIRE(window_end - frozen < kMaxFwdRows, "active window of %d rows exceeds %d", window_end - frozen, kMaxFwdRows - 1);
   for (int i = 0; i < nf; ++i) REQUIRE(frontier[i] >= frozen && frontier[i] < window_end, "frontier position %d outside [%d, %d)", frontier[i], frozen, window_end);
   CK(cudaSetDevice(s->device));
   if (s->g_fwd != nullptr && (s->g_fwd_geom[0] != s->origin || s->g_fwd_geom[1] != s->block_size)) {
@@ -2007,9 +2008,11 @@ extern "C" int drt_session_propose(drt_session* s, const int32_t* frontier, int3
   int cache_end = s->exact_kv ? std::min(hs->cache_end, frozen) : 0;
   CK(cudaEventRecord(s->ev0, s->stream));
   int fwd_rows_total = 0;
-  // Final rows that are not cached yet: prefill them when they exceed one block, and always on the
-  // first forward (the prompt goes through the prefill path, as in drt_session_generate).
-  if (frozen > cache_end && (cache_end == 0 || frozen - cache_end > kMaxFwdRows / 2)) {
+  // Final rows that are not cached yet go through the prefill path on the first forward (the prompt,
+  // as in drt_session_generate) and when they and the window do not fit one decode forward;
+  // otherwise they are forwarded with the window, as the device-resident loop forwards them.
+  const int shift_rows = s->m->cfg.logits_shift ? 1 : 0;
+  if (frozen > cache_end && (cache_end == 0 || window_end - cache_end + shift_rows > kMaxFwdRows)) {
     TRY(prefill(s, cache_end, frozen, s->origin, s->block_size, 0));
     fwd_rows_total += frozen - cache_end;
     cache_end = frozen;
@@ -2029,7 +2032,7 @@ extern "C" int drt_session_propose(drt_session* s, const int32_t* frontier, int3
   }
   hs->cache_end = frozen;
   hs->action = PLAN_PROCEED;
-  hs->exclude_token = s->cfg.decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD ? s->mask_id : -1;
+  hs->exclude_token = s->cfg.decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA ? -1 : s->mask_id;
   hs->forward_count = s->propose_count;  // the sampled draw's forward index
   fwd_rows_total += hs->fwd_rows;
   CK(cudaMemcpyAsync(s->state, hs, sizeof(DecodeState), cudaMemcpyHostToDevice, s->stream));
@@ -2130,8 +2133,16 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
     REQUIRE(p->decode_strategy == DRT_STRATEGY_ENTROPY_COUNT, "an entropy_count session generates with entropy_count only");
     return dream_generate(s, p, prompt, prompt_len, out, result, trace);
   }
-  REQUIRE(p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA || p->decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD,
-          "device generation runs bd3_fixed_quota or block_threshold");
+  const bool pipeline = p->decode_strategy == DRT_STRATEGY_D2F_BLOCK_PIPELINE;
+  REQUIRE(p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA || p->decode_strategy == DRT_STRATEGY_BLOCK_THRESHOLD || pipeline,
+          "device generation runs bd3_fixed_quota, block_threshold or d2f_block_pipeline");
+  if (pipeline) {
+    // D2FBlockPipelineCommit.__post_init__ (diffusion_runtime.py:1500-1550)
+    REQUIRE(std::isfinite(p->add_threshold) && p->add_threshold > 0.0 && p->add_threshold <= 1.0,
+            "add_threshold (tau_add) must be in (0, 1]");
+    REQUIRE(std::isfinite(p->activate_threshold) && p->activate_threshold > 0.0 && p->activate_threshold <= 1.0,
+            "activate_threshold (tau_act) must be in (0, 1]");
+  }
   REQUIRE(p->block_size >= 1 && p->block_size <= 32, "block_size must be in [1, 32]");
   REQUIRE(p->steps >= 1, "steps must be >= 1");
   REQUIRE(p->max_tokens >= 0, "max_tokens must be >= 0");
@@ -2142,7 +2153,7 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
           "confidence_threshold must be finite and in [0, 1]");
   REQUIRE(std::isfinite(p->temperature) && p->temperature >= 0.0, "temperature must be finite and >= 0");
   REQUIRE(p->temperature == 0.0 || p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA,
-          "the block_threshold policy scores at temperature 0 only");
+          "the block_threshold and d2f_block_pipeline policies score at temperature 0 only");
   if (p->decode_strategy == DRT_STRATEGY_BD3_FIXED_QUOTA)
     REQUIRE(prompt_len % p->block_size == 0, "BD3LM Candidate prompt length must be a multiple of block_size");
   for (int i = 0; i < prompt_len; ++i) {
@@ -2161,6 +2172,10 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
   // d2f mask origin: 0 for the BD3LM graph's absolute blocks, the prompt length for the D2F graph
   REQUIRE(p->mask_origin >= -1 && p->mask_origin <= prompt_len, "mask_origin outside [-1, prompt_len]");
   s->origin = p->mask_origin < 0 ? prompt_len : p->mask_origin;
+  // A frozen pipeline block's K/V are final only if no attention block straddles two pipeline blocks.
+  REQUIRE(!pipeline || (prompt_len - s->origin) % p->block_size == 0,
+          "d2f_block_pipeline needs prompt_len - mask_origin (%d) to be a multiple of block_size (%d)",
+          prompt_len - s->origin, p->block_size);
   s->block_size = p->block_size;
   if (s->g_step != nullptr && (s->g_step_geom[0] != s->origin || s->g_step_geom[1] != s->block_size)) {
     cudaGraphExecDestroy(s->g_step);
@@ -2209,6 +2224,13 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
     const int sched = (p->max_tokens + bs - 1) / bs;
     hs->steps_per_block = sched > 0 ? (p->steps + sched - 1) / sched : 0;
     hs->iteration_limit = count * hs->steps_per_block;
+  } else if (pipeline) {
+    hs->policy = POL_D2F_PIPELINE;
+    hs->iteration_limit = p->steps;
+    hs->exclude_token = p->mask_token_id;  // run_decode_loop's exclude_mask_token default
+    hs->add_threshold = p->add_threshold;
+    hs->activate_threshold = p->activate_threshold;
+    hs->pipe_blocks = (p->max_tokens + p->block_size - 1) / p->block_size;
   } else {
     hs->policy = POL_BLOCK_THRESHOLD;
     hs->iteration_limit = p->steps;
@@ -2261,7 +2283,12 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
   for (auto& e : flag_ev) cudaEventDestroy(e);
   TRY(rc);
   TRY(check_status(s));
-  if (hs->error) return set_error(DRT_INTERNAL_ERROR, "device plan rejected the request geometry");
+  if (hs->error)
+    return set_error(hs->policy == POL_D2F_PIPELINE ? DRT_UNSUPPORTED : DRT_INTERNAL_ERROR,
+                     hs->policy == POL_D2F_PIPELINE
+                         ? "the d2f_block_pipeline window grew past %d forwarded rows (drive this request through propose_device)"
+                         : "device plan rejected the request geometry",
+                     kMaxFwdRows);
   if (trace != nullptr && p->trace_steps > 0) {
     const int nt = std::min(hs->forward_count, std::min(p->trace_steps, s->trace_cap));
     static_assert(sizeof(StepTrace) == sizeof(drt_step_trace), "trace layout");

@@ -36,7 +36,7 @@ from . import _lib
 from .config import QWEN3_06B_BD3LM, SYNTHETIC_STD, rope_half_tables
 
 _STRATEGY_IDS = {"block_threshold": _lib.STRATEGY_BLOCK_THRESHOLD, "bd3_fixed_quota": _lib.STRATEGY_BD3_FIXED_QUOTA,
-                 "entropy_count": _lib.STRATEGY_ENTROPY_COUNT}
+                 "d2f_block_pipeline": _lib.STRATEGY_D2F_BLOCK_PIPELINE, "entropy_count": _lib.STRATEGY_ENTROPY_COUNT}
 _COMMIT_IDS = {"threshold": _lib.COMMIT_THRESHOLD, "fixed_quota": _lib.COMMIT_FIXED_QUOTA}
 _MASK_IDS = {"bidirectional": _lib.MASK_BIDIRECTIONAL, "d2f_hybrid": _lib.MASK_D2F_HYBRID}
 
@@ -347,7 +347,8 @@ class Session:
         self.runtime = runtime
         self._lib = runtime._lib
         strategy = _enum(session_config.get("decode_strategy", "bd3_fixed_quota"), _STRATEGY_IDS, "decode_strategy")
-        default_commit = "threshold" if strategy == _lib.STRATEGY_BLOCK_THRESHOLD else "fixed_quota"
+        default_commit = ("threshold" if strategy in (_lib.STRATEGY_BLOCK_THRESHOLD, _lib.STRATEGY_D2F_BLOCK_PIPELINE)
+                          else "fixed_quota")
         commit = _enum(session_config.get("commit_policy", default_commit), _COMMIT_IDS, "commit_policy")
         default_mask = "bidirectional" if strategy == _lib.STRATEGY_ENTROPY_COUNT else "d2f_hybrid"
         mask = _enum(session_config.get("attention_mask_kind", default_mask), _MASK_IDS, "attention_mask_kind")
@@ -425,7 +426,8 @@ class Session:
                  decode_strategy: str | None = None, mask_token_id: int | None = None,
                  eos_token_id: int | None = None, confidence_threshold: float = 0.9, rounds_per_block: int = 0,
                  trace_steps: int = 0, temperature: float | None = None, top_p: float | None = 0.95,
-                 eps: float = 1e-3, seed: int = 0, mask_origin: int | str | None = None) -> dict:
+                 eps: float = 1e-3, seed: int = 0, mask_origin: int | str | None = None,
+                 add_threshold: float = 0.1, activate_threshold: float = 0.95) -> dict:
         """Whole request on the device. ``decode_strategy="entropy_count"`` (a session opened with
         that strategy) runs the Dream full-canvas schedule with NegEntropy(temperature, top_p) and
         linspace(1, eps, steps + 1) timesteps (temperature defaults to 0.2); the others run the BD3 /
@@ -453,7 +455,7 @@ class Session:
             confidence_threshold=float(confidence_threshold), rounds_per_block=int(rounds_per_block),
             trace_steps=int(trace_steps), temperature=float(temperature),
             top_p=1.0 if top_p is None else float(top_p), eps=float(eps), seed=int(seed) & (2**64 - 1),
-            mask_origin=origin)
+            mask_origin=origin, add_threshold=float(add_threshold), activate_threshold=float(activate_threshold))
         out = (ctypes.c_int32 * (len(ids) + int(max_tokens)))()
         res = _lib.GenerateResult()
         trace = (_lib.StepTrace * max(1, int(trace_steps)))() if trace_steps else None

@@ -45,6 +45,7 @@ typedef enum drt_status {
 /* Decode strategies and commit policies: the ABI integers of
  * python/src/edllm/abi/enums.py:14-31. Only these are served by a device session. */
 #define DRT_STRATEGY_BLOCK_THRESHOLD 0
+#define DRT_STRATEGY_D2F_BLOCK_PIPELINE 2
 #define DRT_STRATEGY_ENTROPY_COUNT 5
 #define DRT_STRATEGY_BD3_FIXED_QUOTA 7
 #define DRT_COMMIT_THRESHOLD 2
@@ -111,13 +112,13 @@ typedef struct drt_session_config {
 
 /* Device-resident decode request (drt_session_generate). */
 typedef struct drt_generate_params {
-  int32_t decode_strategy;     /* DRT_STRATEGY_BD3_FIXED_QUOTA, _BLOCK_THRESHOLD or _ENTROPY_COUNT */
+  int32_t decode_strategy;     /* DRT_STRATEGY_BD3_FIXED_QUOTA, _BLOCK_THRESHOLD, _D2F_BLOCK_PIPELINE or _ENTROPY_COUNT */
   int32_t steps;               /* requested denoising steps (the loop's iteration limit) */
   int32_t block_size;
   int32_t max_tokens;          /* generated canvas length */
   int32_t mask_token_id;
   int32_t eos_token_id;
-  double confidence_threshold; /* block threshold tau */
+  double confidence_threshold; /* block threshold tau (conf >= tau); D2F pipeline tau_conf (conf > tau) */
   int32_t rounds_per_block;    /* block threshold: per-block round budget, 0 = none */
   int32_t trace_steps;         /* record up to this many drt_step_trace entries */
   /* entropy_count (full-canvas masked diffusion): EntropyCountStrategy(temperature, top_p, eps),
@@ -131,6 +132,13 @@ typedef struct drt_generate_params {
   int32_t mask_origin;         /* d2f mask geometry origin: 0 = absolute blocks from position 0 (the
                                   BD3LM graph), -1 = the prompt length (prompt bidirectional, blocks
                                   counted from it: the Dream D2F graph), else that position */
+  /* d2f_block_pipeline (D2FBlockPipelineCommit, python/src/edllm/backends/diffusion_runtime.py:1416-1704):
+   * a new block joins the window when the last appended block's decoded ratio is >= add_threshold;
+   * block j is fully activated when block j - 1's ratio is >= activate_threshold. Both in (0, 1]
+   * (the reference defaults are 0.1 and 0.95). The prompt length minus the mask origin must be a
+   * multiple of block_size, so that the pipeline's blocks are the attention's blocks. */
+  double add_threshold;
+  double activate_threshold;
 } drt_generate_params;
 
 typedef struct drt_generate_result {

@@ -893,8 +893,9 @@ struct drt_session {
   int g_step_kernels = 0;             // kernels in one replay of g_step
   cudaGraphExec_t g_step = nullptr;   // plan + forward + score + commit
   cudaGraphExec_t g_fwd = nullptr;    // forward + score (host policy)
-  int g_step_geom[2] = {-1, -1};      // (mask origin, block size) baked into each graph
-  int g_fwd_geom[2] = {-1, -1};
+  int g_step_geom[3] = {-1, -1, -1};  // (mask origin, block size, sampling selector) baked into each graph
+  int g_fwd_geom[3] = {-1, -1, -1};
+  int cap_sample = 0;                 // the graph being captured draws sampled tokens (temperature > 0)
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   // full-canvas (entropy_count) sessions
   bool dream = false;
@@ -1409,7 +1410,10 @@ int enqueue_head(drt_session* s, const int* row_index, int rows, const int* rows
     sa.part_skey2 = s->sel_skey2;
     sa.part_sidx = s->sel_sidx;
     sa.row_tie = s->row_tie;
-    CK(launch_k(sel_pass1_kernel, dim3(s->sel_chunks, rows), dim3(kSelThreads), 0, s->stream, true, sa));
+    if (s->cap_sample)
+      CK(launch_k(sel_pass1_kernel<true>, dim3(s->sel_chunks, rows), dim3(kSelThreads), 0, s->stream, true, sa));
+    else
+      CK(launch_k(sel_pass1_kernel<false>, dim3(s->sel_chunks, rows), dim3(kSelThreads), 0, s->stream, true, sa));
   }
   return DRT_OK;
 }
@@ -1992,14 +1996,18 @@ extern "C" int drt_session_propose(drt_session* s, const int32_t* frontier, int3
   REQUIRE(window_end - frozen < kMaxFwdRows, "active window of %d rows exceeds %d", window_end - frozen, kMaxFwdRows - 1);
   for (int i = 0; i < nf; ++i) REQUIRE(frontier[i] >= frozen && frontier[i] < window_end, "frontier position %d outside [%d, %d)", frontier[i], frozen, window_end);
   CK(cudaSetDevice(s->device));
-  if (s->g_fwd != nullptr && (s->g_fwd_geom[0] != s->origin || s->g_fwd_geom[1] != s->block_size)) {
+  const int fwd_sample = s->hstate->sample_t > 0.0 ? 1 : 0;
+  if (s->g_fwd != nullptr && (s->g_fwd_geom[0] != s->origin || s->g_fwd_geom[1] != s->block_size ||
+                              s->g_fwd_geom[2] != fwd_sample)) {
     cudaGraphExecDestroy(s->g_fwd);
     s->g_fwd = nullptr;
   }
   if (s->g_fwd == nullptr) {
+    s->cap_sample = fwd_sample;
     TRY(capture(s, false, &s->g_fwd));
     s->g_fwd_geom[0] = s->origin;
     s->g_fwd_geom[1] = s->block_size;
+    s->g_fwd_geom[2] = fwd_sample;
   }
   DecodeState* hs = s->hstate;
   // exact_kv: the frozen prefix's K/V from earlier forwards is reused (exact under the block-causal
@@ -2177,16 +2185,20 @@ extern "C" int drt_session_generate(drt_session* s, const drt_generate_params* p
           "d2f_block_pipeline needs prompt_len - mask_origin (%d) to be a multiple of block_size (%d)",
           prompt_len - s->origin, p->block_size);
   s->block_size = p->block_size;
-  if (s->g_step != nullptr && (s->g_step_geom[0] != s->origin || s->g_step_geom[1] != s->block_size)) {
+  const int step_sample = p->temperature > 0.0 ? 1 : 0;
+  if (s->g_step != nullptr && (s->g_step_geom[0] != s->origin || s->g_step_geom[1] != s->block_size ||
+                               s->g_step_geom[2] != step_sample)) {
     cudaGraphExecDestroy(s->g_step);
     s->g_step = nullptr;
   }
   if (s->g_step == nullptr) {
     const int64_t before = g_launches;
+    s->cap_sample = step_sample;
     TRY(capture(s, true, &s->g_step));
     s->g_step_kernels = static_cast<int>(g_launches - before);
     s->g_step_geom[0] = s->origin;
     s->g_step_geom[1] = s->block_size;
+    s->g_step_geom[2] = step_sample;
   }
 
   std::vector<int> canvas(canvas_len, p->mask_token_id);
@@ -2460,7 +2472,7 @@ extern "C" int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows
   a.exclude = -1;
   a.conf = conf;
   a.token = token;
-  CK(launch_k(sel_pass1_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  CK(launch_k(sel_pass1_kernel<false>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
   if (mode == DRT_SELECT_NEG_ENTROPY) CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
   return DRT_OK;
 }
@@ -2498,7 +2510,7 @@ extern "C" int drt_selector_gather(const float* logits, int64_t ld, const int32_
   a.exclude = -1;
   a.conf = conf;
   a.token = token;
-  CK(launch_k(sel_pass1_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  CK(launch_k(sel_pass1_kernel<false>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
   if (mode == DRT_SELECT_NEG_ENTROPY) CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
   return DRT_OK;
 }
@@ -2545,7 +2557,7 @@ extern "C" int drt_selector_sample(const float* logits, int64_t ld, const int32_
   a.row_tie = tie;
   a.conf = conf;
   a.token = token;
-  CK(launch_k(sel_pass1_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  CK(launch_k(sel_pass1_kernel<true>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
   return DRT_OK;
 }
 
@@ -2849,7 +2861,7 @@ extern "C" int drt_selector_rows_noalloc(const float* logits, int64_t ld, int32_
   a.exclude = -1;
   a.conf = conf;
   a.token = token;
-  CK(launch_k(sel_pass1_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  CK(launch_k(sel_pass1_kernel<false>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
   if (mode == DRT_SELECT_NEG_ENTROPY) CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
   return DRT_OK;
 }

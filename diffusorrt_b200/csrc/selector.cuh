@@ -114,7 +114,10 @@ __device__ __forceinline__ void argmax_merge(float& m, int& idx, float m2, int i
 __device__ __forceinline__ double sel_inv_t(double T) { return T > 0.0 ? 1.0 / T : 1.0; }
 __device__ __forceinline__ double sel_adjust(double x, double inv_t) { return x * inv_t; }
 
-// Pass 1: chunk max / argmax / sum of exp relative to the chunk's adjusted max.
+// Pass 1: chunk max / argmax / sum of exp relative to the chunk's adjusted max. kSample adds the
+// sampled draw (SEL_SAMPLE, or SEL_MAXPROB with a device-side temperature above 0); the greedy
+// instantiation carries none of its registers (64 -> 48 per thread, 4 -> 5 resident CTAs per SM).
+template <bool kSample>
 __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a) {
   griddep_wait();
   griddep_launch_dependents();
@@ -131,10 +134,9 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
   const bool vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
   const int excl = a.exclude_dev != nullptr ? *a.exclude_dev : a.exclude;
 
-  // Stage the thread's 32 values in registers (chunk = 8 x 256 float4 groups).
+  // Stage the thread's 32 values in registers (chunk = 8 x 256 float4 groups): value i of thread t
+  // is column lo + ((i / 4) * kSelThreads + t) * 4 + i % 4, ascending in i.
   float vals[32];
-  float m = -INFINITY;
-  int idx = INT_MAX;
 #pragma unroll
   for (int k = 0; k < kSelChunk / (kSelThreads * 4); ++k) {
     const int base = lo + (k * kSelThreads + tid) * 4;
@@ -148,29 +150,43 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
 #pragma unroll
       for (int e = 0; e < 4; ++e) vals[k * 4 + e] = base + e < hi ? x[base + e] : -INFINITY;
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (base + e == excl) vals[k * 4 + e] = -INFINITY;
-      if (vals[k * 4 + e] > m) { m = vals[k * 4 + e]; idx = base + e; }
-    }
   }
+  // The excluded column (scored as -inf): only the thread holding it rewrites its slot.
+  if (excl >= lo && excl < hi && (((excl - lo) >> 2) & (kSelThreads - 1)) == tid) {
+    const int slot = (((excl - lo) >> 2) / kSelThreads) * 4 + ((excl - lo) & 3);
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i == slot) vals[i] = -INFINITY;
+  }
+  // Chunk maximum (NaN ignored, as a > comparison ignores it), then its first column: only the
+  // threads that hold the maximum look for it.
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) m = fmaxf(m, vals[i]);
   __shared__ float s_m[kSelThreads / 32];
   __shared__ int s_i[kSelThreads / 32];
   __shared__ double s_s[kSelThreads / 32];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-    const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
-    argmax_merge(m, idx, m2, i2);
-  }
-  if ((tid & 31) == 0) { s_m[tid >> 5] = m; s_i[tid >> 5] = idx; }
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((tid & 31) == 0) s_m[tid >> 5] = m;
   __syncthreads();
   float bm = s_m[0];
+  for (int w = 1; w < kSelThreads / 32; ++w) bm = fmaxf(bm, s_m[w]);
+  int idx = INT_MAX;
+  if (bm != -INFINITY) {
+#pragma unroll
+    for (int i = 31; i >= 0; --i)
+      if (vals[i] == bm) idx = lo + ((i >> 2) * kSelThreads + tid) * 4 + (i & 3);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) idx = min(idx, __shfl_xor_sync(0xffffffffu, idx, o));
+  if ((tid & 31) == 0) s_i[tid >> 5] = idx;
+  __syncthreads();
   int bi = s_i[0];
-  for (int w = 1; w < kSelThreads / 32; ++w) argmax_merge(bm, bi, s_m[w], s_i[w]);
+  for (int w = 1; w < kSelThreads / 32; ++w) bi = min(bi, s_i[w]);
 
-  const double samp_t = a.sample_t_dev != nullptr ? *a.sample_t_dev : a.sample_t;
-  const bool sample = (a.mode == SEL_SAMPLE || (a.mode == SEL_MAXPROB && a.sample_t_dev != nullptr)) && samp_t > 0.0;
+  const double samp_t = !kSample ? 0.0 : (a.sample_t_dev != nullptr ? *a.sample_t_dev : a.sample_t);
+  const bool sample = kSample && (a.mode == SEL_SAMPLE || (a.mode == SEL_MAXPROB && a.sample_t_dev != nullptr)) && samp_t > 0.0;
   __shared__ double s_k1[kSelThreads / 32], s_k2[kSelThreads / 32];
   __shared__ int s_ki[kSelThreads / 32];
   double k1 = -INFINITY, k2 = -INFINITY;
@@ -207,10 +223,13 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
 
   const double inv_t = sample ? 1.0 : sel_inv_t(a.temperature);
   const double amax = sel_adjust(static_cast<double>(bm), inv_t);
+  // sum of exp(adjusted - chunk max): a -inf (or NaN) term is clamped to exp(-708), about 3e-308,
+  // which leaves a sum holding the chunk maximum's exp(0) = 1 unchanged; a chunk with no finite
+  // value sums nothing.
   double sum = 0.0;
+  if (bm != -INFINITY) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    if (vals[i] != -INFINITY) sum += exp_nonpos(sel_adjust(static_cast<double>(vals[i]), inv_t) - amax);
+    for (int i = 0; i < 32; ++i) sum += exp_nonpos_clamped(sel_adjust(static_cast<double>(vals[i]), inv_t) - amax);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -293,13 +312,31 @@ __global__ void __launch_bounds__(kSelThreads) sel_entropy_kernel(const SelArgs 
   const int excl = a.exclude_dev != nullptr ? *a.exclude_dev : a.exclude;
   const double inv_t = sel_inv_t(a.temperature);
   const double inv_s = 1.0 / S;  // p = e / S taken as e * (1 / S): last-bit differences only
+  // The thread's columns as in sel_pass1_kernel (float4 groups lo + (k * kSelThreads + t) * 4),
+  // one group at a time. A -inf term (p = 0 in the reference, contributing 0 * log(1e-10) = 0) is
+  // clamped to exp(-708): its p log(p + 1e-10), about -7e-307, vanishes in any sum holding a real term.
+  const bool vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
   double acc = 0.0;
-  for (int i = lo + tid; i < hi; i += kSelThreads) {
-    const float v = i == excl ? -INFINITY : x[i];
-    if (v == -INFINITY) continue;  // p = 0 contributes 0 * log(1e-10) = 0
-    const double e = exp_nonpos(sel_adjust(static_cast<double>(v), inv_t) - amax);
-    const double p = __dmul_rn(e, inv_s);
-    acc = __dadd_rn(acc, __dmul_rn(p, log(__dadd_rn(p, 1e-10))));
+  for (int k = 0; k < kSelChunk / (kSelThreads * 4); ++k) {
+    const int base = lo + (k * kSelThreads + tid) * 4;
+    float v[4];
+    if (vec && base + 4 <= hi) {
+      const float4 q = __ldcs(reinterpret_cast<const float4*>(x + base));
+      v[0] = q.x;
+      v[1] = q.y;
+      v[2] = q.z;
+      v[3] = q.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = base + e < hi ? x[base + e] : -INFINITY;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float ve = base + e == excl ? -INFINITY : v[e];
+      const double ex = exp_nonpos_clamped(sel_adjust(static_cast<double>(ve), inv_t) - amax);
+      const double p = __dmul_rn(ex, inv_s);
+      acc = __dadd_rn(acc, __dmul_rn(p, log(__dadd_rn(p, 1e-10))));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);

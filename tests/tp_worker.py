@@ -9,7 +9,7 @@ Every rank holds a shard of the same seeded Dream-architecture model. Checked:
 * entropy_count generation on the group agrees with the oracle loop on certified steps;
 * the vocabulary-parallel lm_head (each rank projects its vocabulary tiles and stores them into
   every rank's logits) gives the same decode, bit for bit, as every rank projecting the whole
-  vocabulary.
+  vocabulary; the vocabulary (35 tiles of 128) splits unevenly over 2, 4 and 8 ranks.
 """
 from __future__ import annotations
 
@@ -23,7 +23,7 @@ ROOT = Path(__file__).resolve().parent.parent
 sys.path.insert(0, str(ROOT))
 
 DREAM_TP = dict(layer_count=2, hidden_size=256, attention_heads=28, num_kv_heads=4, head_dim=128,
-                intermediate_size=512, vocab_size=4096, qk_norm=False, qkv_bias=True, tied_lm_head=False, logits_shift=True,
+                intermediate_size=512, vocab_size=4480, qk_norm=False, qkv_bias=True, tied_lm_head=False, logits_shift=True,
                 rms_norm_eps=1e-6, rope_theta=1e6, mask_token_id=4000, eos_token_id=4001, block_size=8)
 STD = dict(linear_std=0.05, embed_std=0.05, bias_std=0.02)
 SEED = 33

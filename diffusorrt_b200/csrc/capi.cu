@@ -840,7 +840,6 @@ struct drt_session {
   float* h = nullptr;
   __nv_bfloat16 *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *xf = nullptr;
   float* logits = nullptr;
-  float* ss = nullptr;                // [kMaxFwdRows][H / 128] partial sums of squares of h (decode)
   float* part = nullptr;              // [rows_cap][H] f32 linear partials (tensor-parallel models)
   // tensor parallel over peer memory: receive buffers [2][world][rows_cap][H] f32, all-gather
   // buffers [2][rows_cap][H] bf16, flags [3][2][kTpMaxRanks] u64 and the logits [head_cap][V] f32,
@@ -1771,7 +1770,6 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   // a tensor-parallel session's logits live in its peer-mapped buffer (below): with the
   // vocabulary-parallel lm_head every rank's projection stores its tiles there
   if (m->shard.world <= 1 && (rc = salloc(s, &s->logits, static_cast<size_t>(s->head_cap) * m->V)) != DRT_OK) return fail(rc);
-  if ((rc = salloc(s, &s->ss, static_cast<size_t>(kMaxFwdRows) * (H / 128))) != DRT_OK) return fail(rc);
   if (m->shard.world > 1) {
     if ((rc = salloc(s, &s->part, static_cast<size_t>(R) * H)) != DRT_OK) return fail(rc);
     const size_t bytes = tp_buf_bytes(s);

@@ -67,10 +67,6 @@ struct GemmArgs {
   __nv_bfloat16* vtcache;// this layer: [nkv][128][max_seq]
   int max_seq;
   float eps;
-  // EPI_RESID: optional per-row partial sums of squares of the updated rows, for the RMSNorm that
-  // the next linear fuses into its activation load: ss_out[row * ss_ld + m0 / 128].
-  float* ss_out;
-  int ss_ld;
   // 4-bit affine weights (decode linear, quantized instantiation): per (row, group of 64 inputs)
   // bf16 scale and bias, [n_out][q_groups] with q_groups = K / 64; the packed nibbles come from tmA.
   const __nv_bfloat16* q_scale;
@@ -124,7 +120,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Epilogue for up to 32 accumulator columns (activation rows col0 .. col0+ncols-1).
 // v[i] holds this thread's weight row (m0 + tid) for activation row col0 + i. All loops run to
 // 32 with a guard so v stays in registers.
-// xs: shared scratch of at least 32 x 132 floats (SwiGLU, QKV, residual sums of squares).
+// xs: shared scratch of at least 32 x 132 floats (SwiGLU, QKV).
 template <int EPI, bool RND = true>
 __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* v, int col0, int ncols, int m0, int tid,
                                                       float* xs, int pos0) {
@@ -170,21 +166,6 @@ __device__ __forceinline__ void gemm_epilogue_chunk_t(const GemmArgs& a, float* 
       for (int i = 0; i < 32; ++i) {
         cur[i] = __fadd_rn(cur[i], __fadd_rn(out_round<RND>(v[i]), b));
         if (i < ncols) a.out_f32[static_cast<size_t>(col0 + i) * a.ld_out + n] = cur[i];
-      }
-      if (a.ss_out != nullptr) {
-        // Sum of squares over this tile's 128 features for each row: warp tree, then the four
-        // warps in order (fixed order, so the result does not depend on scheduling).
-        const int warp = tid >> 5, lane = tid & 31;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float t = warp_sum(__fmul_rn(cur[i], cur[i]));
-          if (lane == 0) xs[warp * 32 + i] = t;
-        }
-        __syncthreads();
-        if (tid < ncols)
-          a.ss_out[static_cast<size_t>(col0 + tid) * a.ss_ld + (m0 >> 7)] =
-              __fadd_rn(__fadd_rn(__fadd_rn(xs[tid], xs[32 + tid]), xs[64 + tid]), xs[96 + tid]);
-        __syncthreads();
       }
     }
     if constexpr (EPI == EPI_SWIGLU) {

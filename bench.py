@@ -53,6 +53,11 @@ WORKLOADS = {
     # the cfg0 model with 4-bit affine (group 64) layer linears and lm_head,
     # prompt 512, 256 new tokens, 128 steps = 8 blocks x 16 rounds, 2 commits per round.
     "cfg3": dict(prompt=512, gen=256, block=32, strategy="bd3_fixed_quota", steps=128, rounds=0, tau=0.9, quant=True),
+    # Not a BASELINE config: the reference's exact active-window preset (d2f_block_pipeline, block 8,
+    # tau_conf 0.8, tau_add 0.1, tau_act 0.95, exact prefix K/V) on the Dream-7B architecture, prompt
+    # 256, 256 new tokens (the D2F block-pipeline row's measurement).
+    "d2f": dict(model="dream", prompt=256, gen=256, block=8, strategy="d2f_block_pipeline", steps=256, rounds=0,
+                tau=0.8, tau_add=0.1, tau_act=0.95, origin="prompt"),
 }
 
 
@@ -171,7 +176,8 @@ def _frontier_stats(sess, prompt, w, probe) -> dict:
     mask = int(sess.runtime.config["mask_token_id"])
     n = len(prompt)
     scope = list(range(n, n + w["block"]))
-    res = sess.execute_window(list(prompt) + [mask] * w["block"], scope, mask_geometry=(0, w["block"]))
+    origin = n if w.get("origin") == "prompt" else 0
+    res = sess.execute_window(list(prompt) + [mask] * w["block"], scope, mask_geometry=(origin, w["block"]))
     logits = np.frombuffer(res.logits, dtype="<f4").reshape(res.n_rows, res.n_vocab).astype(np.float64)
     x = logits - logits.max(axis=1, keepdims=True)
     max_prob = 1.0 / np.exp(x).sum(axis=1)
@@ -190,7 +196,7 @@ def _run_ours(args, world, rank, local) -> dict | None:
     import torch
 
     from diffusorrt_b200 import Runtime, build
-    from diffusorrt_b200.config import QWEN3_06B_BD3LM
+    from diffusorrt_b200.config import DREAM_7B, QWEN3_06B_BD3LM
 
     if rank == 0:
         build.build()
@@ -200,7 +206,7 @@ def _run_ours(args, world, rank, local) -> dict | None:
         build.build()
     torch.cuda.set_device(local)
     w = WORKLOADS[args.workload]
-    cfg = dict(QWEN3_06B_BD3LM)
+    cfg = dict(DREAM_7B if w.get("model") == "dream" else QWEN3_06B_BD3LM)
     max_seq = ((w["prompt"] + w["gen"] + 127) // 128) * 128
     engine = {"linear_quant_bits": 4, "linear_quant_group_size": 64} if w.get("quant") else None
     rt = Runtime(model_config=cfg, synthetic_seed=0, device_ordinal=local, max_seq=max_seq,
@@ -208,10 +214,16 @@ def _run_ours(args, world, rank, local) -> dict | None:
     sess = rt.session({"decode_strategy": w["strategy"], "block_size": w["block"]})
     prompt = [int(t) for t in np.random.default_rng(rank).integers(0, 151643, size=w["prompt"])]
 
+    extra = {}
+    if w["strategy"] == "d2f_block_pipeline":
+        extra = dict(add_threshold=w["tau_add"], activate_threshold=w["tau_act"])
+    if "origin" in w:
+        extra["mask_origin"] = w["origin"]
+
     def request(trace=0):
         return sess.generate(prompt, max_tokens=w["gen"], steps=w["steps"], block_size=w["block"],
                              decode_strategy=w["strategy"], confidence_threshold=w["tau"],
-                             rounds_per_block=w["rounds"], trace_steps=trace)
+                             rounds_per_block=w["rounds"], trace_steps=trace, **extra)
 
     for _ in range(args.warmup):
         request()
@@ -268,10 +280,12 @@ def _run_ours(args, world, rank, local) -> dict | None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded random-init weights and prompts)",
-        "config": {"workload": f"{args.workload}: Qwen3-0.6B-arch BD3LM{' (4-bit affine g64 linears + lm_head)' if w.get('quant') else ''}, "
+        "config": {"workload": f"{args.workload}: {'Dream-7B-arch D2F' if w.get('model') == 'dream' else 'Qwen3-0.6B-arch BD3LM'}"
+                               f"{' (4-bit affine g64 linears + lm_head)' if w.get('quant') else ''}, "
                                f"prompt {w['prompt']}, gen {w['gen']}, block {w['block']}, {w['strategy']}"
                                + (f" tau {w['tau']} rounds/block {w['rounds']}" if w["strategy"] == "block_threshold" else
-                                  f" steps {w['steps']}"),
+                                  f" tau_conf {w['tau']} tau_add {w['tau_add']} tau_act {w['tau_act']} steps {w['steps']}"
+                                  if w["strategy"] == "d2f_block_pipeline" else f" steps {w['steps']}"),
                    "requests_per_gpu": 1, "parallelism": f"request-parallel x{world}",
                    "committed_tokens_per_request": committed, "denoising_steps_per_request": forwards,
                    "l2": (f"inputs larger than L2: {_weight_bytes(cfg, bool(w.get('quant'))) / 1e9:.2f} GB of weights "
@@ -282,8 +296,10 @@ def _run_ours(args, world, rank, local) -> dict | None:
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
                      "algorithmic_bytes_per_step": int(alg),
-                     "traffic": (int(_measured_traffic(alg)) if _measured_traffic(alg) and not w.get("quant") else None),
-                     "traffic_note": "DRAM bytes per step from profiles/decode_step_cfg1_traffic.json scaled to this K/V length"},
+                     "traffic": (int(_measured_traffic(alg)) if _measured_traffic(alg) and not w.get("quant")
+                                 and w.get("model") != "dream" else None),
+                     "traffic_note": ("DRAM bytes per step from profiles/decode_step_cfg1_traffic.json scaled to this K/V length"
+                                      if w.get("model") != "dream" and not w.get("quant") else None)},
         "e2e": {"value": round(world * committed / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
                 "h2d_bytes_per_step": 4 * (w["prompt"] + w["gen"]),
                 "d2h_bytes_per_step": 4 * (w["prompt"] + w["gen"]) + 512},
@@ -779,6 +795,10 @@ def main():
         if rank != 0:
             return
         w = WORKLOADS[args.workload]
+        if w.get("model") == "dream":
+            print(json.dumps({"impl": "reference", "unavailable": "the d2f workload's CPU reference step is cfg2's "
+                              "(same Dream-7B model): run --impl reference --workload cfg2"}), flush=True)
+            return
         samples = [_cpu_baseline(args) for _ in range(max(1, min(args.steps, 2)))]
         step_s = float(np.mean([s["step_s"] for s in samples]))
         steps_per_request = 16 * 8 if args.workload == "cfg1" else 128
@@ -830,7 +850,8 @@ def main():
         return
     line = _run_ours(args, world, rank, local)
     if rank == 0 and line is not None:
-        if not args.no_cpu_baseline and world == 1:
+        # (the d2f workload's model is cfg2's: its CPU baseline is cfg2's line)
+        if not args.no_cpu_baseline and world == 1 and WORKLOADS[args.workload].get("model") != "dream":
             cb = _cpu_baseline(args)
             steps = line["config"]["denoising_steps_per_request"]
             tokens = line["config"]["committed_tokens_per_request"]

@@ -1818,7 +1818,9 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   {
     const int n_sub = (s->max_seq + 63) / 64;  // sub-tiles of the longest canvas, the last one partial
     const int sp = (n_sub + kDaMaxSub - 1) / kDaMaxSub;
-    const bool fits = m->rep * (kMaxFwdRows / 2) <= 128 && sp <= kDaMaxSplits;
+    // every forwarded row of a decode forward (up to kMaxFwdRows: a finished block forwarded again
+    // plus the window) times the query heads per KV head must fit the kernel's 128 UMMA rows
+    const bool fits = m->rep * kMaxFwdRows <= 128 && sp <= kDaMaxSplits;
     s->da_splits = fits ? sp : 0;
     // One cluster per KV head when every cluster can be resident at once: the split merge then
     // happens in distributed shared memory instead of a second kernel.

@@ -133,6 +133,39 @@ def test_long_prefix_decode_attention(max_seq, n_prefix):
     np.testing.assert_allclose(scores, want_conf, rtol=0.05)
 
 
+def test_four_query_heads_per_kv_head_64_row_forward():
+    """GQA 4:1 (8 query heads on 2 KV heads): after a block is committed, the next proposal forwards
+    64 rows (the finished block again, then the new block), which with 4 query heads per KV head
+    exceeds the decode attention kernel's 128 UMMA rows; the session takes the general attention
+    kernel and the scores agree with the cache-free window forward."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from diffusorrt_b200 import Runtime
+
+    cfg = dict(SMALL, attention_heads=8, num_kv_heads=2)
+    r = Runtime(model_config=cfg, max_seq=256, max_prefill_rows=128)
+    try:
+        r.init_synthetic(SEED, **STD)
+        mask = cfg["mask_token_id"]
+        x = _prompt(64, 8) + [mask] * 64
+        with r.session({"decode_strategy": "bd3_fixed_quota", "block_size": 32}) as s:
+            s.start_device(x, prompt_len=0, block_size=32, mask_token_id=mask, exact_kv=True, steps=4)
+            first = list(range(64, 96))
+            _, tok, _ = s.propose_device(first, window_end=96, frozen_prefix=64)
+            s.commit_device(first, tok)
+            for p, t in zip(first, tok):
+                x[p] = t
+            frontier = list(range(96, 128))
+            scores, tokens, fwd = s.propose_device(frontier, window_end=128, frozen_prefix=96)
+            assert fwd == 64
+            ref = _window_logits(s, x, frontier)
+    finally:
+        r.close()
+    want_conf, want_tok = osel.max_prob_rows(ref)
+    assert np.mean(np.asarray(tokens) == np.asarray(want_tok)) >= 0.9
+    np.testing.assert_allclose(scores, want_conf, rtol=0.05)
+
+
 def test_large_vocab_head_matches_oracle():
     """A vocabulary of 320 weight tiles (more than two per SM) takes the persistent lm_head kernel:
     one CTA per SM over a contiguous run of tiles, activation tile loaded once, TMEM accumulator

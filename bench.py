@@ -677,6 +677,9 @@ def _profile_case(args) -> None:
              drawn by the sampling selector (Gumbel keys, seed 0);
       dream: Dream-7B full canvas (prompt 256 + canvas 256), entropy_count over --pc-steps (4) steps,
              --pc-layers layers (0: the model's 28); ~15 GB of synthetic weights.
+      d2f:   Dream-7B on the D2F graph (prompt 256 as the mask origin), d2f_block_pipeline with the
+             reference's active-window preset (block 8, tau_conf 0.8, tau_add 0.1, tau_act 0.95) over
+             --pc-steps (4) denoising steps of a 256-token canvas.
 
     Kernel order, for a profiler's name filter and skip count: the prompt prefill launches one
     embed_rows_kernel and two rmsnorm_bf16_kernel per layer (with the prefill linears and attention);
@@ -688,6 +691,21 @@ def _profile_case(args) -> None:
     (down)], rmsnorm, gemm_swapab (lm_head), sel_topp_entropy_kernel, dream_commit_kernel.
 
     Prints one JSON line: denoising steps run, kernel launches of the request and ms per step."""
+    if args.profile_case == "d2f":
+        from diffusorrt_b200 import Runtime
+        from diffusorrt_b200.config import DREAM_7B
+
+        rt = Runtime(model_config=dict(DREAM_7B), synthetic_seed=0, device_ordinal=0, max_seq=512, max_prefill_rows=256)
+        sess = rt.session({"decode_strategy": "d2f_block_pipeline", "block_size": 8})
+        prompt = [int(t) for t in np.random.default_rng(0).integers(0, 151643, size=256)]
+        res = sess.generate(prompt, max_tokens=256, steps=args.pc_steps, block_size=8, decode_strategy="d2f_block_pipeline",
+                            confidence_threshold=0.8, add_threshold=0.1, activate_threshold=0.95, mask_origin="prompt")
+        forwards = int(res["forward_count"])
+        print(json.dumps({"prompt": 256, "gen": 256, "forwards": forwards, "kernel_launches": int(res["kernel_launches"]),
+                          "decode_ms_per_step": res["decode_ms"] / max(1, forwards)}), flush=True)
+        sess.close()
+        rt.close()
+        return
     args.dream = args.profile_case == "dream"
     args.quant = args.profile_case == "quant"
     args.prompt, args.gen, args.rounds, args.steps, args.layers = (args.pc_prompt, args.pc_gen, args.pc_rounds,
@@ -743,7 +761,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="cfg1", choices=sorted(WORKLOADS) + ["cfg2", "cfg4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile-case", choices=["cfg1", "quant", "dream"],
+    ap.add_argument("--profile-case", choices=["cfg1", "quant", "dream", "d2f"],
                     help="run one small decode for a profiler instead of the benchmark (see _profile_case)")
     ap.add_argument("--pc-prompt", type=int, default=4096)
     ap.add_argument("--pc-gen", type=int, default=32)

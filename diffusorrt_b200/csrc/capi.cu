@@ -26,6 +26,7 @@
 #include "dream.cuh"
 #include "gemm.cuh"
 #include "gemm_decode.cuh"
+#include "gemm_streamk.cuh"
 #include "policy.cuh"
 #include "quant.cuh"
 #include "rowops.cuh"
@@ -209,6 +210,8 @@ int configure_kernels() {
         cudaFuncSetAttribute(gemm_swapab_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_swapab_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_streamk_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_streamk_kernel<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(attn_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(attn_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(sel_topp_entropy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kToppSmemBytes)) != cudaSuccess ||
@@ -884,6 +887,8 @@ struct drt_session {
   // tensor maps over the activation buffers
   CUtensorMap m_xn64, m_xn128, m_xn256, m_attn64, m_attn128, m_attn256, m_act64, m_act128, m_act256, m_xf64, m_q, m_k, m_v;
   CUtensorMap m_k64;                  // K cache with 64-key boxes (decode attention)
+  float* sk_part = nullptr;           // stream-K linears: per-CTA partial tiles [SMs][128][128] f32
+  int* sk_flag = nullptr;             // and their ready flags [SMs] (zero between launches)
   int da_splits = 0;                  // decode attention CTAs per KV head (0: use attn_prefix_kernel)
   int da_cluster = 0;                 // the splits of a KV head run as one cluster and merge in it
   float* da_part_o = nullptr;         // decode attention split partials
@@ -945,6 +950,8 @@ int check_status(drt_session* s) {
   CK(cudaMemcpy(&code, s->status, sizeof(int), cudaMemcpyDeviceToHost));
   if (code != 0) {
     cudaMemset(s->status, 0, sizeof(int));
+    // a wait that ran out may have left stream-K ready flags raised
+    if (s->sk_flag != nullptr) cudaMemset(s->sk_flag, 0, sizeof(int) * s->sms);
     if (code == DEV_BAD_SHAPE) return set_error(DRT_INVALID_ARGUMENT, "device rejected an input (token id out of range)");
     if (code == DEV_TIMEOUT_PEER) return set_error(DRT_DEVICE_TIMEOUT, "a tensor-parallel peer did not deliver its partials in time");
     if (code == DEV_BAD_GEOMETRY) return set_error(DRT_INTERNAL_ERROR, "a kernel's launch geometry did not cover its work");
@@ -1006,10 +1013,36 @@ int launch_wide(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, Ge
 //   * otherwise: 128 x 128 tiles, two CTAs per SM.
 // mB128 / mB256: the activation map with 128- / 256-row boxes (mB256 null when the buffer is
 // narrower than 256 rows).
+// Stream-K linear (gemm_streamk_kernel): one CTA per SM takes an equal share of the (tile, K block)
+// iterations. BN: activation rows per tile (mB's box).
+template <int BN>
+int launch_streamk(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, GemmArgs a) {
+  using Cfg = GemmCfg<BN, 2>;
+  const long long total = static_cast<long long>(a.n_out / 128) * ((a.rows + BN - 1) / BN) * (a.K / 64);
+  const int grid = static_cast<int>(std::min<long long>(s->sms, total));
+  a.splits = 1;
+  a.kb_per_split = a.K / 64;
+  int stages = 1;
+  while (Cfg::smem_bytes(stages + 1) <= kFullSmPrefill) ++stages;
+  a.stages = stages;
+  a.sk_part = s->sk_part;
+  a.sk_flag = s->sk_flag;
+  CK(launch_k(gemm_streamk_kernel<BN, 2>, dim3(grid), dim3(128), Cfg::smem_bytes(a.stages), s->stream, true, mA, mB, a));
+  return DRT_OK;
+}
+
 int run_wide(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB128, const CUtensorMap* mB256, GemmArgs a) {
   const int tiles_m = a.n_out / 128;
   const int t256 = tiles_m * ((a.rows + 255) / 256);
   const int t128 = tiles_m * ((a.rows + 127) / 128);
+  // One row tile (a decode window) on fewer weight tiles than nine tenths of the SMs, with K long
+  // enough for many K blocks per CTA: the linear is a weight stream that one CTA per tile would read
+  // on a fraction of the SMs. (Full-canvas shapes stay one CTA per tile: with several row tiles the
+  // linear is compute-bound under the power cap, where waking the idle SMs measured slower.)
+  const bool sk_epi = a.epi == EPI_RESID || a.epi == EPI_STORE_F32 || a.epi == EPI_STORE_RAW;
+  if (s->sk_part != nullptr && sk_epi && a.rows <= 128 && t128 * 10 < s->sms * 9 &&
+      t128 * (a.K / 64) >= 16 * s->sms)
+    return launch_streamk<128>(s, mA, mB128, a);
   if (mB256 != nullptr && a.rows > 128 && t256 >= 2 * s->sms) return launch_wide<256, 1>(s, mA, *mB256, a, kHalfSmPrefill);
   if (t128 <= s->sms) return launch_wide<128, 2>(s, mA, mB128, a, kFullSmPrefill);
   return launch_wide<128, 1>(s, mA, mB128, a, kHalfSmPrefill);
@@ -1054,6 +1087,13 @@ int run_dec_gemm(drt_session* s, const CUtensorMap& mA, const CUtensorMap& mB, G
                 true, mA, mB, a));
     return DRT_OK;
   }
+  // Large bf16 weights (a 7B model's MLP and vocabulary projection) over a decode window: the
+  // linear is a weight stream; stream-K over every SM reads it at a higher rate than one split-K
+  // cluster per weight tile (Dream-7B D2F decode step: 6.67 -> 5.31 ms with the down_proj alone).
+  if (q == nullptr && s->sk_part != nullptr && a.rows <= 64 &&
+      static_cast<size_t>(a.n_out) * a.K * 2 >= (size_t{64} << 20) &&
+      (a.epi == EPI_RESID || a.epi == EPI_STORE_F32 || a.epi == EPI_STORE_RAW || a.epi == EPI_SWIGLU))
+    return launch_streamk<64>(s, mA, mB, a);
   dec_split(tiles_m, kb, s->sms, s->max_cluster, &a.splits, &a.kb_per_split);
   if (q != nullptr) {
     // every packed tile of a CTA's K slice stays resident: at most kDecQMaxKb blocks per CTA
@@ -1767,6 +1807,10 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   if ((rc = salloc(s, &s->act, static_cast<size_t>(R) * m->I)) != DRT_OK) return fail(rc);
   const int xf_rows = std::max(s->head_cap, 128);  // the final-norm rows, at least one 128-row box
   if ((rc = salloc(s, &s->xf, static_cast<size_t>(xf_rows) * H)) != DRT_OK) return fail(rc);
+  // stream-K workspace (one 128 x 128 f32 partial per SM) and its flags
+  if ((rc = salloc(s, &s->sk_part, static_cast<size_t>(s->sms) * 128 * 128)) != DRT_OK) return fail(rc);
+  if ((rc = salloc(s, &s->sk_flag, static_cast<size_t>(s->sms))) != DRT_OK) return fail(rc);
+  if (cudaMemset(s->sk_flag, 0, sizeof(int) * s->sms) != cudaSuccess) return fail(set_error(DRT_INTERNAL_ERROR, "memset failed"));
   // a tensor-parallel session's logits live in its peer-mapped buffer (below): with the
   // vocabulary-parallel lm_head every rank's projection stores its tiles there
   if (m->shard.world <= 1 && (rc = salloc(s, &s->logits, static_cast<size_t>(s->head_cap) * m->V)) != DRT_OK) return fail(rc);

@@ -67,6 +67,9 @@ struct GemmArgs {
   __nv_bfloat16* vtcache;// this layer: [nkv][128][max_seq]
   int max_seq;
   float eps;
+  // stream-K (gemm_streamk_kernel): per-CTA partial tiles [grid][BN][128] f32 and ready flags [grid]
+  float* sk_part;
+  int* sk_flag;
   // 4-bit affine weights (decode linear, quantized instantiation): per (row, group of 64 inputs)
   // bf16 scale and bias, [n_out][q_groups] with q_groups = K / 64; the packed nibbles come from tmA.
   const __nv_bfloat16* q_scale;

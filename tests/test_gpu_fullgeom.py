@@ -104,6 +104,33 @@ def test_dream_gqa7_window_logits(dream2):
     assert_logits_close(got, want)
 
 
+def test_dream_width_d2f_decode_window(dream2):
+    """A Dream-width decode window on the D2F graph (prompt bidirectional, blocks of 8 from it): the
+    first proposal prefills the prompt and forwards one block and the shift feeder row. Its
+    down_proj (28 weight tiles, K = 18944) is a stream-K linear over every SM. The proposal's
+    confidences and tokens match the oracle forward of the same window within the stated bf16
+    tolerance: |log conf_dev - log conf_oracle| <= 2 E, each token's oracle logit within 2 E of its
+    row's maximum (E = 48 u of the logit RMS)."""
+    rt, cfg, w = dream2
+    mask = cfg["mask_token_id"]
+    P, BS = 256, 8
+    x = _prompt(P, 9) + [mask] * 32
+    frontier = list(range(P, P + BS))
+    with rt.session({"decode_strategy": "block_threshold", "attention_mask_kind": "d2f_hybrid", "block_size": BS}) as s:
+        s.start_device(x, prompt_len=P, block_size=BS, mask_token_id=mask, exact_kv=True, steps=4)
+        scores, tokens, fwd = s.propose_device(frontier, window_end=P + BS, frozen_prefix=P)
+    assert fwd == P + BS + 1
+    logits = ofwd.forward_mlx(w, cfg, x[:P + BS], prompt_len=P, block_size=BS,
+                              output_rows=ofwd.dream_raw_rows(frontier))
+    logits = osel.exclude_mask_token(logits, mask)
+    want_conf, _ = osel.max_prob_rows(logits)
+    finite = logits[np.isfinite(logits)]
+    E = MAX_FACTOR * U_BF16 * float(np.sqrt(np.mean(finite.astype(np.float64) ** 2)))
+    assert np.all(np.abs(np.log(np.asarray(scores)) - np.log(np.asarray(want_conf))) <= 2 * E)
+    rows = np.arange(len(frontier))
+    assert np.all(logits[rows, np.asarray(tokens)] >= logits.max(axis=1) - 2 * E)
+
+
 def test_dream_gqa7_entropy_count_along_trajectory(dream2):
     """Every step of the device's entropy_count decode (NegEntropy T 0.2 with top-p 0.95, MASK
     excluded, top-k by the f32 entropy) against the oracle on the device's canvas: each frontier

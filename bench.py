@@ -10,7 +10,7 @@ seeded requests run one per GPU (request-parallel, weak scaling, no collective o
 One bench step = one complete request: prompt upload, prefill, every denoising step (forward,
 selector, policy, commit on the GPU), canvas download.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg0|cfg2|cfg3|cfg4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg0|cfg2|cfg3|cfg4|d2f]
 
 --workload cfg0 / cfg3: BASELINE configs[0] / [3] (cfg3: the cfg0 model with 4-bit affine, group 64
 linears and lm_head, prompt 512, 256 new tokens, 2 commits per round).
@@ -19,8 +19,13 @@ linears and lm_head, prompt 512, 256 new tokens, 2 commits per round).
 intermediate 18944, vocab 152064, q/k/v bias, untied lm_head), 256-token prompt plus a 256-token
 all-MASK canvas, entropy_count over 256 steps (NegEntropy T 0.2, top_p 0.95, eps 1e-3, MASK
 excluded): every step forwards the whole 512-row canvas with bidirectional attention. With N > 1
-GPUs the one request runs tensor-parallel over the group (heads and MLP sharded, NCCL all-reduce
-after o_proj and down_proj), strong scaling; its roofline is tensor-core FLOP/s.
+GPUs the one request runs tensor-parallel over the group (heads and MLP sharded, the row-split
+linears reduced over NVLink peer memory, the lm_head split by vocabulary), strong scaling; its
+roofline is tensor-core FLOP/s.
+
+--workload d2f (not a BASELINE config): the reference's exact active-window preset on the Dream-7B
+architecture: D2F graph with the prompt as the mask origin, d2f_block_pipeline (block 8, tau_conf
+0.8, tau_add 0.1, tau_act 0.95), 256-token prompt, 256 new tokens; HBM roofline of the step.
 
 --workload cfg4 is the isolated unmask-selector microbenchmark: fp32 logits
 [B, L, 151936] ~ N(0, 3^2) from a seed, a Bernoulli(0.5) mask of masked positions, max-prob and

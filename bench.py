@@ -10,7 +10,7 @@ seeded requests run one per GPU (request-parallel, weak scaling, no collective o
 One bench step = one complete request: prompt upload, prefill, every denoising step (forward,
 selector, policy, commit on the GPU), canvas download.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg0|cfg2|cfg3|cfg4|d2f]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg0|cfg2|cfg3|cfg4|d2f|d2f_bt]
 
 --workload cfg0 / cfg3: BASELINE configs[0] / [3] (cfg3: the cfg0 model with 4-bit affine, group 64
 linears and lm_head, prompt 512, 256 new tokens, 2 commits per round).
@@ -26,6 +26,8 @@ roofline is tensor-core FLOP/s.
 --workload d2f (not a BASELINE config): the reference's exact active-window preset on the Dream-7B
 architecture: D2F graph with the prompt as the mask origin, d2f_block_pipeline (block 8, tau_conf
 0.8, tau_add 0.1, tau_act 0.95), 256-token prompt, 256 new tokens; HBM roofline of the step.
+--workload d2f_bt: the same model and canvas under the reference's shipped Dream CUDA profile,
+block_threshold (tau 0.9) over blocks of 8 with exact K/V.
 
 --workload cfg4 is the isolated unmask-selector microbenchmark: fp32 logits
 [B, L, 151936] ~ N(0, 3^2) from a seed, a Bernoulli(0.5) mask of masked positions, max-prob and
@@ -63,6 +65,10 @@ WORKLOADS = {
     # 256, 256 new tokens (the D2F block-pipeline row's measurement).
     "d2f": dict(model="dream", prompt=256, gen=256, block=8, strategy="d2f_block_pipeline", steps=256, rounds=0,
                 tau=0.8, tau_add=0.1, tau_act=0.95, origin="prompt"),
+    # Not a BASELINE config: the reference's shipped Dream CUDA profile (cuda_profile.py:63-82, 96-119):
+    # block_threshold (tau 0.9, at least one per step) over blocks of 8 on the D2F graph, exact K/V.
+    "d2f_bt": dict(model="dream", prompt=256, gen=256, block=8, strategy="block_threshold", steps=256, rounds=0,
+                   tau=0.9, origin="prompt"),
 }
 
 

@@ -62,7 +62,7 @@ typedef enum drt_status {
 #define DRT_TIE_NEAR 1
 #define DRT_TIE_EXACT 2
 
-/* Tensor parallelism (BASELINE configs[2] across 2/4/8 GPUs): one rank's shard of the model.
+/* Tensor parallelism (one Dream-7B request across 2/4/8 GPUs): one rank's shard of the model.
  * Attention heads are split by K/V head; when there are more ranks than K/V heads, the ranks
  * sharing a K/V head each project it and split its query heads. MLP intermediate columns are split
  * in 64-column units. Embedding, norms and lm_head are replicated. */

@@ -1,4 +1,4 @@
-"""Dream-style full-canvas masked diffusion on the GPU through the C ABI.
+"""Dream-style full-canvas masked diffusion (the benchmark's Dream configuration) on the GPU through the C ABI.
 
 * The top-p NegEntropy selector equals the oracle's ``_entropy_confidence`` restatement on
   bf16-valued logits (which repeat often, so the nucleus cut falls on tied values): confidences

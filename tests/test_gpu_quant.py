@@ -1,4 +1,4 @@
-"""4-bit affine linear weights on the GPU through the C ABI:
+"""4-bit affine linear weights (the benchmark's quantized configuration) on the GPU through the C ABI:
 
 * the device quantizer equals its NumPy restatement bit for bit (packed nibbles, bf16 scales
   and biases, including constant groups);

@@ -65,7 +65,8 @@ typedef enum drt_status {
 /* Tensor parallelism (one Dream-7B request across 2/4/8 GPUs): one rank's shard of the model.
  * Attention heads are split by K/V head; when there are more ranks than K/V heads, the ranks
  * sharing a K/V head each project it and split its query heads. MLP intermediate columns are split
- * in 64-column units. Embedding, norms and lm_head are replicated. */
+ * in 64-column units. Embedding, norms and the lm_head weight are replicated; a session whose peers
+ * are mapped splits the lm_head's work by vocabulary (drt_session_tp_vocab_parallel). */
 typedef struct drt_tp_shard {
   int32_t rank, world;
   int32_t q_head0, q_heads;    /* global query heads [q_head0, q_head0 + q_heads) */
@@ -125,7 +126,7 @@ typedef struct drt_generate_params {
    * python/src/edllm/backends/diffusion_runtime.py:2079-2110. */
   double temperature;          /* entropy_count: NegEntropy logits / T (<= 0: no scaling);
                                   bd3_fixed_quota: sampling temperature (0: argmax), as drt_selector_sample;
-                                  block_threshold: must be 0 */
+                                  block_threshold and d2f_block_pipeline: must be 0 */
   double top_p;                /* nucleus mass (>= 1: no nucleus) */
   double eps;                  /* last timestep of linspace(1, eps, steps + 1) */
   uint64_t seed;               /* bd3_fixed_quota at temperature > 0: keys the draws */

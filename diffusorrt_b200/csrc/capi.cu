@@ -2504,6 +2504,7 @@ extern "C" int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows
   a.part_max = reinterpret_cast<float*>(take(np * 4));
   a.part_idx = reinterpret_cast<int*>(take(np * 4));
   a.counters = reinterpret_cast<int*>(take(static_cast<size_t>(n_rows) * 4));
+  if (mode == DRT_SELECT_NEG_ENTROPY) a.part_ent = reinterpret_cast<double*>(take(np * 8));
   CK(cudaMemsetAsync(a.counters, 0, sizeof(int) * n_rows, st));
   a.logits = logits;
   a.ld = ld;
@@ -2516,8 +2517,12 @@ extern "C" int drt_selector_rows(const float* logits, int64_t ld, int32_t n_rows
   a.exclude = -1;
   a.conf = conf;
   a.token = token;
-  CK(launch_k(sel_pass1_kernel<false>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
-  if (mode == DRT_SELECT_NEG_ENTROPY) CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  if (mode == DRT_SELECT_NEG_ENTROPY) {
+    CK(launch_k(sel_pass1_kernel<false, true>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+    CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  } else {
+    CK(launch_k(sel_pass1_kernel<false>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  }
   return DRT_OK;
 }
 
@@ -2541,6 +2546,7 @@ extern "C" int drt_selector_gather(const float* logits, int64_t ld, const int32_
   a.part_max = reinterpret_cast<float*>(take(np * 4));
   a.part_idx = reinterpret_cast<int*>(take(np * 4));
   a.counters = reinterpret_cast<int*>(take(static_cast<size_t>(n_rows) * 4));
+  if (mode == DRT_SELECT_NEG_ENTROPY) a.part_ent = reinterpret_cast<double*>(take(np * 8));
   CK(cudaMemsetAsync(a.counters, 0, sizeof(int) * n_rows, st));
   a.logits = logits;
   a.ld = ld;
@@ -2554,8 +2560,12 @@ extern "C" int drt_selector_gather(const float* logits, int64_t ld, const int32_
   a.exclude = -1;
   a.conf = conf;
   a.token = token;
-  CK(launch_k(sel_pass1_kernel<false>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
-  if (mode == DRT_SELECT_NEG_ENTROPY) CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  if (mode == DRT_SELECT_NEG_ENTROPY) {
+    CK(launch_k(sel_pass1_kernel<false, true>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+    CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  } else {
+    CK(launch_k(sel_pass1_kernel<false>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  }
   return DRT_OK;
 }
 
@@ -2795,15 +2805,15 @@ extern "C" int drt_quantize_q4(const void* w, int64_t rows, int32_t K, void* q, 
 // ======================================================================= selector without allocation
 // drt_selector_rows_noalloc: the fused selector with its scratch (chunk partials, row statistics,
 // arrival counters) in one file-scope device array instead of caller memory, for callers that may
-// not allocate device memory. The array is fixed at kNoAllocScratchBytes (about 0.53 MB) and every
+// not allocate device memory. The array is fixed at kNoAllocScratchBytes (about 0.81 MB) and every
 // GPU that loads this library holds one copy until the process exits.
 namespace {
 constexpr int kNoAllocMaxRows = 1024;
 constexpr int kNoAllocMaxVocab = 262144;
 constexpr size_t kNoAllocMaxParts = static_cast<size_t>(kNoAllocMaxRows) * (kNoAllocMaxVocab / kSelChunk);
-// part_sum f64 + part_max f32 + part_idx i32 per (row, chunk); row_amax f64 + row_sum f64 +
-// counter i32 per row; six 256-byte alignment pads.
-constexpr size_t kNoAllocScratchBytes = kNoAllocMaxParts * (8 + 4 + 4) + static_cast<size_t>(kNoAllocMaxRows) * (8 + 8 + 4) + 6 * 256;
+// part_sum f64 + part_max f32 + part_idx i32 + part_ent f64 per (row, chunk); row_amax f64 + row_sum f64 +
+// counter i32 per row; seven 256-byte alignment pads.
+constexpr size_t kNoAllocScratchBytes = kNoAllocMaxParts * (8 + 4 + 4 + 8) + static_cast<size_t>(kNoAllocMaxRows) * (8 + 8 + 4) + 7 * 256;
 static __device__ __align__(256) uint8_t g_selector_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mutex;
@@ -2890,6 +2900,7 @@ extern "C" int drt_selector_rows_noalloc(const float* logits, int64_t ld, int32_
   a.part_max = reinterpret_cast<float*>(take(np * 4));
   a.part_idx = reinterpret_cast<int*>(take(np * 4));
   a.counters = reinterpret_cast<int*>(take(static_cast<size_t>(n_rows) * 4));
+  if (mode == DRT_SELECT_NEG_ENTROPY) a.part_ent = reinterpret_cast<double*>(take(np * 8));
   if (static_cast<size_t>(p - static_cast<uint8_t*>(base)) > kNoAllocScratchBytes)
     return set_error(DRT_INTERNAL_ERROR, "selector scratch layout exceeds the static array");
   // The array keeps the previous call's contents; the arrival counters must start at zero.
@@ -2905,7 +2916,11 @@ extern "C" int drt_selector_rows_noalloc(const float* logits, int64_t ld, int32_
   a.exclude = -1;
   a.conf = conf;
   a.token = token;
-  CK(launch_k(sel_pass1_kernel<false>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
-  if (mode == DRT_SELECT_NEG_ENTROPY) CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  if (mode == DRT_SELECT_NEG_ENTROPY) {
+    CK(launch_k(sel_pass1_kernel<false, true>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+    CK(launch_k(sel_entropy_kernel, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  } else {
+    CK(launch_k(sel_pass1_kernel<false>, dim3(chunks, n_rows), dim3(kSelThreads), 0, st, false, a));
+  }
   return DRT_OK;
 }

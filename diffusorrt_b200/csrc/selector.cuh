@@ -7,6 +7,14 @@
 //   largest f32 logit (integer-exact), and conf = 1 / S with S accumulated in f64.
 // Entropy (NegEntropy, diffusion_runtime.py:90-114 without top-p):
 //   a = f64(x) / T (T > 0), p = softmax(a), conf = f32(sum p * log(p + 1e-10)), token = argmax p.
+//   With m = max a, e = exp(a - m), S = sum e and eps = 1e-10, log(p + eps) = log p + log1p(eps / p)
+//   and log p = (a - m) - log S, so the sum splits into
+//     H = (sum e (a - m)) / S - log S  +  C,   C = sum p log1p(eps / p).
+//   The first part comes out of pass 1 in float64 (one more FMA per logit beside the sum of e;
+//   every term has the same sign, so nothing cancels). 0 <= p log1p(eps / p) <= eps for every p,
+//   so C <= V eps (1.5e-5 at V = 151936), about 15 float32 ulps of a typical |H|: pass 2 evaluates
+//   each term of C / eps in float32 (relative error about 1e-6) and sums in float64, which puts H
+//   within about 1e-13 of the float64 per-logit sum, far inside the half ulp the float32 cast keeps.
 //
 // Layout: grid (chunks, rows); each CTA reduces one chunk of a row to (max, first argmax,
 // sum exp(x - chunk_max)); the last CTA of a row (arrival counter, reset by that CTA) merges
@@ -78,8 +86,10 @@ struct SelArgs {
   float* part_max;        // [rows * nchunks]
   int* part_idx;
   double* part_sum;
+  double* part_ent;       // entropy: [rows * nchunks] sum e (a - chunk max) per chunk; slot 0 of a row
+                          // then holds the row's sum e (a - m) / S - log S
   int* counters;          // [rows]
-  double* row_amax;       // [rows] adjusted max (entropy)
+  double* row_amax;       // [rows] entropy: the row's largest float32 logit
   double* row_sum;        // [rows] S (entropy)
   double* conf;           // [rows]
   int* token;             // [rows]
@@ -117,8 +127,9 @@ __device__ __forceinline__ double sel_adjust(double x, double inv_t) { return x 
 // Pass 1: chunk max / argmax / sum of exp relative to the chunk's adjusted max. kSample adds the
 // sampled draw (SEL_SAMPLE, or SEL_MAXPROB with a device-side temperature above 0); the greedy
 // instantiation carries none of its registers (64 -> 48 per thread, 4 -> 5 resident CTAs per SM).
-template <bool kSample>
-__global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a) {
+// kEntropy (SEL_ENTROPY) also accumulates sum e (a - chunk max) for the entropy's exact part.
+template <bool kSample, bool kEntropy = false>
+__global__ void __launch_bounds__(kSelThreads, kSample ? 4 : 5) sel_pass1_kernel(const SelArgs a) {
   griddep_wait();
   griddep_launch_dependents();
   int rows_valid = a.rows;
@@ -227,13 +238,30 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
   // which leaves a sum holding the chunk maximum's exp(0) = 1 unchanged; a chunk with no finite
   // value sums nothing.
   double sum = 0.0;
+  double ent = 0.0;  // kEntropy: sum e z, z = max(a - chunk max, -708) (a clamped term adds about -2e-305)
   if (bm != -INFINITY) {
+    if constexpr (kEntropy) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) sum += exp_nonpos_clamped(sel_adjust(static_cast<double>(vals[i]), inv_t) - amax);
+      for (int i = 0; i < 32; ++i) {
+        const double z = fmax(sel_adjust(static_cast<double>(vals[i]), inv_t) - amax, -708.0);
+        const double e = exp_nonpos_core(z);  // exp_nonpos_clamped of the same argument
+        sum += e;
+        ent = fma(e, z, ent);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sum += exp_nonpos_clamped(sel_adjust(static_cast<double>(vals[i]), inv_t) - amax);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if ((tid & 31) == 0) s_s[tid >> 5] = sum;
+  __shared__ double s_e[kSelThreads / 32];
+  if constexpr (kEntropy) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ent += __shfl_xor_sync(0xffffffffu, ent, o);
+    if ((tid & 31) == 0) s_e[tid >> 5] = ent;
+  }
   __syncthreads();
   __shared__ int s_last;
   if (tid == 0) {
@@ -243,6 +271,11 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
     a.part_max[slot] = bm;
     a.part_idx[slot] = bi;
     a.part_sum[slot] = bs;
+    if constexpr (kEntropy) {
+      double be = 0.0;
+      for (int w = 0; w < kSelThreads / 32; ++w) be += s_e[w];
+      a.part_ent[slot] = be;
+    }
     if (sample) {
       a.part_skey[slot] = k1;
       a.part_sidx[slot] = ki;
@@ -261,12 +294,19 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
   for (int k = 0; k < a.nchunks; ++k) argmax_merge(gm, gi, __ldcg(&a.part_max[r * a.nchunks + k]), __ldcg(&a.part_idx[r * a.nchunks + k]));
   const double gam = sel_adjust(static_cast<double>(gm), inv_t);
   double S = 0.0;
+  double row_ent = 0.0;  // kEntropy: sum e (a - m) over the row
   for (int k = 0; k < a.nchunks; ++k) {
     const float cm = __ldcg(&a.part_max[r * a.nchunks + k]);
     const double cs = __ldcg(&a.part_sum[r * a.nchunks + k]);
     if (cm == -INFINITY) continue;
     const double cam = sel_adjust(static_cast<double>(cm), inv_t);
-    S += (cam == gam) ? cs : cs * exp_nonpos(cam - gam);
+    const double f = (cam == gam) ? 1.0 : exp_nonpos(cam - gam);
+    S += (cam == gam) ? cs : cs * f;
+    if constexpr (kEntropy) {
+      // chunk terms e_c z_c with e = e_c f and a - m = z_c + (cam - gam): both parts <= 0
+      const double ce = __ldcg(&a.part_ent[r * a.nchunks + k]);
+      row_ent += (cam == gam) ? ce : f * fma(cam - gam, cs, ce);
+    }
   }
   if (sample) {
     double g1 = -INFINITY, g2 = -INFINITY;
@@ -287,13 +327,35 @@ __global__ void __launch_bounds__(kSelThreads) sel_pass1_kernel(const SelArgs a)
   if (a.mode == SEL_MAXPROB || a.mode == SEL_SAMPLE) {
     a.conf[r] = 1.0 / S;
   } else {
-    a.row_amax[r] = gam;
+    a.row_amax[r] = static_cast<double>(gm);
     a.row_sum[r] = S;
+    if constexpr (kEntropy) a.part_ent[r * a.nchunks] = row_ent / S - log(S);  // every chunk value is read
   }
   a.counters[r] = 0;
 }
 
-// Pass 2 (entropy): sum p log(p + 1e-10) with the row's global max and S.
+// Pass 2 (entropy): C / eps = sum p log1p(eps / p) / eps in float32 per logit, then the row's
+// H = (exact part from pass 1) + eps (C / eps). With d = log2(p / eps) and q = 2^-|d| in (0, 1]:
+//   d >= 0 (p >= eps): p log1p(eps / p) / eps = log1p(q) / q;
+//   d <  0 (p <  eps): p log1p(eps / p) / eps = q (log1p(q) + |d| ln 2)   (log(eps / p) = |d| ln 2).
+// d = (x - max x) (log2(e) / T) - log2(S) - log2(eps), the two constants split into float32 head
+// and tail so that only the rounding of d itself (relative 6e-8, about 1e-6 on q) is left; |d| is
+// capped at 200, and q below 2^-126 flushes to 0 (such a term is below 1e-36 and dropped). A -inf
+// logit (the excluded column, p = 0 in the reference) and a NaN one land on that cap and add nothing.
+// log1p(q) = 2 atanh(s) = 2 s P(s^2) with s = q / (2 + q) <= 1/3 and P the atanh series through
+// s^14 / 15 (truncation below 2e-8 relative), so log1p(q) / q = 2 P / (2 + q): no division by q and
+// no cancellation at small q. 2^w and 1 / (2 + q) are the hardware approximations (ex2.approx,
+// rcp.approx: relative error within a few 2^-23).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __global__ void __launch_bounds__(kSelThreads) sel_entropy_kernel(const SelArgs a) {
   griddep_wait();
   griddep_launch_dependents();
@@ -307,36 +369,54 @@ __global__ void __launch_bounds__(kSelThreads) sel_entropy_kernel(const SelArgs 
   const int lo = c * a.chunk;
   const int hi = min(a.vocab, lo + a.chunk);
   const int tid = threadIdx.x;
-  const double amax = a.row_amax[r];
+  const float gm = static_cast<float>(a.row_amax[r]);
   const double S = a.row_sum[r];
   const int excl = a.exclude_dev != nullptr ? *a.exclude_dev : a.exclude;
-  const double inv_t = sel_inv_t(a.temperature);
-  const double inv_s = 1.0 / S;  // p = e / S taken as e * (1 / S): last-bit differences only
-  // The thread's columns as in sel_pass1_kernel (float4 groups lo + (k * kSelThreads + t) * 4),
-  // one group at a time. A -inf term (p = 0 in the reference, contributing 0 * log(1e-10) = 0) is
-  // clamped to exp(-708): its p log(p + 1e-10), about -7e-307, vanishes in any sum holding a real term.
+  constexpr double kLog2e = 1.4426950408889634074;
+  constexpr double kLog2Eps = -33.219280948873623479;  // log2(1e-10)
+  constexpr float kLn2 = 0.693147180559945309f;
+  const double s1 = sel_inv_t(a.temperature) * kLog2e;
+  const float s1h = static_cast<float>(s1), s1l = static_cast<float>(s1 - static_cast<double>(s1h));
+  const double c0 = -(log2(S) + kLog2Eps);
+  const float c0h = static_cast<float>(c0), c0l = static_cast<float>(c0 - static_cast<double>(c0h));
+  // The thread's columns as in sel_pass1_kernel (float4 groups lo + (k * kSelThreads + t) * 4).
   const bool vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
   double acc = 0.0;
+#pragma unroll 2
   for (int k = 0; k < kSelChunk / (kSelThreads * 4); ++k) {
     const int base = lo + (k * kSelThreads + tid) * 4;
     float v[4];
     if (vec && base + 4 <= hi) {
-      const float4 q = __ldcs(reinterpret_cast<const float4*>(x + base));
-      v[0] = q.x;
-      v[1] = q.y;
-      v[2] = q.z;
-      v[3] = q.w;
+      const float4 q4 = __ldcs(reinterpret_cast<const float4*>(x + base));
+      v[0] = q4.x;
+      v[1] = q4.y;
+      v[2] = q4.z;
+      v[3] = q4.w;
     } else {
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[e] = base + e < hi ? x[base + e] : -INFINITY;
     }
+    float g = 0.0f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float ve = base + e == excl ? -INFINITY : v[e];
-      const double ex = exp_nonpos_clamped(sel_adjust(static_cast<double>(ve), inv_t) - amax);
-      const double p = __dmul_rn(ex, inv_s);
-      acc = __dadd_rn(acc, __dmul_rn(p, log(__dadd_rn(p, 1e-10))));
+      const float dx = (base + e == excl ? -INFINITY : v[e]) - gm;
+      const float d = fmaf(dx, s1h, c0h) + fmaf(dx, s1l, c0l);
+      const float w = fmaxf(-fabsf(d), -200.0f);
+      const float q = ex2_approx(w);
+      const float rq = rcp_approx(2.0f + q);
+      const float sq = q * rq;
+      const float t = sq * sq;
+      float P = 1.0f / 15.0f;
+      P = fmaf(P, t, 1.0f / 13.0f);
+      P = fmaf(P, t, 1.0f / 11.0f);
+      P = fmaf(P, t, 1.0f / 9.0f);
+      P = fmaf(P, t, 1.0f / 7.0f);
+      P = fmaf(P, t, 1.0f / 5.0f);
+      P = fmaf(P, t, 1.0f / 3.0f);
+      P = fmaf(P, t, 1.0f);
+      g += d >= 0.0f ? 2.0f * rq * P : q * fmaf(2.0f * sq, P, -w * kLn2);
     }
+    acc += static_cast<double>(g);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -355,8 +435,9 @@ __global__ void __launch_bounds__(kSelThreads) sel_entropy_kernel(const SelArgs 
   __syncthreads();
   if (!s_last || tid != 0) return;
   __threadfence();
-  double H = 0.0;
-  for (int k = 0; k < a.nchunks; ++k) H += __ldcg(&a.part_sum[r * a.nchunks + k]);
+  double Ce = 0.0;
+  for (int k = 0; k < a.nchunks; ++k) Ce += __ldcg(&a.part_sum[r * a.nchunks + k]);
+  const double H = __ldcg(&a.part_ent[r * a.nchunks]) + 1e-10 * Ce;
   a.conf[r] = static_cast<double>(static_cast<float>(H));
   a.counters[r] = 0;
 }

@@ -350,7 +350,7 @@ int drt_select_choices(const double* conf, const int32_t* offsets, int32_t n_ite
  * memory: a host whose GPU memory is owned by its own pool or fixed budget (outside of which it
  * may not cudaMalloc), or a latency-critical caller that cannot afford cudaMalloc's implicit
  * synchronization. No counterpart in the reference. The scratch is one static device array of
- * about 0.53 MB that every GPU loading this library keeps until exit; calls are limited to
+ * about 0.81 MB that every GPU loading this library keeps until exit; calls are limited to
  * n_rows <= 1024 and vocab <= 262144 (larger calls fail with DRT_INVALID_ARGUMENT). The first call
  * in each CUDA context looks up the array's device address (cached under the context's id, so a
  * context made after cudaDeviceReset, or a second context on the same device, looks it up again),

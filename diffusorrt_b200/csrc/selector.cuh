@@ -174,6 +174,7 @@ __global__ void __launch_bounds__(kSelThreads, kSample ? 4 : 5) sel_pass1_kernel
   float m = -INFINITY;
 #pragma unroll
   for (int i = 0; i < 32; ++i) m = fmaxf(m, vals[i]);
+  const float own_max = m;
   __shared__ float s_m[kSelThreads / 32];
   __shared__ int s_i[kSelThreads / 32];
   __shared__ double s_s[kSelThreads / 32];
@@ -184,7 +185,7 @@ __global__ void __launch_bounds__(kSelThreads, kSample ? 4 : 5) sel_pass1_kernel
   float bm = s_m[0];
   for (int w = 1; w < kSelThreads / 32; ++w) bm = fmaxf(bm, s_m[w]);
   int idx = INT_MAX;
-  if (bm != -INFINITY) {
+  if (bm != -INFINITY && own_max == bm) {
 #pragma unroll
     for (int i = 31; i >= 0; --i)
       if (vals[i] == bm) idx = lo + ((i >> 2) * kSelThreads + tid) * 4 + (i & 3);
@@ -240,7 +241,10 @@ __global__ void __launch_bounds__(kSelThreads, kSample ? 4 : 5) sel_pass1_kernel
   double sum = 0.0;
   double ent = 0.0;  // kEntropy: sum e z, z = max(a - chunk max, -708) (a clamped term adds about -2e-305)
   if (bm != -INFINITY) {
-    if constexpr (kEntropy) {
+    if (!kEntropy && inv_t == 1.0) {  // no temperature (max-prob, sampled): a = x exactly
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sum += exp_nonpos_clamped(static_cast<double>(vals[i]) - amax);
+    } else if constexpr (kEntropy) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const double z = fmax(sel_adjust(static_cast<double>(vals[i]), inv_t) - amax, -708.0);

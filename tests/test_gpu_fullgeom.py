@@ -131,6 +131,46 @@ def test_dream_width_d2f_decode_window(dream2):
     assert np.all(logits[rows, np.asarray(tokens)] >= logits.max(axis=1) - 2 * E)
 
 
+def test_dream_width_d2f_decode_rounds(dream2):
+    """Six D2F proposals at the Dream width (three blocks of 8 after a 256-token prompt, two rounds
+    each). After the first, which prefills the prompt, every proposal is a decode forward of the
+    window (with the finished block before it on a block's first round) over the K/V cache: the
+    decode graph is sized for 64 rows, four query tiles of 18 positions at GQA 7:1, of which the
+    live rows fill one or two, each tile's keys split over a cluster. Each proposal's confidences
+    and tokens match the oracle forward of the same canvas within the stated bf16 tolerance
+    (|log conf_dev - log conf_oracle| <= 2 E, each token's oracle logit within 2 E of its row's
+    maximum, E = 48 u of the logit RMS)."""
+    rt, cfg, w = dream2
+    mask = cfg["mask_token_id"]
+    P, BS = 256, 8
+    x = _prompt(P, 12) + [mask] * 3 * BS
+    mode = {"decode_strategy": "block_threshold", "attention_mask_kind": "d2f_hybrid", "block_size": BS}
+    with rt.session(mode) as s:
+        s.start_device(x, prompt_len=P, block_size=BS, mask_token_id=mask, exact_kv=True, steps=8)
+        for lo in (P, P + BS, P + 2 * BS):
+            for rnd, frontier in enumerate((list(range(lo, lo + BS)), list(range(lo + BS // 2, lo + BS)))):
+                scores, tokens, fwd = s.propose_device(frontier, window_end=lo + BS, frozen_prefix=lo)
+                if lo == P and rnd == 0:
+                    assert fwd == P + BS + 1
+                elif rnd == 0:
+                    assert fwd == 2 * BS  # the finished block is recomputed with its final tokens
+                else:
+                    assert fwd == BS + 1
+                logits = ofwd.forward_mlx(w, cfg, x[:lo + BS], prompt_len=P, block_size=BS,
+                                          output_rows=ofwd.dream_raw_rows(frontier))
+                logits = osel.exclude_mask_token(logits, mask)
+                want_conf, _ = osel.max_prob_rows(logits)
+                finite = logits[np.isfinite(logits)]
+                E = MAX_FACTOR * U_BF16 * float(np.sqrt(np.mean(finite.astype(np.float64) ** 2)))
+                assert np.all(np.abs(np.log(np.asarray(scores)) - np.log(np.asarray(want_conf))) <= 2 * E), (lo, rnd)
+                rows = np.arange(len(frontier))
+                assert np.all(logits[rows, np.asarray(tokens)] >= logits.max(axis=1) - 2 * E), (lo, rnd)
+                take = BS // 2 if rnd == 0 else len(frontier)
+                s.commit_device(frontier[:take], tokens[:take])
+                for q, t in zip(frontier[:take], tokens[:take]):
+                    x[q] = t
+
+
 def test_dream_gqa7_entropy_count_along_trajectory(dream2):
     """Every step of the device's entropy_count decode (NegEntropy T 0.2 with top-p 0.95, MASK
     excluded, top-k by the f32 entropy) against the oracle on the device's canvas: each frontier

@@ -1858,7 +1858,8 @@ extern "C" int drt_session_open(drt_model* m, const drt_session_config* cfg, drt
   s->attn_splits = asp;
   s->attn_tps = (kv_tiles + asp - 1) / asp;
   // Decode attention: enough CTAs per KV head that each covers at most kDaMaxSub 64-key sub-tiles
-  // of the longest canvas, all CTAs resident at once (one per SM); otherwise the general kernel.
+  // of the longest canvas (one CTA per SM; without the cluster merge the CTAs wait on nothing, so a
+  // long canvas may take more than one wave); otherwise the general kernel.
   {
     const int n_sub = (s->max_seq + 63) / 64;  // sub-tiles of the longest canvas, the last one partial
     const int sp = (n_sub + kDaMaxSub - 1) / kDaMaxSub;
